@@ -1,0 +1,105 @@
+"""ctypes binding of libsrdit_b200.so.
+
+The library is the only compute path of this package: there is no CPU or
+PyTorch fallback. ``lib()`` raises if the shared object is missing or does not
+export every entry point of ``include/srdit_b200.h``; every call raises
+``SrditError`` on a non-zero return code.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = PKG / "lib" / "libsrdit_b200.so"
+HEADER = PKG.parent / "include" / "srdit_b200.h"
+
+SRDIT_EPI_STORE, SRDIT_EPI_GELU, SRDIT_EPI_GATED_RES, SRDIT_EPI_RES = 0, 1, 2, 3
+SRDIT_P_FRAME, SRDIT_P_PLAIN = 17, 19
+SRDIT_ANCHOR_NONE, SRDIT_ANCHOR_CHUNK, SRDIT_ANCHOR_FRAME = 0, 1, 2
+SRDIT_STATUS_TIMEOUT = 1
+
+c_int, c_ll, c_float, c_vp = ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_void_p
+
+
+class WinattnGeom(ctypes.Structure):
+    _fields_ = [("q_frames", c_int), ("q_h", c_int), ("q_w", c_int),
+                ("kv_h", c_int), ("kv_w", c_int), ("kv_slots", c_int), ("kv_slot0", c_int),
+                ("a_frames", c_int), ("a_h", c_int), ("a_w", c_int),
+                ("n_heads", c_int), ("head_dim", c_int),
+                ("q_stride", c_ll), ("kv_stride", c_ll), ("a_stride", c_ll),
+                ("o_stride", c_ll), ("scale", c_float)]
+
+
+class WinattnTiling(ctypes.Structure):
+    _fields_ = [("bw_q", c_int), ("bh_q", c_int), ("qboxes_per_tile", c_int),
+                ("m_tiles", c_int), ("bw_k", c_int), ("bh_k", c_int),
+                ("kboxes_per_tile", c_int), ("bw_a", c_int), ("bh_a", c_int),
+                ("aboxes_per_tile", c_int), ("has_anchor", c_int)]
+
+
+# name -> argtypes (every function returns int)
+SIGNATURES = {
+    "srdit_version": [],
+    "srdit_fp8_gemm": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
+                       c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp],
+    "srdit_quant_rowwise": [c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_vp],
+    "srdit_ln_mod_quant": [c_vp, c_ll, c_int, c_int, c_float, c_vp, c_vp, c_vp, c_vp, c_vp,
+                           c_ll, c_vp, c_vp],
+    "srdit_rms_rope": [c_vp, c_ll, c_int, c_int, c_vp, c_float, c_vp, c_ll, c_int, c_int,
+                       c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_ll,
+                       c_vp],
+    "srdit_winattn_plan": [c_vp, c_int, c_int, c_int, ctypes.POINTER(WinattnTiling)],
+    "srdit_winattn_fwd": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
+                          ctypes.POINTER(WinattnGeom), ctypes.POINTER(WinattnTiling), c_vp,
+                          c_vp],
+}
+
+
+class SrditError(RuntimeError):
+    pass
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Every entry point declared in include/srdit_b200.h."""
+    import re
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(srdit_\w+)\(", text, re.M)))
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the library; raise if it is absent or incomplete."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise SrditError(
+                f"{LIB_PATH} is missing: build it with `python {PKG / 'build.py'}` "
+                "(there is no fallback path).")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = argtypes
+            fn.restype = c_int
+        L.srdit_strerror.argtypes = [c_int]
+        L.srdit_strerror.restype = ctypes.c_char_p
+        _lib = L
+        return L
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().srdit_strerror(rc).decode()
+        raise SrditError(f"{what} failed with code {rc}: {msg}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)

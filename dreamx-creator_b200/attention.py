@@ -1,0 +1,251 @@
+"""Drop-in block-grid window attention on the B200 kernel.
+
+Two seams of the reference (video_refiner/wan/modules/sr_dit/attention.py):
+
+* ``run_blockgrid_b200`` has the signature of the reference's launcher
+  ``run_blockgrid_triton(q, k_ext, v_ext, out, *, plan, f_cur, h, w, n, d,
+  anchor_mode=None)`` (blockgrid_triton.py:392-422) and accepts the reference's
+  own plan dicts. ``install(attention_module)`` points the reference's
+  call-time-looked-up global ``_run_blockgrid_triton`` (attention.py:45-46) at it,
+  so an unmodified reference model running ``attn_impl="triton"`` launches the
+  B200 kernel.
+* ``mask_free_window_attention`` has the reference op's signature
+  (attention.py:1376-1395) and semantics -- validation, KV-cache concat and
+  tail truncation, per-sample loop -- with ``attn_impl="b200"``.
+
+Unsupported cases raise; nothing falls back to another backend.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib, blockgrid, ops
+
+BLOCKGRID_IMPLS = ("b200",)
+
+
+def check_rows(params: torch.Tensor, p_stride: int, *, f_cur, h, w, kv_frames, a_hw=None,
+               a_frames=0) -> None:
+    """Every cuboid a params row addresses lies inside its tensor.
+
+    The kernel addresses tokens straight from the rows, so this is the check that
+    keeps a malformed plan from turning into an out-of-bounds store.
+    """
+    p = params.to(torch.int64)
+    if p.dim() != 2 or p.shape[1] != p_stride:
+        raise ValueError(f"params rows must be [n_w, {p_stride}], got {tuple(p.shape)}")
+    if p_stride == blockgrid.P_FRAME:
+        q_t0, q_tL = torch.zeros_like(p[:, 0]), p[:, 10]
+        q_h0, q_w0, qhL, qwL, kv0, kvL, kh0, khL, kw0, kwL = (p[:, i] for i in range(10))
+        a_f = p[:, 10]
+        kh0a, khLa, kw0a, kwLa = p[:, 11], p[:, 12], p[:, 13], p[:, 14]
+    else:
+        (q_t0, q_tL, q_h0, q_w0, qhL, qwL, kv0, kvL, kh0, khL, kw0, kwL, a_f,
+         kh0a, khLa, kw0a, kwLa) = (p[:, i] for i in range(17))
+    ok = ((q_t0 >= 0) & (q_tL > 0) & (q_t0 + q_tL <= f_cur) & (q_h0 >= 0) & (qhL > 0)
+          & (q_h0 + qhL <= h) & (q_w0 >= 0) & (qwL > 0) & (q_w0 + qwL <= w)
+          & (kv0 >= 0) & (kvL > 0) & (kv0 + kvL <= kv_frames) & (kh0 >= 0) & (khL > 0)
+          & (kh0 + khL <= h) & (kw0 >= 0) & (kwL > 0) & (kw0 + kwL <= w))
+    if not bool(ok.all()):
+        raise ValueError("a window params row addresses tokens outside the q/KV grids")
+    if a_hw is not None:
+        has = a_f > 0
+        ok_a = (~has) | ((a_f <= a_frames) & (kh0a >= 0) & (khLa > 0) & (kh0a + khLa <= a_hw[0])
+                         & (kw0a >= 0) & (kwLa > 0) & (kw0a + kwLa <= a_hw[1]))
+        if not bool(ok_a.all()):
+            raise ValueError("a window params row addresses anchor tokens outside the anchor")
+
+
+def _plan_device_state(plan: dict, device: torch.device, anchor_mode, check_key, check_kw):
+    """Device params + kernel tiling, cached inside the plan dict per device; the
+    rows are bounds-checked once per (device, tensor geometry)."""
+    key = ("b200", device)
+    st = plan.get(key)
+    if st is None:
+        params = plan["params"]
+        if not torch.is_tensor(params):
+            params = torch.as_tensor(params)
+        params = params.to(torch.int32).contiguous().cpu()
+        mode = blockgrid.ANCHOR_MODES[anchor_mode]
+        tiling = ops.winattn_plan(params, int(plan["p_stride"]), mode)
+        st = plan[key] = (params.to(device), tiling, params.shape[0], mode, params, set())
+    if check_key not in st[5]:
+        check_rows(st[4], int(plan["p_stride"]), **check_kw)
+        st[5].add(check_key)
+    return st[:4]
+
+
+def _geom(q, k_hr, *, f_cur, h, w, n, d, kv_frames, kv_slot0=0, anchor=None, a_hw=None):
+    g = _lib.WinattnGeom()
+    g.q_frames, g.q_h, g.q_w = f_cur, h, w
+    g.kv_h, g.kv_w = h, w
+    g.kv_slots, g.kv_slot0 = kv_frames, kv_slot0
+    if anchor is not None:
+        g.a_h, g.a_w = a_hw
+        g.a_frames = anchor.shape[0] // (a_hw[0] * a_hw[1])
+        g.a_stride = anchor.stride(0)
+    g.n_heads, g.head_dim = n, d
+    g.q_stride = q.stride(0)
+    g.kv_stride = k_hr.stride(0)
+    g.o_stride = q.stride(0)
+    g.scale = d ** -0.5
+    return g
+
+
+def run_blockgrid_b200(q, k_ext, v_ext, out, *, plan, f_cur, h, w, n, d, anchor_mode=None,
+                       status=None):
+    """Launch the B200 kernel for one sample; writes ``out`` and returns it.
+
+    ``q``/``out``: [f_cur*h*w, n, d]; ``k_ext``/``v_ext``: ``cat([anchor, HR])``
+    when an anchor is present (HR starts at ``plan["hr_base"]``), else the HR
+    KV alone -- the layout the reference's launcher takes.
+    """
+    if d != 128:
+        raise _lib.SrditError(f"the B200 window kernel supports head_dim 128, got {d}")
+    for t in (q, k_ext, v_ext, out):
+        if not t.is_contiguous():
+            raise _lib.SrditError("q/k/v/out must be contiguous with a stride-1 head dim")
+    hr_base = int(plan.get("hr_base", f_cur * h * w if anchor_mode is not None else 0))
+    L = h * w
+    if q.numel() != f_cur * L * n * d or out.shape != q.shape:
+        raise ValueError("q/out must be [f_cur*h*w, n, d]")
+    qf, of = q.view(-1, n * d), out.view(-1, n * d)
+    kf, vf = k_ext.view(-1, n * d), v_ext.view(-1, n * d)
+    if kf.shape != vf.shape or kf.shape[0] < hr_base or (kf.shape[0] - hr_base) % L:
+        raise ValueError("k_ext/v_ext must hold the anchor prefix plus whole HR frames")
+    k_hr, v_hr = kf[hr_base:], vf[hr_base:]
+    kv_frames = k_hr.shape[0] // L
+    ka = va = None
+    a_hw = None
+    a_frames = 0
+    if anchor_mode is not None and hr_base > 0:
+        ka, va = kf[:hr_base], vf[:hr_base]
+        p0 = plan["params"][0]
+        a_hw = (int(p0[-2]), int(p0[-1]))
+        a_frames = hr_base // (a_hw[0] * a_hw[1])
+    params_dev, tiling, n_w, mode = _plan_device_state(
+        plan, q.device, anchor_mode, (f_cur, h, w, kv_frames, a_hw, a_frames),
+        dict(f_cur=f_cur, h=h, w=w, kv_frames=kv_frames, a_hw=a_hw, a_frames=a_frames))
+    g = _geom(qf, k_hr, f_cur=f_cur, h=h, w=w, n=n, d=d, kv_frames=kv_frames, anchor=ka, a_hw=a_hw)
+    g.o_stride = of.stride(0)
+    ops.winattn(qf, k_hr, v_hr, of, params_dev=params_dev, n_w=n_w,
+                p_stride=int(plan["p_stride"]), anchor_mode=mode, geom=g, tiling=tiling,
+                k_anchor=ka, v_anchor=va, status=status)
+    return out
+
+
+_PLAN_CACHE: dict = {}
+
+
+def cached_plan(spec: blockgrid.WindowSpec, anchor_mode=None) -> dict:
+    """Plan dict for ``spec`` (host rows + per-device kernel state), memoised."""
+    key = (spec, anchor_mode)
+    plan = _PLAN_CACHE.get(key)
+    if plan is None:
+        rows, stride, hr_base = blockgrid.plan_rows(spec, anchor_mode)
+        plan = _PLAN_CACHE[key] = {"params": rows, "n_w": rows.shape[0], "p_stride": stride,
+                                   "hr_base": hr_base}
+    return plan
+
+
+def install(attention_module) -> None:
+    """Route the reference's ``attn_impl="triton"`` launches to the B200 kernel.
+
+    ``attention_module`` is the reference's ``wan.modules.sr_dit.attention``;
+    its ``_run_blockgrid_triton`` global is looked up at call time
+    (attention.py:45-46), which is the seam swapped here.
+    """
+    attention_module._run_blockgrid_triton = run_blockgrid_b200
+
+
+def _truncate(full_k, full_v, kv_len, L, f_kv):
+    if kv_len is None or f_kv <= kv_len:
+        return full_k, full_v
+    keep = int(kv_len) * L
+    return full_k[-keep:], full_v[-keep:]
+
+
+def mask_free_window_attention(q, k, v, grid_sizes, pre_cache_k=None, pre_cache_v=None,
+                               kv_len=None, anchor_k=None, anchor_v=None, anchor_align="frame",
+                               anchor_window_scope="window", anchor_hw=None, anchor_keep=None,
+                               attn_impl="b200", win_chunk=None, causal_chunk_frames=None,
+                               causal_kv_span=None, block_t=None, block_hw=(4, 4),
+                               block_radius_hw=(2, 2), block_radius_t=None):
+    """The reference op (attention.py:1376-1648) on the B200 kernel.
+
+    Returns ``(out [b, s_cur, n, d], new_cache_k, new_cache_v)``.
+    """
+    if str(attn_impl) not in BLOCKGRID_IMPLS:
+        raise ValueError(f"attn_impl must be one of {BLOCKGRID_IMPLS}, got {attn_impl!r}.")
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad
+                                       for t in (q, k, v, anchor_k, anchor_v)):
+        raise RuntimeError("the B200 window kernel is forward-only; an input requires grad.")
+    b, s_cur, n, d = q.shape
+    anchor_given = anchor_k is not None or anchor_v is not None
+    if anchor_given and (anchor_k is None or anchor_v is None):
+        raise ValueError("mask_free_window_attention: anchor_k and anchor_v must be provided together.")
+    if anchor_given and anchor_align not in ("frame", "chunk"):
+        raise ValueError(f"anchor_align must be 'frame' or 'chunk', got {anchor_align!r}.")
+    if anchor_given and anchor_window_scope != "window":
+        raise ValueError("the B200 window kernel supports anchor_window_scope='window' only "
+                         "(one spatial extent per params row, as the fused reference kernel).")
+    outs, cks, cvs = [], [], []
+    for i in range(b):
+        f_cur, h, w = (int(x) for x in grid_sizes[i].tolist())
+        if f_cur * h * w != s_cur:
+            raise ValueError(f"grid {(f_cur, h, w)} inconsistent with s_cur={s_cur}")
+        L = h * w
+        if pre_cache_k is not None and pre_cache_v is not None:
+            full_k = torch.cat([pre_cache_k[i], k[i]], dim=0)
+            full_v = torch.cat([pre_cache_v[i], v[i]], dim=0)
+        else:
+            full_k, full_v = k[i], v[i]
+        f_kv = full_k.shape[0] // L
+        if f_kv * L != full_k.shape[0]:
+            raise ValueError("KV cache is not aligned to whole frames")
+        a_hw = None if anchor_hw is None or tuple(int(x) for x in anchor_hw) == (h, w) \
+            else (int(anchor_hw[0]), int(anchor_hw[1]))
+        use_anchor = anchor_given
+        if anchor_given:
+            s_h, s_w = blockgrid.anchor_stride(h, w, int(block_hw[0]), int(block_hw[1]), a_hw)
+            La = (h // s_h) * (w // s_w)
+            if anchor_k.shape[1] != f_cur * La:
+                raise ValueError(f"frame-aligned LQ-anchor needs {f_cur * La} tokens per sample, "
+                                 f"got {anchor_k.shape[1]}.")
+            if (causal_chunk_frames is not None and causal_kv_span is not None
+                    and pre_cache_k is None and pre_cache_v is None):
+                raise NotImplementedError("LQ-anchor in the parallel chunk-causal window path is "
+                                          "not supported.")
+            if anchor_keep is not None:
+                keep = anchor_keep.view(-1)[i] if torch.is_tensor(anchor_keep) else anchor_keep[i]
+                use_anchor = bool(keep)
+        bt = int(block_t if block_t is not None else causal_chunk_frames)
+        streaming = pre_cache_k is not None or pre_cache_v is not None or anchor_given
+        if block_radius_t is None and not streaming and f_cur % bt != 0 and f_cur >= bt:
+            raise ValueError(f"block-grid window attention needs f_cur ({f_cur}) to be a "
+                             f"multiple of block_t ({bt}).")
+        spec = blockgrid.make_spec(f_cur=f_cur, f_kv=f_kv, h=h, w=w, block_t=bt, block_hw=block_hw,
+                                   block_radius_hw=block_radius_hw,
+                                   block_radius_t=block_radius_t, streaming=streaming,
+                                   causal_chunk_frames=causal_chunk_frames,
+                                   causal_kv_span=causal_kv_span,
+                                   anchor_hw=a_hw if anchor_given else None)
+        mode = None if not use_anchor else ("frame" if anchor_align == "frame" else "chunk")
+        plan = cached_plan(spec, mode)
+        q_i = q[i].contiguous()
+        out_i = torch.empty_like(q_i)
+        if use_anchor:
+            k_ext = torch.cat([anchor_k[i], full_k], dim=0)
+            v_ext = torch.cat([anchor_v[i], full_v], dim=0)
+        else:
+            k_ext, v_ext = full_k.contiguous(), full_v.contiguous()
+        run_blockgrid_b200(q_i, k_ext, v_ext, out_i, plan=plan, f_cur=f_cur, h=h, w=w, n=n,
+                           d=d, anchor_mode=mode)
+        outs.append(out_i)
+        ck, cv = _truncate(full_k, full_v, kv_len, L, f_kv)
+        cks.append(ck)
+        cvs.append(cv)
+    out = torch.stack(outs, dim=0)
+    if b == 1:
+        return out, cks[0].unsqueeze(0), cvs[0].unsqueeze(0)
+    return out, torch.stack(cks, dim=0), torch.stack(cvs, dim=0)

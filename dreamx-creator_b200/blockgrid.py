@@ -1,0 +1,168 @@
+"""Block-grid window geometry -> int32 params rows for the window kernel.
+
+The visibility rule has to be the reference's exactly, so this module states the
+same rules (video_refiner/wan/modules/sr_dit/attention.py):
+  * spatial: query blocks tile each axis; block b sees blocks [b-r, b+r] clamped
+    to the grid, one contiguous interval (attention.py:244-290);
+  * temporal: the chunk-anchored ``hist`` rule or the legacy derived-``rt`` rule
+    (``_BlockGridSpec.temporal_runs``, attention.py:442-512);
+  * the anchor's own coarser grid (attention.py:293-328, 417-440);
+and emits rows in the reference's params layouts (blockgrid_triton.py:77-80),
+so a plan built here and a plan built by the reference's ``build_plan`` are
+interchangeable at the launcher seam. What differs is the kernel tiling: the
+B200 kernel packs whole (frame x rows x cols) boxes into 128-row tiles, which
+``srdit_winattn_plan`` derives from the same rows.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+P_FRAME, P_PLAIN = 17, 19
+ANCHOR_MODES = {None: 0, "chunk": 1, "frame": 2}
+
+
+def axis_extents(size: int, block: int, radius: int):
+    """[(q_start, q_len, kv_start, kv_len)] per block along one axis."""
+    n_blocks = -(-size // block)
+    spans = []
+    for b in range(n_blocks):
+        q_start = b * block
+        q_len = min(q_start + block, size) - q_start
+        first = max(b - radius, 0)
+        last = min(b + radius, n_blocks - 1)
+        kv_start = first * block
+        kv_len = min((last + 1) * block, size) - kv_start
+        spans.append((q_start, q_len, kv_start, kv_len))
+    return spans
+
+
+def anchor_stride(h, w, bh, bw, anchor_hw):
+    if anchor_hw is None:
+        return 1, 1
+    h_a, w_a = int(anchor_hw[0]), int(anchor_hw[1])
+    if h_a <= 0 or w_a <= 0:
+        raise ValueError(f"anchor_hw must be positive, got {(h_a, w_a)}.")
+    if h % h_a or w % w_a:
+        raise ValueError(f"anchor grid {(h_a, w_a)} must divide the query token grid {(h, w)}.")
+    s_h, s_w = h // h_a, w // w_a
+    if bh % s_h or bw % s_w:
+        raise ValueError(f"anchor stride {(s_h, s_w)} must divide the query block size {(bh, bw)}.")
+    return s_h, s_w
+
+
+@dataclass(frozen=True)
+class WindowSpec:
+    """One window geometry; the fields mean what ``_BlockGridSpec``'s do."""
+    f_cur: int
+    f_kv: int
+    h: int
+    w: int
+    block_t: int
+    bh: int
+    bw: int
+    rh: int
+    rw: int
+    hist: int | None = None
+    rt: int = 0
+    chunk_frames: int | None = None
+    streaming: bool = False
+    anchor_hw: tuple | None = None
+
+    @property
+    def single_query_run(self) -> bool:
+        return self.streaming or self.f_kv != self.f_cur
+
+    def frame_runs(self):
+        """[(q_f0, q_f1, kv_f0, kv_f1)] partitioning the query frames."""
+        f_cur, f_kv = self.f_cur, self.f_kv
+        if self.hist is not None:
+            cf = self.chunk_frames or max(1, f_cur)
+            if self.single_query_run or f_cur <= cf:
+                runs = [(0, f_cur, max(0, f_kv - f_cur - self.hist), f_kv)]
+            else:
+                runs = []
+                for c0 in range(0, f_cur, cf):
+                    c1 = min(c0 + cf, f_cur)
+                    runs.append((c0, c1, max(0, c0 - self.hist), min(f_kv, c1)))
+        else:
+            bt, rt = self.block_t, self.rt
+            if self.single_query_run:
+                runs = [(0, f_cur, max(0, f_kv - (rt + 1) * bt), f_kv)]
+            elif f_cur < bt:
+                runs = [(0, f_cur, 0, f_kv)]
+            else:
+                runs = [(i * bt, (i + 1) * bt, max(0, i - rt) * bt, (i + 1) * bt)
+                        for i in range(f_cur // bt)]
+        if sum(b - a for a, b, _, _ in runs) != f_cur or runs[0][0] != 0 or runs[-1][1] != f_cur:
+            raise ValueError(f"temporal runs {runs} do not partition the {f_cur} query frames; "
+                             f"block_t={self.block_t} must divide f_cur.")
+        return runs
+
+    def anchor_grid(self):
+        if self.anchor_hw is None:
+            return self.h, self.w
+        return int(self.anchor_hw[0]), int(self.anchor_hw[1])
+
+
+def make_spec(*, f_cur, f_kv, h, w, block_t, block_hw, block_radius_hw, block_radius_t=None,
+              streaming=False, causal_chunk_frames=None, causal_kv_span=None,
+              anchor_hw=None) -> WindowSpec:
+    """The spec the op derives from its arguments (attention.py:1559-1616)."""
+    bt = int(block_t)
+    if bt <= 0:
+        raise ValueError(f"block_t must be positive, got {bt}.")
+    hist = None if block_radius_t is None else (2 * int(block_radius_t) + 1) * bt
+    span = int(causal_kv_span) if causal_kv_span is not None else int(f_kv)
+    return WindowSpec(f_cur=int(f_cur), f_kv=int(f_kv), h=int(h), w=int(w), block_t=bt,
+                      bh=int(block_hw[0]), bw=int(block_hw[1]), rh=int(block_radius_hw[0]),
+                      rw=int(block_radius_hw[1]), hist=hist, rt=max(span // bt - 1, 0),
+                      chunk_frames=None if causal_chunk_frames is None else int(causal_chunk_frames),
+                      streaming=bool(streaming), anchor_hw=anchor_hw)
+
+
+def plan_rows(spec: WindowSpec, anchor_mode=None):
+    """Params rows in the reference layout: (int32 [n_w, P], p_stride, hr_base)."""
+    hb = axis_extents(spec.h, spec.bh, spec.rh)
+    wb = axis_extents(spec.w, spec.bw, spec.rw)
+    s_h, s_w = anchor_stride(spec.h, spec.w, spec.bh, spec.bw, spec.anchor_hw)
+    h_a, w_a = spec.anchor_grid()
+    runs = spec.frame_runs()
+    rows = []
+    if anchor_mode == "frame":
+        if len(runs) != 1 or runs[0][:2] != (0, spec.f_cur):
+            raise ValueError(f'anchor_mode="frame" needs one query run [0, {spec.f_cur}), got {runs}.')
+        kv0, kv1 = runs[0][2:]
+        for (qh0, qhL, kh0, khL) in hb:
+            for (qw0, qwL, kw0, kwL) in wb:
+                rows.append([qh0, qw0, qhL, qwL, kv0, kv1 - kv0, kh0, khL, kw0, kwL, spec.f_cur,
+                             kh0 // s_h, khL // s_h, kw0 // s_w, kwL // s_w, h_a, w_a])
+        stride = P_FRAME
+    elif anchor_mode in (None, "chunk"):
+        a_frames = spec.f_cur if anchor_mode == "chunk" else 0
+        for (q0, q1, kv0, kv1) in runs:
+            for (qh0, qhL, kh0, khL) in hb:
+                for (qw0, qwL, kw0, kwL) in wb:
+                    rows.append([q0, q1 - q0, qh0, qw0, qhL, qwL, kv0, kv1 - kv0, kh0, khL, kw0,
+                                 kwL, a_frames, kh0 // s_h, khL // s_h, kw0 // s_w, kwL // s_w,
+                                 h_a, w_a])
+        stride = P_PLAIN
+    else:
+        raise ValueError(f"anchor_mode must be None, 'chunk' or 'frame', got {anchor_mode!r}.")
+    hr_base = spec.f_cur * h_a * w_a if anchor_mode is not None else 0
+    return torch.tensor(rows, dtype=torch.int32), stride, hr_base
+
+
+def visible_flops(params: torch.Tensor, p_stride: int, n_heads: int, head_dim: int) -> int:
+    """4*d*heads*sum(Lq*Lkv) over visible query-key pairs (no tile padding)."""
+    p = params.tolist()
+    tot = 0
+    for r in p:
+        if p_stride == P_FRAME:
+            qhL, qwL, kvL, khL, kwL, fc, khLa, kwLa = r[2], r[3], r[5], r[7], r[9], r[10], r[12], r[14]
+            tot += fc * qhL * qwL * (kvL * khL * kwL + khLa * kwLa)
+        else:
+            qL, qhL, qwL, kvL, khL, kwL, af, khLa, kwLa = r[1], r[4], r[5], r[7], r[9], r[11], r[12], r[14], r[16]
+            tot += qL * qhL * qwL * (kvL * khL * kwL + af * khLa * kwLa)
+    return 4 * head_dim * n_heads * tot

@@ -1,0 +1,757 @@
+// winattn.cu -- block-grid window attention (sm_100a, tcgen05 + TMA).
+//
+// Computes, for every (window, query-tile, head), the softmax attention of the
+// window's query cuboid over its visible KV: an optional LQ-anchor prefix
+// ("chunk": every anchor frame visible to every query; "frame": query frame t
+// sees only anchor frame t) followed by the window's HR KV cuboid. This is the
+// computation of the reference's fused Triton kernels
+// (video_refiner/wan/modules/sr_dit/blockgrid_triton.py:184-278 plain/chunk and
+// :281-389 per-frame anchor), driven by the same int32 params rows
+// (blockgrid_triton.py:68-80), and follows their numerics: scores scaled by
+// d^-0.5 in fp32, natural-exp online softmax with the fully-masked-row guard
+// (:264-268), P rounded to bf16 before P.V, fp32 accumulation, final acc / l.
+//
+// B200 mapping (one CTA = 128 query rows x one head, 192 threads):
+//   warp 0     TMA producer: Q boxes once, then K and V boxes per KV tile
+//              (2-stage ring each). Each box is one frame x bh rows x bw
+//              columns of the token grid x 64 head dims, read in place from the
+//              token-major [frames, h, w, heads*128] tensor, so nothing is
+//              gathered and the KV cache is never concatenated.
+//   warp 1     tcgen05.mma issuer: S_j = Q.K_j^T into a double-buffered TMEM
+//              score tile, O += P_j.V_j into a TMEM accumulator.
+//   warps 2-5  softmax: one thread per query row. Reads S_j from TMEM, masks
+//              columns outside the window, updates (m, l), rescales O in TMEM
+//              when the row max moves, writes P_j (bf16, 128B-swizzled) to smem.
+//              At the end: O / l -> bf16 -> the row's token in `out`.
+#include "sm100.cuh"
+#include "srdit_internal.h"
+
+#include <cuda_bf16.h>
+
+namespace srdit {
+namespace attn {
+
+constexpr int D = 128;
+constexpr int TILE = 128;
+constexpr int SLAB = TILE * 128;  // 128 rows x 128 bytes (64 bf16 head dims)
+constexpr int QKV_TILE_BYTES = 2 * SLAB;
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + QKV_TILE_BYTES;
+constexpr int OFF_V = OFF_K + 2 * QKV_TILE_BYTES;
+constexpr int OFF_P = OFF_V + 2 * QKV_TILE_BYTES;
+constexpr int OFF_BAR = OFF_P + QKV_TILE_BYTES;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;  // S0 @0, S1 @128, O @256
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Args {
+  const int32_t* params;
+  int p_stride;
+  int frame_mode;  // 1: params rows use the per-frame-anchor layout
+  int n_w;
+  int m_tiles;
+  // geometry
+  int q_h, q_w;
+  int kv_slots, kv_slot0;
+  int n_heads;
+  // tiling
+  int bw_q, bh_q, qb_per_tile;
+  int bw_k, bh_k, kb_per_tile;
+  int bw_a, bh_a, ab_per_tile;
+  int has_anchor;
+  __nv_bfloat16* out;
+  long long o_stride;
+  float scale;
+  uint32_t* status;
+};
+
+struct Row {
+  int q_t0, q_tL, q_h0, q_w0, qhL, qwL;
+  int kv_t0, kv_tL, kh0, khL, kw0, kwL;
+  int a_frames, a_per_frame;
+  int kh0_a, khL_a, kw0_a, kwL_a;
+};
+
+SRDIT_DEV Row read_row(const int32_t* base, int w, int p_stride, int frame_mode) {
+  const int32_t* p = base + static_cast<size_t>(w) * p_stride;
+  Row r;
+  if (frame_mode) {
+    // q_h0 q_w0 qhL qwL kv_t0 kv_tL kh0 khL kw0 kwL f_cur kh0_a khL_a kw0_a kwL_a H_a W_a
+    r.q_t0 = 0;
+    r.q_h0 = __ldg(p + 0);
+    r.q_w0 = __ldg(p + 1);
+    r.qhL = __ldg(p + 2);
+    r.qwL = __ldg(p + 3);
+    r.kv_t0 = __ldg(p + 4);
+    r.kv_tL = __ldg(p + 5);
+    r.kh0 = __ldg(p + 6);
+    r.khL = __ldg(p + 7);
+    r.kw0 = __ldg(p + 8);
+    r.kwL = __ldg(p + 9);
+    r.q_tL = __ldg(p + 10);
+    r.a_frames = r.q_tL;
+    r.a_per_frame = 1;
+    r.kh0_a = __ldg(p + 11);
+    r.khL_a = __ldg(p + 12);
+    r.kw0_a = __ldg(p + 13);
+    r.kwL_a = __ldg(p + 14);
+  } else {
+    // q_t0 q_tL q_h0 q_w0 qhL qwL kv_t0 kv_tL kh0 khL kw0 kwL a_frames kh0_a khL_a kw0_a kwL_a H_a W_a
+    r.q_t0 = __ldg(p + 0);
+    r.q_tL = __ldg(p + 1);
+    r.q_h0 = __ldg(p + 2);
+    r.q_w0 = __ldg(p + 3);
+    r.qhL = __ldg(p + 4);
+    r.qwL = __ldg(p + 5);
+    r.kv_t0 = __ldg(p + 6);
+    r.kv_tL = __ldg(p + 7);
+    r.kh0 = __ldg(p + 8);
+    r.khL = __ldg(p + 9);
+    r.kw0 = __ldg(p + 10);
+    r.kwL = __ldg(p + 11);
+    r.a_frames = __ldg(p + 12);
+    r.a_per_frame = 0;
+    r.kh0_a = __ldg(p + 13);
+    r.khL_a = __ldg(p + 14);
+    r.kw0_a = __ldg(p + 15);
+    r.kwL_a = __ldg(p + 16);
+  }
+  return r;
+}
+
+// The KV walk of one CTA: anchor tiles (grouped per anchor frame, never mixing
+// frames) followed by HR tiles over (frame, h-chunk) boxes.
+struct Walk {
+  int qbox0, nqbox, hq_chunks;
+  int t_lo, t_hi;
+  int a_f0, a_nframes, a_hchunks, a_tpf;
+  int hr_hchunks, hr_boxes, hr_tiles;
+  int n_tiles;
+};
+
+SRDIT_DEV Walk make_walk(const Args& a, const Row& r, int mt) {
+  Walk w;
+  w.hq_chunks = (r.qhL + a.bh_q - 1) / a.bh_q;
+  const int q_boxes = r.q_tL * w.hq_chunks;
+  w.qbox0 = mt * a.qb_per_tile;
+  w.nqbox = min(a.qb_per_tile, q_boxes - w.qbox0);
+  w.t_lo = w.qbox0 / w.hq_chunks;
+  w.t_hi = (w.qbox0 + max(w.nqbox, 1) - 1) / w.hq_chunks;
+  if (a.has_anchor && r.a_frames > 0) {
+    w.a_hchunks = (r.khL_a + a.bh_a - 1) / a.bh_a;
+    w.a_tpf = (w.a_hchunks + a.ab_per_tile - 1) / a.ab_per_tile;
+    if (r.a_per_frame) {
+      w.a_f0 = w.t_lo;
+      w.a_nframes = w.t_hi - w.t_lo + 1;
+    } else {
+      w.a_f0 = 0;
+      w.a_nframes = r.a_frames;
+    }
+  } else {
+    w.a_hchunks = 0;
+    w.a_tpf = 0;
+    w.a_f0 = 0;
+    w.a_nframes = 0;
+  }
+  w.hr_hchunks = (r.khL + a.bh_k - 1) / a.bh_k;
+  w.hr_boxes = r.kv_tL * w.hr_hchunks;
+  w.hr_tiles = (w.hr_boxes + a.kb_per_tile - 1) / a.kb_per_tile;
+  w.n_tiles = w.a_nframes * w.a_tpf + w.hr_tiles;
+  return w;
+}
+
+struct TileInfo {
+  int anchor;      // 1: anchor segment
+  int frame;       // anchor frame (anchor tiles)
+  int box0, nbox;  // boxes [box0, box0 + nbox) of the segment walk
+  int bw, bh;      // box geometry
+  int rows;        // nbox * bw * bh
+  int n16;         // rows rounded up to 16 (MMA N / K extent)
+};
+
+SRDIT_DEV TileInfo tile_info(const Args& a, const Walk& w, int j) {
+  TileInfo t;
+  const int a_tiles = w.a_nframes * w.a_tpf;
+  if (j < a_tiles) {
+    const int fi = j / w.a_tpf, i = j % w.a_tpf;
+    t.anchor = 1;
+    t.frame = w.a_f0 + fi;
+    t.box0 = i * a.ab_per_tile;
+    t.nbox = min(a.ab_per_tile, w.a_hchunks - t.box0);
+    t.bw = a.bw_a;
+    t.bh = a.bh_a;
+  } else {
+    const int i = j - a_tiles;
+    t.anchor = 0;
+    t.frame = -1;
+    t.box0 = i * a.kb_per_tile;
+    t.nbox = min(a.kb_per_tile, w.hr_boxes - t.box0);
+    t.bw = a.bw_k;
+    t.bh = a.bh_k;
+  }
+  t.rows = t.nbox * t.bw * t.bh;
+  t.n16 = (t.rows + 15) & ~15;
+  return t;
+}
+
+SRDIT_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    winattn_kernel(const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV,
+                   const __grid_constant__ CUtensorMap tmKA,
+                   const __grid_constant__ CUtensorMap tmVA, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* o_full = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int win = blockIdx.x / a.m_tiles;
+  const int mt = blockIdx.x % a.m_tiles;
+  const int head = blockIdx.y;
+
+  const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
+  const Walk w = make_walk(a, r, mt);
+  if (w.nqbox <= 0) return;  // shorter windows skip their tail tiles (uniform grid)
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp >= 2) {
+    // Rows of the Q tile that no box fills, and every V row, start at zero: an
+    // unwritten row must never feed a NaN into the tensor core (P = 0 there,
+    // but 0 * NaN is NaN).
+    const int row = (warp & 3) * 32 + lane;
+    const int qrows = w.nqbox * a.bw_q * a.bh_q;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    if (row >= qrows) {
+      for (int h = 0; h < 2; ++h) {
+        uint4* dst = reinterpret_cast<uint4*>(smem + OFF_Q + h * SLAB + row * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) dst[c] = z;
+      }
+    }
+    for (int st = 0; st < 2; ++st)
+      for (int h = 0; h < 2; ++h) {
+        uint4* dst = reinterpret_cast<uint4*>(smem + OFF_V + st * QKV_TILE_BYTES + h * SLAB +
+                                              row * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) dst[c] = z;
+      }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int T = w.n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const uint32_t q_box_bytes = static_cast<uint32_t>(a.bw_q * a.bh_q * 128);
+      mbar_arrive_expect_tx(q_full, q_box_bytes * 2u * static_cast<uint32_t>(w.nqbox));
+      for (int qb = 0; qb < w.nqbox; ++qb) {
+        const int g = w.qbox0 + qb;
+        const int t = g / w.hq_chunks, hc = g % w.hq_chunks;
+        for (int h = 0; h < 2; ++h)
+          tma_load_4d(smem + OFF_Q + h * SLAB + qb * static_cast<int>(q_box_bytes), &tmQ, q_full,
+                      head * D + h * 64, r.q_w0, r.q_h0 + hc * a.bh_q, r.q_t0 + t);
+      }
+      bool ok = true;
+      int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
+      for (int j = 0; j < T && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
+        const TileInfo ti = tile_info(a, w, j);
+        const uint32_t box_bytes = static_cast<uint32_t>(ti.bw * ti.bh * 128);
+        const uint32_t bytes = box_bytes * 2u * static_cast<uint32_t>(ti.nbox);
+        for (int kv = 0; kv < 2 && ok; ++kv) {
+          uint64_t* emp = kv ? &v_empty[st] : &k_empty[st];
+          uint64_t* ful = kv ? &v_full[st] : &k_full[st];
+          if (!mbar_wait(emp, ph ^ 1u, a.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          (kv ? last_v : last_k)[st] = static_cast<int>(ph);
+          mbar_arrive_expect_tx(ful, bytes);
+          uint8_t* base = smem + (kv ? OFF_V : OFF_K) + st * QKV_TILE_BYTES;
+          for (int b = 0; b < ti.nbox; ++b) {
+            const int gb = ti.box0 + b;
+            int c1, c2, c3;
+            const CUtensorMap* map;
+            if (ti.anchor) {
+              c1 = r.kw0_a;
+              c2 = r.kh0_a + gb * ti.bh;
+              c3 = ti.frame;
+              map = kv ? &tmVA : &tmKA;
+            } else {
+              const int t = gb / w.hr_hchunks, hc = gb % w.hr_hchunks;
+              c1 = r.kw0;
+              c2 = r.kh0 + hc * ti.bh;
+              c3 = (a.kv_slot0 + r.kv_t0 + t) % a.kv_slots;
+              map = kv ? &tmV : &tmK;
+            }
+            for (int h = 0; h < 2; ++h)
+              tma_load_4d(base + h * SLAB + b * static_cast<int>(box_bytes), map, ful,
+                          head * D + h * 64, c1, c2, c3);
+          }
+        }
+      }
+      // Every load issued must land before the CTA can exit.
+      mbar_wait(q_full, 0, nullptr, nullptr);
+      for (int st = 0; st < 2; ++st) {
+        if (last_k[st] >= 0) mbar_wait(&k_full[st], static_cast<uint32_t>(last_k[st]), nullptr, nullptr);
+        if (last_v[st] >= 0) mbar_wait(&v_full[st], static_cast<uint32_t>(last_v[st]), nullptr, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      const uint32_t q_addr = smem_u32(smem + OFF_Q);
+      const uint32_t p_addr = smem_u32(smem + OFF_P);
+      // S_j = Q . K_j^T  (M=128, N=n16, K=128 over 8 steps of 16)
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
+        const TileInfo ti = tile_info(a, w, j);
+        if (!mbar_wait(&k_full[st], ph, a.status, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + OFF_K + st * QKV_TILE_BYTES);
+        const uint32_t idesc = idesc_make(1u, 1u, 0u, 0u, 128u, static_cast<uint32_t>(ti.n16));
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(st * 128);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = static_cast<uint32_t>((k >> 2) * SLAB + (k & 3) * 32);
+          mma_bf16_ss(d_tmem, sdesc_sw128(q_addr + off, 16, 1024),
+                      sdesc_sw128(k_addr + off, 16, 1024), idesc, k > 0 ? 1u : 0u);
+        }
+        tc_commit(&k_empty[st]);
+        tc_commit(&s_full[st]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, a.status, abort_flag);
+      tc_fence_after();
+      if (ok) ok = issue_s(0);
+      if (ok && T > 1) ok = issue_s(1);
+      for (int j = 0; j < T && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
+        const TileInfo ti = tile_info(a, w, j);
+        if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, a.status, abort_flag)) break;
+        if (!mbar_wait(&v_full[st], ph, a.status, abort_flag)) break;
+        tc_fence_after();
+        // O += P_j . V_j  (M=128, N=128 head dims, K=n16 over steps of 16)
+        const uint32_t v_addr = smem_u32(smem + OFF_V + st * QKV_TILE_BYTES);
+        const uint32_t idesc = idesc_make(1u, 1u, 0u, 1u, 128u, 128u);
+        const int ksteps = ti.n16 / 16;
+        for (int k = 0; k < ksteps; ++k) {
+          const uint32_t poff = static_cast<uint32_t>((k >> 2) * SLAB + (k & 3) * 32);
+          const uint32_t voff = static_cast<uint32_t>(k * 16 * 128);
+          mma_bf16_ss(tmem_base + 256u, sdesc_sw128(p_addr + poff, 16, 1024),
+                      sdesc_sw128(v_addr + voff, SLAB, 1024), idesc,
+                      (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(&v_empty[st]);
+        tc_commit(o_full);
+        if (j + 2 < T) ok = issue_s(j + 2);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(sub * 32) << 16;
+    // this row's query token
+    const int rq = a.bw_q * a.bh_q;
+    const int qb = row / rq, rr = row % rq;
+    const int g = w.qbox0 + qb;
+    const int t_row = g / w.hq_chunks;
+    const int hh = (g % w.hq_chunks) * a.bh_q + rr / a.bw_q;
+    const int ww = rr % a.bw_q;
+    const bool row_ok = qb < w.nqbox && t_row < r.q_tL && hh < r.qhL && ww < r.qwL;
+    const float neg_inf = -__int_as_float(0x7f800000);
+    float m_i = neg_inf, l_i = 0.f;
+    bool ok = true;
+    uint8_t* prow = smem + OFF_P + row * 128;
+    const int sw = row & 7;
+
+    for (int j = 0; j < T && ok; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
+      const TileInfo ti = tile_info(a, w, j);
+      // column validity bitmask, 4 words, computed per warp by ballot
+      uint32_t vmask[4];
+      const int seg_khL = ti.anchor ? r.khL_a : r.khL;
+      const int seg_kwL = ti.anchor ? r.kwL_a : r.kwL;
+      const int hchunks = ti.anchor ? w.a_hchunks : w.hr_hchunks;
+      const int box_rows = ti.bw * ti.bh;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int c = q * 32 + lane;
+        const int bi = c / box_rows, cr = c % box_rows;
+        const int hc = (ti.box0 + bi) % hchunks;
+        const bool v = (c < ti.rows) && (hc * ti.bh + cr / ti.bw < seg_khL) &&
+                       (cr % ti.bw < seg_kwL);
+        vmask[q] = __ballot_sync(0xffffffffu, v);
+      }
+      const bool row_sees = !(ti.anchor && r.a_per_frame) || (t_row == ti.frame);
+
+      if (!mbar_wait(&s_full[st], ph, a.status, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // scores -> registers
+      float s[128];
+      const uint32_t s_tmem = tmem_base + t_lane + static_cast<uint32_t>(st * 128);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t u[32];
+        tmem_ld32(s_tmem + q * 32, u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const bool v = row_sees && ((vmask[q] >> i) & 1u);
+          s[q * 32 + i] = v ? __fmul_rn(__uint_as_float(u[i]), a.scale) : neg_inf;
+        }
+      }
+      float row_max = neg_inf;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) row_max = fmaxf(row_max, s[c]);
+      const bool row_valid = row_max != neg_inf;
+      const float m_new = row_valid ? fmaxf(m_i, row_max) : m_i;
+      const float alpha = row_valid ? ex2_approx(__fmul_rn(__fsub_rn(m_i, m_new), kLog2e)) : 1.f;
+      float psum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float pv = (row_valid && s[c] != neg_inf)
+                             ? ex2_approx(__fmul_rn(__fsub_rn(s[c], m_new), kLog2e))
+                             : 0.f;
+        s[c] = pv;
+        psum = __fadd_rn(psum, pv);
+      }
+      l_i = __fadd_rn(__fmul_rn(alpha, l_i), psum);
+      m_i = m_new;
+
+      // PV_{j-1} must be complete before O is rescaled and P is overwritten.
+      if (j > 0) {
+        if (!mbar_wait(o_full, static_cast<uint32_t>(j - 1) & 1u, a.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+          const uint32_t o_tmem = tmem_base + t_lane + 256u;
+#pragma unroll 1
+          for (int q = 0; q < 4; ++q) {
+            uint32_t u[32];
+            tmem_ld32(o_tmem + q * 32, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__fmul_rn(__uint_as_float(u[i]), alpha));
+            tmem_st32(o_tmem + q * 32, u);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P_j (bf16) -> smem, K-major 128B-swizzled, 2 slabs of 64 columns
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        uint4 pk;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(s[q * 8 + 2 * h], s[q * 8 + 2 * h + 1]);
+          pw[h] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        const int slab = q >> 3, chunk = (q & 7) ^ sw;
+        *reinterpret_cast<uint4*>(prow + slab * SLAB + chunk * 16) = pk;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+
+    if (ok && T > 0 && mbar_wait(o_full, static_cast<uint32_t>(T - 1) & 1u, a.status, abort_flag)) {
+      tc_fence_after();
+      const uint32_t o_tmem = tmem_base + t_lane + 256u;
+      const long long tok = static_cast<long long>(r.q_t0 + t_row) * a.q_h * a.q_w +
+                            static_cast<long long>(r.q_h0 + hh) * a.q_w + (r.q_w0 + ww);
+      __nv_bfloat16* orow = a.out + tok * a.o_stride + head * D;
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        uint32_t u[32];
+        tmem_ld32(o_tmem + q * 32, u);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint4 pk;
+            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const float o0 = __fdiv_rn(__uint_as_float(u[v4 * 8 + 2 * h]), l_i);
+              const float o1 = __fdiv_rn(__uint_as_float(u[v4 * 8 + 2 * h + 1]), l_i);
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(o0, o1);
+              pw[h] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            *reinterpret_cast<uint4*>(orow + q * 32 + v4 * 8) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace attn
+}  // namespace srdit
+
+using namespace srdit;
+
+namespace {
+
+int pick_box(int bw_max, int bh_max, int* bw_out, int* bh_out, int* per_tile_out) {
+  // Box = one frame x bh rows x bw columns. Rows per box must be a multiple of
+  // 8 (whole 1024-byte swizzle atoms) and at most 128; a tile packs as many
+  // boxes as fit in 128 rows. Prefer the most rows per tile, then taller boxes.
+  if (bw_max <= 0 || bh_max <= 0) return SRDIT_EINVAL;
+  for (int bw = bw_max; bw <= 128; ++bw) {
+    int best_rows = 0, best_bh = 0, best_n = 0;
+    for (int bh = 1; bh <= bh_max && bw * bh <= 128; ++bh) {
+      if ((bw * bh) % 8) continue;
+      const int n = 128 / (bw * bh);
+      const int rows = n * bw * bh;
+      if (rows > best_rows || (rows == best_rows && bh > best_bh)) {
+        best_rows = rows;
+        best_bh = bh;
+        best_n = n;
+      }
+    }
+    if (best_rows > 0) {
+      *bw_out = bw;
+      *bh_out = best_bh;
+      *per_tile_out = best_n;
+      return 0;
+    }
+    if (bh_max >= 8 && bw * 8 > 128) break;  // nothing taller can fit either
+  }
+  return SRDIT_EUNSUPPORTED;
+}
+
+struct RowHost {
+  int q_tL, qhL, qwL, khL, kwL, a_frames, khL_a, kwL_a;
+};
+
+RowHost read_row_host(const int32_t* p, int frame_mode) {
+  RowHost r;
+  if (frame_mode) {
+    r.qhL = p[2];
+    r.qwL = p[3];
+    r.khL = p[7];
+    r.kwL = p[9];
+    r.q_tL = p[10];
+    r.a_frames = p[10];
+    r.khL_a = p[12];
+    r.kwL_a = p[14];
+  } else {
+    r.q_tL = p[1];
+    r.qhL = p[4];
+    r.qwL = p[5];
+    r.khL = p[9];
+    r.kwL = p[11];
+    r.a_frames = p[12];
+    r.khL_a = p[14];
+    r.kwL_a = p[16];
+  }
+  return r;
+}
+
+}  // namespace
+
+extern "C" int srdit_winattn_plan(const int32_t* params_host, int n_w, int p_stride,
+                                  int anchor_mode, srdit_winattn_tiling* out) {
+  if (!params_host || !out || n_w <= 0) return SRDIT_EINVAL;
+  const int frame_mode = (anchor_mode == SRDIT_ANCHOR_FRAME);
+  if (p_stride != (frame_mode ? SRDIT_P_FRAME : SRDIT_P_PLAIN)) return SRDIT_EINVAL;
+  int qh = 0, qw = 0, kh = 0, kw = 0, ah = 0, aw = 0, anyA = 0;
+  for (int i = 0; i < n_w; ++i) {
+    const RowHost r = read_row_host(params_host + static_cast<size_t>(i) * p_stride, frame_mode);
+    if (r.q_tL <= 0 || r.qhL <= 0 || r.qwL <= 0 || r.khL <= 0 || r.kwL <= 0) return SRDIT_EINVAL;
+    qh = r.qhL > qh ? r.qhL : qh;
+    qw = r.qwL > qw ? r.qwL : qw;
+    kh = r.khL > kh ? r.khL : kh;
+    kw = r.kwL > kw ? r.kwL : kw;
+    if (anchor_mode != SRDIT_ANCHOR_NONE && r.a_frames > 0) {
+      anyA = 1;
+      ah = r.khL_a > ah ? r.khL_a : ah;
+      aw = r.kwL_a > aw ? r.kwL_a : aw;
+    }
+  }
+  int rc = pick_box(qw, qh, &out->bw_q, &out->bh_q, &out->qboxes_per_tile);
+  if (rc) return rc;
+  rc = pick_box(kw, kh, &out->bw_k, &out->bh_k, &out->kboxes_per_tile);
+  if (rc) return rc;
+  if (anyA) {
+    rc = pick_box(aw, ah, &out->bw_a, &out->bh_a, &out->aboxes_per_tile);
+    if (rc) return rc;
+  } else {
+    out->bw_a = out->bw_k;
+    out->bh_a = out->bh_k;
+    out->aboxes_per_tile = out->kboxes_per_tile;
+  }
+  int m_tiles = 1;
+  for (int i = 0; i < n_w; ++i) {
+    const RowHost r = read_row_host(params_host + static_cast<size_t>(i) * p_stride, frame_mode);
+    const int boxes = r.q_tL * ((r.qhL + out->bh_q - 1) / out->bh_q);
+    const int mt = (boxes + out->qboxes_per_tile - 1) / out->qboxes_per_tile;
+    m_tiles = mt > m_tiles ? mt : m_tiles;
+  }
+  out->m_tiles = m_tiles;
+  out->has_anchor = anyA;
+  return 0;
+}
+
+extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_hr,
+                                 const void* k_anchor, const void* v_anchor, void* out,
+                                 const int32_t* params_dev, int n_w, int p_stride,
+                                 int anchor_mode, const srdit_winattn_geom* g,
+                                 const srdit_winattn_tiling* t, uint32_t* status,
+                                 cudaStream_t stream) {
+  if (!q || !k_hr || !v_hr || !out || !params_dev || !g || !t) return SRDIT_EINVAL;
+  if (n_w <= 0) return 0;
+  if (g->head_dim != attn::D || g->n_heads <= 0) return SRDIT_EUNSUPPORTED;
+  const int frame_mode = (anchor_mode == SRDIT_ANCHOR_FRAME);
+  if (p_stride != (frame_mode ? SRDIT_P_FRAME : SRDIT_P_PLAIN)) return SRDIT_EINVAL;
+  if (t->has_anchor && (!k_anchor || !v_anchor || g->a_frames <= 0)) return SRDIT_EINVAL;
+  if (g->kv_slots <= 0 || g->kv_slot0 < 0) return SRDIT_EINVAL;
+  if (g->q_frames <= 0 || g->q_h <= 0 || g->q_w <= 0 || g->kv_h <= 0 || g->kv_w <= 0)
+    return SRDIT_EINVAL;
+  // a TMA box never exceeds the tensor it reads
+  if (t->bw_q > g->q_w || t->bh_q > g->q_h || t->bw_k > g->kv_w || t->bh_k > g->kv_h)
+    return SRDIT_EUNSUPPORTED;
+  if (t->has_anchor && (t->bw_a > g->a_w || t->bh_a > g->a_h)) return SRDIT_EUNSUPPORTED;
+  if (t->m_tiles <= 0 || t->qboxes_per_tile <= 0 || t->kboxes_per_tile <= 0 ||
+      t->aboxes_per_tile <= 0 || t->bw_q * t->bh_q * t->qboxes_per_tile > 128 ||
+      t->bw_k * t->bh_k * t->kboxes_per_tile > 128 || t->bw_a * t->bh_a * t->aboxes_per_tile > 128 ||
+      (t->bw_q * t->bh_q) % 8 || (t->bw_k * t->bh_k) % 8 || (t->bw_a * t->bh_a) % 8)
+    return SRDIT_EINVAL;
+
+  const long long C = static_cast<long long>(g->n_heads) * attn::D;
+  CUtensorMap mq, mk, mv, mka, mva;
+  {
+    const long long dims[4] = {C, g->q_w, g->q_h, g->q_frames};
+    const long long st[3] = {g->q_stride * 2, g->q_stride * 2 * g->q_w,
+                             g->q_stride * 2 * g->q_w * g->q_h};
+    const int box[4] = {64, t->bw_q, t->bh_q, 1};
+    int rc = make_tmap_4d(&mq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, st, box);
+    if (rc) return rc;
+  }
+  {
+    const long long dims[4] = {C, g->kv_w, g->kv_h, g->kv_slots};
+    const long long st[3] = {g->kv_stride * 2, g->kv_stride * 2 * g->kv_w,
+                             g->kv_stride * 2 * g->kv_w * g->kv_h};
+    const int box[4] = {64, t->bw_k, t->bh_k, 1};
+    int rc = make_tmap_4d(&mk, k_hr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, st, box);
+    if (rc) return rc;
+    rc = make_tmap_4d(&mv, v_hr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, st, box);
+    if (rc) return rc;
+  }
+  if (t->has_anchor) {
+    const long long dims[4] = {C, g->a_w, g->a_h, g->a_frames};
+    const long long st[3] = {g->a_stride * 2, g->a_stride * 2 * g->a_w,
+                             g->a_stride * 2 * g->a_w * g->a_h};
+    const int box[4] = {64, t->bw_a, t->bh_a, 1};
+    int rc = make_tmap_4d(&mka, k_anchor, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, st, box);
+    if (rc) return rc;
+    rc = make_tmap_4d(&mva, v_anchor, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, st, box);
+    if (rc) return rc;
+  } else {
+    mka = mk;
+    mva = mv;
+  }
+
+  attn::Args a;
+  a.params = params_dev;
+  a.p_stride = p_stride;
+  a.frame_mode = frame_mode;
+  a.n_w = n_w;
+  a.m_tiles = t->m_tiles;
+  a.q_h = g->q_h;
+  a.q_w = g->q_w;
+  a.kv_slots = g->kv_slots;
+  a.kv_slot0 = g->kv_slot0;
+  a.n_heads = g->n_heads;
+  a.bw_q = t->bw_q;
+  a.bh_q = t->bh_q;
+  a.qb_per_tile = t->qboxes_per_tile;
+  a.bw_k = t->bw_k;
+  a.bh_k = t->bh_k;
+  a.kb_per_tile = t->kboxes_per_tile;
+  a.bw_a = t->bw_a;
+  a.bh_a = t->bh_a;
+  a.ab_per_tile = t->aboxes_per_tile;
+  a.has_anchor = t->has_anchor;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_stride = g->o_stride;
+  a.scale = g->scale;
+  a.status = status;
+
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_done[kMaxDevices] = {};
+  if (dev < kMaxDevices && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn::winattn_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         attn::SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_done[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>(n_w * t->m_tiles), static_cast<unsigned>(g->n_heads));
+  attn::winattn_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(mq, mk, mv, mka,
+                                                                               mva, a);
+  return static_cast<int>(cudaGetLastError());
+}

@@ -1,0 +1,139 @@
+"""Tensor-level wrappers over the C ABI (torch tensors in, device pointers out).
+
+Each function validates dtype / device / layout, then calls exactly one entry
+point of libsrdit_b200.so on the current CUDA stream. Nothing here computes:
+there is no fallback when the library or a GPU is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+EPILOGUES = {"store": _lib.SRDIT_EPI_STORE, "gelu": _lib.SRDIT_EPI_GELU,
+             "gated_res": _lib.SRDIT_EPI_GATED_RES, "res": _lib.SRDIT_EPI_RES}
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device=None):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise _lib.SrditError("the B200 kernels need CUDA tensors (there is no CPU path)")
+
+
+def _rows(t: torch.Tensor):
+    """(row stride in elements) of a 2-D row-major view with unit inner stride."""
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise _lib.SrditError(f"expected a 2-D row-major tensor, got shape {tuple(t.shape)} "
+                              f"strides {t.stride()}")
+    return t.stride(0)
+
+
+def fp8_gemm(a_fp8, a_scale, w_fp8, w_scale, bias=None, out=None, *, epilogue="store",
+             residual=None, gate=None, row_amax=None, status=None):
+    """out[M,N] = epilogue(a_fp8 @ w_fp8^T * a_scale[:,None] * w_scale[None,:] + bias)."""
+    _need_cuda(a_fp8, a_scale, w_fp8, w_scale, bias, out, residual, gate, row_amax)
+    if a_fp8.dtype != torch.float8_e4m3fn or w_fp8.dtype != torch.float8_e4m3fn:
+        raise _lib.SrditError("fp8_gemm operands must be float8_e4m3fn")
+    M, K = a_fp8.shape
+    N, K2 = w_fp8.shape
+    if K != K2:
+        raise _lib.SrditError(f"K mismatch {K} vs {K2}")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a_fp8.device)
+    for t, nm in ((a_scale, "a_scale"), (w_scale, "w_scale"), (gate, "gate"),
+                  (row_amax, "row_amax")):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
+            raise _lib.SrditError(f"{nm} must be contiguous float32")
+    if bias is not None and (bias.dtype != torch.bfloat16 or not bias.is_contiguous()):
+        raise _lib.SrditError("bias must be contiguous bf16")
+    ldr = _rows(residual) if residual is not None else 0
+    _lib.call("srdit_fp8_gemm", _ptr(a_fp8), _ptr(a_scale), _ptr(w_fp8), _ptr(w_scale),
+              _ptr(bias), _ptr(out), M, N, K, _rows(a_fp8), _rows(w_fp8), _rows(out),
+              EPILOGUES[epilogue], _ptr(residual), ldr, _ptr(gate), _ptr(row_amax),
+              _ptr(status), _stream(a_fp8.device))
+    return out
+
+
+def quant_rowwise(x, amax=None, q=None, scale=None):
+    """(e4m3 [M,K], fp32 scale [M]) of a bf16 [M,K] matrix (fp8_linear.py:93-103)."""
+    _need_cuda(x, amax, q, scale)
+    if x.dtype != torch.bfloat16:
+        raise _lib.SrditError("quant_rowwise takes bf16")
+    M, K = x.shape
+    if q is None:
+        q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    if scale is None:
+        scale = torch.empty(M, dtype=torch.float32, device=x.device)
+    _lib.call("srdit_quant_rowwise", _ptr(x), _rows(x), M, K, _ptr(amax), _ptr(q), _rows(q),
+              _ptr(scale), _stream(x.device))
+    return q, scale
+
+
+def ln_mod_quant(x, eps=1e-6, *, ln_weight=None, ln_bias=None, shift=None, scale=None,
+                 q=None, qscale=None):
+    """LayerNorm (+affine) -> bf16 -> adaLN modulate -> row-wise e4m3."""
+    _need_cuda(x, ln_weight, ln_bias, shift, scale, q, qscale)
+    if x.dtype != torch.bfloat16:
+        raise _lib.SrditError("ln_mod_quant takes bf16")
+    M, K = x.shape
+    if q is None:
+        q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    if qscale is None:
+        qscale = torch.empty(M, dtype=torch.float32, device=x.device)
+    _lib.call("srdit_ln_mod_quant", _ptr(x), _rows(x), M, K, float(eps), _ptr(ln_weight),
+              _ptr(ln_bias), _ptr(shift), _ptr(scale), _ptr(q), _rows(q), _ptr(qscale),
+              _stream(x.device))
+    return q, qscale
+
+
+def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, cos=None,
+             sin=None, grid_h=0, grid_w=0, t_offset=0, v_src=None, v_dst=None):
+    """RMSNorm(src) * weight [-> 3-D RoPE] -> dst frame slots (+ V copy)."""
+    _need_cuda(src, weight, dst, cos, sin, v_src, v_dst)
+    M, K = src.shape
+    if cos is not None and (cos.dtype != torch.float64 or sin.dtype != torch.float64
+                            or cos.shape != sin.shape or cos.shape[1] != 64
+                            or not cos.is_contiguous() or not sin.is_contiguous()):
+        raise _lib.SrditError("RoPE tables must be contiguous float64 [rows, 64]")
+    tab_rows = cos.shape[0] if cos is not None else 0
+    _lib.call("srdit_rms_rope", _ptr(src), _rows(src), M, K, _ptr(weight), float(eps),
+              _ptr(dst), _rows(dst), int(frame_tokens), int(slot0), int(n_slots), _ptr(cos),
+              _ptr(sin), int(tab_rows), int(grid_h), int(grid_w), int(t_offset), _ptr(v_src),
+              _rows(v_src) if v_src is not None else 0, _ptr(v_dst),
+              _rows(v_dst) if v_dst is not None else 0, _stream(src.device))
+    return dst
+
+
+def winattn_plan(params_host: torch.Tensor, p_stride: int, anchor_mode: int):
+    """Tiling of a window plan (int32 [n_w, p_stride] rows on the host)."""
+    p = params_host.contiguous()
+    if p.dtype != torch.int32 or p.device.type != "cpu":
+        raise _lib.SrditError("params rows must be a CPU int32 tensor")
+    t = _lib.WinattnTiling()
+    _lib.call("srdit_winattn_plan", ctypes.c_void_p(p.data_ptr()), p.shape[0], int(p_stride),
+              int(anchor_mode), ctypes.byref(t))
+    return t
+
+
+def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom, tiling,
+            k_anchor=None, v_anchor=None, status=None):
+    """One window-attention launch (see include/srdit_b200.h, srdit_winattn_fwd)."""
+    _need_cuda(q, k_hr, v_hr, out, params_dev, k_anchor, v_anchor)
+    for t in (q, k_hr, v_hr, out, k_anchor, v_anchor):
+        if t is not None and t.dtype != torch.bfloat16:
+            raise _lib.SrditError("window attention takes bf16 q/k/v")
+    _lib.call("srdit_winattn_fwd", _ptr(q), _ptr(k_hr), _ptr(v_hr), _ptr(k_anchor),
+              _ptr(v_anchor), _ptr(out), _ptr(params_dev), int(n_w), int(p_stride),
+              int(anchor_mode), ctypes.byref(geom), ctypes.byref(tiling), _ptr(status),
+              _stream(q.device))
+    return out

@@ -1,0 +1,240 @@
+"""Parity of the sm_100a kernels with the CPU oracle (GPU required)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import blockgrid as obg
+from oracle import numerics as onum
+from oracle import winattn as owa
+from tests.golden_cases import config1_inputs, stream_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16_bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy()
+
+
+# --------------------------------------------------------------------------- quantiser
+@pytest.mark.parametrize("M,K", [(64, 512), (300, 3072), (7, 14336)])
+def test_quant_rowwise_bit_exact(srdit, cuda_device, M, K):
+    g = torch.Generator().manual_seed(M + K)
+    x = torch.randn(M, K, generator=g)
+    x = torch.where(torch.rand(M, K, generator=g) < 1e-3, x * 20, x).to(torch.bfloat16)
+    x[M // 2] = 0
+    q, s = srdit.ops.quant_rowwise(x.to(cuda_device))
+    qo, so = onum.quantize_rowwise(x)
+    np.testing.assert_array_equal(q.view(torch.uint8).cpu().numpy(), qo.view(torch.uint8).numpy())
+    np.testing.assert_array_equal(s.cpu().numpy(), so.reshape(-1).numpy())
+    # with a precomputed amax the single-pass path gives the same bytes
+    amax = x.float().abs().amax(-1).to(cuda_device)
+    q2, s2 = srdit.ops.quant_rowwise(x.to(cuda_device), amax=amax)
+    assert torch.equal(q2.view(torch.uint8), q.view(torch.uint8)) and torch.equal(s2, s)
+
+
+@pytest.mark.parametrize("affine,modulate", [(False, True), (True, False), (False, False)])
+def test_ln_mod_quant(srdit, cuda_device, affine, modulate):
+    M, K = 200, 3072
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(M, K, generator=g) * 2 + 0.3).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16) if affine else None
+    b = (0.1 * torch.randn(K, generator=g)).to(torch.bfloat16) if affine else None
+    shift = (0.1 * torch.randn(K, generator=g)) if modulate else None
+    scale = (0.1 * torch.randn(K, generator=g)) if modulate else None
+    dev = lambda t: None if t is None else t.to(cuda_device)  # noqa: E731
+    q, qs = srdit.ops.ln_mod_quant(dev(x), 1e-6, ln_weight=dev(w), ln_bias=dev(b),
+                                   shift=dev(shift), scale=dev(scale))
+    n = onum.layer_norm(x, 1e-6, w, b)
+    if modulate:
+        n = (n.float() * (1 + scale) + shift).to(torch.bfloat16)
+    qo, so = onum.quantize_rowwise(n)
+    # LayerNorm statistics are reduced in a different order than torch's: allow
+    # the rare bf16 tie to round the other way, nothing more.
+    deq = q.float().cpu() * qs.cpu()[:, None]
+    deq_o = qo.float() * so
+    assert onum.rel_fro(deq, deq_o) < 2e-3
+    assert (q.view(torch.uint8).cpu() == qo.view(torch.uint8)).float().mean() > 0.995
+    np.testing.assert_allclose(qs.cpu().numpy(), so.reshape(-1).numpy(), rtol=1e-2)
+
+
+def test_rms_rope_matches_reference_math(srdit, cuda_device):
+    f, h, w, n = 2, 5, 7, 24
+    K = n * 128
+    M = f * h * w
+    g = torch.Generator().manual_seed(9)
+    src = torch.randn(M, 3 * K, generator=g).to(torch.bfloat16)   # fused [q | k | v] rows
+    wq = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
+    freqs = onum.rope_freqs()
+    cos, sin = onum.rope_tables(freqs)
+    d_src = src.to(cuda_device)
+    q_out = torch.empty(M, K, dtype=torch.bfloat16, device=cuda_device)
+    # K/V into a 4-frame ring starting at slot 3 (frames land in slots 3, 0)
+    k_ring = torch.zeros(4 * h * w, K, dtype=torch.bfloat16, device=cuda_device)
+    v_ring = torch.zeros_like(k_ring)
+    srdit.ops.rms_rope(d_src[:, :K], wq.to(cuda_device), 1e-6, q_out, frame_tokens=h * w,
+                       cos=cos.to(cuda_device), sin=sin.to(cuda_device), grid_h=h, grid_w=w,
+                       t_offset=4)
+    srdit.ops.rms_rope(d_src[:, K:2 * K], wq.to(cuda_device), 1e-6, k_ring, frame_tokens=h * w,
+                       slot0=3, n_slots=4, cos=cos.to(cuda_device), sin=sin.to(cuda_device),
+                       grid_h=h, grid_w=w, t_offset=4, v_src=d_src[:, 2 * K:], v_dst=v_ring)
+    ref_q = onum.rope_apply(onum.rms_norm(src[:, :K], wq).view(M, n, 128), (f, h, w), freqs, 4)
+    ref_k = onum.rope_apply(onum.rms_norm(src[:, K:2 * K], wq).view(M, n, 128), (f, h, w),
+                            freqs, 4)
+    got_q = q_out.cpu().view(M, n, 128)
+    # mean() is reduced in another order than torch's CPU kernel: rare 1-ulp ties
+    assert (got_q.view(torch.int16) == ref_q.view(torch.int16)).float().mean() > 0.99
+    assert onum.rel_fro(got_q.float(), ref_q.float()) < 1e-3
+    L = h * w
+    ring = k_ring.cpu()
+    got_k = torch.cat([ring[3 * L:4 * L], ring[0:L]]).view(M, n, 128)
+    assert onum.rel_fro(got_k.float(), ref_k.float()) < 1e-3
+    vr = v_ring.cpu()
+    assert torch.equal(torch.cat([vr[3 * L:4 * L], vr[0:L]]), src[:, 2 * K:])
+    assert ring[L:3 * L].abs().sum() == 0  # untouched slots stay untouched
+
+
+# --------------------------------------------------------------------------- fp8 GEMM
+def _gemm_inputs(M, N, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(M, K, generator=g)
+    a = torch.where(torch.rand(M, K, generator=g) < 1e-3, a * 20, a).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(N, generator=g) * 0.01).to(torch.bfloat16)
+    aq, as_ = onum.quantize_rowwise(a)
+    wq, ws = onum.fp8_linear_weights(w)
+    return a, aq, as_.reshape(-1).contiguous(), wq, ws, bias
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 320, 640), (512, 3072, 3072),
+                                   (130, 9216, 256)])
+def test_fp8_gemm_store(srdit, cuda_device, M, N, K):
+    a, aq, as_, wq, ws, bias = _gemm_inputs(M, N, K, M * 7 + N)
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    out = srdit.ops.fp8_gemm(d(aq), d(as_), d(wq), d(ws), d(bias))
+    ref = onum.fp8_linear(a, wq, ws, bias)
+    assert onum.rel_fro(out.cpu().float(), ref.float()) < 1e-3
+    # against the reference's own GPU call (cuBLASLt row-wise torch._scaled_mm)
+    if K % 16 == 0 and N % 16 == 0:
+        sm = torch._scaled_mm(d(aq), d(wq).t(), scale_a=d(as_).view(-1, 1),
+                              scale_b=d(ws).view(1, -1), bias=d(bias), out_dtype=torch.bfloat16)
+        assert onum.rel_fro(out.float(), sm.float()) < 1e-3
+
+
+def test_fp8_gemm_gelu_amax(srdit, cuda_device):
+    M, N, K = 256, 1024, 512
+    a, aq, as_, wq, ws, bias = _gemm_inputs(M, N, K, 11)
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    amax = torch.zeros(M, device=cuda_device)
+    out = srdit.ops.fp8_gemm(d(aq), d(as_), d(wq), d(ws), d(bias), epilogue="gelu",
+                             row_amax=amax)
+    ref = onum.gelu_tanh(onum.fp8_linear(a, wq, ws, bias))
+    assert onum.rel_fro(out.cpu().float(), ref.float()) < 2e-3
+    np.testing.assert_array_equal(amax.cpu().numpy(), out.float().abs().amax(-1).cpu().numpy())
+
+
+@pytest.mark.parametrize("kind", ["gated_res", "res"])
+def test_fp8_gemm_residual(srdit, cuda_device, kind):
+    M, N, K = 384, 512, 768
+    a, aq, as_, wq, ws, bias = _gemm_inputs(M, N, K, 13)
+    g = torch.Generator().manual_seed(14)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    gate = torch.randn(N, generator=g) * 0.5
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    out = srdit.ops.fp8_gemm(d(aq), d(as_), d(wq), d(ws), d(bias), epilogue=kind,
+                             residual=d(res), gate=d(gate) if kind == "gated_res" else None)
+    y = onum.fp8_linear(a, wq, ws, bias)
+    ref = (res.float() + y.float() * gate) if kind == "gated_res" else (res.float() + y.float())
+    ref = ref.to(torch.bfloat16)
+    assert onum.rel_fro(out.cpu().float(), ref.float()) < 1e-3
+
+
+# --------------------------------------------------------------------------- window attention
+def _check_attn(got, ref, max_abs=2e-2, rel=5e-3):
+    got = got.float().cpu().double()
+    ref = ref.double()
+    err = (got - ref).abs().max().item()
+    r = onum.rel_fro(got, ref)
+    assert err <= max_abs and r <= rel, (err, r)
+    return err, r
+
+
+@pytest.mark.parametrize("bhw,rhw", [((8, 8), (0, 0)), ((4, 4), (3, 3))])
+def test_winattn_config1(srdit, cuda_device, golden, bhw, rhw):
+    """BASELINE config 1 (3x18x32 grid, 24 heads, RoPE'd N(0,1) q/k/v, seed 0)."""
+    qr, kr, v = config1_inputs()
+    qb, kb, vb = (t.to(torch.bfloat16) for t in (qr, kr, v))
+    out, _, _ = srdit.attention.mask_free_window_attention(
+        qb[None].to(cuda_device), kb[None].to(cuda_device), vb[None].to(cuda_device),
+        torch.tensor([[3, 18, 32]]), attn_impl="b200", block_t=3, block_hw=bhw,
+        block_radius_hw=rhw)
+    spec = obg.make_spec(3, 3, 18, 32, block_t=3, block_hw=bhw, block_radius_hw=rhw)
+    ref = owa.run_plan(qb, kb, vb, obg.build_plan(spec), f_cur=3, h=18, w=32)
+    _check_attn(out[0], ref)
+    # and against the reference's own fp32 output (bf16 input rounding included)
+    tag = "cfg1_%dx%d_r%d" % (bhw[0], bhw[1], rhw[0])
+    gold = torch.from_numpy(golden("winattn")[f"{tag}.out_h0"])
+    _check_attn(out[0, :, 0], gold, max_abs=3e-2, rel=1e-2)
+
+
+@pytest.mark.parametrize("tag", ["none", "frame", "chunk"])
+def test_winattn_streaming_cache_anchor(srdit, cuda_device, tag):
+    ins = {k: v.to(torch.bfloat16) for k, v in stream_inputs().items()}
+    d = lambda t: t[None].to(cuda_device)  # noqa: E731
+    kw = {} if tag == "none" else dict(anchor_k=d(ins["ak"]), anchor_v=d(ins["av"]),
+                                       anchor_align=tag)
+    out, nck, ncv = srdit.attention.mask_free_window_attention(
+        d(ins["q"]), d(ins["k"]), d(ins["v"]), torch.tensor([[3, 8, 12]]),
+        pre_cache_k=d(ins["ck"]), pre_cache_v=d(ins["cv"]), kv_len=4, attn_impl="b200",
+        block_t=3, block_hw=(4, 4), block_radius_hw=(1, 1), **kw)
+    spec = obg.make_spec(3, 6, 8, 12, block_t=3, block_hw=(4, 4), block_radius_hw=(1, 1),
+                         streaming=True)
+    anchor = None if tag == "none" else tag
+    plan = obg.build_plan(spec, anchor)
+    k_full = torch.cat([ins["ck"], ins["k"]])
+    v_full = torch.cat([ins["cv"], ins["v"]])
+    if anchor:
+        k_full = torch.cat([ins["ak"], k_full])
+        v_full = torch.cat([ins["av"], v_full])
+    ref = owa.run_plan(ins["q"], k_full, v_full, plan, f_cur=3, h=8, w=12)
+    _check_attn(out[0], ref)
+    assert torch.equal(nck[0].cpu(), torch.cat([ins["ck"], ins["k"]])[-4 * 96:])
+
+
+@pytest.mark.parametrize("geom", ["2k_4x4_r3_f12_frame", "2k_8x8_r0_f6", "odd_frame",
+                                  "native_anchor", "hist_rt1", "parallel_causal"])
+def test_winattn_reference_plans(srdit, cuda_device, golden, geom):
+    """Launch with the reference's own params rows (the launcher seam)."""
+    from tests.golden_cases import spec_fields
+    g = golden("plans")
+    vals, mode = spec_fields(g, geom)
+    f_cur, f_kv, h, w = vals["f_cur"], vals["f_kv"], vals["h"], vals["w"]
+    n = 2
+    L = h * w
+    ahw = vals["anchor_hw"] or (h, w)
+    La = ahw[0] * ahw[1]
+    gen = torch.Generator().manual_seed(21)
+    q = torch.randn(f_cur * L, n, 128, generator=gen).to(torch.bfloat16)
+    a_tok = f_cur * La if mode else 0
+    k = torch.randn(a_tok + f_kv * L, n, 128, generator=gen).to(torch.bfloat16)
+    v = torch.randn(a_tok + f_kv * L, n, 128, generator=gen).to(torch.bfloat16)
+    meta = g[f"{geom}.meta"]
+    plan = {"params": torch.from_numpy(g[f"{geom}.params"]), "n_w": int(meta[0]),
+            "block_m": int(meta[1]), "m_tiles": int(meta[2]), "block_n": int(meta[3]),
+            "hr_base": int(meta[4]), "p_stride": int(meta[5])}
+    out = torch.empty_like(q, device=cuda_device)
+    srdit.attention.run_blockgrid_b200(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                                       out, plan=plan, f_cur=f_cur, h=h, w=w, n=n, d=128,
+                                       anchor_mode=mode)
+    oplan = {**plan, "params": g[f"{geom}.params"]}
+    ref = owa.run_plan(q, k, v, oplan, f_cur=f_cur, h=h, w=w)
+    _check_attn(out, ref)
+
+
+def test_winattn_deterministic(srdit, cuda_device):
+    ins = {k: v.to(torch.bfloat16) for k, v in stream_inputs().items()}
+    d = lambda t: t[None].to(cuda_device)  # noqa: E731
+    outs = [srdit.attention.mask_free_window_attention(
+        d(ins["q"]), d(ins["k"]), d(ins["v"]), torch.tensor([[3, 8, 12]]),
+        pre_cache_k=d(ins["ck"]), pre_cache_v=d(ins["cv"]), attn_impl="b200", block_t=3,
+        block_hw=(4, 4), block_radius_hw=(2, 2))[0] for _ in range(2)]
+    assert torch.equal(outs[0], outs[1])

@@ -1,0 +1,99 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import blockgrid as obg
+from oracle import numerics as onum
+from oracle import winattn as owa
+from tests.golden_cases import PLAN_NAMES, spec_from_golden
+
+
+def bf16(a):
+    return torch.from_numpy(np.asarray(a)).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("name", PLAN_NAMES)
+def test_oracle_plan_matches_reference(golden, name):
+    g = golden("plans")
+    spec, mode = spec_from_golden(g, name, obg.Spec)
+    plan = obg.build_plan(spec, mode)
+    np.testing.assert_array_equal(plan["params"], g[f"{name}.params"])
+    meta = [plan["n_w"], plan["block_m"], plan["m_tiles"], plan["block_n"], plan["hr_base"],
+            plan["p_stride"]]
+    np.testing.assert_array_equal(meta, g[f"{name}.meta"])
+
+
+@pytest.mark.parametrize("name", PLAN_NAMES)
+def test_oracle_plan_partitions_queries(golden, name):
+    g = golden("plans")
+    spec, mode = spec_from_golden(g, name, obg.Spec)
+    plan = obg.build_plan(spec, mode)
+    cnt = owa.coverage(plan, spec.f_cur, spec.h, spec.w)
+    assert (cnt == 1).all()
+
+
+def test_oracle_quant_bit_exact(golden):
+    g = golden("quant")
+    q, s = onum.quantize_rowwise(bf16(g["x"]))
+    np.testing.assert_array_equal(q.view(torch.uint8).numpy(), g["q"])
+    np.testing.assert_array_equal(s.numpy(), g["s"])
+
+
+def test_oracle_norms_bit_exact(golden):
+    g = golden("norms")
+    x = bf16(g["x"])
+    np.testing.assert_array_equal(onum.layer_norm(x).view(torch.int16).numpy(), g["ln"])
+    y = onum.layer_norm(x, weight=bf16(g["lna_w"]), bias=bf16(g["lna_b"]))
+    np.testing.assert_array_equal(y.view(torch.int16).numpy(), g["lna"])
+    y = onum.rms_norm(x, bf16(g["rms_w"]))
+    np.testing.assert_array_equal(y.view(torch.int16).numpy(), g["rms"])
+
+
+def test_oracle_rope_bit_exact(golden):
+    g = golden("rope")
+    freqs = onum.rope_freqs()
+    np.testing.assert_array_equal(freqs.real.numpy()[:16], g["freqs_re"])
+    np.testing.assert_array_equal(freqs.imag.numpy()[:16], g["freqs_im"])
+    y = onum.rope_apply(bf16(g["x"]), (2, 5, 7), freqs, t_offset=3)
+    np.testing.assert_array_equal(y.view(torch.int16).numpy(), g["y"])
+    yf = onum.rope_apply(torch.from_numpy(g["xf"]), (2, 5, 7), freqs, t_offset=0)
+    np.testing.assert_array_equal(yf.numpy(), g["yf"])
+
+
+@pytest.mark.parametrize("tag,bhw,rhw", [("cfg1_8x8_r0", (8, 8), (0, 0)),
+                                         ("cfg1_4x4_r3", (4, 4), (3, 3))])
+def test_oracle_window_attention_config1(golden, tag, bhw, rhw):
+    """the reference's sdpa path, fp32, seed 0."""
+    g = golden("winattn")
+    from tests.golden_cases import config1_inputs
+    qr, kr, v = config1_inputs()
+    spec = obg.make_spec(3, 3, 18, 32, block_t=3, block_hw=bhw, block_radius_hw=rhw)
+    plan = obg.build_plan(spec)
+    out = owa.run_plan(qr, kr, v, plan, f_cur=3, h=18, w=32, dtype=torch.float64)
+    np.testing.assert_allclose(out[:, 0].numpy(), g[f"{tag}.out_h0"], rtol=0, atol=2e-5)
+    np.testing.assert_allclose(out[::97].numpy(), g[f"{tag}.rows"], rtol=0, atol=2e-5)
+    sums = [float(out.sum()), float(out.abs().sum()), float((out ** 2).sum())]
+    np.testing.assert_allclose(sums, g[f"{tag}.sum"], rtol=1e-6)
+
+
+@pytest.mark.parametrize("tag", ["none", "frame", "chunk"])
+def test_oracle_window_attention_streaming(golden, tag):
+    """KV cache + LQ anchor (frame / chunk align), small grid, 2 heads."""
+    g = golden("winattn")
+    from tests.golden_cases import stream_inputs
+    ins = stream_inputs()
+    np.testing.assert_allclose([float(t.double().sum()) for t in ins.values()],
+                               g["stream.input_sums"], rtol=1e-12)
+    f_cur, h, w = 3, 8, 12
+    anchor = None if tag == "none" else tag
+    spec = obg.make_spec(3, 6, h, w, block_t=3, block_hw=(4, 4), block_radius_hw=(1, 1),
+                         streaming=True)
+    plan = obg.build_plan(spec, anchor)
+    k_full = torch.cat([ins["ck"], ins["k"]])
+    v_full = torch.cat([ins["cv"], ins["v"]])
+    if anchor is not None:
+        k_full = torch.cat([ins["ak"], k_full])
+        v_full = torch.cat([ins["av"], v_full])
+    out = owa.run_plan(ins["q"], k_full, v_full, plan, f_cur=f_cur, h=h, w=w)
+    np.testing.assert_allclose(out.numpy(), g[f"stream.{tag}.out"], rtol=0, atol=2e-5)
