@@ -1,0 +1,338 @@
+#!/usr/bin/env python
+"""SR-DiT 5B 2K refinement throughput on B200 (latent-frames/s).
+
+One step = one autoregressive refinement chunk of BASELINE config 3: 3 latent
+frames at 2048x1152 (latent 48x3x72x128 -> 36x64 tokens/frame, 6912 tokens),
+a 3-frame KV-cache prefix (the denoise forward attends f_kv = 6 frames), a
+512-token N(0,1) 4096-d text context, 3x8x8 block-grid windows, fp8 Linears.
+The step is the reference pipeline's per-chunk work
+(pipeline_sr/causal_inference.py:858-976): a denoise forward at t=625, the
+flow->x0 update, and the KV-refresh forward at t=0 -- 2 x 30 blocks. The ring is
+restored to the 3-frame prefix before every step, so every step does the same
+work. Weights are seeded random (no checkpoint); inputs are seeded synthetic.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+N > 1 (under torchrun): every rank refines its own clip (replicas, weak
+scaling); the step time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "2K SR-DiT refine latent-frames/s @1/2/4/8 B200; fp8 GEMM & win-attn % of roofline"
+UNIT = "latent-frames/s"
+FRAMES_PER_STEP = 3
+LAT_SHAPE = (48, 3, 72, 128)
+CTX_SHAPE = (512, 4096)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--geometry", default="8x8r0", choices=["8x8r0", "4x4r3"])
+    ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_setup(n):
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group(
+            "nccl" if torch.cuda.is_available() else "gloo",
+            timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def geometry(name):
+    return ((8, 8), (0, 0)) if name == "8x8r0" else ((4, 4), (3, 3))
+
+
+# --------------------------------------------------------------------------- CPU arm
+def cpu_block_sample(args, seed=0):
+    """Time one full-size SR-DiT block of the denoise forward on the host cores,
+    with the oracle's restatement of the reference block (bf16 Linears, fp32
+    window softmax), the reference's CPU-runnable computation."""
+    from oracle import block as oblock
+    from oracle import numerics as onum
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    D, F = 3072, 14336
+    r = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16)  # noqa: E731
+    wts = {}
+    for m in ("self_attn", "cross_attn"):
+        for n in ("q", "k", "v", "o"):
+            wts[f"{m}.{n}.weight"], wts[f"{m}.{n}.bias"] = r(D, D), r(D)
+        wts[f"{m}.norm_q.weight"] = torch.ones(D, dtype=torch.bfloat16)
+        wts[f"{m}.norm_k.weight"] = torch.ones(D, dtype=torch.bfloat16)
+    wts["norm3.weight"], wts["norm3.bias"] = torch.ones(D, dtype=torch.bfloat16), r(D)
+    wts["ffn.0.weight"], wts["ffn.0.bias"] = r(F, D), r(F)
+    wts["ffn.2.weight"], wts["ffn.2.bias"] = r(D, F), r(D)
+    wts["modulation"] = torch.randn(1, 6, D, generator=g) / D ** 0.5
+    L = 36 * 64
+    x = torch.randn(3 * L, D, generator=g).to(torch.bfloat16)
+    ctx = torch.randn(512, D, generator=g).to(torch.bfloat16)
+    ck = torch.randn(3 * L, 24, 128, generator=g).to(torch.bfloat16)
+    cv = torch.randn(3 * L, 24, 128, generator=g).to(torch.bfloat16)
+    e0 = torch.randn(6, D, generator=g) * 0.1
+    bhw, rhw = geometry(args.geometry)
+    freqs = onum.rope_freqs()
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        oblock.block_forward(wts, x, e0, ctx, grid=(3, 36, 64), freqs=freqs, t_offset=3,
+                             cache_k=ck, cache_v=cv, kv_len=9, block_hw=bhw, radius_hw=rhw,
+                             block_t=3, heads=24, linear="bf16")
+    return time.perf_counter() - t0, torch.get_num_threads()
+
+
+def cpu_value(block_s, layers=30):
+    # a step is 2 forwards x `layers` blocks (embeddings / head are < 1% and omitted)
+    return FRAMES_PER_STEP / (2 * layers * block_s)
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    times = []
+    cores = 1
+    for i in range(args.warmup + args.steps):
+        t, cores = cpu_block_sample(args, seed=i)
+        if i >= args.warmup:
+            times.append(t)
+    blk = statistics.mean(times)
+    val = cpu_value(blk)
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * FRAMES_PER_STEP / val, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": "one full-size SR-DiT block per step (CPU restatement "
+                                       "of WanAttentionBlock, bf16 Linears), x60 for the "
+                                       "2-forward chunk"},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def workload_config(args):
+    bhw, rhw = geometry(args.geometry)
+    return {"workload": "config3: SR-DiT 5B 2K AR chunk (denoise t=625 + KV refresh t=0), "
+                        "3 latent frames 36x64 tokens, 3-frame KV prefix, 512 text tokens",
+            "model": "SR-DiT 5B (30 blocks, dim 3072, 24x128 heads, ffn 14336)",
+            "layers": args.layers, "tokens": 6912, "window": f"3x{bhw[0]}x{bhw[1]} r{rhw}",
+            "global_batch": args.gpus, "seq_len": 6912,
+            "parallelism": "replicas" if args.gpus > 1 else "single",
+            "l2": "inputs larger than L2 (5 GB of fp8 weights stream every forward)"}
+
+
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = pathlib.Path(f"/tmp/srdit_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return None
+        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                mx = float(r[1])
+                for n, v in zip(names, r[4:8]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def run_gpu_arm(args, rank, world, local):
+    srdit = importlib.import_module("dreamx-creator_b200")
+    from importlib import import_module
+    model_mod = import_module("dreamx-creator_b200.model")
+    pipe_mod = import_module("dreamx-creator_b200.pipeline")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    bhw, rhw = geometry(args.geometry)
+    cfg = model_mod.SRDiTConfig(num_layers=args.layers, block_hw=bhw, block_radius_hw=rhw)
+    model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
+    g = torch.Generator().manual_seed(1000 + rank)
+    ctx_host = torch.randn(*CTX_SHAPE, generator=g).to(torch.bfloat16).pin_memory()
+    noisy_host = torch.randn(*LAT_SHAPE, generator=g).to(torch.bfloat16).pin_memory()
+    prefix_host = torch.randn(*LAT_SHAPE, generator=g).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty(*LAT_SHAPE, dtype=torch.bfloat16).pin_memory()
+    ctx = ctx_host.to(dev)
+    noisy = noisy_host.to(dev)
+    stream = pipe_mod.RefinerStream(model, ctx)
+    # prefill: the previous chunk's refresh forward leaves a 3-frame cache
+    stream.step(prefix_host.to(dev))
+    ring = stream.cache
+    prefix_state = (ring.start, ring.frames, stream.t_offset)
+
+    def one_step(inp):
+        ring.start, ring.frames, stream.t_offset = prefix_state
+        return stream.step(inp)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            one_step(noisy)
+        model.check_status()
+        barrier()
+        # ---- device-timed region: inputs resident in HBM
+        ops = srdit.ops
+        ops.Stats.gemm_events = []
+        l0 = ops.Stats.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            barrier()
+            e0.record()
+            for _ in range(args.steps):
+                one_step(noisy)
+            e1.record()
+            barrier()
+        launches = ops.Stats.launches - l0
+        gemm_ev = ops.Stats.gemm_events
+        ops.Stats.gemm_events = None
+        dev_ms = max_over_ranks(e0.elapsed_time(e1))
+        gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gemm_ev)
+        gemm_flop = sum(f for _, _, f in gemm_ev)
+        model.check_status()
+        # ---- end-to-end region: the public API with host buffers
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            c = ctx_host.to(dev, non_blocking=True)
+            stream.context = c
+            x = noisy_host.to(dev, non_blocking=True)
+            y = one_step(x)
+            out_host.copy_(y, non_blocking=True)
+        s1.record()
+        barrier()
+        e2e_ms = max_over_ranks(s0.elapsed_time(s1))
+        stream.context = ctx
+
+    if rank != 0:
+        return
+    peaks, peak_kind = load_peaks()
+    fp8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))
+    achieved = gemm_flop / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    value = world * FRAMES_PER_STEP * args.steps / (dev_ms * 1e-3)
+    e2e_val = world * FRAMES_PER_STEP * args.steps / (e2e_ms * 1e-3)
+    n_gemm = len(gemm_ev) // max(args.steps, 1)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 GEMM (fp32 acc) / bf16 attention", "data": "synthetic (seeded N(0,1) "
+        "latent + text context, seeded random weights)",
+        "config": workload_config(args),
+        "roofline": {"bound": "tensor", "kernel": "srdit_fp8_gemm (tcgen05 e4m3)",
+                     "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": (achieved / fp8_peak) if achieved else None,
+                     "traffic": None,
+                     "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json "
+                                    f"({peak_kind}); e4m3 tcgen05 rate = 2 x bf16",
+                     "gemm_ms_per_step": gemm_ms / args.steps,
+                     "gemm_launches_per_step": n_gemm,
+                     "gemm_share_of_step": gemm_ms / (dev_ms if world == 1 else dev_ms)},
+        "e2e": {"value": e2e_val, "unit": UNIT,
+                "h2d_bytes_per_step": noisy_host.numel() * 2 + ctx_host.numel() * 2,
+                "d2h_bytes_per_step": out_host.numel() * 2},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        t, cores = cpu_block_sample(args)
+        line["cpu_baseline"] = {"value": cpu_value(t), "unit": UNIT, "cores": cores,
+                                "kind": "port",
+                                "sample": f"one full-size block on the host ({t:.2f} s), x60 "
+                                          f"for the 2-forward chunk"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference_arm(args, rank)
+        else:
+            run_gpu_arm(args, rank, world, local)
+    finally:
+        if world > 1 and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

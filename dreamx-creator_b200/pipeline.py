@@ -1,0 +1,71 @@
+"""The refiner's autoregressive chunk loop on the B200 model.
+
+Mirrors ``CausalInferencePipeline.inference_sr``'s hot loop
+(video_refiner/pipeline_sr/causal_inference.py:858-976) for the shipped
+1-step schedule: per 3-latent-frame chunk,
+  1. optional LQ-anchor harvest: the LR chunk's frames run as independent
+     1-frame forwards with no cache; their per-layer roped K / V become the
+     anchor (causal_inference.py:426-508);
+  2. denoise: one forward at t = 625 over the rolling cache (+ anchor), then
+     x0 = x_t - (t/1000) * flow in fp64 (utils/sr_dit_wrapper.py:551-558);
+  3. KV refresh: one forward over x0 at t = context_noise (0) that writes the
+     chunk's K / V into the cache, which keeps the newest ``kv_len`` frames.
+"""
+from __future__ import annotations
+
+import torch
+
+from .model import KVRing, SRDiT
+
+
+class RefinerStream:
+    def __init__(self, model: SRDiT, context: torch.Tensor, *, denoise_t: float = 625.0,
+                 context_noise: float = 0.0, num_train_timesteps: int = 1000,
+                 frame_tokens: int | None = None):
+        self.model = model
+        self.context = context
+        self.denoise_t = float(denoise_t)
+        self.context_noise = float(context_noise)
+        self.ntt = num_train_timesteps
+        self.cache: KVRing | None = None
+        self.t_offset = 0
+        self._frame_tokens = frame_tokens
+
+    def reset(self):
+        self.cache = None
+        self.t_offset = 0
+
+    def harvest_anchor(self, lq_chunk, harvest_t=0.0):
+        """Per-frame anchor K / V (each LR frame an independent 1-frame forward)."""
+        f = lq_chunk.shape[1]
+        ks, vs = None, None
+        for j in range(f):
+            _, kv = self.model.forward_chunk(lq_chunk[:, j:j + 1], harvest_t, self.context,
+                                             cache=None, t_offset=self.t_offset + j,
+                                             return_kv=True)
+            if ks is None:
+                ks = [[k] for k, _ in kv]
+                vs = [[v] for _, v in kv]
+            else:
+                for li, (k, v) in enumerate(kv):
+                    ks[li].append(k)
+                    vs[li].append(v)
+        return [(torch.cat(k), torch.cat(v)) for k, v in zip(ks, vs)]
+
+    def step(self, noisy_chunk: torch.Tensor, lq_chunk: torch.Tensor | None = None,
+             anchor_harvest_t: float = 0.0):
+        """Refine one chunk [C, f, H, W] (device, bf16); returns x0 [C, f, H, W] bf16."""
+        m = self.model
+        if self.cache is None:
+            ph, pw = m.cfg.patch_size[1], m.cfg.patch_size[2]
+            L = (noisy_chunk.shape[2] // ph) * (noisy_chunk.shape[3] // pw)
+            self.cache = m.new_cache(L)
+        anchor = self.harvest_anchor(lq_chunk, anchor_harvest_t) if lq_chunk is not None else None
+        flow = m.forward_chunk(noisy_chunk, self.denoise_t, self.context, cache=self.cache,
+                               t_offset=self.t_offset, anchor_kv=anchor)
+        sigma = self.denoise_t / self.ntt
+        x0 = (noisy_chunk.double() - sigma * flow.double()).to(noisy_chunk.dtype)
+        m.forward_chunk(x0, self.context_noise, self.context, cache=self.cache,
+                        t_offset=self.t_offset, update_cache=True)
+        self.t_offset += noisy_chunk.shape[1]
+        return x0

@@ -1,0 +1,105 @@
+"""End-to-end parity of the B200 model / AR chunk loop with the CPU oracle."""
+import importlib
+
+import pytest
+import torch
+
+from oracle import model as omodel
+from oracle import numerics as onum
+
+pytestmark = pytest.mark.gpu
+
+
+def small_cfg(mod, **kw):
+    base = dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16,
+                text_dim=64, freq_dim=256, text_len=16, block_hw=(2, 2), block_radius_hw=(1, 1),
+                kv_len=9)
+    base.update(kw)
+    return mod.SRDiTConfig(**base)
+
+
+def random_sd(mod, cfg, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    sd = {}
+    for name, shape in mod.SRDiT.param_shapes(cfg).items():
+        if name.endswith("modulation"):
+            sd[name] = torch.randn(shape, generator=g) / cfg.dim ** 0.5
+            continue
+        if "norm" in name:
+            t = 1 + 0.1 * torch.randn(shape, generator=g)
+        elif name.endswith("bias"):
+            t = torch.randn(shape, generator=g) * 0.01
+        else:
+            t = torch.randn(shape, generator=g) * (0.05 if "weight" in name else 0.02)
+        sd[name] = t.to(torch.bfloat16)
+    return sd
+
+
+@pytest.fixture(scope="module")
+def mods(srdit):
+    return (importlib.import_module("dreamx-creator_b200.model"),
+            importlib.import_module("dreamx-creator_b200.pipeline"))
+
+
+@pytest.mark.parametrize("geom", [dict(), dict(block_hw=(8, 8), block_radius_hw=(0, 0))])
+def test_streaming_two_chunks_match_oracle(srdit, mods, cuda_device, geom):
+    """Chunk 0 (no cache) then chunk 1 over the refreshed 3-frame cache:
+    denoise flow at t=625 and the refresh, B200 vs oracle (fp8 Linears)."""
+    M, P = mods
+    cfg = small_cfg(M, **geom)
+    sd = random_sd(M, cfg)
+    model = M.SRDiT.from_state_dict(cfg, sd, cuda_device)
+    g = torch.Generator().manual_seed(1)
+    ctx = torch.randn(16, 64, generator=g).to(torch.bfloat16)
+    lat = [torch.randn(16, 3, 8, 16, generator=g).to(torch.bfloat16) for _ in range(2)]
+    ring = model.new_cache(4 * 8)
+    caches = None
+    fp8c = [dict() for _ in range(cfg.num_layers)]
+    for ci, x in enumerate(lat):
+        flow = model.forward_chunk(x.to(cuda_device), 625.0, ctx.to(cuda_device), cache=ring,
+                                   t_offset=3 * ci)
+        ref_flow, _ = omodel.forward_chunk(sd, cfg, x, 625.0, ctx, caches=caches, t_offset=3 * ci,
+                                           fp8caches=fp8c)
+        c = onum.cosine(flow.float().cpu(), ref_flow.float())
+        assert c >= 0.999, (ci, c)
+        x0 = (x.double() - 0.625 * ref_flow.double()).to(torch.bfloat16)
+        model.forward_chunk(x0.to(cuda_device), 0.0, ctx.to(cuda_device), cache=ring,
+                            t_offset=3 * ci, update_cache=True)
+        _, caches = omodel.forward_chunk(sd, cfg, x0, 0.0, ctx, caches=caches, t_offset=3 * ci,
+                                         fp8caches=fp8c)
+    model.check_status()
+    assert ring.frames == 6
+
+
+def test_anchor_harvest_and_frame_anchor(srdit, mods, cuda_device):
+    """LQ-anchor: per-frame 1-frame harvest forwards, then a frame-aligned denoise."""
+    M, P = mods
+    cfg = small_cfg(M)
+    sd = random_sd(M, cfg, seed=3)
+    model = M.SRDiT.from_state_dict(cfg, sd, cuda_device)
+    g = torch.Generator().manual_seed(4)
+    ctx = torch.randn(16, 64, generator=g).to(torch.bfloat16)
+    lq = torch.randn(16, 3, 8, 16, generator=g).to(torch.bfloat16)
+    x = torch.randn(16, 3, 8, 16, generator=g).to(torch.bfloat16)
+    stream = P.RefinerStream(model, ctx.to(cuda_device))
+    anchor = stream.harvest_anchor(lq.to(cuda_device))
+    fp8c = [dict() for _ in range(cfg.num_layers)]
+    ref_anchor = None
+    for j in range(3):
+        _, kv = omodel.forward_chunk(sd, cfg, lq[:, j:j + 1], 0.0, ctx, t_offset=j, fp8caches=fp8c)
+        if ref_anchor is None:
+            ref_anchor = [([k], [v]) for k, v in kv]
+        else:
+            for li, (k, v) in enumerate(kv):
+                ref_anchor[li][0].append(k)
+                ref_anchor[li][1].append(v)
+    ref_anchor = [(torch.cat(k), torch.cat(v)) for k, v in ref_anchor]
+    for (k, v), (rk, rv) in zip(anchor, ref_anchor):
+        assert onum.cosine(k.float().cpu(), rk.float().reshape(k.shape)) > 0.999
+        assert onum.cosine(v.float().cpu(), rv.float().reshape(v.shape)) > 0.999
+    flow = model.forward_chunk(x.to(cuda_device), 625.0, ctx.to(cuda_device), cache=None,
+                               anchor_kv=anchor)
+    ref_flow, _ = omodel.forward_chunk(sd, cfg, x, 625.0, ctx, fp8caches=fp8c,
+                                       anchor=ref_anchor, anchor_align="frame")
+    assert onum.cosine(flow.float().cpu(), ref_flow.float()) >= 0.999
+    model.check_status()

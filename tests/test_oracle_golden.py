@@ -97,3 +97,33 @@ def test_oracle_window_attention_streaming(golden, tag):
         v_full = torch.cat([ins["av"], v_full])
     out = owa.run_plan(ins["q"], k_full, v_full, plan, f_cur=f_cur, h=h, w=w)
     np.testing.assert_allclose(out.numpy(), g[f"stream.{tag}.out"], rtol=0, atol=2e-5)
+
+
+def _block_golden(golden):
+    g = golden("block")
+    dim, ffn, heads, f_cur, h, w, ctx_len, f_cache = (int(x) for x in g["dims"])
+    wts = {}
+    for k, v in g.items():
+        if k.startswith("w."):
+            t = torch.from_numpy(v)
+            wts[k[2:]] = t.view(torch.bfloat16) if t.dtype == torch.int16 else t
+    t = {k: bf16(g[k]) for k in ("x", "ctx", "ck", "cv", "y", "nk", "nv")}
+    return g, wts, t, (dim, ffn, heads, f_cur, h, w)
+
+
+def test_oracle_block_matches_reference_block(golden):
+    """oracle.block (bf16 Linears) vs the reference WanAttentionBlock, streaming + cache."""
+    from oracle import block as oblock
+    g, wts, t, (dim, ffn, heads, f_cur, h, w) = _block_golden(golden)
+    d = dim // heads
+    tdim, hdim, wdim = onum.rope_axis_dims(d)
+    freqs = torch.cat([onum.rope_params(1024, tdim), onum.rope_params(1024, hdim),
+                       onum.rope_params(1024, wdim)], dim=1)
+    y, nk, nv = oblock.block_forward(
+        wts, t["x"][0], torch.from_numpy(g["e"])[0], t["ctx"][0], grid=(f_cur, h, w),
+        freqs=freqs, t_offset=3, cache_k=t["ck"][0], cache_v=t["cv"][0], kv_len=9,
+        block_hw=(2, 2), radius_hw=(1, 1), block_t=3, heads=heads, linear="bf16")
+    ref = t["y"][0]
+    assert onum.cosine(y.float(), ref.float()) > 0.99999
+    assert (y.float() - ref.float()).abs().max() < 0.05
+    assert torch.equal(nk, t["nk"][0]) and torch.equal(nv, t["nv"][0])
