@@ -49,7 +49,91 @@ def parse():
     ap.add_argument("--geometry", default="8x8r0", choices=["8x8r0", "4x4r3"])
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", default=None, choices=["gemm", "attn", "quant", "ln", "rope"],
+                    help="time one kernel in isolation instead of the model step")
+    ap.add_argument("--shape", default=None,
+                    help="micro shape: gemm M,N,K | attn f_kv | quant/ln/rope M,K")
+    ap.add_argument("--iters", type=int, default=20)
     return ap.parse_args()
+
+
+def run_micro(args):
+    """One kernel in isolation: median CUDA-event time over --iters launches, the L2
+    cleaned between launches by reading a 512 MB buffer (no dirty lines left)."""
+    srdit = importlib.import_module("dreamx-creator_b200")
+    ops = srdit.ops
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def timeit(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(args.iters):
+            flush.max()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    peaks, kind = load_peaks()
+    res = {"micro": args.micro}
+    if args.micro == "gemm":
+        M, N, K = (int(v) for v in (args.shape or "6912,14336,3072").split(","))
+        a = torch.randn(M, K, device=dev, generator=g).to(torch.float8_e4m3fn)
+        w = torch.randn(N, K, device=dev, generator=g).to(torch.float8_e4m3fn)
+        sa, sb = torch.rand(M, device=dev), torch.rand(N, device=dev)
+        bias = torch.randn(N, device=dev).to(torch.bfloat16)
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda: ops.fp8_gemm(a, sa, w, sb, bias, out))
+        ref = timeit(lambda: torch._scaled_mm(a, w.t(), scale_a=sa.view(-1, 1),
+                                              scale_b=sb.view(1, -1), bias=bias,
+                                              out_dtype=torch.bfloat16))
+        fl = 2 * M * N * K
+        res.update(shape=[M, N, K], ms=ms, tflops=fl / ms / 1e9, cublaslt_ms=ref,
+                   cublaslt_tflops=fl / ref / 1e9,
+                   frac_of_2x_bf16_burst=fl / ms / 1e9 / (2 * peaks["bf16_tflops"]))
+    elif args.micro == "attn":
+        fkv = int(args.shape or 6)
+        bhw, rhw = geometry(args.geometry)
+        spec = srdit.blockgrid.make_spec(f_cur=3, f_kv=fkv, h=36, w=64, block_t=3, block_hw=bhw,
+                                         block_radius_hw=rhw, streaming=True)
+        plan = srdit.attention.cached_plan(spec)
+        q = torch.randn(6912, 24, 128, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(fkv * 2304, 24, 128, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(fkv * 2304, 24, 128, device=dev, generator=g).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        ms = timeit(lambda: srdit.attention.run_blockgrid_b200(q, k, v, o, plan=plan, f_cur=3,
+                                                               h=36, w=64, n=24, d=128))
+        fl = srdit.blockgrid.visible_flops(plan["params"], plan["p_stride"], 24, 128)
+        res.update(geometry=args.geometry, f_kv=fkv, ms=ms, gflop=fl / 1e9,
+                   tflops=fl / ms / 1e9, frac_of_bf16_burst=fl / ms / 1e9 / peaks["bf16_tflops"])
+    else:
+        M, K = (int(v) for v in (args.shape or "6912,3072").split(","))
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        if args.micro == "quant":
+            ms = timeit(lambda: ops.quant_rowwise(x))
+            byts = M * K * 2 + M * K + 4 * M
+        elif args.micro == "ln":
+            sh, sc = torch.randn(K, device=dev), torch.randn(K, device=dev)
+            ms = timeit(lambda: ops.ln_mod_quant(x, 1e-6, shift=sh, scale=sc))
+            byts = M * K * 2 + M * K + 4 * M
+        else:
+            mm = importlib.import_module("dreamx-creator_b200.model")
+            cos, sin = mm.rope_tables(128, 1024, 1e4, dev)
+            wt = torch.ones(K, device=dev, dtype=torch.bfloat16)
+            dst = torch.empty_like(x)
+            ms = timeit(lambda: ops.rms_rope(x, wt, 1e-6, dst, frame_tokens=2304, cos=cos, sin=sin,
+                                             grid_h=36, grid_w=64))
+            byts = 2 * M * K * 2
+        res.update(shape=[M, K], ms=ms, gbs=byts / ms / 1e6,
+                   frac_of_hbm=byts / ms / 1e6 / peaks["hbm_gbs"])
+    res["peaks"] = kind
+    print(json.dumps(res), flush=True)
 
 
 def dist_setup(n):
@@ -255,10 +339,12 @@ def run_gpu_arm(args, rank, world, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clk:
             barrier()
+            torch.cuda.nvtx.range_push("srdit_step")
             e0.record()
             for _ in range(args.steps):
                 one_step(noisy)
             e1.record()
+            torch.cuda.nvtx.range_pop()
             barrier()
         launches = ops.Stats.launches - l0
         gemm_ev = ops.Stats.gemm_events
@@ -323,6 +409,8 @@ def run_gpu_arm(args, rank, world, local):
 
 def main():
     args = parse()
+    if args.micro:
+        return run_micro(args)
     rank, world, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":

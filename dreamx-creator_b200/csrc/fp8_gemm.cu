@@ -13,11 +13,16 @@
 //   EPI_GATED_RES  bf16(res + bf16(y) * gate[n])  (fp32)     x + y*e_gate (models.py:1349-1350, :1261)
 //   EPI_RES        bf16(res + bf16(y))                       x + cross_attn(...) (models.py:1257)
 //
-// Design (one CTA per SM, persistent over output tiles):
-//   tile 128 x 256, K step 128 bytes, 4-stage TMA ring (48 KB per stage),
-//   warp 0 = TMA producer, warp 1 = tcgen05.mma issuer (also owns TMEM),
-//   warps 2-5 = epilogue; two 256-column TMEM accumulators so the epilogue of
-//   tile i overlaps the MMAs of tile i+1.
+// Design: a CTA pair (cluster of 2) computes a 256 x BN output tile with one
+// tcgen05.mma.cta_group::2 per 32-deep K step: each CTA stages its own 128 rows
+// of A and BN/2 rows of B (TMA, 128-byte swizzle, 5-stage ring), the even CTA
+// issues the MMAs, and each CTA's TMEM holds its 128 accumulator rows. Per CTA:
+// warp 0 = TMA producer, warp 1 = MMA issuer / TMEM owner, warps 2-5 =
+// epilogue. Two TMEM accumulators let the epilogue of one tile overlap the MMAs
+// of the next. The epilogue reads column scales / bias from shared memory,
+// stages bf16 rows in a swizzled buffer and writes them with TMA tile stores
+// (which also clip the M / N edges). The kernel is persistent: one pair per two
+// SMs walks the tile list.
 #include "sm100.cuh"
 #include "srdit_internal.h"
 
@@ -27,26 +32,34 @@
 namespace srdit {
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 128;  // bytes == e4m3 elements
-constexpr int STAGES = 4;
+constexpr int BM = 128;  // rows per CTA (256 per pair)
+constexpr int BK = 128;  // bytes == e4m3 elements per stage
+constexpr int STAGES = 5;
 constexpr int A_BYTES = BM * BK;
-constexpr int B_BYTES = BN * BK;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;
 constexpr int NUM_THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int EPI_WARPS = 4;
+constexpr int STG_BYTES = 32 * 128;  // per-warp staging tile: 32 rows x 64 bf16
+constexpr uint32_t TMEM_COLS = 512;
+
+template <int BN>
+struct Cfg {
+  static constexpr int B_BYTES = (BN / 2) * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OFF_STG = STAGES * STAGE_BYTES;
+  static constexpr int OFF_COL = OFF_STG + EPI_WARPS * 2 * STG_BYTES;
+  static constexpr int OFF_BAR = OFF_COL + 2 * 2 * 256 * 4;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
 
 struct Params {
   int M, N, K;
   const float* a_scale;
   const float* b_scale;
   const __nv_bfloat16* bias;
-  __nv_bfloat16* out;
-  int ldo;
   const __nv_bfloat16* res;
-  int ldr;
+  long long ldr;
   const float* gate;
   float* row_amax;
   uint32_t* status;
@@ -61,80 +74,36 @@ SRDIT_DEV float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanhf(inner));
 }
 
-template <int EPI>
-SRDIT_DEV void epilogue_chunk(const Params& p, const uint32_t (&r)[32], int row, int col0,
-                              float sa, float& amax) {
-  const int ncols = min(32, p.N - col0);
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int c = col0 + j;
-    const float sb = (j < ncols) ? __ldg(p.b_scale + c) : 0.f;
-    float y = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), sa), sb);
-    if (p.bias != nullptr && j < ncols) y = __fadd_rn(y, __bfloat162float(p.bias[c]));
-    v[j] = y;
-  }
-  if constexpr (EPI == EPI_GELU) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float h = __bfloat162float(__float2bfloat16_rn(v[j]));
-      const float g = __bfloat162float(__float2bfloat16_rn(gelu_tanh(h)));
-      v[j] = g;
-      if (j < ncols) amax = fmaxf(amax, fabsf(g));
-    }
-  } else if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
-    const __nv_bfloat16* rp = p.res + static_cast<size_t>(row) * p.ldr + col0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < ncols) {
-        const float y = __bfloat162float(__float2bfloat16_rn(v[j]));
-        const float xr = __bfloat162float(rp[j]);
-        if constexpr (EPI == EPI_GATED_RES) {
-          v[j] = __fadd_rn(xr, __fmul_rn(y, __ldg(p.gate + col0 + j)));
-        } else {
-          v[j] = __fadd_rn(xr, y);
-        }
-      }
-    }
-  }
-  __nv_bfloat16* op = p.out + static_cast<size_t>(row) * p.ldo + col0;
-  if (ncols == 32 && ((reinterpret_cast<uintptr_t>(op) & 15u) == 0)) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 pk;
-      uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[q * 8 + 2 * h], v[q * 8 + 2 * h + 1]);
-        w[h] = *reinterpret_cast<uint32_t*>(&b2);
-      }
-      *reinterpret_cast<uint4*>(op + q * 8) = pk;
-    }
-  } else {
-    for (int j = 0; j < ncols; ++j) op[j] = __float2bfloat16_rn(v[j]);
-  }
-}
+SRDIT_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-template <int EPI>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int EPI, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                    const __grid_constant__ CUtensorMap tmB, const Params p) {
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmO, const Params p) {
+  using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;                     // [STAGES], completed in the even CTA
+  uint64_t* empty = bars + STAGES;           // [STAGES], one per CTA
+  uint64_t* tfull = bars + 2 * STAGES;       // [2]
+  uint64_t* tempty = bars + 2 * STAGES + 2;  // [2], in the even CTA, 8 arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  float* col_s = reinterpret_cast<float*>(smem + C::OFF_COL);  // [2][256] b_scale
+  float* col_b = col_s + 512;                                  // [2][256] bias
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (p.M + BM - 1) / BM;
+  const uint32_t rank = cluster_ctarank();
+  const int num_m = (p.M + 2 * BM - 1) / (2 * BM);
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + BK - 1) / BK;
+  const int cid = static_cast<int>(cluster_id_x());
+  const int ncl = static_cast<int>(num_clusters_x());
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -143,7 +112,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);
     }
     *abort_flag = 0u;
     fence_barrier_init();
@@ -151,55 +120,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_2sm(tmem_slot, TMEM_COLS);
+    tmem_relinquish_2sm();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- producer
     if (elect_one()) {
+      const uint32_t full_even = mapa_shared(smem_u32(&full[0]), 0);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      int last_ph[STAGES];
-      for (int i = 0; i < STAGES; ++i) last_ph[i] = -1;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
         const int mt = tile / num_n, nt = tile % num_n;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, p.status, abort_flag)) {
             ok = false;
             break;
           }
-          last_ph[s] = static_cast<int>(ph);
-          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          uint8_t* st = smem + s * STAGE_BYTES;
-          tma_load_2d(st, &tmA, &full[s], kb * BK, mt * BM);
-          tma_load_2d(st + A_BYTES, &tmB, &full[s], kb * BK, nt * BN);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2u * C::STAGE_BYTES);
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          tma_load_2d_2sm(st, &tmA, full_even + 8u * s, kb * BK, mt * 2 * BM + rank * BM);
+          tma_load_2d_2sm(st + A_BYTES, &tmB, full_even + 8u * s, kb * BK,
+                          nt * BN + rank * (BN / 2));
           if (++s == STAGES) {
             s = 0;
             ph ^= 1u;
           }
         }
       }
-      if (!ok) {
-        // Drain: every load already issued lands before the CTA may exit.
-        for (int i = 0; i < STAGES; ++i)
-          if (last_ph[i] >= 0) mbar_wait(&full[i], static_cast<uint32_t>(last_ph[i]), nullptr, nullptr);
-      }
+      // After giving up, let the loads already issued land before the CTA exits
+      // (their completions are counted on the even CTA's barriers).
+      if (!ok)
+        for (int i = 0; i < 200; ++i) __nanosleep(1000);
     }
   } else if (warp == 1) {
-    if (elect_one()) {
-      const uint32_t idesc = idesc_make(0u, 0u, 0u, 0u, BM, BN);
+    // ---------------------------------------------------------------- MMA issuer
+    if (rank == 0 && elect_one()) {
+      const uint32_t idesc = idesc_make(0u, 0u, 0u, 0u, 2 * BM, BN);
+      const uint32_t empty_own = mapa_shared(smem_u32(&empty[0]), 0);
+      const uint32_t empty_peer = mapa_shared(smem_u32(&empty[0]), 1);
+      const uint32_t tfull_own = mapa_shared(smem_u32(&tfull[0]), 0);
+      const uint32_t tfull_peer = mapa_shared(smem_u32(&tfull[0]), 1);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
       int local = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = cid; tile < num_tiles && ok; tile += ncl, ++local) {
         const int acc = local & 1;
         const uint32_t aph = static_cast<uint32_t>(local >> 1) & 1u;
         if (!mbar_wait(&tempty[acc], aph ^ 1u, p.status, abort_flag)) break;
@@ -211,81 +185,197 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t a_addr = smem_u32(smem + s * C::STAGE_BYTES);
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
-            const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
-            mma_f8_ss(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_f8_ss_2sm(d_tmem, sdesc_sw128(a_addr + k * 32, 16, 1024),
+                          sdesc_sw128(b_addr + k * 32, 16, 1024), idesc,
+                          (kb > 0 || k > 0) ? 1u : 0u);
           }
-          tc_commit(&empty[s]);
+          tc_commit_2sm(empty_own + 8u * s);
+          tc_commit_2sm(empty_peer + 8u * s);
           if (++s == STAGES) {
             s = 0;
             ph ^= 1u;
           }
         }
-        if (ok) tc_commit(&tfull[acc]);
+        if (ok) {
+          tc_commit_2sm(tfull_own + 8u * acc);
+          tc_commit_2sm(tfull_peer + 8u * acc);
+        }
       }
     }
-  } else {
-    const int sub = warp & 3;
-    const int row_in_tile = sub * 32 + lane;
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------------- epilogue
+    const int sub = warp & 3;               // TMEM lane quarter of this warp
+    const int ep_tid = threadIdx.x - 64;    // 0..127
+    uint8_t* stg = smem + C::OFF_STG + sub * 2 * STG_BYTES;
+    const uint32_t tempty_even = mapa_shared(smem_u32(&tempty[0]), 0);
+    int stores = 0;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = cid; tile < num_tiles; tile += ncl, ++local) {
       const int acc = local & 1;
       const uint32_t aph = static_cast<uint32_t>(local >> 1) & 1u;
+      const int mt = tile / num_n, nt = tile % num_n;
+      const int n0 = nt * BN;
+      // column scale and bias of this tile -> shared memory (double-buffered)
+      for (int c = ep_tid; c < BN; c += 128) {
+        const int col = n0 + c;
+        col_s[acc * 256 + c] = col < p.N ? __ldg(p.b_scale + col) : 0.f;
+        col_b[acc * 256 + c] = (p.bias != nullptr && col < p.N) ? __bfloat162float(p.bias[col]) : 0.f;
+      }
+      named_barrier_sync(1, 128);
       if (!mbar_wait(&tfull[acc], aph, p.status, abort_flag)) break;
       tc_fence_after();
-      const int mt = tile / num_n, nt = tile % num_n;
-      const int row = mt * BM + row_in_tile;
+      const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM + sub * 32;
+      const int row = row0 + lane;
       const bool row_ok = row < p.M;
       const float sa = row_ok ? __ldg(p.a_scale + row) : 0.f;
+      const float* cs = col_s + acc * 256;
+      const float* cb = col_b + acc * 256;
       float amax = 0.f;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = nt * BN + c * 32;
-        if (row_ok && col0 < p.N) epilogue_chunk<EPI>(p, r, row, col0, sa, amax);
+      for (int ch = 0; ch < BN / 64; ++ch) {
+        uint8_t* buf = stg + (stores & 1) * STG_BYTES;
+        if (stores >= 2) {
+          if (lane == 0) bulk_wait_group_read1();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c0 = ch * 64 + h * 32;  // column within the tile
+          uint32_t r[32];
+          tmem_ld32(t_row + c0, r);
+          uint4 rv[4];
+          if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+            const int col = n0 + c0;
+            const __nv_bfloat16* rp = p.res + static_cast<long long>(row) * p.ldr + col;
+            if (row_ok && col + 32 <= p.N) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) rv[q] = *reinterpret_cast<const uint4*>(rp + q * 8);
+            } else {
+              __nv_bfloat16* rb = reinterpret_cast<__nv_bfloat16*>(rv);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                rb[j] = (row_ok && col + j < p.N) ? rp[j] : __float2bfloat16_rn(0.f);
+            }
+          }
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float y = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), sa), cs[c0 + j]);
+            v[j] = __fadd_rn(y, cb[c0 + j]);
+          }
+          if constexpr (EPI == EPI_GELU) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float g = bf16r(gelu_tanh(bf16r(v[j])));
+              v[j] = g;
+              amax = fmaxf(amax, fabsf(g));  // columns past N hold y = 0 -> g = 0
+            }
+          } else if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(rv);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float y = bf16r(v[j]);
+              const float xr = __bfloat162float(rb[j]);
+              if constexpr (EPI == EPI_GATED_RES) {
+                const int col = n0 + c0 + j;
+                const float gt = col < p.N ? __ldg(p.gate + col) : 0.f;
+                v[j] = __fadd_rn(xr, __fmul_rn(y, gt));
+              } else {
+                v[j] = __fadd_rn(xr, y);
+              }
+            }
+          }
+          // this row's 32 values -> 64 bytes of the 128-byte staging row
+          // (16-byte chunk q stored at q ^ (row & 7): the 128B TMA swizzle)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+              w[e] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            const int chunk = (h * 4 + q) ^ (lane & 7);
+            *reinterpret_cast<uint4*>(buf + lane * 128 + chunk * 16) = pk;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < p.M && n0 + ch * 64 < p.N) {  // boxes start inside the tensor
+          tma_store_2d(&tmO, buf, n0 + ch * 64, row0);
+          bulk_commit_group();
+        }
+        ++stores;
       }
       if constexpr (EPI == EPI_GELU) {
         if (row_ok) atomicMax(reinterpret_cast<unsigned int*>(p.row_amax + row), __float_as_uint(amax));
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) mbar_arrive_cluster(tempty_even + 8u * acc);
     }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
   }
 
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc_2sm(tmem_base, TMEM_COLS);
   }
 }
 
-template <int EPI>
-static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
-                  cudaStream_t stream) {
-  auto kern = fp8_gemm_kernel<EPI>;
+template <int EPI, int BN>
+static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                  const Params& p, cudaStream_t stream) {
+  auto kern = fp8_gemm_kernel<EPI, BN>;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr_done[kMaxDevices] = {};
   if (dev < kMaxDevices && !attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES);
+                                         Cfg<BN>::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done[dev] = true;
   }
-  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
-  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
+  const int pairs = num_sms(dev) / 2;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  kern<<<grid, NUM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, to, p);
   return static_cast<int>(cudaGetLastError());
+}
+
+// Output tile width: the one that minimises (waves of tile pairs) x width.
+static int pick_bn(int M, int N, int pairs) {
+  const int cands[2] = {256, 192};
+  int best = 256;
+  long long best_cost = -1;
+  for (int bn : cands) {
+    const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + bn - 1) / bn);
+    const long long waves = (tiles + pairs - 1) / pairs;
+    const long long cost = waves * bn;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int EPI>
+static int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const CUtensorMap& to, const Params& p, cudaStream_t stream) {
+  return bn == 256 ? launch<EPI, 256>(ta, tb, to, p, stream)
+                   : launch<EPI, 192>(ta, tb, to, p, stream);
 }
 
 }  // namespace gemm
@@ -301,20 +391,28 @@ extern "C" int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const voi
   if (M <= 0 || N <= 0 || K <= 0) return (M == 0 || N == 0) ? 0 : SRDIT_EINVAL;
   if (!a_fp8 || !a_scale || !b_fp8 || !b_scale || !out) return SRDIT_EINVAL;
   if (lda < K || ldb < K || ldo < N) return SRDIT_EINVAL;
-  if ((lda % 16) || (ldb % 16)) return SRDIT_EALIGN;  // TMA row strides: multiples of 16 B
-  if ((reinterpret_cast<uintptr_t>(a_fp8) & 15u) || (reinterpret_cast<uintptr_t>(b_fp8) & 15u))
+  if ((lda % 16) || (ldb % 16) || (ldo % 8)) return SRDIT_EALIGN;  // TMA strides: 16 B
+  if ((reinterpret_cast<uintptr_t>(a_fp8) & 15u) || (reinterpret_cast<uintptr_t>(b_fp8) & 15u) ||
+      (reinterpret_cast<uintptr_t>(out) & 15u))
     return SRDIT_EALIGN;
   if (epilogue < EPI_STORE || epilogue > EPI_RES) return SRDIT_EINVAL;
-  if ((epilogue == EPI_GATED_RES || epilogue == EPI_RES) && (!residual || ldr < N))
-    return SRDIT_EINVAL;
+  if (epilogue == EPI_GATED_RES || epilogue == EPI_RES) {
+    if (!residual || ldr < N) return SRDIT_EINVAL;
+    if ((ldr % 8) || (reinterpret_cast<uintptr_t>(residual) & 15u)) return SRDIT_EALIGN;
+  }
   if (epilogue == EPI_GATED_RES && !gate) return SRDIT_EINVAL;
   if (epilogue == EPI_GELU && !row_amax) return SRDIT_EINVAL;
 
-  CUtensorMap ta, tb;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int bn = gemm::pick_bn(M, N, num_sms(dev) / 2);
+  CUtensorMap ta, tb, to;
   int rc = make_tmap_2d(&ta, a_fp8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, lda, gemm::BK,
                         gemm::BM);
   if (rc) return rc;
-  rc = make_tmap_2d(&tb, b_fp8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldb, gemm::BK, gemm::BN);
+  rc = make_tmap_2d(&tb, b_fp8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldb, gemm::BK, bn / 2);
+  if (rc) return rc;
+  rc = make_tmap_2d(&to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldo, 64, 32);
   if (rc) return rc;
 
   gemm::Params p;
@@ -324,17 +422,15 @@ extern "C" int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const voi
   p.a_scale = a_scale;
   p.b_scale = b_scale;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.ldo = ldo;
   p.res = static_cast<const __nv_bfloat16*>(residual);
   p.ldr = ldr;
   p.gate = gate;
   p.row_amax = row_amax;
   p.status = status;
   switch (epilogue) {
-    case EPI_STORE: return gemm::launch<EPI_STORE>(ta, tb, p, stream);
-    case EPI_GELU: return gemm::launch<EPI_GELU>(ta, tb, p, stream);
-    case EPI_GATED_RES: return gemm::launch<EPI_GATED_RES>(ta, tb, p, stream);
-    default: return gemm::launch<EPI_RES>(ta, tb, p, stream);
+    case EPI_STORE: return gemm::launch_bn<EPI_STORE>(bn, ta, tb, to, p, stream);
+    case EPI_GELU: return gemm::launch_bn<EPI_GELU>(bn, ta, tb, to, p, stream);
+    case EPI_GATED_RES: return gemm::launch_bn<EPI_GATED_RES>(bn, ta, tb, to, p, stream);
+    default: return gemm::launch_bn<EPI_RES>(bn, ta, tb, to, p, stream);
   }
 }
