@@ -35,14 +35,14 @@ constexpr int D = 128;
 constexpr int TILE = 128;
 constexpr int SLAB = TILE * 128;  // 128 rows x 128 bytes (64 bf16 head dims)
 constexpr int QKV_TILE_BYTES = 2 * SLAB;
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + QKV_TILE_BYTES;
+constexpr int OFF_Q = 0;  // two Q buffers (the next item's Q loads during this item)
+constexpr int OFF_K = OFF_Q + 2 * QKV_TILE_BYTES;
 constexpr int OFF_V = OFF_K + 2 * QKV_TILE_BYTES;
 constexpr int OFF_P = OFF_V + 2 * QKV_TILE_BYTES;
 constexpr int OFF_BAR = OFF_P + QKV_TILE_BYTES;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;  // S0 @0, S1 @128, O @256
+constexpr uint32_t TMEM_COLS = 512;  // S0 @0, S1 @128, O0 @256, O1 @384
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Args {
@@ -201,6 +201,16 @@ SRDIT_DEV float ex2_approx(float x) {
   return y;
 }
 
+// Work item = (window, 128-row query tile, head); items are walked head-major
+// so concurrently running CTAs share one head's K/V in L2.
+SRDIT_DEV void item_coords(const Args& a, int item, int& win, int& mt, int& head) {
+  const int per_head = a.n_w * a.m_tiles;
+  head = item / per_head;
+  const int r = item % per_head;
+  win = r / a.m_tiles;
+  mt = r % a.m_tiles;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     winattn_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmK,
@@ -211,35 +221,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_full = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* q_full = bars + 0;    // [2]
+  uint64_t* q_empty = bars + 2;   // [2]
+  uint64_t* k_full = bars + 4;    // [2]
+  uint64_t* k_empty = bars + 6;   // [2]
+  uint64_t* v_full = bars + 8;    // [2]
+  uint64_t* v_empty = bars + 10;  // [2]
+  uint64_t* s_full = bars + 12;   // [2]
+  uint64_t* p_full = bars + 14;
+  uint64_t* o_full = bars + 15;
+  uint64_t* o_empty = bars + 16;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int win = blockIdx.x / a.m_tiles;
-  const int mt = blockIdx.x % a.m_tiles;
-  const int head = blockIdx.y;
-
-  const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
-  const Walk w = make_walk(a, r, mt);
-  if (w.nqbox <= 0) return;  // shorter windows skip their tail tiles (uniform grid)
+  const int n_items = a.n_w * a.m_tiles * a.n_heads;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
+      mbar_init(&o_empty[i], 128);
     }
     mbar_init(p_full, 128);
     mbar_init(o_full, 1);
@@ -251,19 +259,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tmem_relinquish();
   }
   if (warp >= 2) {
-    // Rows of the Q tile that no box fills, and every V row, start at zero: an
-    // unwritten row must never feed a NaN into the tensor core (P = 0 there,
-    // but 0 * NaN is NaN).
+    // V rows that a tile shorter than its 16-row MMA extent leaves unwritten must
+    // never hold NaN (P is 0 there, but 0 * NaN is NaN): zero both V stages once.
     const int row = (warp & 3) * 32 + lane;
-    const int qrows = w.nqbox * a.bw_q * a.bh_q;
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-    if (row >= qrows) {
-      for (int h = 0; h < 2; ++h) {
-        uint4* dst = reinterpret_cast<uint4*>(smem + OFF_Q + h * SLAB + row * 128);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) dst[c] = z;
-      }
-    }
     for (int st = 0; st < 2; ++st)
       for (int h = 0; h < 2; ++h) {
         uint4* dst = reinterpret_cast<uint4*>(smem + OFF_V + st * QKV_TILE_BYTES + h * SLAB +
@@ -277,7 +276,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int T = w.n_tiles;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -286,73 +284,109 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const uint32_t q_box_bytes = static_cast<uint32_t>(a.bw_q * a.bh_q * 128);
-      mbar_arrive_expect_tx(q_full, q_box_bytes * 2u * static_cast<uint32_t>(w.nqbox));
-      for (int qb = 0; qb < w.nqbox; ++qb) {
-        const int g = w.qbox0 + qb;
-        const int t = g / w.hq_chunks, hc = g % w.hq_chunks;
-        for (int h = 0; h < 2; ++h)
-          tma_load_4d(smem + OFF_Q + h * SLAB + qb * static_cast<int>(q_box_bytes), &tmQ, q_full,
-                      head * D + h * 64, r.q_w0, r.q_h0 + hc * a.bh_q, r.q_t0 + t);
-      }
       bool ok = true;
-      int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
-      for (int j = 0; j < T && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-        const TileInfo ti = tile_info(a, w, j);
-        const uint32_t box_bytes = static_cast<uint32_t>(ti.bw * ti.bh * 128);
-        const uint32_t bytes = box_bytes * 2u * static_cast<uint32_t>(ti.nbox);
-        for (int kv = 0; kv < 2 && ok; ++kv) {
-          uint64_t* emp = kv ? &v_empty[st] : &k_empty[st];
-          uint64_t* ful = kv ? &v_full[st] : &k_full[st];
-          if (!mbar_wait(emp, ph ^ 1u, a.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          (kv ? last_v : last_k)[st] = static_cast<int>(ph);
-          mbar_arrive_expect_tx(ful, bytes);
-          uint8_t* base = smem + (kv ? OFF_V : OFF_K) + st * QKV_TILE_BYTES;
-          for (int b = 0; b < ti.nbox; ++b) {
-            const int gb = ti.box0 + b;
-            int c1, c2, c3;
-            const CUtensorMap* map;
-            if (ti.anchor) {
-              c1 = r.kw0_a;
-              c2 = r.kh0_a + gb * ti.bh;
-              c3 = ti.frame;
-              map = kv ? &tmVA : &tmKA;
-            } else {
-              const int t = gb / w.hr_hchunks, hc = gb % w.hr_hchunks;
-              c1 = r.kw0;
-              c2 = r.kh0 + hc * ti.bh;
-              c3 = (a.kv_slot0 + r.kv_t0 + t) % a.kv_slots;
-              map = kv ? &tmV : &tmK;
+      int g = 0, it = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        int win, mt, head;
+        item_coords(a, item, win, mt, head);
+        const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
+        const Walk w = make_walk(a, r, mt);
+        if (w.nqbox <= 0) continue;
+        const int b = it & 1;
+        if (!mbar_wait(&q_empty[b], (static_cast<uint32_t>(it >> 1) & 1u) ^ 1u, a.status,
+                       abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&q_full[b], q_box_bytes * 2u * static_cast<uint32_t>(w.nqbox));
+        for (int qb = 0; qb < w.nqbox; ++qb) {
+          const int gq = w.qbox0 + qb;
+          const int t = gq / w.hq_chunks, hc = gq % w.hq_chunks;
+          for (int h = 0; h < 2; ++h)
+            tma_load_4d(smem + OFF_Q + b * QKV_TILE_BYTES + h * SLAB +
+                            qb * static_cast<int>(q_box_bytes),
+                        &tmQ, &q_full[b], head * D + h * 64, r.q_w0, r.q_h0 + hc * a.bh_q,
+                        r.q_t0 + t);
+        }
+        for (int j = 0; j < w.n_tiles && ok; ++j, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
+          const TileInfo ti = tile_info(a, w, j);
+          const uint32_t box_bytes = static_cast<uint32_t>(ti.bw * ti.bh * 128);
+          const uint32_t bytes = box_bytes * 2u * static_cast<uint32_t>(ti.nbox);
+          for (int kv = 0; kv < 2; ++kv) {
+            uint64_t* emp = kv ? &v_empty[st] : &k_empty[st];
+            uint64_t* ful = kv ? &v_full[st] : &k_full[st];
+            if (!mbar_wait(emp, ph ^ 1u, a.status, abort_flag)) {
+              ok = false;
+              break;
             }
-            for (int h = 0; h < 2; ++h)
-              tma_load_4d(base + h * SLAB + b * static_cast<int>(box_bytes), map, ful,
-                          head * D + h * 64, c1, c2, c3);
+            mbar_arrive_expect_tx(ful, bytes);
+            uint8_t* base = smem + (kv ? OFF_V : OFF_K) + st * QKV_TILE_BYTES;
+            for (int bx = 0; bx < ti.nbox; ++bx) {
+              const int gb = ti.box0 + bx;
+              int c1, c2, c3;
+              const CUtensorMap* map;
+              if (ti.anchor) {
+                c1 = r.kw0_a;
+                c2 = r.kh0_a + gb * ti.bh;
+                c3 = ti.frame;
+                map = kv ? &tmVA : &tmKA;
+              } else {
+                const int t = gb / w.hr_hchunks, hc = gb % w.hr_hchunks;
+                c1 = r.kw0;
+                c2 = r.kh0 + hc * ti.bh;
+                c3 = (a.kv_slot0 + r.kv_t0 + t) % a.kv_slots;
+                map = kv ? &tmV : &tmK;
+              }
+              for (int h = 0; h < 2; ++h)
+                tma_load_4d(base + h * SLAB + bx * static_cast<int>(box_bytes), map, ful,
+                            head * D + h * 64, c1, c2, c3);
+            }
           }
         }
+        ++it;
       }
-      // Every load issued must land before the CTA can exit.
-      mbar_wait(q_full, 0, nullptr, nullptr);
-      for (int st = 0; st < 2; ++st) {
-        if (last_k[st] >= 0) mbar_wait(&k_full[st], static_cast<uint32_t>(last_k[st]), nullptr, nullptr);
-        if (last_v[st] >= 0) mbar_wait(&v_full[st], static_cast<uint32_t>(last_v[st]), nullptr, nullptr);
-      }
+      // after giving up, let issued loads land before the CTA exits
+      if (!ok)
+        for (int i = 0; i < 200; ++i) __nanosleep(1000);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      const uint32_t q_addr = smem_u32(smem + OFF_Q);
       const uint32_t p_addr = smem_u32(smem + OFF_P);
-      // S_j = Q . K_j^T  (M=128, N=n16, K=128 over 8 steps of 16)
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-        const TileInfo ti = tile_info(a, w, j);
+      bool ok = true;
+      // The flat tile sequence over this CTA's items; S MMAs run two tiles ahead
+      // of the P.V MMAs (double-buffered score tile).
+      int it_s = 0, item_s = blockIdx.x, j_s = 0, g_s = 0;  // next S to issue
+      Walk w_s;
+      int head_s = 0;
+      bool have_s = false;
+      auto next_item = [&](int& item, int& it, Walk& w, int& head) -> bool {
+        while (item < n_items) {
+          int win, mt;
+          item_coords(a, item, win, mt, head);
+          const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
+          w = make_walk(a, r, mt);
+          if (w.nqbox > 0) return true;
+          item += gridDim.x;
+        }
+        return false;
+      };
+      (void)head_s;
+      have_s = next_item(item_s, it_s, w_s, head_s);
+      auto issue_s = [&]() -> bool {
+        // S_g = Q . K_g^T into S[g & 1]
+        const int b = it_s & 1;
+        const int st = g_s & 1;
+        const uint32_t ph = static_cast<uint32_t>(g_s >> 1) & 1u;
+        const TileInfo ti = tile_info(a, w_s, j_s);
+        if (j_s == 0 &&
+            !mbar_wait(&q_full[b], static_cast<uint32_t>(it_s >> 1) & 1u, a.status, abort_flag))
+          return false;
         if (!mbar_wait(&k_full[st], ph, a.status, abort_flag)) return false;
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + OFF_Q + b * QKV_TILE_BYTES);
         const uint32_t k_addr = smem_u32(smem + OFF_K + st * QKV_TILE_BYTES);
         const uint32_t idesc = idesc_make(1u, 1u, 0u, 0u, 128u, static_cast<uint32_t>(ti.n16));
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(st * 128);
@@ -364,33 +398,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_commit(&k_empty[st]);
         tc_commit(&s_full[st]);
+        if (j_s == w_s.n_tiles - 1) tc_commit(&q_empty[b]);
+        // advance
+        ++g_s;
+        if (++j_s == w_s.n_tiles) {
+          j_s = 0;
+          ++it_s;
+          item_s += gridDim.x;
+          have_s = next_item(item_s, it_s, w_s, head_s);
+        }
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, a.status, abort_flag);
-      tc_fence_after();
-      if (ok) ok = issue_s(0);
-      if (ok && T > 1) ok = issue_s(1);
-      for (int j = 0; j < T && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-        const TileInfo ti = tile_info(a, w, j);
-        if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, a.status, abort_flag)) break;
-        if (!mbar_wait(&v_full[st], ph, a.status, abort_flag)) break;
-        tc_fence_after();
-        // O += P_j . V_j  (M=128, N=128 head dims, K=n16 over steps of 16)
-        const uint32_t v_addr = smem_u32(smem + OFF_V + st * QKV_TILE_BYTES);
-        const uint32_t idesc = idesc_make(1u, 1u, 0u, 1u, 128u, 128u);
-        const int ksteps = ti.n16 / 16;
-        for (int k = 0; k < ksteps; ++k) {
-          const uint32_t poff = static_cast<uint32_t>((k >> 2) * SLAB + (k & 3) * 32);
-          const uint32_t voff = static_cast<uint32_t>(k * 16 * 128);
-          mma_bf16_ss(tmem_base + 256u, sdesc_sw128(p_addr + poff, 16, 1024),
-                      sdesc_sw128(v_addr + voff, SLAB, 1024), idesc,
-                      (j > 0 || k > 0) ? 1u : 0u);
+      if (have_s) ok = issue_s();
+      if (ok && have_s) ok = issue_s();
+      // P.V side
+      int it = 0, item = blockIdx.x, g = 0, head = 0;
+      Walk w;
+      bool have = next_item(item, it, w, head);
+      while (ok && have) {
+        const int b = it & 1;
+        for (int j = 0; j < w.n_tiles && ok; ++j, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
+          const TileInfo ti = tile_info(a, w, j);
+          if (!mbar_wait(p_full, static_cast<uint32_t>(g) & 1u, a.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&v_full[st], ph, a.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (j == 0 && !mbar_wait(&o_empty[b], (static_cast<uint32_t>(it >> 1) & 1u) ^ 1u,
+                                   a.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // O[b] += P_g . V_g  (M=128, N=128 head dims, K=n16 in steps of 16)
+          const uint32_t v_addr = smem_u32(smem + OFF_V + st * QKV_TILE_BYTES);
+          const uint32_t idesc = idesc_make(1u, 1u, 0u, 1u, 128u, 128u);
+          const uint32_t o_tmem = tmem_base + 256u + static_cast<uint32_t>(b * 128);
+          const int ksteps = ti.n16 / 16;
+          for (int k = 0; k < ksteps; ++k) {
+            const uint32_t poff = static_cast<uint32_t>((k >> 2) * SLAB + (k & 3) * 32);
+            const uint32_t voff = static_cast<uint32_t>(k * 16 * 128);
+            mma_bf16_ss(o_tmem, sdesc_sw128(p_addr + poff, 16, 1024),
+                        sdesc_sw128(v_addr + voff, SLAB, 1024), idesc,
+                        (j > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&v_empty[st]);
+          tc_commit(o_full);
+          if (have_s) ok = issue_s();
         }
-        tc_commit(&v_empty[st]);
-        tc_commit(o_full);
-        if (j + 2 < T) ok = issue_s(j + 2);
+        ++it;
+        item += gridDim.x;
+        have = next_item(item, it, w, head);
       }
     }
   } else {
@@ -398,123 +461,136 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(sub * 32) << 16;
-    // this row's query token
-    const int rq = a.bw_q * a.bh_q;
-    const int qb = row / rq, rr = row % rq;
-    const int g = w.qbox0 + qb;
-    const int t_row = g / w.hq_chunks;
-    const int hh = (g % w.hq_chunks) * a.bh_q + rr / a.bw_q;
-    const int ww = rr % a.bw_q;
-    const bool row_ok = qb < w.nqbox && t_row < r.q_tL && hh < r.qhL && ww < r.qwL;
     const float neg_inf = -__int_as_float(0x7f800000);
-    float m_i = neg_inf, l_i = 0.f;
-    bool ok = true;
+    const float c_scale = a.scale * kLog2e;  // scores in log2 units
     uint8_t* prow = smem + OFF_P + row * 128;
     const int sw = row & 7;
-
-    for (int j = 0; j < T && ok; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-      const TileInfo ti = tile_info(a, w, j);
-      // column validity bitmask, 4 words, computed per warp by ballot
-      uint32_t vmask[4];
-      const int seg_khL = ti.anchor ? r.khL_a : r.khL;
-      const int seg_kwL = ti.anchor ? r.kwL_a : r.kwL;
-      const int hchunks = ti.anchor ? w.a_hchunks : w.hr_hchunks;
-      const int box_rows = ti.bw * ti.bh;
+    bool ok = true;
+    int g = 0, it = 0;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      int win, mt, head;
+      item_coords(a, item, win, mt, head);
+      const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
+      const Walk w = make_walk(a, r, mt);
+      if (w.nqbox <= 0) continue;
+      const int b = it & 1;
+      const int rq = a.bw_q * a.bh_q;
+      const int qb = row / rq, rr = row % rq;
+      const int gq = w.qbox0 + qb;
+      const int t_row = gq / w.hq_chunks;
+      const int hh = (gq % w.hq_chunks) * a.bh_q + rr / a.bw_q;
+      const int ww = rr % a.bw_q;
+      const bool row_ok = qb < w.nqbox && t_row < r.q_tL && hh < r.qhL && ww < r.qwL;
+      const uint32_t o_tmem = tmem_base + t_lane + 256u + static_cast<uint32_t>(b * 128);
+      float m_i = neg_inf, l_i = 0.f;
+      for (int j = 0; j < w.n_tiles; ++j, ++g) {
+        const int st = g & 1;
+        const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
+        const TileInfo ti = tile_info(a, w, j);
+        uint32_t vmask[4];
+        const int seg_khL = ti.anchor ? r.khL_a : r.khL;
+        const int seg_kwL = ti.anchor ? r.kwL_a : r.kwL;
+        const int hchunks = ti.anchor ? w.a_hchunks : w.hr_hchunks;
+        const int box_rows = ti.bw * ti.bh;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int c = q * 32 + lane;
-        const int bi = c / box_rows, cr = c % box_rows;
-        const int hc = (ti.box0 + bi) % hchunks;
-        const bool v = (c < ti.rows) && (hc * ti.bh + cr / ti.bw < seg_khL) &&
-                       (cr % ti.bw < seg_kwL);
-        vmask[q] = __ballot_sync(0xffffffffu, v);
-      }
-      const bool row_sees = !(ti.anchor && r.a_per_frame) || (t_row == ti.frame);
-
-      if (!mbar_wait(&s_full[st], ph, a.status, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // scores -> registers
-      float s[128];
-      const uint32_t s_tmem = tmem_base + t_lane + static_cast<uint32_t>(st * 128);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t u[32];
-        tmem_ld32(s_tmem + q * 32, u);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const bool v = row_sees && ((vmask[q] >> i) & 1u);
-          s[q * 32 + i] = v ? __fmul_rn(__uint_as_float(u[i]), a.scale) : neg_inf;
+        for (int q = 0; q < 4; ++q) {
+          const int c = q * 32 + lane;
+          const int bi = c / box_rows, cr = c % box_rows;
+          const int hc = (ti.box0 + bi) % hchunks;
+          const bool v = (c < ti.rows) && (hc * ti.bh + cr / ti.bw < seg_khL) &&
+                         (cr % ti.bw < seg_kwL);
+          vmask[q] = __ballot_sync(0xffffffffu, v);
         }
-      }
-      float row_max = neg_inf;
+        if (!(!(ti.anchor && r.a_per_frame) || (t_row == ti.frame))) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) row_max = fmaxf(row_max, s[c]);
-      const bool row_valid = row_max != neg_inf;
-      const float m_new = row_valid ? fmaxf(m_i, row_max) : m_i;
-      const float alpha = row_valid ? ex2_approx(__fmul_rn(__fsub_rn(m_i, m_new), kLog2e)) : 1.f;
-      float psum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float pv = (row_valid && s[c] != neg_inf)
-                             ? ex2_approx(__fmul_rn(__fsub_rn(s[c], m_new), kLog2e))
-                             : 0.f;
-        s[c] = pv;
-        psum = __fadd_rn(psum, pv);
-      }
-      l_i = __fadd_rn(__fmul_rn(alpha, l_i), psum);
-      m_i = m_new;
-
-      // PV_{j-1} must be complete before O is rescaled and P is overwritten.
-      if (j > 0) {
-        if (!mbar_wait(o_full, static_cast<uint32_t>(j - 1) & 1u, a.status, abort_flag)) {
+          for (int q = 0; q < 4; ++q) vmask[q] = 0u;
+        }
+        if (!mbar_wait(&s_full[st], ph, a.status, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          const uint32_t o_tmem = tmem_base + t_lane + 256u;
+        const uint32_t s_tmem = tmem_base + t_lane + static_cast<uint32_t>(st * 128);
+        const int nchunks = (ti.n16 + 31) >> 5;
+        // pass 1: row max (log2 units)
+        float row_max = neg_inf;
+        for (int q = 0; q < nchunks; ++q) {
+          uint32_t u[32];
+          tmem_ld32(s_tmem + q * 32, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if ((vmask[q] >> i) & 1u) row_max = fmaxf(row_max, __uint_as_float(u[i]) * c_scale);
+        }
+        const bool row_valid = row_max != neg_inf;
+        const float m_new = row_valid ? fmaxf(m_i, row_max) : m_i;
+        const float alpha = row_valid ? ex2_approx(m_i - m_new) : 1.f;
+        // P_g can only be written once P.V of the previous tile is done; that
+        // wait also makes O safe to rescale.
+        if (j > 0) {
+          if (!mbar_wait(o_full, static_cast<uint32_t>(g - 1) & 1u, a.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 4; ++q) {
+              uint32_t u[32];
+              tmem_ld32(o_tmem + q * 32, u);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+              tmem_st32(o_tmem + q * 32, u);
+            }
+            tmem_st_wait();
+          }
+        }
+        // pass 2: P = exp2(s - m) -> bf16 -> smem (K-major, 128B-swizzled)
+        float psum = 0.f;
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pw[16];
+          if (q < nchunks) {
             uint32_t u[32];
-            tmem_ld32(o_tmem + q * 32, u);
+            tmem_ld32(s_tmem + q * 32, u);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__fmul_rn(__uint_as_float(u[i]), alpha));
-            tmem_st32(o_tmem + q * 32, u);
+            for (int i = 0; i < 32; i += 2) {
+              const bool v0 = row_valid && ((vmask[q] >> i) & 1u);
+              const bool v1 = row_valid && ((vmask[q] >> (i + 1)) & 1u);
+              const float p0 = v0 ? ex2_approx(__uint_as_float(u[i]) * c_scale - m_new) : 0.f;
+              const float p1 = v1 ? ex2_approx(__uint_as_float(u[i + 1]) * c_scale - m_new) : 0.f;
+              psum += p0 + p1;
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+              pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pw[i] = 0u;
           }
-          tmem_st_wait();
-        }
-      }
-      // P_j (bf16) -> smem, K-major 128B-swizzled, 2 slabs of 64 columns
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        uint4 pk;
-        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          __nv_bfloat162 b2 = __floats2bfloat162_rn(s[q * 8 + 2 * h], s[q * 8 + 2 * h + 1]);
-          pw[h] = *reinterpret_cast<uint32_t*>(&b2);
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const int qq = q * 4 + c4;  // 16-byte chunk index of the 256-byte P row
+            const int slab = qq >> 3, chunk = (qq & 7) ^ sw;
+            *reinterpret_cast<uint4*>(prow + slab * SLAB + chunk * 16) =
+                make_uint4(pw[c4 * 4], pw[c4 * 4 + 1], pw[c4 * 4 + 2], pw[c4 * 4 + 3]);
+          }
         }
-        const int slab = q >> 3, chunk = (q & 7) ^ sw;
-        *reinterpret_cast<uint4*>(prow + slab * SLAB + chunk * 16) = pk;
+        l_i = alpha * l_i + psum;
+        m_i = m_new;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(p_full);
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-
-    if (ok && T > 0 && mbar_wait(o_full, static_cast<uint32_t>(T - 1) & 1u, a.status, abort_flag)) {
+      if (!ok) break;
+      // item done: the last P.V must land, then O / l -> bf16 -> out
+      if (!mbar_wait(o_full, static_cast<uint32_t>(g - 1) & 1u, a.status, abort_flag)) break;
       tc_fence_after();
-      const uint32_t o_tmem = tmem_base + t_lane + 256u;
       const long long tok = static_cast<long long>(r.q_t0 + t_row) * a.q_h * a.q_w +
                             static_cast<long long>(r.q_h0 + hh) * a.q_w + (r.q_w0 + ww);
       __nv_bfloat16* orow = a.out + tok * a.o_stride + head * D;
+      const float inv_l = 1.0f / l_i;
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
         uint32_t u[32];
@@ -527,15 +603,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-              const float o0 = __fdiv_rn(__uint_as_float(u[v4 * 8 + 2 * h]), l_i);
-              const float o1 = __fdiv_rn(__uint_as_float(u[v4 * 8 + 2 * h + 1]), l_i);
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(o0, o1);
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(u[v4 * 8 + 2 * h]) * inv_l,
+                                                        __uint_as_float(u[v4 * 8 + 2 * h + 1]) * inv_l);
               pw[h] = *reinterpret_cast<uint32_t*>(&b2);
             }
             *reinterpret_cast<uint4*>(orow + q * 32 + v4 * 8) = pk;
           }
         }
       }
+      tc_fence_before();
+      mbar_arrive(&o_empty[b]);
+      ++it;
     }
   }
 
@@ -546,6 +624,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
+
 
 }  // namespace attn
 }  // namespace srdit
@@ -750,7 +829,9 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>(n_w * t->m_tiles), static_cast<unsigned>(g->n_heads));
+  const long long items = static_cast<long long>(n_w) * t->m_tiles * g->n_heads;
+  const int sms = num_sms(dev);
+  dim3 grid(static_cast<unsigned>(items < sms ? items : sms));
   attn::winattn_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(mq, mk, mv, mka,
                                                                                mva, a);
   return static_cast<int>(cudaGetLastError());
