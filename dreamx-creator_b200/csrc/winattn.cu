@@ -463,8 +463,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t t_lane = static_cast<uint32_t>(sub * 32) << 16;
     const float neg_inf = -__int_as_float(0x7f800000);
     const float c_scale = a.scale * kLog2e;  // scores in log2 units
+    // The running max is only raised (and O rescaled) once a tile's max exceeds
+    // it by more than this many log2 units; in between, P = exp2(s - m_stale) is
+    // at most 2^8, so the sum and the P.V accumulation stay exact up to rounding.
+    const float kRescale = 8.0f;
     uint8_t* prow = smem + OFF_P + row * 128;
     const int sw = row & 7;
+    // Column c of a KV tile -> (box within the tile, row of the box, column of
+    // the box): fixed for the whole launch, one decomposition per segment.
+    int bi_k[4], hr_k[4], cw_k[4], bi_a[4], hr_a[4], cw_a[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = q * 32 + lane;
+      const int rk = a.bw_k * a.bh_k, ra = a.bw_a * a.bh_a;
+      bi_k[q] = c / rk;
+      hr_k[q] = (c % rk) / a.bw_k;
+      cw_k[q] = (c % rk) % a.bw_k;
+      bi_a[q] = c / ra;
+      hr_a[q] = (c % ra) / a.bw_a;
+      cw_a[q] = (c % ra) % a.bw_a;
+    }
     bool ok = true;
     int g = 0, it = 0;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -487,24 +505,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int st = g & 1;
         const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
         const TileInfo ti = tile_info(a, w, j);
+        // column validity (ballot over lanes: bit i of vmask[q] = column 32q + i)
         uint32_t vmask[4];
-        const int seg_khL = ti.anchor ? r.khL_a : r.khL;
-        const int seg_kwL = ti.anchor ? r.kwL_a : r.kwL;
-        const int hchunks = ti.anchor ? w.a_hchunks : w.hr_hchunks;
-        const int box_rows = ti.bw * ti.bh;
+        {
+          const int khl = ti.anchor ? r.khL_a : r.khL;
+          const int kwl = ti.anchor ? r.kwL_a : r.kwL;
+          const int hch = ti.anchor ? w.a_hchunks : w.hr_hchunks;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int c = q * 32 + lane;
-          const int bi = c / box_rows, cr = c % box_rows;
-          const int hc = (ti.box0 + bi) % hchunks;
-          const bool v = (c < ti.rows) && (hc * ti.bh + cr / ti.bw < seg_khL) &&
-                         (cr % ti.bw < seg_kwL);
-          vmask[q] = __ballot_sync(0xffffffffu, v);
+          for (int q = 0; q < 4; ++q) {
+            const int c = q * 32 + lane;
+            const int bi = ti.anchor ? bi_a[q] : bi_k[q];
+            const int hr = ti.anchor ? hr_a[q] : hr_k[q];
+            const int cw = ti.anchor ? cw_a[q] : cw_k[q];
+            const int hc = (ti.box0 + bi) % hch;
+            const bool v = (c < ti.rows) && (hc * ti.bh + hr < khl) && (cw < kwl);
+            vmask[q] = __ballot_sync(0xffffffffu, v);
+          }
         }
-        if (!(!(ti.anchor && r.a_per_frame) || (t_row == ti.frame))) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) vmask[q] = 0u;
-        }
+        const bool sees = !(ti.anchor && r.a_per_frame) || (t_row == ti.frame);
         if (!mbar_wait(&s_full[st], ph, a.status, abort_flag)) {
           ok = false;
           break;
@@ -512,19 +530,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t s_tmem = tmem_base + t_lane + static_cast<uint32_t>(st * 128);
         const int nchunks = (ti.n16 + 31) >> 5;
-        // pass 1: row max (log2 units)
-        float row_max = neg_inf;
-        for (int q = 0; q < nchunks; ++q) {
-          uint32_t u[32];
-          tmem_ld32(s_tmem + q * 32, u);
-          tmem_ld_wait();
+        // pass 1: tile row max (log2 units), two 32-column chunks per TMEM wait
+        float tmax = neg_inf;
+        auto chunk_max = [&](const uint32_t (&u)[32], uint32_t vm) {
+          float mx = neg_inf;
+          if (vm == 0xffffffffu) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if ((vmask[q] >> i) & 1u) row_max = fmaxf(row_max, __uint_as_float(u[i]) * c_scale);
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(u[i]));
+          } else if (vm != 0u) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              mx = fmaxf(mx, ((vm >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf);
+          }
+          tmax = fmaxf(tmax, mx);
+        };
+#pragma unroll
+        for (int q0 = 0; q0 < 4; q0 += 2) {
+          if (q0 < nchunks) {
+            uint32_t u0[32], u1[32];
+            tmem_ld32(s_tmem + q0 * 32, u0);
+            if (q0 + 1 < nchunks) tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
+            tmem_ld_wait();
+            chunk_max(u0, vmask[q0]);
+            if (q0 + 1 < nchunks) chunk_max(u1, vmask[q0 + 1]);
+          }
         }
-        const bool row_valid = row_max != neg_inf;
-        const float m_new = row_valid ? fmaxf(m_i, row_max) : m_i;
-        const float alpha = row_valid ? ex2_approx(m_i - m_new) : 1.f;
+        tmax = sees ? tmax * c_scale : neg_inf;
+        const bool row_valid = tmax != neg_inf;
+        // new running max: raised only past the rescale threshold
+        const bool raise = row_valid && (tmax > m_i + kRescale || m_i == neg_inf);
+        const float m_new = raise ? tmax : m_i;
+        const float alpha = raise ? ex2_approx(m_i - m_new) : 1.f;
         // P_g can only be written once P.V of the previous tile is done; that
         // wait also makes O safe to rescale.
         if (j > 0) {
@@ -535,47 +571,71 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-            for (int q = 0; q < 4; ++q) {
-              uint32_t u[32];
-              tmem_ld32(o_tmem + q * 32, u);
+            for (int q = 0; q < 4; q += 2) {
+              uint32_t u0[32], u1[32];
+              tmem_ld32(o_tmem + q * 32, u0);
+              tmem_ld32(o_tmem + (q + 1) * 32, u1);
               tmem_ld_wait();
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-              tmem_st32(o_tmem + q * 32, u);
+              for (int i = 0; i < 32; ++i) {
+                u0[i] = __float_as_uint(__uint_as_float(u0[i]) * alpha);
+                u1[i] = __float_as_uint(__uint_as_float(u1[i]) * alpha);
+              }
+              tmem_st32(o_tmem + q * 32, u0);
+              tmem_st32(o_tmem + (q + 1) * 32, u1);
             }
             tmem_st_wait();
           }
         }
-        // pass 2: P = exp2(s - m) -> bf16 -> smem (K-major, 128B-swizzled)
+        // pass 2: P = exp2(s*c - m) -> bf16 -> smem (K-major, 128B-swizzled)
         float psum = 0.f;
-        for (int q = 0; q < 4; ++q) {
-          uint32_t pw[16];
-          if (q < nchunks) {
-            uint32_t u[32];
-            tmem_ld32(s_tmem + q * 32, u);
-            tmem_ld_wait();
+        const float neg_m = -m_new;
+        auto chunk_p = [&](const uint32_t (&u)[32], int q) {
+            const uint32_t vm = (q < nchunks && row_valid) ? vmask[q] : 0u;
+            uint32_t pw[16];
+            if (vm == 0xffffffffu) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const bool v0 = row_valid && ((vmask[q] >> i) & 1u);
-              const bool v1 = row_valid && ((vmask[q] >> (i + 1)) & 1u);
-              const float p0 = v0 ? ex2_approx(__uint_as_float(u[i]) * c_scale - m_new) : 0.f;
-              const float p1 = v1 ? ex2_approx(__uint_as_float(u[i + 1]) * c_scale - m_new) : 0.f;
-              psum += p0 + p1;
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-              pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+              for (int i = 0; i < 32; i += 2) {
+                const float p0 = ex2_approx(fmaf(__uint_as_float(u[i]), c_scale, neg_m));
+                const float p1 = ex2_approx(fmaf(__uint_as_float(u[i + 1]), c_scale, neg_m));
+                psum += p0 + p1;
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+                pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+              }
+            } else if (vm != 0u) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const float p0 = ((vm >> i) & 1u)
+                                     ? ex2_approx(fmaf(__uint_as_float(u[i]), c_scale, neg_m))
+                                     : 0.f;
+                const float p1 = ((vm >> (i + 1)) & 1u)
+                                     ? ex2_approx(fmaf(__uint_as_float(u[i + 1]), c_scale, neg_m))
+                                     : 0.f;
+                psum += p0 + p1;
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+                pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) pw[i] = 0u;
             }
-          } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) pw[i] = 0u;
-          }
+            for (int c4 = 0; c4 < 4; ++c4) {
+              const int qq = q * 4 + c4;  // 16-byte chunk index of the 256-byte P row
+              const int slab = qq >> 3, chunk = (qq & 7) ^ sw;
+              *reinterpret_cast<uint4*>(prow + slab * SLAB + chunk * 16) =
+                  make_uint4(pw[c4 * 4], pw[c4 * 4 + 1], pw[c4 * 4 + 2], pw[c4 * 4 + 3]);
+            }
+        };
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            const int qq = q * 4 + c4;  // 16-byte chunk index of the 256-byte P row
-            const int slab = qq >> 3, chunk = (qq & 7) ^ sw;
-            *reinterpret_cast<uint4*>(prow + slab * SLAB + chunk * 16) =
-                make_uint4(pw[c4 * 4], pw[c4 * 4 + 1], pw[c4 * 4 + 2], pw[c4 * 4 + 3]);
-          }
+        for (int q0 = 0; q0 < 4; q0 += 2) {
+          uint32_t u0[32], u1[32];
+          const bool ld0 = q0 < nchunks, ld1 = q0 + 1 < nchunks;
+          if (ld0) tmem_ld32(s_tmem + q0 * 32, u0);
+          if (ld1) tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
+          if (ld0) tmem_ld_wait();
+          chunk_p(u0, q0);
+          chunk_p(u1, q0 + 1);
         }
         l_i = alpha * l_i + psum;
         m_i = m_new;
