@@ -83,13 +83,27 @@ SRDIT_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 //
 // `abort_flag` (shared memory, may be null) lets one role that already gave up
 // release the others quickly: every waiter polls it and returns false once set.
+// try_wait that lets the thread sleep (up to `hint_ns`) until the phase completes,
+// instead of re-issuing the poll.
+SRDIT_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 SRDIT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
                          volatile uint32_t* abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    for (int i = 0; i < 64; ++i) {
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 8; ++i) {
+      if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     }
     if (abort_flag && *abort_flag) return false;
     if (global_timer_ns() - t0 > kWaitBudgetNs) {

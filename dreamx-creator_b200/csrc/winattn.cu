@@ -353,38 +353,55 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Two cursors walk this CTA's flat tile sequence: the S cursor issues
+    // S_g = Q.K_g^T (up to two tiles ahead, double-buffered score tile), the PV
+    // cursor issues O += P_g.V_g once the softmax published P_g. Whichever is
+    // ready goes first, so a late K tile never holds back the P.V chain.
     if (elect_one()) {
       const uint32_t p_addr = smem_u32(smem + OFF_P);
-      bool ok = true;
-      // The flat tile sequence over this CTA's items; S MMAs run two tiles ahead
-      // of the P.V MMAs (double-buffered score tile).
-      int it_s = 0, item_s = blockIdx.x, j_s = 0, g_s = 0;  // next S to issue
-      Walk w_s;
-      int head_s = 0;
-      bool have_s = false;
-      auto next_item = [&](int& item, int& it, Walk& w, int& head) -> bool {
-        while (item < n_items) {
-          int win, mt;
-          item_coords(a, item, win, mt, head);
-          const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
-          w = make_walk(a, r, mt);
-          if (w.nqbox > 0) return true;
-          item += gridDim.x;
-        }
-        return false;
+      struct Cursor {
+        int item, it, j, g, head;
+        Walk w;
+        bool have;
       };
-      (void)head_s;
-      have_s = next_item(item_s, it_s, w_s, head_s);
-      auto issue_s = [&]() -> bool {
-        // S_g = Q . K_g^T into S[g & 1]
-        const int b = it_s & 1;
-        const int st = g_s & 1;
-        const uint32_t ph = static_cast<uint32_t>(g_s >> 1) & 1u;
-        const TileInfo ti = tile_info(a, w_s, j_s);
-        if (j_s == 0 &&
-            !mbar_wait(&q_full[b], static_cast<uint32_t>(it_s >> 1) & 1u, a.status, abort_flag))
+      auto seek = [&](Cursor& c) {
+        c.have = false;
+        while (c.item < n_items) {
+          int win, mt;
+          item_coords(a, c.item, win, mt, c.head);
+          const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
+          c.w = make_walk(a, r, mt);
+          if (c.w.nqbox > 0) {
+            c.have = true;
+            return;
+          }
+          c.item += gridDim.x;
+        }
+      };
+      auto advance = [&](Cursor& c) {
+        ++c.g;
+        if (++c.j == c.w.n_tiles) {
+          c.j = 0;
+          ++c.it;
+          c.item += gridDim.x;
+          seek(c);
+        }
+      };
+      Cursor cs{static_cast<int>(blockIdx.x), 0, 0, 0, 0, Walk{}, false};
+      Cursor cp = cs;
+      seek(cs);
+      seek(cp);
+      auto s_ready = [&]() -> bool {
+        if (!cs.have || cs.g >= cp.g + 2) return false;  // score buffer still in use
+        const int st = cs.g & 1;
+        if (cs.j == 0 && !mbar_try_wait(&q_full[cs.it & 1], static_cast<uint32_t>(cs.it >> 1) & 1u))
           return false;
-        if (!mbar_wait(&k_full[st], ph, a.status, abort_flag)) return false;
+        return mbar_try_wait(&k_full[st], static_cast<uint32_t>(cs.g >> 1) & 1u);
+      };
+      auto issue_s = [&]() {
+        const int b = cs.it & 1;
+        const int st = cs.g & 1;
+        const TileInfo ti = tile_info(a, cs.w, cs.j);
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + OFF_Q + b * QKV_TILE_BYTES);
         const uint32_t k_addr = smem_u32(smem + OFF_K + st * QKV_TILE_BYTES);
@@ -398,62 +415,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_commit(&k_empty[st]);
         tc_commit(&s_full[st]);
-        if (j_s == w_s.n_tiles - 1) tc_commit(&q_empty[b]);
-        // advance
-        ++g_s;
-        if (++j_s == w_s.n_tiles) {
-          j_s = 0;
-          ++it_s;
-          item_s += gridDim.x;
-          have_s = next_item(item_s, it_s, w_s, head_s);
-        }
+        if (cs.j == cs.w.n_tiles - 1) tc_commit(&q_empty[b]);
+        advance(cs);
+      };
+      auto pv_ready = [&]() -> bool {
+        if (!cp.have || cp.g >= cs.g) return false;  // S_g not issued yet
+        const int st = cp.g & 1;
+        if (!mbar_try_wait(p_full, static_cast<uint32_t>(cp.g) & 1u)) return false;
+        if (!mbar_try_wait(&v_full[st], static_cast<uint32_t>(cp.g >> 1) & 1u)) return false;
+        if (cp.j == 0 && !mbar_try_wait(&o_empty[cp.it & 1],
+                                        (static_cast<uint32_t>(cp.it >> 1) & 1u) ^ 1u))
+          return false;
         return true;
       };
-      if (have_s) ok = issue_s();
-      if (ok && have_s) ok = issue_s();
-      // P.V side
-      int it = 0, item = blockIdx.x, g = 0, head = 0;
-      Walk w;
-      bool have = next_item(item, it, w, head);
-      while (ok && have) {
-        const int b = it & 1;
-        for (int j = 0; j < w.n_tiles && ok; ++j, ++g) {
-          const int st = g & 1;
-          const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
-          const TileInfo ti = tile_info(a, w, j);
-          if (!mbar_wait(p_full, static_cast<uint32_t>(g) & 1u, a.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          if (!mbar_wait(&v_full[st], ph, a.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          if (j == 0 && !mbar_wait(&o_empty[b], (static_cast<uint32_t>(it >> 1) & 1u) ^ 1u,
-                                   a.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // O[b] += P_g . V_g  (M=128, N=128 head dims, K=n16 in steps of 16)
-          const uint32_t v_addr = smem_u32(smem + OFF_V + st * QKV_TILE_BYTES);
-          const uint32_t idesc = idesc_make(1u, 1u, 0u, 1u, 128u, 128u);
-          const uint32_t o_tmem = tmem_base + 256u + static_cast<uint32_t>(b * 128);
-          const int ksteps = ti.n16 / 16;
-          for (int k = 0; k < ksteps; ++k) {
-            const uint32_t poff = static_cast<uint32_t>((k >> 2) * SLAB + (k & 3) * 32);
-            const uint32_t voff = static_cast<uint32_t>(k * 16 * 128);
-            mma_bf16_ss(o_tmem, sdesc_sw128(p_addr + poff, 16, 1024),
-                        sdesc_sw128(v_addr + voff, SLAB, 1024), idesc,
-                        (j > 0 || k > 0) ? 1u : 0u);
-          }
-          tc_commit(&v_empty[st]);
-          tc_commit(o_full);
-          if (have_s) ok = issue_s();
+      auto issue_pv = [&]() {
+        const int b = cp.it & 1;
+        const int st = cp.g & 1;
+        const TileInfo ti = tile_info(a, cp.w, cp.j);
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + OFF_V + st * QKV_TILE_BYTES);
+        const uint32_t idesc = idesc_make(1u, 1u, 0u, 1u, 128u, 128u);
+        const uint32_t o_tmem = tmem_base + 256u + static_cast<uint32_t>(b * 128);
+        const int ksteps = ti.n16 / 16;
+        for (int k = 0; k < ksteps; ++k) {
+          const uint32_t poff = static_cast<uint32_t>((k >> 2) * SLAB + (k & 3) * 32);
+          const uint32_t voff = static_cast<uint32_t>(k * 16 * 128);
+          mma_bf16_ss(o_tmem, sdesc_sw128(p_addr + poff, 16, 1024),
+                      sdesc_sw128(v_addr + voff, SLAB, 1024), idesc,
+                      (cp.j > 0 || k > 0) ? 1u : 0u);
         }
-        ++it;
-        item += gridDim.x;
-        have = next_item(item, it, w, head);
+        tc_commit(&v_empty[st]);
+        tc_commit(o_full);
+        advance(cp);
+      };
+      uint64_t idle_since = 0;
+      while (cp.have) {
+        bool did = false;
+        if (pv_ready()) {
+          issue_pv();
+          did = true;
+        }
+        if (s_ready()) {
+          issue_s();
+          did = true;
+        }
+        if (did) {
+          idle_since = 0;
+        } else {
+          const uint64_t now = global_timer_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > kWaitBudgetNs || *abort_flag) {
+            atomicOr(a.status, kStatusTimeout);
+            *abort_flag = 1u;
+            break;
+          }
+        }
       }
     }
   } else {
@@ -499,6 +516,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int hh = (gq % w.hq_chunks) * a.bh_q + rr / a.bw_q;
       const int ww = rr % a.bw_q;
       const bool row_ok = qb < w.nqbox && t_row < r.q_tL && hh < r.qhL && ww < r.qwL;
+      // A warp whose rows are all padding keeps the barrier protocol but skips
+      // the math (its rows are never stored).
+      const bool active = __any_sync(0xffffffffu, row_ok);
       const uint32_t o_tmem = tmem_base + t_lane + 256u + static_cast<uint32_t>(b * 128);
       float m_i = neg_inf, l_i = 0.f;
       for (int j = 0; j < w.n_tiles; ++j, ++g) {
@@ -532,30 +552,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int nchunks = (ti.n16 + 31) >> 5;
         // pass 1: tile row max (log2 units), two 32-column chunks per TMEM wait
         float tmax = neg_inf;
-        auto chunk_max = [&](const uint32_t (&u)[32], uint32_t vm) {
-          float mx = neg_inf;
-          if (vm == 0xffffffffu) {
+        // masked-out columns become -inf in place, then one body for every chunk
+        auto mask_chunk = [&](uint32_t (&u)[32], uint32_t vm) {
+          if (vm != 0xffffffffu) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(u[i]));
-          } else if (vm != 0u) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              mx = fmaxf(mx, ((vm >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf);
+            for (int i = 0; i < 32; ++i) u[i] = ((vm >> i) & 1u) ? u[i] : 0xff800000u;
           }
-          tmax = fmaxf(tmax, mx);
         };
+        auto chunk_max = [&](const uint32_t (&u)[32]) {
+          float m0 = neg_inf, m1 = neg_inf;
 #pragma unroll
-        for (int q0 = 0; q0 < 4; q0 += 2) {
-          if (q0 < nchunks) {
+          for (int i = 0; i < 32; i += 2) {
+            m0 = fmaxf(m0, __uint_as_float(u[i]));
+            m1 = fmaxf(m1, __uint_as_float(u[i + 1]));
+          }
+          tmax = fmaxf(tmax, fmaxf(m0, m1));
+        };
+        // this row's masks (a per-frame anchor tile is invisible to other frames)
+        uint32_t vm_row[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) vm_row[q] = (sees && q < nchunks) ? vmask[q] : 0u;
+        if (active) {  // warp-uniform: tcgen05.ld is a warp-collective instruction
+          for (int q0 = 0; q0 < nchunks; q0 += 2) {
             uint32_t u0[32], u1[32];
             tmem_ld32(s_tmem + q0 * 32, u0);
-            if (q0 + 1 < nchunks) tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
+            tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
             tmem_ld_wait();
-            chunk_max(u0, vmask[q0]);
-            if (q0 + 1 < nchunks) chunk_max(u1, vmask[q0 + 1]);
+            mask_chunk(u0, vm_row[q0]);
+            mask_chunk(u1, vm_row[q0 + 1]);
+            chunk_max(u0);
+            chunk_max(u1);
           }
         }
-        tmax = sees ? tmax * c_scale : neg_inf;
+        tmax = tmax * c_scale;
         const bool row_valid = tmax != neg_inf;
         // new running max: raised only past the rescale threshold
         const bool raise = row_valid && (tmax > m_i + kRescale || m_i == neg_inf);
@@ -589,35 +618,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         // pass 2: P = exp2(s*c - m) -> bf16 -> smem (K-major, 128B-swizzled)
         float psum = 0.f;
-        const float neg_m = -m_new;
-        auto chunk_p = [&](const uint32_t (&u)[32], int q) {
-            const uint32_t vm = (q < nchunks && row_valid) ? vmask[q] : 0u;
+        const float neg_m = row_valid ? -m_new : 0.f;  // rows seeing nothing: all P = 0
+        float ps0 = 0.f, ps1 = 0.f;
+        auto chunk_p = [&](uint32_t (&u)[32], int q) {
+            // u already has its masked columns at -inf: exp2(-inf) = 0
             uint32_t pw[16];
-            if (vm == 0xffffffffu) {
 #pragma unroll
-              for (int i = 0; i < 32; i += 2) {
-                const float p0 = ex2_approx(fmaf(__uint_as_float(u[i]), c_scale, neg_m));
-                const float p1 = ex2_approx(fmaf(__uint_as_float(u[i + 1]), c_scale, neg_m));
-                psum += p0 + p1;
-                __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-                pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
-              }
-            } else if (vm != 0u) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 2) {
-                const float p0 = ((vm >> i) & 1u)
-                                     ? ex2_approx(fmaf(__uint_as_float(u[i]), c_scale, neg_m))
-                                     : 0.f;
-                const float p1 = ((vm >> (i + 1)) & 1u)
-                                     ? ex2_approx(fmaf(__uint_as_float(u[i + 1]), c_scale, neg_m))
-                                     : 0.f;
-                psum += p0 + p1;
-                __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-                pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) pw[i] = 0u;
+            for (int i = 0; i < 32; i += 2) {
+              const float p0 = ex2_approx(fmaf(__uint_as_float(u[i]), c_scale, neg_m));
+              const float p1 = ex2_approx(fmaf(__uint_as_float(u[i + 1]), c_scale, neg_m));
+              ps0 += p0;
+              ps1 += p1;
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+              pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
             }
 #pragma unroll
             for (int c4 = 0; c4 < 4; ++c4) {
@@ -627,16 +640,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   make_uint4(pw[c4 * 4], pw[c4 * 4 + 1], pw[c4 * 4 + 2], pw[c4 * 4 + 3]);
             }
         };
-#pragma unroll
-        for (int q0 = 0; q0 < 4; q0 += 2) {
-          uint32_t u0[32], u1[32];
-          const bool ld0 = q0 < nchunks, ld1 = q0 + 1 < nchunks;
-          if (ld0) tmem_ld32(s_tmem + q0 * 32, u0);
-          if (ld1) tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
-          if (ld0) tmem_ld_wait();
-          chunk_p(u0, q0);
-          chunk_p(u1, q0 + 1);
+        if (active) {
+          for (int q0 = 0; q0 < nchunks; q0 += 2) {
+            uint32_t u0[32], u1[32];
+            tmem_ld32(s_tmem + q0 * 32, u0);
+            tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
+            tmem_ld_wait();
+            mask_chunk(u0, row_valid ? vm_row[q0] : 0u);
+            mask_chunk(u1, row_valid ? vm_row[q0 + 1] : 0u);
+            chunk_p(u0, q0);
+            chunk_p(u1, q0 + 1);
+          }
         }
+        psum = ps0 + ps1;
         l_i = alpha * l_i + psum;
         m_i = m_new;
         fence_proxy_async_smem();
@@ -652,7 +668,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __nv_bfloat16* orow = a.out + tok * a.o_stride + head * D;
       const float inv_l = 1.0f / l_i;
 #pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < (active ? 4 : 0); ++q) {
         uint32_t u[32];
         tmem_ld32(o_tmem + q * 32, u);
         tmem_ld_wait();
