@@ -54,15 +54,27 @@ SRDIT_DEV uint4 pack8(const float (&f)[8]) {
 }
 SRDIT_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// x / s rounded to nearest, for a per-row divisor s with its correctly rounded
+// reciprocal r: q0 = x*r, then one residual correction q0 + (x - q0*s)*r with
+// the residual formed exactly by an FMA (Markstein's division correction,
+// IBM J. Res. Dev. 34(1), 1990). Here |x/s| <= 448 and s >= 1e-12, far from
+// the exponent range where the correction can be off; the GPU tests compare the
+// quantised bytes bit for bit with an IEEE-division reference.
+SRDIT_DEV float div_by(float x, float s, float r) {
+  const float q0 = x * r;
+  const float e = fmaf(-q0, s, x);
+  return fmaf(e, r, q0);
+}
+
 // e4m3 of (x / scale) clamped to +-448: the reference's
 // (x.float() / scale).clamp(-FP8_MAX, FP8_MAX).to(float8_e4m3fn).
-SRDIT_DEV uint2 quant8(const float (&f)[8], float scale) {
+SRDIT_DEV uint2 quant8(const float (&f)[8], float scale, float rscale) {
   uint2 out;
   uint16_t* h = reinterpret_cast<uint16_t*>(&out);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float a = fminf(fmaxf(__fdiv_rn(f[2 * i], scale), -kFp8Max), kFp8Max);
-    const float b = fminf(fmaxf(__fdiv_rn(f[2 * i + 1], scale), -kFp8Max), kFp8Max);
+    const float a = fminf(fmaxf(div_by(f[2 * i], scale, rscale), -kFp8Max), kFp8Max);
+    const float b = fminf(fmaxf(div_by(f[2 * i + 1], scale, rscale), -kFp8Max), kFp8Max);
     h[i] = static_cast<uint16_t>(
         __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
   }
@@ -95,11 +107,12 @@ __global__ void quant_rowwise_kernel(const __nv_bfloat16* __restrict__ x, long l
     amax = warp_max(amax);
   }
   const float s = scale_of(amax);
+  const float rs = __frcp_rn(s);
   uint8_t* qr = q + row * ldq;
   for (int c = lane * 8; c < K; c += 256) {
     float f[8];
     unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
-    *reinterpret_cast<uint2*>(qr + c) = quant8(f, s);
+    *reinterpret_cast<uint2*>(qr + c) = quant8(f, s, rs);
   }
   if (lane == 0) scale_out[row] = s;
 }
@@ -144,6 +157,16 @@ __global__ void ln_mod_quant_kernel(const __nv_bfloat16* __restrict__ x, long lo
     float wv[8], bv[8];
     if (ln_w) unpack8(*reinterpret_cast<const uint4*>(ln_w + c0), wv);
     if (ln_b) unpack8(*reinterpret_cast<const uint4*>(ln_b + c0), bv);
+    float sc[8], sh[8];
+    if (scale) {
+      const float4* s4 = reinterpret_cast<const float4*>(scale + c0);
+      const float4* h4 = reinterpret_cast<const float4*>(shift + c0);
+      const float4 s0 = __ldg(s4), s1 = __ldg(s4 + 1), h0 = __ldg(h4), h1 = __ldg(h4 + 1);
+      sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w;
+      sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+      sh[0] = h0.x; sh[1] = h0.y; sh[2] = h0.z; sh[3] = h0.w;
+      sh[4] = h1.x; sh[5] = h1.y; sh[6] = h1.z; sh[7] = h1.w;
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       float n = (v[i][e] - mean) * rstd;
@@ -151,8 +174,8 @@ __global__ void ln_mod_quant_kernel(const __nv_bfloat16* __restrict__ x, long lo
       if (ln_b) n = n + bv[e];
       n = bf16_round(n);  // WanLayerNorm returns .type_as(x)
       if (scale) {
-        const float one_p = __fadd_rn(1.0f, __ldg(scale + c0 + e));
-        n = bf16_round(__fadd_rn(__fmul_rn(n, one_p), __ldg(shift + c0 + e)));
+        const float one_p = __fadd_rn(1.0f, sc[e]);
+        n = bf16_round(__fadd_rn(__fmul_rn(n, one_p), sh[e]));
       }
       v[i][e] = n;
       amax = fmaxf(amax, fabsf(n));
@@ -160,10 +183,11 @@ __global__ void ln_mod_quant_kernel(const __nv_bfloat16* __restrict__ x, long lo
   }
   amax = warp_max(amax);
   const float s = scale_of(amax);
+  const float rs = __frcp_rn(s);
   uint8_t* qr = q + row * ldq;
 #pragma unroll
   for (int i = 0; i < VEC; ++i)
-    *reinterpret_cast<uint2*>(qr + i * 256 + lane * 8) = quant8(v[i], s);
+    *reinterpret_cast<uint2*>(qr + i * 256 + lane * 8) = quant8(v[i], s, rs);
   if (lane == 0) qscale[row] = s;
 }
 
@@ -311,6 +335,9 @@ extern "C" int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, fl
   if (!x || !q || !qscale || M < 0) return SRDIT_EINVAL;
   if ((scale == nullptr) != (shift == nullptr)) return SRDIT_EINVAL;
   if ((ldx % 8) || (ldq % 16) || !aligned16(x) || !aligned16(q)) return SRDIT_EALIGN;
+  if ((scale && (!aligned16(scale) || !aligned16(shift))) ||
+      (ln_weight && !aligned16(ln_weight)) || (ln_bias && !aligned16(ln_bias)))
+    return SRDIT_EALIGN;
   return ew::dispatch_vec<ew::LnLaunch>(
       K, static_cast<const __nv_bfloat16*>(x), ldx, M, eps,
       static_cast<const __nv_bfloat16*>(ln_weight), static_cast<const __nv_bfloat16*>(ln_bias),

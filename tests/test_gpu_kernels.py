@@ -16,7 +16,7 @@ def _bf16_bits(t):
 
 
 # --------------------------------------------------------------------------- quantiser
-@pytest.mark.parametrize("M,K", [(64, 512), (300, 3072), (7, 14336)])
+@pytest.mark.parametrize("M,K", [(64, 512), (300, 3072), (7, 14336), (4096, 3072)])
 def test_quant_rowwise_bit_exact(srdit, cuda_device, M, K):
     g = torch.Generator().manual_seed(M + K)
     x = torch.randn(M, K, generator=g)
