@@ -36,6 +36,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "2K SR-DiT refine latent-frames/s @1/2/4/8 B200; fp8 GEMM & win-attn % of roofline"
 UNIT = "latent-frames/s"
 FRAMES_PER_STEP = 3
+# DRAM bytes (read + write) per srdit_fp8_gemm launch, averaged over the GEMM
+# launches of one step, from an ncu capture of dram__bytes_read.sum +
+# dram__bytes_write.sum (profiles/fp8_gemm_step_traffic.md); None until captured.
+GEMM_TRAFFIC_PER_LAUNCH = None
 LAT_SHAPE = (48, 3, 72, 128)
 CTX_SHAPE = (512, 4096)
 
@@ -43,7 +47,7 @@ CTX_SHAPE = (512, 4096)
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--geometry", default="8x8r0", choices=["8x8r0", "4x4r3"])
@@ -328,16 +332,15 @@ def run_gpu_arm(args, rank, world, local):
         return float(t.item())
 
     with torch.no_grad():
-        for _ in range(args.warmup):
-            one_step(noisy)
-        model.check_status()
-        barrier()
-        # ---- device-timed region: inputs resident in HBM
         ops = srdit.ops
-        ops.Stats.gemm_events = []
-        l0 = ops.Stats.launches
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as clk:
+        with ClockSampler(local) as clk:   # samples warm-up and the timed region
+            for _ in range(args.warmup):
+                one_step(noisy)
+            model.check_status()
+            barrier()
+            # ---- device-timed region: inputs resident in HBM, nothing but the steps
+            l0 = ops.Stats.launches
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             barrier()
             torch.cuda.nvtx.range_push("srdit_step")
             e0.record()
@@ -347,12 +350,20 @@ def run_gpu_arm(args, rank, world, local):
             torch.cuda.nvtx.range_pop()
             barrier()
         launches = ops.Stats.launches - l0
-        gemm_ev = ops.Stats.gemm_events
-        ops.Stats.gemm_events = None
         dev_ms = max_over_ranks(e0.elapsed_time(e1))
-        gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gemm_ev)
-        gemm_flop = sum(f for _, _, f in gemm_ev)
         model.check_status()
+        # ---- attribution pass (outside the timed region): one more step with CUDA
+        # events around every launch on the launching stream
+        ops.Stats.events = []
+        one_step(noisy)
+        torch.cuda.synchronize()
+        kinds = {}
+        for kind, a, b, work in ops.Stats.events:
+            k = kinds.setdefault(kind, [0, 0.0, 0])
+            k[0] += 1
+            k[1] += a.elapsed_time(b)
+            k[2] += work
+        ops.Stats.events = None
         # ---- end-to-end region: the public API with host buffers
         barrier()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -372,13 +383,24 @@ def run_gpu_arm(args, rank, world, local):
         return
     peaks, peak_kind = load_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))
-    achieved = gemm_flop / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    bf16_peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     value = world * FRAMES_PER_STEP * args.steps / (dev_ms * 1e-3)
     e2e_val = world * FRAMES_PER_STEP * args.steps / (e2e_ms * 1e-3)
-    n_gemm = len(gemm_ev) // max(args.steps, 1)
+    step_ms = dev_ms / args.steps
+    n_gemm, gemm_ms, gemm_flop = kinds.get("fp8_gemm", [0, 0.0, 0])
+    achieved = gemm_flop / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    breakdown = {}
+    for kind, (n, ms, work) in sorted(kinds.items(), key=lambda kv: -kv[1][1]):
+        tensor = kind in ("fp8_gemm", "winattn")
+        rate = work / (ms * 1e-3) / (1e12 if tensor else 1e9) if ms > 0 else None
+        peak = fp8_peak if kind == "fp8_gemm" else bf16_peak if kind == "winattn" else hbm_peak
+        breakdown[kind] = {"launches": n, "ms": round(ms, 3), "share": round(ms / step_ms, 4),
+                           "rate": rate, "rate_unit": "TFLOP/s" if tensor else "GB/s",
+                           "frac": (rate / peak) if rate else None}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e4m3 GEMM (fp32 acc) / bf16 attention", "data": "synthetic (seeded N(0,1) "
         "latent + text context, seeded random weights)",
@@ -386,12 +408,12 @@ def run_gpu_arm(args, rank, world, local):
         "roofline": {"bound": "tensor", "kernel": "srdit_fp8_gemm (tcgen05 e4m3)",
                      "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": (achieved / fp8_peak) if achieved else None,
-                     "traffic": None,
+                     "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                     "algorithmic_flop_per_launch": gemm_flop / max(n_gemm, 1),
                      "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json "
                                     f"({peak_kind}); e4m3 tcgen05 rate = 2 x bf16",
-                     "gemm_ms_per_step": gemm_ms / args.steps,
-                     "gemm_launches_per_step": n_gemm,
-                     "gemm_share_of_step": gemm_ms / (dev_ms if world == 1 else dev_ms)},
+                     "launches_per_step": n_gemm, "ms_per_step": gemm_ms},
+        "kernels": breakdown,
         "e2e": {"value": e2e_val, "unit": UNIT,
                 "h2d_bytes_per_step": noisy_host.numel() * 2 + ctx_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2},

@@ -350,6 +350,9 @@ class SRDiT:
         mode = None if anchor_kv is None else anchor_align
         from .attention import cached_plan, _plan_device_state
         plan = cached_plan(spec, mode)
+        if "flops" not in plan:
+            plan["flops"] = blockgrid.visible_flops(plan["params"], int(plan["p_stride"]),
+                                                    c.num_heads, 128)
         a_hw = (h, w) if anchor_kv is not None else None
         params_dev, tiling, n_w, amode = _plan_device_state(
             plan, dev, mode, (f, h, w, f_kv, a_hw, f if a_hw else 0),
@@ -405,7 +408,8 @@ class SRDiT:
                 ak, av = anchor_kv[li]
             ops.winattn(qb, kr, vr, att, params_dev=params_dev, n_w=n_w,
                         p_stride=int(plan["p_stride"]), anchor_mode=amode, geom=geom,
-                        tiling=tiling, k_anchor=ak, v_anchor=av, status=st)
+                        tiling=tiling, k_anchor=ak, v_anchor=av, status=st,
+                        flops=plan["flops"])
             if return_kv:
                 idx = (torch.arange(f, device=dev) + slot_cur) % cache.cap
                 kv_out.append((kr.view(cache.cap, L, D)[idx].reshape(M, D).clone(),
@@ -421,7 +425,7 @@ class SRDiT:
             ops.rms_rope(ckv[:, :D], ly.cnk, c.eps, ckv[:, :D], frame_tokens=Lc)
             ops.winattn(qb, ckv[:, :D], ckv[:, D:], att, params_dev=cp_params, n_w=cp_nw,
                         p_stride=blockgrid.P_PLAIN, anchor_mode=0, geom=cgeom, tiling=cp_tiling,
-                        status=st)
+                        status=st, flops=4 * 128 * c.num_heads * M * Lc)
             ops.quant_rowwise(att, q=xq, scale=xs)
             ops.fp8_gemm(xq, xs, ly.w_co, ly.s_co, ly.b_co, x, epilogue="res", residual=x)
             # --- FFN

@@ -17,16 +17,30 @@ EPILOGUES = {"store": _lib.SRDIT_EPI_STORE, "gelu": _lib.SRDIT_EPI_GELU,
 
 
 class Stats:
-    """Launch accounting: ``launches`` counts kernels this module launched;
-    when ``gemm_events`` is a list, every GEMM launch appends
-    (start_event, end_event, flops) recorded on the launching stream."""
+    """Launch accounting.
+
+    ``launches`` counts the kernels this module launched. When ``events`` is a
+    list, every launch appends ``(kind, start_event, end_event, work)``, the
+    events recorded on the launching stream around the launch and ``work`` its
+    algorithmic FLOPs (GEMM, attention) or bytes (row kernels), so a profiling
+    pass can attribute time per kernel kind. Leave it None in timed regions:
+    the event records themselves cost time.
+    """
     launches = 0
-    gemm_events = None
+    events = None
 
 
-def _launch(name, *args):
+def _launch(name, *args, kind=None, work=0):
+    ev = Stats.events
+    if ev is not None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
     _lib.call(name, *args)
     Stats.launches += 1
+    if ev is not None:
+        e1.record()
+        ev.append((kind or name, e0, e1, int(work)))
 
 
 def _ptr(t):
@@ -70,18 +84,10 @@ def fp8_gemm(a_fp8, a_scale, w_fp8, w_scale, bias=None, out=None, *, epilogue="s
     if bias is not None and (bias.dtype != torch.bfloat16 or not bias.is_contiguous()):
         raise _lib.SrditError("bias must be contiguous bf16")
     ldr = _rows(residual) if residual is not None else 0
-    ev = Stats.gemm_events
-    if ev is not None:
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
     _launch("srdit_fp8_gemm", _ptr(a_fp8), _ptr(a_scale), _ptr(w_fp8), _ptr(w_scale),
             _ptr(bias), _ptr(out), M, N, K, _rows(a_fp8), _rows(w_fp8), _rows(out),
             EPILOGUES[epilogue], _ptr(residual), ldr, _ptr(gate), _ptr(row_amax),
-            _ptr(status), _stream(a_fp8.device))
-    if ev is not None:
-        e1.record()
-        ev.append((e0, e1, 2 * M * N * K))
+            _ptr(status), _stream(a_fp8.device), kind="fp8_gemm", work=2 * M * N * K)
     return out
 
 
@@ -96,7 +102,8 @@ def quant_rowwise(x, amax=None, q=None, scale=None):
     if scale is None:
         scale = torch.empty(M, dtype=torch.float32, device=x.device)
     _launch("srdit_quant_rowwise", _ptr(x), _rows(x), M, K, _ptr(amax), _ptr(q), _rows(q),
-              _ptr(scale), _stream(x.device))
+            _ptr(scale), _stream(x.device), kind="quant_rowwise",
+            work=M * K * 3 + 4 * M)
     return q, scale
 
 
@@ -112,8 +119,8 @@ def ln_mod_quant(x, eps=1e-6, *, ln_weight=None, ln_bias=None, shift=None, scale
     if qscale is None:
         qscale = torch.empty(M, dtype=torch.float32, device=x.device)
     _launch("srdit_ln_mod_quant", _ptr(x), _rows(x), M, K, float(eps), _ptr(ln_weight),
-              _ptr(ln_bias), _ptr(shift), _ptr(scale), _ptr(q), _rows(q), _ptr(qscale),
-              _stream(x.device))
+            _ptr(ln_bias), _ptr(shift), _ptr(scale), _ptr(q), _rows(q), _ptr(qscale),
+            _stream(x.device), kind="ln_mod_quant", work=M * K * 2 + M * K + 4 * M)
     return q, qscale
 
 
@@ -128,10 +135,11 @@ def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, c
         raise _lib.SrditError("RoPE tables must be contiguous float64 [rows, 64]")
     tab_rows = cos.shape[0] if cos is not None else 0
     _launch("srdit_rms_rope", _ptr(src), _rows(src), M, K, _ptr(weight), float(eps),
-              _ptr(dst), _rows(dst), int(frame_tokens), int(slot0), int(n_slots), _ptr(cos),
-              _ptr(sin), int(tab_rows), int(grid_h), int(grid_w), int(t_offset), _ptr(v_src),
-              _rows(v_src) if v_src is not None else 0, _ptr(v_dst),
-              _rows(v_dst) if v_dst is not None else 0, _stream(src.device))
+            _ptr(dst), _rows(dst), int(frame_tokens), int(slot0), int(n_slots), _ptr(cos),
+            _ptr(sin), int(tab_rows), int(grid_h), int(grid_w), int(t_offset), _ptr(v_src),
+            _rows(v_src) if v_src is not None else 0, _ptr(v_dst),
+            _rows(v_dst) if v_dst is not None else 0, _stream(src.device), kind="rms_rope",
+            work=M * K * 2 * (4 if v_src is not None else 2))
     return dst
 
 
@@ -147,14 +155,15 @@ def winattn_plan(params_host: torch.Tensor, p_stride: int, anchor_mode: int):
 
 
 def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom, tiling,
-            k_anchor=None, v_anchor=None, status=None):
-    """One window-attention launch (see include/srdit_b200.h, srdit_winattn_fwd)."""
+            k_anchor=None, v_anchor=None, status=None, flops=0):
+    """One window-attention launch (see include/srdit_b200.h, srdit_winattn_fwd).
+    ``flops``: the launch's visible-pair FLOPs, for launch accounting only."""
     _need_cuda(q, k_hr, v_hr, out, params_dev, k_anchor, v_anchor)
     for t in (q, k_hr, v_hr, out, k_anchor, v_anchor):
         if t is not None and t.dtype != torch.bfloat16:
             raise _lib.SrditError("window attention takes bf16 q/k/v")
     _launch("srdit_winattn_fwd", _ptr(q), _ptr(k_hr), _ptr(v_hr), _ptr(k_anchor),
-              _ptr(v_anchor), _ptr(out), _ptr(params_dev), int(n_w), int(p_stride),
-              int(anchor_mode), ctypes.byref(geom), ctypes.byref(tiling), _ptr(status),
-              _stream(q.device))
+            _ptr(v_anchor), _ptr(out), _ptr(params_dev), int(n_w), int(p_stride),
+            int(anchor_mode), ctypes.byref(geom), ctypes.byref(tiling), _ptr(status),
+            _stream(q.device), kind="winattn", work=flops)
     return out
