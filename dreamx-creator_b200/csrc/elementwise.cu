@@ -82,81 +82,182 @@ SRDIT_DEV uint2 quant8(const float (&f)[8], float scale, float rscale) {
 }
 SRDIT_DEV float scale_of(float amax) { return fmaxf(__fdiv_rn(amax, kFp8Max), 1e-12f); }
 
+// ---------------------------------------------------------------- row I/O
+// Each lane owns the 16-byte chunks lane, lane + 32, ... of its row: a warp
+// access covers 512 contiguous bytes. Rows are held as packed bf16 (4
+// registers per chunk), unpacked on each pass, so a 3072-wide row costs 48
+// registers and several rows stay resident per SM.
+SRDIT_DEV uint4 ld_stream(const uint4* p) { return __ldcs(p); }
+
+SRDIT_DEV float2 bf2f(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+SRDIT_DEV float chunk_absmax(const uint4& u) {
+  const float2 a = bf2f(u.x), b = bf2f(u.y), c = bf2f(u.z), d = bf2f(u.w);
+  return fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))),
+               fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(d.x), fabsf(d.y))));
+}
+
 // ---------------------------------------------------------------- quant_rowwise
-// amax_in != null: the per-row amax is already known (e.g. accumulated by the
-// producing GEMM's epilogue) and the row is streamed once.
-__global__ void quant_rowwise_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, int M,
-                                     int K, const float* __restrict__ amax_in,
-                                     uint8_t* __restrict__ q, long long ldq,
-                                     float* __restrict__ scale_out) {
+// K = VEC * 256 (VEC <= 16): the row stays in registers, read once.
+// amax_in != null: the per-row amax is already known (accumulated by the
+// producing GEMM's epilogue).
+template <int VEC>
+__global__ void __launch_bounds__(128) quant_rowwise_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, int M,
+    const float* __restrict__ amax_in, uint8_t* __restrict__ q, long long ldq,
+    float* __restrict__ scale_out) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  const __nv_bfloat16* xr = x + row * ldx;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx) + lane;
+  uint4 raw[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) raw[i] = ld_stream(xr + i * 32);
   float amax;
   if (amax_in) {
-    amax = amax_in[row];
+    amax = __ldg(amax_in + row);
   } else {
     amax = 0.f;
-    for (int c = lane * 8; c < K; c += 256) {
-      float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+    for (int i = 0; i < VEC; ++i) amax = fmaxf(amax, chunk_absmax(raw[i]));
+    amax = warp_max(amax);
+  }
+  const float s = scale_of(amax);
+  const float rs = __frcp_rn(s);
+  uint2* qr = reinterpret_cast<uint2*>(q + row * ldq) + lane;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    float f[8];
+    unpack8(raw[i], f);
+    qr[i * 32] = quant8(f, s, rs);
+  }
+  if (lane == 0) scale_out[row] = s;
+}
+
+// Any K multiple of 256: streamed in groups of UNR chunks per lane (the loads of
+// a group are issued together). Without amax_in the row is read twice.
+template <int UNR>
+__global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K,
+    const float* __restrict__ amax_in, uint8_t* __restrict__ q, long long ldq,
+    float* __restrict__ scale_out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int nch = K >> 8;  // chunks per lane
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx) + lane;
+  float amax;
+  if (amax_in) {
+    amax = __ldg(amax_in + row);
+  } else {
+    amax = 0.f;
+    for (int i0 = 0; i0 < nch; i0 += UNR) {
+      uint4 raw[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u)
+        if (i0 + u < nch) raw[u] = __ldg(xr + (i0 + u) * 32);
+#pragma unroll
+      for (int u = 0; u < UNR; ++u)
+        if (i0 + u < nch) amax = fmaxf(amax, chunk_absmax(raw[u]));
     }
     amax = warp_max(amax);
   }
   const float s = scale_of(amax);
   const float rs = __frcp_rn(s);
-  uint8_t* qr = q + row * ldq;
-  for (int c = lane * 8; c < K; c += 256) {
-    float f[8];
-    unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
-    *reinterpret_cast<uint2*>(qr + c) = quant8(f, s, rs);
+  uint2* qr = reinterpret_cast<uint2*>(q + row * ldq) + lane;
+  for (int i0 = 0; i0 < nch; i0 += UNR) {
+    uint4 raw[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u)
+      if (i0 + u < nch) raw[u] = ld_stream(xr + (i0 + u) * 32);
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      if (i0 + u < nch) {
+        float f[8];
+        unpack8(raw[u], f);
+        qr[(i0 + u) * 32] = quant8(f, s, rs);
+      }
+    }
   }
   if (lane == 0) scale_out[row] = s;
 }
 
+// ---------------------------------------------------------------- packed rows
+// ln_mod_quant and rms_rope keep one warp per row, with the row held as packed
+// bf16 (4 registers per 8 values) across the passes. The unpack below is a
+// volatile asm, so the compiler re-unpacks on every pass (two ALU ops per
+// value) instead of caching 8 floats per chunk: a 3072-wide row then costs 48
+// registers, and 24 rows stay in flight per SM.
+SRDIT_DEV void unpack8_v(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t lo, hi;
+    asm volatile("shl.b32 %0, %1, 16;" : "=r"(lo) : "r"(w[i]));
+    asm volatile("and.b32 %0, %1, 0xffff0000;" : "=r"(hi) : "r"(w[i]));
+    f[2 * i] = __uint_as_float(lo);
+    f[2 * i + 1] = __uint_as_float(hi);
+  }
+}
+
+// A read-only 16-byte load that the compiler keeps in program order (volatile
+// asm): used for per-column vectors inside the unrolled row loops, so their
+// loads are not all hoisted ahead of the loop into live registers.
+SRDIT_DEV uint4 ldg_inorder(const void* p) {
+  uint4 u;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+               : "l"(p));
+  return u;
+}
+
 // ---------------------------------------------------------------- ln_mod_quant
 template <int VEC>
-__global__ void ln_mod_quant_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, int M,
-                                    float eps, const __nv_bfloat16* __restrict__ ln_w,
-                                    const __nv_bfloat16* __restrict__ ln_b,
-                                    const float* __restrict__ shift,
-                                    const float* __restrict__ scale,
-                                    uint8_t* __restrict__ q, long long ldq,
-                                    float* __restrict__ qscale) {
+__global__ void __launch_bounds__(128, (VEC <= 12 ? 5 : 3)) ln_mod_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, int M, float eps,
+    const __nv_bfloat16* __restrict__ ln_w, const __nv_bfloat16* __restrict__ ln_b,
+    const float* __restrict__ shift, const float* __restrict__ scale,
+    uint8_t* __restrict__ q, long long ldq, float* __restrict__ qscale) {
   constexpr int K = VEC * 256;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  const __nv_bfloat16* xr = x + row * ldx;
-  float v[VEC][8];
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx) + lane;
+  uint4 raw[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) raw[i] = ld_stream(xr + i * 32);
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
-    unpack8(*reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8), v[i]);
+    float f[8];
+    unpack8_v(raw[i], f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sum += v[i][e];
+    for (int e = 0; e < 8; ++e) sum += f[e];
   }
   const float mean = warp_sum(sum) / static_cast<float>(K);
   float sq = 0.f;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i)
+  for (int i = 0; i < VEC; ++i) {
+    float f[8];
+    unpack8_v(raw[i], f);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float d = v[i][e] - mean;
+      const float d = f[e] - mean;
       sq += d * d;
     }
+  }
   const float var = warp_sum(sq) / static_cast<float>(K);
   const float rstd = rsqrtf(var + eps);
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
     const int c0 = i * 256 + lane * 8;
+    float v[8];
+    unpack8_v(raw[i], v);
     float wv[8], bv[8];
-    if (ln_w) unpack8(*reinterpret_cast<const uint4*>(ln_w + c0), wv);
-    if (ln_b) unpack8(*reinterpret_cast<const uint4*>(ln_b + c0), bv);
+    if (ln_w) unpack8(__ldg(reinterpret_cast<const uint4*>(ln_w + c0)), wv);
+    if (ln_b) unpack8(__ldg(reinterpret_cast<const uint4*>(ln_b + c0)), bv);
     float sc[8], sh[8];
     if (scale) {
       const float4* s4 = reinterpret_cast<const float4*>(scale + c0);
@@ -169,7 +270,7 @@ __global__ void ln_mod_quant_kernel(const __nv_bfloat16* __restrict__ x, long lo
     }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      float n = (v[i][e] - mean) * rstd;
+      float n = (v[e] - mean) * rstd;
       if (ln_w) n = n * wv[e];
       if (ln_b) n = n + bv[e];
       n = bf16_round(n);  // WanLayerNorm returns .type_as(x)
@@ -177,17 +278,21 @@ __global__ void ln_mod_quant_kernel(const __nv_bfloat16* __restrict__ x, long lo
         const float one_p = __fadd_rn(1.0f, sc[e]);
         n = bf16_round(__fadd_rn(__fmul_rn(n, one_p), sh[e]));
       }
-      v[i][e] = n;
+      v[e] = n;
       amax = fmaxf(amax, fabsf(n));
     }
+    raw[i] = pack8(v);  // exact: every v[e] is already a bf16 value
   }
   amax = warp_max(amax);
   const float s = scale_of(amax);
   const float rs = __frcp_rn(s);
-  uint8_t* qr = q + row * ldq;
+  uint2* qr = reinterpret_cast<uint2*>(q + row * ldq) + lane;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i)
-    *reinterpret_cast<uint2*>(qr + i * 256 + lane * 8) = quant8(v[i], s, rs);
+  for (int i = 0; i < VEC; ++i) {
+    float f[8];
+    unpack8_v(raw[i], f);
+    qr[i * 32] = quant8(f, s, rs);
+  }
   if (lane == 0) qscale[row] = s;
 }
 
@@ -214,60 +319,78 @@ struct RopeArgs {
 };
 
 template <int VEC>
-__global__ void rms_rope_kernel(RopeArgs a, int M) {
+__global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(RopeArgs a, int M) {
   constexpr int K = VEC * 256;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  const __nv_bfloat16* xr = a.src + row * a.ld_src;
-  float v[VEC][8];
-  float ss = 0.f;
+  const uint4* xr = reinterpret_cast<const uint4*>(a.src + row * a.ld_src) + lane;
+  uint4 raw[VEC];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    unpack8(*reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8), v[i]);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
-  }
-  const float r = rsqrtf(warp_sum(ss) * (1.0f / static_cast<float>(K)) + a.eps);
+  for (int i = 0; i < VEC; ++i) raw[i] = ld_stream(xr + i * 32);
   const int f = row / a.frame_tokens, sp = row % a.frame_tokens;
   const long long drow =
       static_cast<long long>((a.slot0 + f) % a.n_slots) * a.frame_tokens + sp;
-  __nv_bfloat16* dr = a.dst + drow * a.ld_dst;
-  const int pos_t = a.t_offset + f;
-  const int pos_h = sp / a.grid_w, pos_w = sp % a.grid_w;
+  // The V copy is independent of the norm: issue it first so its traffic
+  // overlaps the reduction (4 chunks at a time, to bound the registers it holds).
+  if (a.v_src) {
+    const uint4* vr = reinterpret_cast<const uint4*>(a.v_src + row * a.ld_vsrc) + lane;
+    uint4* vd = reinterpret_cast<uint4*>(a.v_dst + drow * a.ld_vdst) + lane;
+#pragma unroll
+    for (int i0 = 0; i0 < VEC; i0 += 4) {
+      uint4 t[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u < VEC) t[u] = ldg_inorder(vr + (i0 + u) * 32);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u < VEC) vd[(i0 + u) * 32] = t[u];
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    float v[8];
+    unpack8_v(raw[i], v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+  }
+  const float r = rsqrtf(warp_sum(ss) * (1.0f / static_cast<float>(K)) + a.eps);
+  // A lane's columns are lane*8 + 256*i: inside each 128-wide head that is the
+  // same 4 complex pairs d = (lane & 15) * 4 + p for every chunk, so the lane
+  // needs only these 4 rotations per row.
+  double cr[4], si[4];
+  if (a.cos_tab) {
+    const int pos_t = a.t_offset + f;
+    const int pos_h = sp / a.grid_w, pos_w = sp % a.grid_w;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int d = (lane & 15) * 4 + p;
+      const int pos = d < 22 ? pos_t : (d < 43 ? pos_h : pos_w);
+      cr[p] = __ldg(a.cos_tab + pos * 64 + d);
+      si[p] = __ldg(a.sin_tab + pos * 64 + d);
+    }
+  }
+  uint4* dr = reinterpret_cast<uint4*>(a.dst + drow * a.ld_dst) + lane;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
     const int c0 = i * 256 + lane * 8;
-    float wv[8];
-    unpack8(*reinterpret_cast<const uint4*>(a.weight + c0), wv);
+    float v[8], wv[8];
+    unpack8_v(raw[i], v);
+    unpack8(ldg_inorder(a.weight + c0), wv);
     float o[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = bf16_round(bf16_round(v[i][e] * r) * wv[e]);
+    for (int e = 0; e < 8; ++e) o[e] = bf16_round(bf16_round(v[e] * r) * wv[e]);
     if (a.cos_tab) {
 #pragma unroll
-      for (int pr = 0; pr < 4; ++pr) {
-        const int d = ((c0 + 2 * pr) & 127) >> 1;  // complex index inside the head
-        const int pos = d < 22 ? pos_t : (d < 43 ? pos_h : pos_w);
-        const double c = __ldg(a.cos_tab + pos * 64 + d);
-        const double s = __ldg(a.sin_tab + pos * 64 + d);
-        const double xr0 = static_cast<double>(o[2 * pr]);
-        const double xi0 = static_cast<double>(o[2 * pr + 1]);
-        const double yr = xr0 * c - xi0 * s;
-        const double yi = xr0 * s + xi0 * c;
-        o[2 * pr] = static_cast<float>(yr);
-        o[2 * pr + 1] = static_cast<float>(yi);
+      for (int p = 0; p < 4; ++p) {
+        const double x0 = static_cast<double>(o[2 * p]);
+        const double x1 = static_cast<double>(o[2 * p + 1]);
+        o[2 * p] = static_cast<float>(x0 * cr[p] - x1 * si[p]);
+        o[2 * p + 1] = static_cast<float>(x0 * si[p] + x1 * cr[p]);
       }
     }
-    *reinterpret_cast<uint4*>(dr + c0) = pack8(o);
-  }
-  if (a.v_src) {
-    const __nv_bfloat16* vr = a.v_src + row * a.ld_vsrc;
-    __nv_bfloat16* vd = a.v_dst + drow * a.ld_vdst;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      const int c0 = i * 256 + lane * 8;
-      *reinterpret_cast<uint4*>(vd + c0) = *reinterpret_cast<const uint4*>(vr + c0);
-    }
+    dr[i * 32] = pack8(o);
   }
 }
 
@@ -284,7 +407,17 @@ int dispatch_vec(int K, A&&... args) {
   }
 }
 
-constexpr int kRowsPerBlock = 8;  // 8 warps
+constexpr int kRowsPerBlock = 4;  // 4 warps, one row each
+
+template <int VEC>
+struct QuantLaunch {
+  static int run(const __nv_bfloat16* x, long long ldx, int M, const float* amax_in,
+                 uint8_t* q, long long ldq, float* s, cudaStream_t st) {
+    const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
+    quant_rowwise_kernel<VEC><<<grid, kRowsPerBlock * 32, 0, st>>>(x, ldx, M, amax_in, q, ldq, s);
+    return static_cast<int>(cudaGetLastError());
+  }
+};
 
 template <int VEC>
 struct LnLaunch {
@@ -320,10 +453,13 @@ extern "C" int srdit_quant_rowwise(const void* x, long long ldx, int M, int K,
   if (M == 0) return 0;
   if (!x || !q || !scale || M < 0 || K <= 0) return SRDIT_EINVAL;
   if ((K % 256) || (ldx % 8) || (ldq % 16) || !aligned16(x) || !aligned16(q)) return SRDIT_EALIGN;
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  uint8_t* qb = static_cast<uint8_t*>(q);
+  const int rc = ew::dispatch_vec<ew::QuantLaunch>(K, xb, ldx, M, amax_in, qb, ldq, scale, stream);
+  if (rc != SRDIT_EUNSUPPORTED) return rc;
   const int grid = (M + ew::kRowsPerBlock - 1) / ew::kRowsPerBlock;
-  ew::quant_rowwise_kernel<<<grid, ew::kRowsPerBlock * 32, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, M, K, amax_in, static_cast<uint8_t*>(q), ldq,
-      scale);
+  ew::quant_rowwise_stream_kernel<8><<<grid, ew::kRowsPerBlock * 32, 0, stream>>>(
+      xb, ldx, M, K, amax_in, qb, ldq, scale);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -65,13 +65,22 @@ struct Params {
   uint32_t* status;
 };
 
+// tanh on the SFU (PTX tanh.approx.f32, max relative error about 2^-11). The
+// GELU output is rounded to bf16 (2^-9) and then quantised to e4m3 (2^-4) for
+// the next GEMM, so the approximation is far below both roundings.
+SRDIT_DEV float tanh_sfu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 SRDIT_DEV float gelu_tanh(float x) {
   // 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3)))
   const float kBeta = 0.7978845608028654f;
   const float kKappa = 0.044715f;
   const float x3 = x * x * x;
   const float inner = kBeta * (x + kKappa * x3);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  return 0.5f * x * (1.0f + tanh_sfu(inner));
 }
 
 SRDIT_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }

@@ -237,6 +237,19 @@ SRDIT_DEV void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, ui
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D(tmem) (+)= A(tmem) * B(smem), bf16/fp16 inputs, fp32 accumulate. A is M x K
+// in tensor memory: row m in lane m, K packed two 16-bit values per 32-bit
+// column (element 2c in the low half of column c), so a 16-deep K step spans
+// 8 columns.
+SRDIT_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // D(tmem) (+)= A(smem) * B(smem)^T, e4m3/e5m2 inputs, fp32 accumulate.
 SRDIT_DEV void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                          uint32_t accumulate) {

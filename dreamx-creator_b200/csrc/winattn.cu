@@ -38,11 +38,14 @@ constexpr int QKV_TILE_BYTES = 2 * SLAB;
 constexpr int OFF_Q = 0;  // two Q buffers (the next item's Q loads during this item)
 constexpr int OFF_K = OFF_Q + 2 * QKV_TILE_BYTES;
 constexpr int OFF_V = OFF_K + 2 * QKV_TILE_BYTES;
-constexpr int OFF_P = OFF_V + 2 * QKV_TILE_BYTES;
-constexpr int OFF_BAR = OFF_P + QKV_TILE_BYTES;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
-constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;  // S0 @0, S1 @128, O0 @256, O1 @384
+constexpr int OFF_BAR = OFF_V + 2 * QKV_TILE_BYTES;
+constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: 768 floats
+constexpr int SMEM_BYTES = OFF_XCH + 768 * 4 + 1024;
+constexpr int NUM_SOFTMAX = 256;        // warps 2-9: two threads per query row
+constexpr int NUM_THREADS = 64 + NUM_SOFTMAX;
+// TMEM: S0 @0, S1 @128 (P_g is written back over S_g as packed bf16 in its first
+// 64 columns), O0 @256, O1 @384.
+constexpr uint32_t TMEM_COLS = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Args {
@@ -195,10 +198,41 @@ SRDIT_DEV TileInfo tile_info(const Args& a, const Walk& w, int j) {
   return t;
 }
 
+// 2^x on the SFU, subnormal results flushed to zero: P values below 2^-126
+// contribute nothing to a bf16 P.V product, and the flush keeps this a single
+// SFU operation.
 SRDIT_DEV float ex2_approx(float x) {
   float y;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+SRDIT_DEV float max3f(float x, float y, float z) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+  return r;
+}
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes'
+// worth of fma / add, each element rounded exactly as its scalar form).
+SRDIT_DEV uint64_t pack_f2(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+SRDIT_DEV float2 unpack_f2(uint64_t r) {
+  float2 f;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(r));
+  return f;
+}
+SRDIT_DEV uint64_t fma_f2(uint64_t x, uint64_t y, uint64_t z) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(y), "l"(z));
+  return r;
+}
+SRDIT_DEV uint64_t add_f2(uint64_t x, uint64_t y) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+  return r;
 }
 
 // Work item = (window, 128-row query tile, head); items are walked head-major
@@ -247,9 +281,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+      mbar_init(&o_empty[i], NUM_SOFTMAX);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, NUM_SOFTMAX);
     mbar_init(o_full, 1);
     *abort_flag = 0u;
     fence_barrier_init();
@@ -258,7 +292,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp >= 2) {
+  if (warp >= 2 && warp < 6) {
     // V rows that a tile shorter than its 16-row MMA extent leaves unwritten must
     // never hold NaN (P is 0 there, but 0 * NaN is NaN): zero both V stages once.
     const int row = (warp & 3) * 32 + lane;
@@ -358,7 +392,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // cursor issues O += P_g.V_g once the softmax published P_g. Whichever is
     // ready goes first, so a late K tile never holds back the P.V chain.
     if (elect_one()) {
-      const uint32_t p_addr = smem_u32(smem + OFF_P);
       struct Cursor {
         int item, it, j, g, head;
         Walk w;
@@ -436,11 +469,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t v_addr = smem_u32(smem + OFF_V + st * QKV_TILE_BYTES);
         const uint32_t idesc = idesc_make(1u, 1u, 0u, 1u, 128u, 128u);
         const uint32_t o_tmem = tmem_base + 256u + static_cast<uint32_t>(b * 128);
+        const uint32_t p_tmem = tmem_base + static_cast<uint32_t>(st * 128);
         const int ksteps = ti.n16 / 16;
         for (int k = 0; k < ksteps; ++k) {
-          const uint32_t poff = static_cast<uint32_t>((k >> 2) * SLAB + (k & 3) * 32);
           const uint32_t voff = static_cast<uint32_t>(k * 16 * 128);
-          mma_bf16_ss(o_tmem, sdesc_sw128(p_addr + poff, 16, 1024),
+          mma_bf16_ts(o_tmem, p_tmem + static_cast<uint32_t>(k * 8),
                       sdesc_sw128(v_addr + voff, SLAB, 1024), idesc,
                       (cp.j > 0 || k > 0) ? 1u : 0u);
         }
@@ -462,6 +495,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (did) {
           idle_since = 0;
         } else {
+          // Nothing issuable: sleep on the barrier the next P.V needs (the
+          // softmax is the usual laggard) instead of spinning, so this warp does
+          // not take issue slots from the softmax warp sharing its SM
+          // sub-partition. The suspend hint bounds the sleep; the loop re-checks.
+          if (cp.have && cp.g < cs.g)
+            mbar_try_wait_sleep(p_full, static_cast<uint32_t>(cp.g) & 1u, 1000u);
+          else if (cs.have)
+            mbar_try_wait_sleep(&k_full[cs.g & 1], static_cast<uint32_t>(cs.g >> 1) & 1u, 1000u);
           const uint64_t now = global_timer_ns();
           if (idle_since == 0) {
             idle_since = now;
@@ -475,30 +516,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
+    // Two threads per query row: warps 2-5 own score columns 0-63 and warps 6-9
+    // columns 64-127 of the same rows (warps w and w + 4 share a TMEM lane
+    // quarter). The pair exchanges one partial row max per tile through shared
+    // memory (named barrier 1 + lane quarter, 64 threads) and combines its
+    // partial row sums once per item. Each thread writes its half of P back
+    // over S, rescales and stores its half of O.
     const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = sub * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(sub * 32) << 16;
+    const uint32_t pair_bar = 1u + static_cast<uint32_t>(sub);
+    float* xmax = reinterpret_cast<float*>(smem + OFF_XCH);  // [tile parity][half][128]
+    float* xsum = xmax + 512;                                 // [half][128]
     const float neg_inf = -__int_as_float(0x7f800000);
     const float c_scale = a.scale * kLog2e;  // scores in log2 units
+    const uint64_t c_scale2 = pack_f2(c_scale, c_scale);
     // The running max is only raised (and O rescaled) once a tile's max exceeds
     // it by more than this many log2 units; in between, P = exp2(s - m_stale) is
     // at most 2^8, so the sum and the P.V accumulation stay exact up to rounding.
     const float kRescale = 8.0f;
-    uint8_t* prow = smem + OFF_P + row * 128;
-    const int sw = row & 7;
     // Column c of a KV tile -> (box within the tile, row of the box, column of
     // the box): fixed for the whole launch, one decomposition per segment.
-    int bi_k[4], hr_k[4], cw_k[4], bi_a[4], hr_a[4], cw_a[4];
+    // Packed one byte each (all three are below 128): box | row << 8 | col << 16.
+    uint32_t geo_k[2], geo_a[2];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int c = q * 32 + lane;
+    for (int qq = 0; qq < 2; ++qq) {
+      const int c = (2 * half + qq) * 32 + lane;
       const int rk = a.bw_k * a.bh_k, ra = a.bw_a * a.bh_a;
-      bi_k[q] = c / rk;
-      hr_k[q] = (c % rk) / a.bw_k;
-      cw_k[q] = (c % rk) % a.bw_k;
-      bi_a[q] = c / ra;
-      hr_a[q] = (c % ra) / a.bw_a;
-      cw_a[q] = (c % ra) % a.bw_a;
+      geo_k[qq] = static_cast<uint32_t>(c / rk) | static_cast<uint32_t>((c % rk) / a.bw_k) << 8 |
+                  static_cast<uint32_t>((c % rk) % a.bw_k) << 16;
+      geo_a[qq] = static_cast<uint32_t>(c / ra) | static_cast<uint32_t>((c % ra) / a.bw_a) << 8 |
+                  static_cast<uint32_t>((c % ra) % a.bw_a) << 16;
     }
     bool ok = true;
     int g = 0, it = 0;
@@ -517,81 +566,130 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int ww = rr % a.bw_q;
       const bool row_ok = qb < w.nqbox && t_row < r.q_tL && hh < r.qhL && ww < r.qwL;
       // A warp whose rows are all padding keeps the barrier protocol but skips
-      // the math (its rows are never stored).
+      // the math (its rows are never stored; the P it leaves in TMEM only feeds
+      // its own, never-stored O rows). Both warps of a pair agree on this.
       const bool active = __any_sync(0xffffffffu, row_ok);
-      const uint32_t o_tmem = tmem_base + t_lane + 256u + static_cast<uint32_t>(b * 128);
+      const uint32_t o_tmem =
+          tmem_base + t_lane + 256u + static_cast<uint32_t>(b * 128 + half * 64);
       float m_i = neg_inf, l_i = 0.f;
       for (int j = 0; j < w.n_tiles; ++j, ++g) {
         const int st = g & 1;
         const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
         const TileInfo ti = tile_info(a, w, j);
-        // column validity (ballot over lanes: bit i of vmask[q] = column 32q + i)
-        uint32_t vmask[4];
-        {
-          const int khl = ti.anchor ? r.khL_a : r.khL;
-          const int kwl = ti.anchor ? r.kwL_a : r.kwL;
+        const int nchunks = (ti.n16 + 31) >> 5;
+        // validity of this thread's 64 columns (bit i of vm[qq] = column
+        // (2*half + qq)*32 + i); a per-frame anchor tile is invisible to the
+        // other frames' rows; columns past the tile's MMA extent are never read
+        uint32_t vm[2];
+        const int khl = ti.anchor ? r.khL_a : r.khL;
+        const int kwl = ti.anchor ? r.kwL_a : r.kwL;
+        const bool sees = !(ti.anchor && r.a_per_frame) || (t_row == ti.frame);
+        if (kwl == ti.bw && khl % ti.bh == 0) {
+          // every box row and column lies inside the window: only the tile's
+          // row count masks
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            const int n = ti.rows - (2 * half + qq) * 32;
+            vm[qq] = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
+          }
+        } else {
           const int hch = ti.anchor ? w.a_hchunks : w.hr_hchunks;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int c = q * 32 + lane;
-            const int bi = ti.anchor ? bi_a[q] : bi_k[q];
-            const int hr = ti.anchor ? hr_a[q] : hr_k[q];
-            const int cw = ti.anchor ? cw_a[q] : cw_k[q];
+          for (int qq = 0; qq < 2; ++qq) {
+            const int c = (2 * half + qq) * 32 + lane;
+            const uint32_t geo = ti.anchor ? geo_a[qq] : geo_k[qq];
+            const int bi = static_cast<int>(geo & 0xffu);
+            const int hr = static_cast<int>((geo >> 8) & 0xffu);
+            const int cw = static_cast<int>(geo >> 16);
             const int hc = (ti.box0 + bi) % hch;
             const bool v = (c < ti.rows) && (hc * ti.bh + hr < khl) && (cw < kwl);
-            vmask[q] = __ballot_sync(0xffffffffu, v);
+            vm[qq] = __ballot_sync(0xffffffffu, v);
           }
         }
-        const bool sees = !(ti.anchor && r.a_per_frame) || (t_row == ti.frame);
+        const int my_chunks = min(max(nchunks - 2 * half, 0), 2);  // warp-uniform
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) vm[qq] = (sees && qq < my_chunks) ? vm[qq] : 0u;
         if (!mbar_wait(&s_full[st], ph, a.status, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t s_tmem = tmem_base + t_lane + static_cast<uint32_t>(st * 128);
-        const int nchunks = (ti.n16 + 31) >> 5;
-        // pass 1: tile row max (log2 units), two 32-column chunks per TMEM wait
-        float tmax = neg_inf;
-        // masked-out columns become -inf in place, then one body for every chunk
-        auto mask_chunk = [&](uint32_t (&u)[32], uint32_t vm) {
-          if (vm != 0xffffffffu) {
+        const uint32_t s_tmem = tmem_base + t_lane + static_cast<uint32_t>(st * 128 + half * 64);
+        // this thread's 64 scores into registers, masked columns -> -inf
+        uint32_t u[64];
+        float pmax = neg_inf;
+        const bool work = active && my_chunks > 0;  // warp-uniform
+        if (work) {  // tcgen05.ld is a warp-collective instruction
+          tmem_ld32(s_tmem, *reinterpret_cast<uint32_t(*)[32]>(u));
+          if (my_chunks > 1) tmem_ld32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = ((vm >> i) & 1u) ? u[i] : 0xff800000u;
-          }
-        };
-        auto chunk_max = [&](const uint32_t (&u)[32]) {
-          float m0 = neg_inf, m1 = neg_inf;
+          for (int qq = 0; qq < 2; ++qq) {
+            const uint32_t m = vm[qq];
+            if (m != 0xffffffffu) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            m0 = fmaxf(m0, __uint_as_float(u[i]));
-            m1 = fmaxf(m1, __uint_as_float(u[i + 1]));
+              for (int i = 0; i < 32; ++i)
+                u[qq * 32 + i] = ((m >> i) & 1u) ? u[qq * 32 + i] : 0xff800000u;
+            }
           }
-          tmax = fmaxf(tmax, fmaxf(m0, m1));
-        };
-        // this row's masks (a per-frame anchor tile is invisible to other frames)
-        uint32_t vm_row[4];
+          float m0 = neg_inf, m1 = neg_inf, m2 = neg_inf, m3 = neg_inf;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) vm_row[q] = (sees && q < nchunks) ? vmask[q] : 0u;
-        if (active) {  // warp-uniform: tcgen05.ld is a warp-collective instruction
-          for (int q0 = 0; q0 < nchunks; q0 += 2) {
-            uint32_t u0[32], u1[32];
-            tmem_ld32(s_tmem + q0 * 32, u0);
-            tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
-            tmem_ld_wait();
-            mask_chunk(u0, vm_row[q0]);
-            mask_chunk(u1, vm_row[q0 + 1]);
-            chunk_max(u0);
-            chunk_max(u1);
+          for (int i = 0; i < 64; i += 8) {
+            m0 = max3f(m0, __uint_as_float(u[i]), __uint_as_float(u[i + 1]));
+            m1 = max3f(m1, __uint_as_float(u[i + 2]), __uint_as_float(u[i + 3]));
+            m2 = max3f(m2, __uint_as_float(u[i + 4]), __uint_as_float(u[i + 5]));
+            m3 = max3f(m3, __uint_as_float(u[i + 6]), __uint_as_float(u[i + 7]));
           }
+          pmax = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
         }
-        tmax = tmax * c_scale;
+        // The pair's barrier also orders this thread's S reads before the
+        // partner's P writes into the same TMEM columns (half 1's P lands in
+        // columns 32-63, which half 0 reads as scores).
+        xmax[((g & 1) * 2 + half) * 128 + row] = pmax;
+        tc_fence_before();
+        named_barrier_sync(pair_bar, 64);
+        tc_fence_after();
+        const float tmax = fmaxf(pmax, xmax[((g & 1) * 2 + (half ^ 1)) * 128 + row]) * c_scale;
         const bool row_valid = tmax != neg_inf;
         // new running max: raised only past the rescale threshold
         const bool raise = row_valid && (tmax > m_i + kRescale || m_i == neg_inf);
         const float m_new = raise ? tmax : m_i;
         const float alpha = raise ? ex2_approx(m_i - m_new) : 1.f;
-        // P_g can only be written once P.V of the previous tile is done; that
-        // wait also makes O safe to rescale.
+        // P = exp2(s*c - m) -> bf16 pairs, written back over S in TMEM
+        const float neg_m = row_valid ? -m_new : 0.f;
+        const uint64_t neg_m2 = pack_f2(neg_m, neg_m);
+        uint64_t sum2 = pack_f2(0.f, 0.f);
+        if (work) {
+          uint32_t pw[32];
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            if (qq < my_chunks) {
+#pragma unroll
+              for (int i = qq * 32; i < qq * 32 + 32; i += 2) {
+                // masked columns hold -inf: exp2(-inf) = 0; a row that sees
+                // nothing has every column masked, so all of its P is 0
+                const float2 x = unpack_f2(fma_f2(
+                    pack_f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1])), c_scale2, neg_m2));
+                const float p0 = ex2_approx(x.x);
+                const float p1 = ex2_approx(x.y);
+                sum2 = add_f2(sum2, pack_f2(p0, p1));
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+                pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+              }
+            } else {
+#pragma unroll
+              for (int i = qq * 16; i < qq * 16 + 16; ++i) pw[i] = 0u;
+            }
+          }
+          tmem_st32(tmem_base + t_lane + static_cast<uint32_t>(st * 128 + half * 32), pw);
+          tmem_st_wait();
+        }
+        const float2 sp = unpack_f2(sum2);
+        l_i = alpha * l_i + (sp.x + sp.y);
+        m_i = m_new;
+        // O may only be rescaled, and P_g handed to the MMA, once P.V of the
+        // previous tile is done (every P.V completion is waited here or at the
+        // item's end, so the o_full phases never run ahead of this thread).
         if (j > 0) {
           if (!mbar_wait(o_full, static_cast<uint32_t>(g - 1) & 1u, a.status, abort_flag)) {
             ok = false;
@@ -599,76 +697,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-            for (int q = 0; q < 4; q += 2) {
-              uint32_t u0[32], u1[32];
-              tmem_ld32(o_tmem + q * 32, u0);
-              tmem_ld32(o_tmem + (q + 1) * 32, u1);
-              tmem_ld_wait();
+            uint32_t u0[32], u1[32];
+            tmem_ld32(o_tmem, u0);
+            tmem_ld32(o_tmem + 32, u1);
+            tmem_ld_wait();
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                u0[i] = __float_as_uint(__uint_as_float(u0[i]) * alpha);
-                u1[i] = __float_as_uint(__uint_as_float(u1[i]) * alpha);
-              }
-              tmem_st32(o_tmem + q * 32, u0);
-              tmem_st32(o_tmem + (q + 1) * 32, u1);
+            for (int i = 0; i < 32; ++i) {
+              u0[i] = __float_as_uint(__uint_as_float(u0[i]) * alpha);
+              u1[i] = __float_as_uint(__uint_as_float(u1[i]) * alpha);
             }
+            tmem_st32(o_tmem, u0);
+            tmem_st32(o_tmem + 32, u1);
             tmem_st_wait();
           }
         }
-        // pass 2: P = exp2(s*c - m) -> bf16 -> smem (K-major, 128B-swizzled)
-        float psum = 0.f;
-        const float neg_m = row_valid ? -m_new : 0.f;  // rows seeing nothing: all P = 0
-        float ps0 = 0.f, ps1 = 0.f;
-        auto chunk_p = [&](uint32_t (&u)[32], int q) {
-            // u already has its masked columns at -inf: exp2(-inf) = 0
-            uint32_t pw[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float p0 = ex2_approx(fmaf(__uint_as_float(u[i]), c_scale, neg_m));
-              const float p1 = ex2_approx(fmaf(__uint_as_float(u[i + 1]), c_scale, neg_m));
-              ps0 += p0;
-              ps1 += p1;
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-              pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
-            }
-#pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) {
-              const int qq = q * 4 + c4;  // 16-byte chunk index of the 256-byte P row
-              const int slab = qq >> 3, chunk = (qq & 7) ^ sw;
-              *reinterpret_cast<uint4*>(prow + slab * SLAB + chunk * 16) =
-                  make_uint4(pw[c4 * 4], pw[c4 * 4 + 1], pw[c4 * 4 + 2], pw[c4 * 4 + 3]);
-            }
-        };
-        if (active) {
-          for (int q0 = 0; q0 < nchunks; q0 += 2) {
-            uint32_t u0[32], u1[32];
-            tmem_ld32(s_tmem + q0 * 32, u0);
-            tmem_ld32(s_tmem + (q0 + 1) * 32, u1);
-            tmem_ld_wait();
-            mask_chunk(u0, row_valid ? vm_row[q0] : 0u);
-            mask_chunk(u1, row_valid ? vm_row[q0 + 1] : 0u);
-            chunk_p(u0, q0);
-            chunk_p(u1, q0 + 1);
-          }
-        }
-        psum = ps0 + ps1;
-        l_i = alpha * l_i + psum;
-        m_i = m_new;
-        fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(p_full);
       }
       if (!ok) break;
-      // item done: the last P.V must land, then O / l -> bf16 -> out
+      // item done: combine the pair's row sums, then (after the last P.V)
+      // O / l -> bf16 -> this thread's 64 output columns
+      xsum[half * 128 + row] = l_i;
+      named_barrier_sync(pair_bar, 64);
+      const float l_tot = l_i + xsum[(half ^ 1) * 128 + row];
       if (!mbar_wait(o_full, static_cast<uint32_t>(g - 1) & 1u, a.status, abort_flag)) break;
       tc_fence_after();
       const long long tok = static_cast<long long>(r.q_t0 + t_row) * a.q_h * a.q_w +
                             static_cast<long long>(r.q_h0 + hh) * a.q_w + (r.q_w0 + ww);
-      __nv_bfloat16* orow = a.out + tok * a.o_stride + head * D;
-      const float inv_l = 1.0f / l_i;
+      __nv_bfloat16* orow = a.out + tok * a.o_stride + head * D + half * 64;
+      const float inv_l = 1.0f / l_tot;
 #pragma unroll 1
-      for (int q = 0; q < (active ? 4 : 0); ++q) {
+      for (int q = 0; q < (active ? 2 : 0); ++q) {
         uint32_t u[32];
         tmem_ld32(o_tmem + q * 32, u);
         tmem_ld_wait();
