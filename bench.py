@@ -13,8 +13,10 @@ work. Weights are seeded random (no checkpoint); inputs are seeded synthetic.
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
-N > 1 (under torchrun): every rank refines its own clip (replicas, weak
-scaling); the step time is the max over ranks.
+N > 1 (under torchrun): tensor parallelism over N ranks on one clip (heads and
+FFN sharded, sequence-parallel residual stream; strong scaling), or with
+--parallel replicas every rank refines its own clip (weak scaling); the step
+time is the max over ranks.
 """
 from __future__ import annotations
 
@@ -52,6 +54,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--geometry", default="8x8r0", choices=["8x8r0", "4x4r3"])
     ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                    help="N > 1: tensor parallelism over one clip (strong scaling, the "
+                         "reference's DTensor-style TP) or one clip per GPU (weak scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", default=None, choices=["gemm", "attn", "quant", "ln", "rope"],
                     help="time one kernel in isolation instead of the model step")
@@ -148,6 +153,8 @@ def dist_setup(n):
         raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}: launch N>1 under torchrun")
     if world > 1:
         import datetime
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
         torch.distributed.init_process_group(
             "nccl" if torch.cuda.is_available() else "gloo",
             timeout=datetime.timedelta(seconds=120))
@@ -232,8 +239,10 @@ def workload_config(args):
                         "3 latent frames 36x64 tokens, 3-frame KV prefix, 512 text tokens",
             "model": "SR-DiT 5B (30 blocks, dim 3072, 24x128 heads, ffn 14336)",
             "layers": args.layers, "tokens": 6912, "window": f"3x{bhw[0]}x{bhw[1]} r{rhw}",
-            "global_batch": args.gpus, "seq_len": 6912,
-            "parallelism": "replicas" if args.gpus > 1 else "single",
+            "global_batch": 1 if args.parallel == "tp" else args.gpus, "seq_len": 6912,
+            "parallelism": (f"tp{args.gpus} (sequence-parallel residual stream)"
+                            if args.parallel == "tp" else "replicas") if args.gpus > 1
+            else "single",
             "l2": "inputs larger than L2 (5 GB of fp8 weights stream every forward)"}
 
 
@@ -301,8 +310,14 @@ def run_gpu_arm(args, rank, world, local):
     torch.cuda.set_device(dev)
     bhw, rhw = geometry(args.geometry)
     cfg = model_mod.SRDiTConfig(num_layers=args.layers, block_hw=bhw, block_radius_hw=rhw)
-    model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
-    g = torch.Generator().manual_seed(1000 + rank)
+    tp = world > 1 and args.parallel == "tp"
+    if tp:
+        tp_mod = import_module("dreamx-creator_b200.tp")
+        model = tp_mod.TPSRDiT.random_init(cfg, dev, seed=0)
+    else:
+        model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
+    # tensor parallelism refines one clip on all ranks; replicas one clip each
+    g = torch.Generator().manual_seed(1000 if tp else 1000 + rank)
     ctx_host = torch.randn(*CTX_SHAPE, generator=g).to(torch.bfloat16).pin_memory()
     noisy_host = torch.randn(*LAT_SHAPE, generator=g).to(torch.bfloat16).pin_memory()
     prefix_host = torch.randn(*LAT_SHAPE, generator=g).to(torch.bfloat16).pin_memory()
@@ -385,8 +400,9 @@ def run_gpu_arm(args, rank, world, local):
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))
     bf16_peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    value = world * FRAMES_PER_STEP * args.steps / (dev_ms * 1e-3)
-    e2e_val = world * FRAMES_PER_STEP * args.steps / (e2e_ms * 1e-3)
+    clips = 1 if tp else world   # clips refined per step, over all ranks
+    value = clips * FRAMES_PER_STEP * args.steps / (dev_ms * 1e-3)
+    e2e_val = clips * FRAMES_PER_STEP * args.steps / (e2e_ms * 1e-3)
     step_ms = dev_ms / args.steps
     n_gemm, gemm_ms, gemm_flop = kinds.get("fp8_gemm", [0, 0.0, 0])
     achieved = gemm_flop / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
@@ -401,7 +417,7 @@ def run_gpu_arm(args, rank, world, local):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "e4m3 GEMM (fp32 acc) / bf16 attention", "data": "synthetic (seeded N(0,1) "
         "latent + text context, seeded random weights)",
         "config": workload_config(args),

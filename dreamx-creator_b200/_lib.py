@@ -19,6 +19,7 @@ SRDIT_EPI_STORE, SRDIT_EPI_GELU, SRDIT_EPI_GATED_RES, SRDIT_EPI_RES = 0, 1, 2, 3
 SRDIT_P_FRAME, SRDIT_P_PLAIN = 17, 19
 SRDIT_ANCHOR_NONE, SRDIT_ANCHOR_CHUNK, SRDIT_ANCHOR_FRAME = 0, 1, 2
 SRDIT_STATUS_TIMEOUT = 1
+SRDIT_ROW_SUMSQ, SRDIT_ROW_ABSMAX = 0, 1
 
 c_int, c_ll, c_float, c_vp = ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_void_p
 
@@ -49,7 +50,9 @@ SIGNATURES = {
                            c_ll, c_vp, c_vp],
     "srdit_rms_rope": [c_vp, c_ll, c_int, c_int, c_vp, c_float, c_vp, c_ll, c_int, c_int,
                        c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_ll,
-                       c_vp],
+                       c_vp, c_int, c_vp],
+    "srdit_row_reduce": [c_vp, c_ll, c_int, c_int, c_int, c_vp, c_vp],
+    "srdit_residual": [c_vp, c_ll, c_int, c_int, c_vp, c_int, c_ll, c_ll, c_vp, c_vp, c_vp],
     "srdit_winattn_plan": [c_vp, c_int, c_int, c_int, ctypes.POINTER(WinattnTiling)],
     "srdit_winattn_fwd": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
                           ctypes.POINTER(WinattnGeom), ctypes.POINTER(WinattnTiling), c_vp,

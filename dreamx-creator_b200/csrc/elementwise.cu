@@ -135,8 +135,10 @@ __global__ void __launch_bounds__(128) quant_rowwise_kernel(
   if (lane == 0) scale_out[row] = s;
 }
 
-// Any K multiple of 256: streamed in groups of UNR chunks per lane (the loads of
-// a group are issued together). Without amax_in the row is read twice.
+// Any K multiple of 8: streamed in groups of UNR chunks per lane (the loads of
+// a group are issued together; chunk i of a lane covers columns
+// i*256 + lane*8 .. +7 and exists while that start is below K). Without
+// amax_in the row is read twice.
 template <int UNR>
 __global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
     const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K,
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  const int nch = K >> 8;  // chunks per lane
+  const int nch = (K + 255) >> 8;  // chunk slots per lane
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx) + lane;
   float amax;
   if (amax_in) {
@@ -156,10 +158,10 @@ __global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
       uint4 raw[UNR];
 #pragma unroll
       for (int u = 0; u < UNR; ++u)
-        if (i0 + u < nch) raw[u] = __ldg(xr + (i0 + u) * 32);
+        if ((i0 + u) * 256 + lane * 8 < K) raw[u] = __ldg(xr + (i0 + u) * 32);
 #pragma unroll
       for (int u = 0; u < UNR; ++u)
-        if (i0 + u < nch) amax = fmaxf(amax, chunk_absmax(raw[u]));
+        if ((i0 + u) * 256 + lane * 8 < K) amax = fmaxf(amax, chunk_absmax(raw[u]));
     }
     amax = warp_max(amax);
   }
@@ -170,10 +172,10 @@ __global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
     uint4 raw[UNR];
 #pragma unroll
     for (int u = 0; u < UNR; ++u)
-      if (i0 + u < nch) raw[u] = ld_stream(xr + (i0 + u) * 32);
+      if ((i0 + u) * 256 + lane * 8 < K) raw[u] = ld_stream(xr + (i0 + u) * 32);
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
-      if (i0 + u < nch) {
+      if ((i0 + u) * 256 + lane * 8 < K) {
         float f[8];
         unpack8(raw[u], f);
         qr[(i0 + u) * 32] = quant8(f, s, rs);
@@ -181,6 +183,80 @@ __global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
     }
   }
   if (lane == 0) scale_out[row] = s;
+}
+
+// ---------------------------------------------------------------- row reductions
+// out[m] = sum_k x[m,k]^2 (op 0, fp32) or max_k |x[m,k]| (op 1), K multiple of 8:
+// the partial statistics a tensor-parallel rank holds for its column slice.
+__global__ void __launch_bounds__(128) row_reduce_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         long long ldx, int M, int K, int op,
+                                                         float* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx) + lane;
+  float acc = 0.f;
+  for (int c = lane * 8, i = 0; c < K; c += 256, ++i) {
+    float f[8];
+    unpack8(__ldg(xr + i * 32), f);
+    if (op == 0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += f[e] * f[e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaxf(acc, fabsf(f[e]));
+    }
+  }
+  acc = op == 0 ? warp_sum(acc) : warp_max(acc);
+  if (lane == 0) out[row] = acc;
+}
+
+// ---------------------------------------------------------------- residual update
+// x[m,n] = bf16(x + bf16(sum_s part_s[m,n] + bias[n]) * gate[n])   (gate given)
+// x[m,n] = bf16(x + bf16(sum_s part_s[m,n] + bias[n]))             (gate null)
+// The parts are the bf16 partial products of a row-parallel Linear; the sum is
+// fp32. This is the reference's gated / plain residual after o / cross-o /
+// ffn.2 (models.py:1349-1351, :1257, :1261) applied to a tensor-parallel sum.
+__global__ void __launch_bounds__(256) residual_kernel(
+    __nv_bfloat16* __restrict__ x, long long ldx, int M, int N,
+    const __nv_bfloat16* __restrict__ parts, int n_parts, long long part_stride,
+    long long ld_part, const __nv_bfloat16* __restrict__ bias, const float* __restrict__ gate) {
+  const int per_row = N >> 3;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<long long>(M) * per_row) return;
+  const int row = static_cast<int>(idx / per_row);
+  const int c0 = static_cast<int>(idx % per_row) * 8;
+  float y[8];
+  unpack8(ld_stream(reinterpret_cast<const uint4*>(parts + row * ld_part + c0)), y);
+  for (int s = 1; s < n_parts; ++s) {
+    float t[8];
+    unpack8(ld_stream(reinterpret_cast<const uint4*>(parts + s * part_stride + row * ld_part + c0)), t);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] += t[e];
+  }
+  float bv[8];
+  if (bias) {
+    unpack8(__ldg(reinterpret_cast<const uint4*>(bias + c0)), bv);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bv[e] = 0.f;
+  }
+  uint4* xp = reinterpret_cast<uint4*>(x + row * ldx + c0);
+  float xv[8];
+  unpack8(*xp, xv);
+  float o[8];
+  if (gate) {
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + c0));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + c0) + 1);
+    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      o[e] = __fadd_rn(xv[e], __fmul_rn(bf16_round(__fadd_rn(y[e], bv[e])), gv[e]));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(xv[e], bf16_round(__fadd_rn(y[e], bv[e])));
+  }
+  *xp = pack8(o);
 }
 
 // ---------------------------------------------------------------- packed rows
@@ -311,6 +387,8 @@ struct RopeArgs {
   const double* sin_tab;
   int grid_h, grid_w, t_offset;
   float eps;
+  const float* ss_in;  // optional per-row sum of squares over norm_width columns
+  int norm_width;      // columns the RMS mean is taken over
   // optional V copy with the same destination mapping
   const __nv_bfloat16* v_src;
   long long ld_vsrc;
@@ -318,16 +396,22 @@ struct RopeArgs {
   long long ld_vdst;
 };
 
+// VEC chunk slots of 256 columns per row; the last slot is partial when K is an
+// odd multiple of 128 (lanes 16-31 then have no chunk there). With a.ss_in the
+// sum of squares over the full norm width (norm_width columns, of which this
+// row slice is a part) is given, as a tensor-parallel rank has it after the
+// all-reduce of its partial sums.
 template <int VEC>
-__global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(RopeArgs a, int M) {
-  constexpr int K = VEC * 256;
+__global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(RopeArgs a, int M, int K) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
+  const bool tail_ok = (VEC - 1) * 256 + lane * 8 < K;  // this lane has the last chunk
   const uint4* xr = reinterpret_cast<const uint4*>(a.src + row * a.ld_src) + lane;
   uint4 raw[VEC];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) raw[i] = ld_stream(xr + i * 32);
+  for (int i = 0; i < VEC; ++i)
+    raw[i] = (i < VEC - 1 || tail_ok) ? ld_stream(xr + i * 32) : make_uint4(0u, 0u, 0u, 0u);
   const int f = row / a.frame_tokens, sp = row % a.frame_tokens;
   const long long drow =
       static_cast<long long>((a.slot0 + f) % a.n_slots) * a.frame_tokens + sp;
@@ -341,21 +425,27 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
       uint4 t[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        if (i0 + u < VEC) t[u] = ldg_inorder(vr + (i0 + u) * 32);
+        if (i0 + u < VEC && (i0 + u < VEC - 1 || tail_ok)) t[u] = ldg_inorder(vr + (i0 + u) * 32);
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        if (i0 + u < VEC) vd[(i0 + u) * 32] = t[u];
+        if (i0 + u < VEC && (i0 + u < VEC - 1 || tail_ok)) vd[(i0 + u) * 32] = t[u];
     }
   }
-  float ss = 0.f;
+  float ssum;
+  if (a.ss_in) {
+    ssum = __ldg(a.ss_in + row);
+  } else {
+    float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    float v[8];
-    unpack8_v(raw[i], v);
+    for (int i = 0; i < VEC; ++i) {
+      float v[8];
+      unpack8_v(raw[i], v);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+    }
+    ssum = warp_sum(ss);
   }
-  const float r = rsqrtf(warp_sum(ss) * (1.0f / static_cast<float>(K)) + a.eps);
+  const float r = rsqrtf(ssum * (1.0f / static_cast<float>(a.norm_width)) + a.eps);
   // A lane's columns are lane*8 + 256*i: inside each 128-wide head that is the
   // same 4 complex pairs d = (lane & 15) * 4 + p for every chunk, so the lane
   // needs only these 4 rotations per row.
@@ -374,6 +464,7 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
   uint4* dr = reinterpret_cast<uint4*>(a.dst + drow * a.ld_dst) + lane;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
+    if (i == VEC - 1 && !tail_ok) break;
     const int c0 = i * 256 + lane * 8;
     float v[8], wv[8];
     unpack8_v(raw[i], v);
@@ -432,13 +523,26 @@ struct LnLaunch {
 };
 
 template <int VEC>
-struct RopeLaunch {
-  static int run(const RopeArgs& a, int M, cudaStream_t st) {
-    const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
-    rms_rope_kernel<VEC><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M);
-    return static_cast<int>(cudaGetLastError());
+int rope_launch(const RopeArgs& a, int M, int K, cudaStream_t st) {
+  const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
+  rms_rope_kernel<VEC><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M, K);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// K a multiple of 128, ceil(K / 256) chunk slots per lane.
+inline int rope_dispatch(const RopeArgs& a, int M, int K, cudaStream_t st) {
+  switch ((K + 255) / 256) {
+    case 1: return rope_launch<1>(a, M, K, st);
+    case 2: return rope_launch<2>(a, M, K, st);
+    case 3: return rope_launch<3>(a, M, K, st);
+    case 4: return rope_launch<4>(a, M, K, st);
+    case 6: return rope_launch<6>(a, M, K, st);
+    case 8: return rope_launch<8>(a, M, K, st);
+    case 12: return rope_launch<12>(a, M, K, st);
+    case 16: return rope_launch<16>(a, M, K, st);
+    default: return SRDIT_EUNSUPPORTED;
   }
-};
+}
 
 }  // namespace ew
 }  // namespace srdit
@@ -452,11 +556,13 @@ extern "C" int srdit_quant_rowwise(const void* x, long long ldx, int M, int K,
                                    cudaStream_t stream) {
   if (M == 0) return 0;
   if (!x || !q || !scale || M < 0 || K <= 0) return SRDIT_EINVAL;
-  if ((K % 256) || (ldx % 8) || (ldq % 16) || !aligned16(x) || !aligned16(q)) return SRDIT_EALIGN;
+  if ((K % 8) || (ldx % 8) || (ldq % 16) || !aligned16(x) || !aligned16(q)) return SRDIT_EALIGN;
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
   uint8_t* qb = static_cast<uint8_t*>(q);
-  const int rc = ew::dispatch_vec<ew::QuantLaunch>(K, xb, ldx, M, amax_in, qb, ldq, scale, stream);
-  if (rc != SRDIT_EUNSUPPORTED) return rc;
+  if (K % 256 == 0) {
+    const int rc = ew::dispatch_vec<ew::QuantLaunch>(K, xb, ldx, M, amax_in, qb, ldq, scale, stream);
+    if (rc != SRDIT_EUNSUPPORTED) return rc;
+  }
   const int grid = (M + ew::kRowsPerBlock - 1) / ew::kRowsPerBlock;
   ew::quant_rowwise_stream_kernel<8><<<grid, ew::kRowsPerBlock * 32, 0, stream>>>(
       xb, ldx, M, K, amax_in, qb, ldq, scale);
@@ -486,16 +592,19 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
                               const double* sin_tab, int tab_rows, int grid_h, int grid_w,
                               int t_offset,
                               const void* v_src, long long ld_vsrc, void* v_dst,
-                              long long ld_vdst, cudaStream_t stream) {
+                              long long ld_vdst, const float* ss_in, int norm_width,
+                              cudaStream_t stream) {
   if (M == 0) return 0;
   if (!src || !weight || !dst || M < 0 || frame_tokens <= 0 || n_slots <= 0 || slot0 < 0)
     return SRDIT_EINVAL;
+  if (K <= 0 || K % 128) return SRDIT_EUNSUPPORTED;
+  if (ss_in && norm_width < K) return SRDIT_EINVAL;
   if ((cos_tab == nullptr) != (sin_tab == nullptr)) return SRDIT_EINVAL;
   if (cos_tab) {
     // every table row the kernel indexes must exist: temporal positions
     // t_offset .. t_offset + frames - 1, spatial positions < grid_h / grid_w
     const int frames = (M + frame_tokens - 1) / frame_tokens;
-    if (K % 128 || grid_w <= 0 || grid_h <= 0 || grid_h * grid_w != frame_tokens ||
+    if (grid_w <= 0 || grid_h <= 0 || grid_h * grid_w != frame_tokens ||
         t_offset < 0 || tab_rows <= 0 || t_offset + frames > tab_rows || grid_h > tab_rows ||
         grid_w > tab_rows)
       return SRDIT_EINVAL;
@@ -519,9 +628,39 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
   a.grid_w = grid_w;
   a.t_offset = t_offset;
   a.eps = eps;
+  a.ss_in = ss_in;
+  a.norm_width = ss_in ? norm_width : K;
   a.v_src = static_cast<const __nv_bfloat16*>(v_src);
   a.ld_vsrc = ld_vsrc;
   a.v_dst = static_cast<__nv_bfloat16*>(v_dst);
   a.ld_vdst = ld_vdst;
-  return ew::dispatch_vec<ew::RopeLaunch>(K, a, M, stream);
+  return ew::rope_dispatch(a, M, K, stream);
+}
+
+extern "C" int srdit_row_reduce(const void* x, long long ldx, int M, int K, int op, float* out,
+                                cudaStream_t stream) {
+  if (M == 0) return 0;
+  if (!x || !out || M < 0 || K <= 0 || (op != SRDIT_ROW_SUMSQ && op != SRDIT_ROW_ABSMAX))
+    return SRDIT_EINVAL;
+  if ((K % 8) || (ldx % 8) || !aligned16(x)) return SRDIT_EALIGN;
+  const int grid = (M + ew::kRowsPerBlock - 1) / ew::kRowsPerBlock;
+  ew::row_reduce_kernel<<<grid, ew::kRowsPerBlock * 32, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, M, K, op, out);
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int srdit_residual(void* x, long long ldx, int M, int N, const void* parts,
+                              int n_parts, long long part_stride, long long ld_part,
+                              const void* bias, const float* gate, cudaStream_t stream) {
+  if (M == 0) return 0;
+  if (!x || !parts || M < 0 || N <= 0 || n_parts <= 0) return SRDIT_EINVAL;
+  if ((N % 8) || (ldx % 8) || (ld_part % 8) || (part_stride % 8) || !aligned16(x) ||
+      !aligned16(parts) || (bias && !aligned16(bias)) || (gate && !aligned16(gate)))
+    return SRDIT_EALIGN;
+  const long long work = static_cast<long long>(M) * (N / 8);
+  const unsigned grid = static_cast<unsigned>((work + 255) / 256);
+  ew::residual_kernel<<<grid, 256, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(x), ldx, M, N, static_cast<const __nv_bfloat16*>(parts),
+      n_parts, part_stride, ld_part, static_cast<const __nv_bfloat16*>(bias), gate);
+  return static_cast<int>(cudaGetLastError());
 }

@@ -179,7 +179,7 @@ class SRDiT:
         self.head_mod = f32("head.modulation").reshape(2, D)
         self.layers = []
         for i in range(cfg.num_layers):
-            self.layers.append(_Layer(sd, f"blocks.{i}.", cfg, dev))
+            self.layers.append(self._make_layer(sd, f"blocks.{i}."))
         self.rope_cos, self.rope_sin = rope_tables(self.head_dim, cfg.rope_rows, cfg.rope_theta, dev)
         self._bufs = {}
         self._cross_plans = {}
@@ -217,41 +217,54 @@ class SRDiT:
             shapes[f"{b}modulation"] = (1, 6, D)
         return shapes
 
-    @classmethod
-    def random_init(cls, cfg: SRDiTConfig, device="cuda", seed=0):
+    @staticmethod
+    def seeded_state_dict(cfg: SRDiTConfig, device="cuda", seed=0):
         """Seeded random weights of the reference architecture, generated on the
-        device one block at a time (the 5B model never exists in bf16 at once).
+        device on first access, one tensor at a time (the 5B model never exists
+        in bf16 at once). Each tensor has its own generator seeded from (seed,
+        name), so its values do not depend on the order tensors are read in --
+        a tensor-parallel rank slicing them gets exactly the full model's values.
 
         Linear weights N(0, 0.02), biases N(0, 0.01) (the reference zero-inits
         biases and the head, models.py:2259-2281, which would make any block math
         indistinguishable at the output), norm weights 1 + N(0, 0.1),
         modulations N(0, 1)/sqrt(dim).
         """
-        shapes = cls.param_shapes(cfg)
-        gen = torch.Generator(device=device)
-        gen.manual_seed(seed)
+        import zlib
+        shapes = SRDiT.param_shapes(cfg)
 
         def make(name, shape):
+            gen = torch.Generator(device=device)
+            gen.manual_seed(seed * 1000003 + zlib.crc32(name.encode()))
             if name.endswith("modulation"):
                 return torch.randn(shape, generator=gen, device=device) / cfg.dim ** 0.5
             if "norm" in name:
-                return 1 + 0.1 * torch.randn(shape, generator=gen, device=device)
-            if name.endswith("bias"):
-                return torch.randn(shape, generator=gen, device=device) * 0.01
-            return torch.randn(shape, generator=gen, device=device) * 0.02
+                t = 1 + 0.1 * torch.randn(shape, generator=gen, device=device)
+            elif name.endswith("bias"):
+                t = torch.randn(shape, generator=gen, device=device) * 0.01
+            else:
+                t = torch.randn(shape, generator=gen, device=device) * 0.02
+            return t.to(torch.bfloat16)
 
         class LazySD(dict):
             def __missing__(self, key):
-                t = make(key, shapes[key])
-                return t.to(torch.bfloat16) if not key.endswith("modulation") else t
+                return make(key, shapes[key])
 
-        return cls(cfg, LazySD(), device)
+        return LazySD()
+
+    @classmethod
+    def random_init(cls, cfg: SRDiTConfig, device="cuda", seed=0, **kw):
+        """The model with ``seeded_state_dict`` weights."""
+        return cls(cfg, SRDiT.seeded_state_dict(cfg, device, seed), device, **kw)
 
     @classmethod
     def from_state_dict(cls, cfg: SRDiTConfig, sd: dict, device="cuda"):
         return cls(cfg, sd, device)
 
     # ------------------------------------------------------------------ helpers
+    def _make_layer(self, sd, prefix):
+        return _Layer(sd, prefix, self.cfg, self.device)
+
     def _buf(self, name, shape, dtype):
         t = self._bufs.get(name)
         if t is None or t.shape != torch.Size(shape) or t.dtype != dtype:
@@ -259,8 +272,14 @@ class SRDiT:
         return t
 
     def new_cache(self, frame_tokens):
+        """K/V ring for this model's heads (all heads; a tensor-parallel rank's slice)."""
         c = self.cfg
-        return KVRing(c.num_layers, frame_tokens, c.dim, c.kv_len, c.chunk_frames, self.device)
+        return KVRing(c.num_layers, frame_tokens, self.kv_width, c.kv_len, c.chunk_frames,
+                      self.device)
+
+    @property
+    def kv_width(self):
+        return self.cfg.dim
 
     def _cross_plan(self, M, Lc):
         """Dense cross attention as one 'window' per query row of a (1, M/W, W) grid
@@ -315,26 +334,19 @@ class SRDiT:
         y = torch.einsum("fhwpqrc->cfphqwr", y).reshape(c.out_dim, f * p[0], h * p[1], w * p[2])
         return y.to(torch.bfloat16)
 
-    # ------------------------------------------------------------------ forward
-    def forward_chunk(self, latent, t, context, *, cache: KVRing | None = None,
-                      t_offset=0, update_cache=False, anchor_kv=None, anchor_align="frame",
-                      return_kv=False, ctx_emb=None):
-        """One streaming forward over a chunk (``_forward_inference`` for one sample).
+    def _setup(self, latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, n_heads,
+               width):
+        """Embeddings, the window plan and the attention geometries of one forward.
 
-        latent [C_in, f, H, W]; ``cache`` holds the previous chunks' K/V (read in
-        place); ``update_cache=True`` makes this the cache-refresh forward (the
-        chunk's K/V are kept, the ring advances). ``anchor_kv``: per-layer (K, V)
-        [f*h*w, D] bf16 LQ anchor (never cached). ``return_kv`` returns the
-        per-layer roped K / V of this chunk (the anchor harvest).
-        Returns the refined prediction [C_out, f, H, W] bf16 (and the K/V list).
-        """
+        ``n_heads`` / ``width``: the heads and row width of the q/k/v/out
+        tensors this process holds (all heads, or a tensor-parallel slice)."""
+        from types import SimpleNamespace
         c = self.cfg
         x, e0, e, ctx, grid = self.embed(latent, t, context) if ctx_emb is None else \
             self._embed_with_ctx(latent, t, ctx_emb)
         f, h, w = grid
         L = h * w
         M = f * L
-        D = c.dim
         dev = self.device
         if cache is None:
             cache = self._scratch_cache(L)
@@ -350,9 +362,10 @@ class SRDiT:
         mode = None if anchor_kv is None else anchor_align
         from .attention import cached_plan, _plan_device_state
         plan = cached_plan(spec, mode)
-        if "flops" not in plan:
-            plan["flops"] = blockgrid.visible_flops(plan["params"], int(plan["p_stride"]),
-                                                    c.num_heads, 128)
+        fkey = ("flops", n_heads)
+        if fkey not in plan:
+            plan[fkey] = blockgrid.visible_flops(plan["params"], int(plan["p_stride"]),
+                                                 n_heads, 128)
         a_hw = (h, w) if anchor_kv is not None else None
         params_dev, tiling, n_w, amode = _plan_device_state(
             plan, dev, mode, (f, h, w, f_kv, a_hw, f if a_hw else 0),
@@ -360,21 +373,51 @@ class SRDiT:
         geom = _lib.WinattnGeom()
         geom.q_frames, geom.q_h, geom.q_w = f, h, w
         geom.kv_h, geom.kv_w, geom.kv_slots, geom.kv_slot0 = h, w, cache.cap, cache.start
-        geom.n_heads, geom.head_dim = c.num_heads, 128
-        geom.q_stride = geom.kv_stride = geom.o_stride = D
+        geom.n_heads, geom.head_dim = n_heads, 128
+        geom.q_stride = geom.kv_stride = geom.o_stride = width
         geom.scale = 128 ** -0.5
         if anchor_kv is not None:
-            geom.a_frames, geom.a_h, geom.a_w, geom.a_stride = f, h, w, D
+            geom.a_frames, geom.a_h, geom.a_w, geom.a_stride = f, h, w, width
 
         Lc = ctx.shape[0]
         cp_params, cp_tiling, cp_nw, cwq, chk, cwk = self._cross_plan(M, Lc)
         cgeom = _lib.WinattnGeom()
         cgeom.q_frames, cgeom.q_h, cgeom.q_w = 1, M // cwq, cwq
         cgeom.kv_h, cgeom.kv_w, cgeom.kv_slots, cgeom.kv_slot0 = chk, cwk, 1, 0
-        cgeom.n_heads, cgeom.head_dim = c.num_heads, 128
-        cgeom.q_stride = cgeom.o_stride = D
-        cgeom.kv_stride = 2 * D
+        cgeom.n_heads, cgeom.head_dim = n_heads, 128
+        cgeom.q_stride = cgeom.o_stride = width
+        cgeom.kv_stride = 2 * width
         cgeom.scale = 128 ** -0.5
+        return SimpleNamespace(x=x, e0=e0, e=e, ctx=ctx, grid=grid, cache=cache, L=L, M=M,
+                               Lc=Lc, slot_cur=slot_cur, plan=plan, params_dev=params_dev,
+                               tiling=tiling, n_w=n_w, amode=amode, geom=geom,
+                               cp_params=cp_params, cp_tiling=cp_tiling, cp_nw=cp_nw,
+                               cgeom=cgeom, flops=plan[fkey],
+                               cross_flops=4 * 128 * n_heads * M * Lc)
+
+    # ------------------------------------------------------------------ forward
+    def forward_chunk(self, latent, t, context, *, cache: KVRing | None = None,
+                      t_offset=0, update_cache=False, anchor_kv=None, anchor_align="frame",
+                      return_kv=False, ctx_emb=None):
+        """One streaming forward over a chunk (``_forward_inference`` for one sample).
+
+        latent [C_in, f, H, W]; ``cache`` holds the previous chunks' K/V (read in
+        place); ``update_cache=True`` makes this the cache-refresh forward (the
+        chunk's K/V are kept, the ring advances). ``anchor_kv``: per-layer (K, V)
+        [f*h*w, D] bf16 LQ anchor (never cached). ``return_kv`` returns the
+        per-layer roped K / V of this chunk (the anchor harvest).
+        Returns the refined prediction [C_out, f, H, W] bf16 (and the K/V list).
+        """
+        c = self.cfg
+        S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb,
+                        c.num_heads, c.dim)
+        x, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
+        f, h, w = grid
+        L, M, D, Lc = S.L, S.M, c.dim, S.Lc
+        dev = self.device
+        slot_cur, plan, params_dev, tiling, n_w, amode, geom = (
+            S.slot_cur, S.plan, S.params_dev, S.tiling, S.n_w, S.amode, S.geom)
+        cp_params, cp_tiling, cp_nw, cgeom = S.cp_params, S.cp_tiling, S.cp_nw, S.cgeom
 
         bf16, f32, f8 = torch.bfloat16, torch.float32, torch.float8_e4m3fn
         xq = self._buf("xq", (M, D), f8)
@@ -409,7 +452,7 @@ class SRDiT:
             ops.winattn(qb, kr, vr, att, params_dev=params_dev, n_w=n_w,
                         p_stride=int(plan["p_stride"]), anchor_mode=amode, geom=geom,
                         tiling=tiling, k_anchor=ak, v_anchor=av, status=st,
-                        flops=plan["flops"])
+                        flops=S.flops)
             if return_kv:
                 idx = (torch.arange(f, device=dev) + slot_cur) % cache.cap
                 kv_out.append((kr.view(cache.cap, L, D)[idx].reshape(M, D).clone(),
@@ -425,7 +468,7 @@ class SRDiT:
             ops.rms_rope(ckv[:, :D], ly.cnk, c.eps, ckv[:, :D], frame_tokens=Lc)
             ops.winattn(qb, ckv[:, :D], ckv[:, D:], att, params_dev=cp_params, n_w=cp_nw,
                         p_stride=blockgrid.P_PLAIN, anchor_mode=0, geom=cgeom, tiling=cp_tiling,
-                        status=st, flops=4 * 128 * c.num_heads * M * Lc)
+                        status=st, flops=S.cross_flops)
             ops.quant_rowwise(att, q=xq, scale=xs)
             ops.fp8_gemm(xq, xs, ly.w_co, ly.s_co, ly.b_co, x, epilogue="res", residual=x)
             # --- FFN

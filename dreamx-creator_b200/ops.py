@@ -125,9 +125,15 @@ def ln_mod_quant(x, eps=1e-6, *, ln_weight=None, ln_bias=None, shift=None, scale
 
 
 def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, cos=None,
-             sin=None, grid_h=0, grid_w=0, t_offset=0, v_src=None, v_dst=None):
-    """RMSNorm(src) * weight [-> 3-D RoPE] -> dst frame slots (+ V copy)."""
-    _need_cuda(src, weight, dst, cos, sin, v_src, v_dst)
+             sin=None, grid_h=0, grid_w=0, t_offset=0, v_src=None, v_dst=None, ss=None,
+             norm_width=0):
+    """RMSNorm(src) * weight [-> 3-D RoPE] -> dst frame slots (+ V copy).
+
+    ``ss`` ([M] fp32, optional): per-row sum of squares over ``norm_width``
+    columns (a tensor-parallel slice's all-reduced statistic)."""
+    _need_cuda(src, weight, dst, cos, sin, v_src, v_dst, ss)
+    if ss is not None and (ss.dtype != torch.float32 or not ss.is_contiguous()):
+        raise _lib.SrditError("ss must be contiguous float32")
     M, K = src.shape
     if cos is not None and (cos.dtype != torch.float64 or sin.dtype != torch.float64
                             or cos.shape != sin.shape or cos.shape[1] != 64
@@ -138,9 +144,41 @@ def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, c
             _ptr(dst), _rows(dst), int(frame_tokens), int(slot0), int(n_slots), _ptr(cos),
             _ptr(sin), int(tab_rows), int(grid_h), int(grid_w), int(t_offset), _ptr(v_src),
             _rows(v_src) if v_src is not None else 0, _ptr(v_dst),
-            _rows(v_dst) if v_dst is not None else 0, _stream(src.device), kind="rms_rope",
+            _rows(v_dst) if v_dst is not None else 0, _ptr(ss), int(norm_width),
+            _stream(src.device), kind="rms_rope",
             work=M * K * 2 * (4 if v_src is not None else 2))
     return dst
+
+
+def row_reduce(x, op, out=None):
+    """Per-row sum of squares (op "sumsq") or max |x| (op "absmax") of a bf16 [M, K]."""
+    _need_cuda(x, out)
+    if x.dtype != torch.bfloat16:
+        raise _lib.SrditError("row_reduce takes bf16")
+    M, K = x.shape
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=x.device)
+    code = {"sumsq": _lib.SRDIT_ROW_SUMSQ, "absmax": _lib.SRDIT_ROW_ABSMAX}[op]
+    _launch("srdit_row_reduce", _ptr(x), _rows(x), M, K, code, _ptr(out), _stream(x.device),
+            kind="row_reduce", work=M * K * 2 + 4 * M)
+    return out
+
+
+def residual(x, parts, bias=None, gate=None):
+    """x = bf16(x + bf16(sum(parts) + bias) [* gate]) in place; parts [S, M, N] or [M, N]."""
+    _need_cuda(x, parts, bias, gate)
+    p3 = parts if parts.dim() == 3 else parts.unsqueeze(0)
+    if p3.dtype != torch.bfloat16 or p3.stride(2) != 1:
+        raise _lib.SrditError("residual parts must be bf16 with unit inner stride")
+    S, M, N = p3.shape
+    if x.shape != (M, N):
+        raise _lib.SrditError(f"x {tuple(x.shape)} vs parts {tuple(p3.shape)}")
+    if gate is not None and (gate.dtype != torch.float32 or not gate.is_contiguous()):
+        raise _lib.SrditError("gate must be contiguous float32")
+    _launch("srdit_residual", _ptr(x), _rows(x), M, N, _ptr(p3), S, p3.stride(0), p3.stride(1),
+            _ptr(bias), _ptr(gate), _stream(x.device), kind="residual",
+            work=M * N * 2 * (S + 2))
+    return x
 
 
 def winattn_plan(params_host: torch.Tensor, p_stride: int, anchor_mode: int):

@@ -74,7 +74,7 @@ int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const void* b_fp8,
  * Per-row e4m3 quantisation of a bf16 [M, K] matrix (row stride ldx elements):
  *   scale[m] = max(amax_m / 448, 1e-12);  q = e4m3(clamp(x / scale, -448, 448)).
  * amax_in [M] (optional): precomputed per-row max |x| (skips the reduction pass).
- * K multiple of 256, ldq multiple of 16.
+ * K multiple of 8, ldq multiple of 16.
  * Replaces: _quantize_rowwise_impl / quantize_rowwise
  *   (video_refiner/wan/modules/sr_dit/fp8_linear.py:93-103, :146-171).
  */
@@ -96,14 +96,18 @@ int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, float eps,
                        cudaStream_t stream);
 
 /*
- * RMSNorm over the full K-wide row (x * rsqrt(mean(x^2) + eps) -> bf16 -> x
+ * RMSNorm over the K-wide row slice (x * rsqrt(mean(x^2) + eps) -> bf16 -> x
  * weight), then optional 3-D RoPE per 128-wide head in fp64 with the tables
  * cos_tab/sin_tab [tab_rows, 64] (columns 0-21 temporal, 22-42 height, 43-63
  * width), token position (t_offset + f, h, w) on the grid_h x grid_w frame grid.
  * Row r = f * frame_tokens + s is written to destination row
  *   ((slot0 + f) % n_slots) * frame_tokens + s
  * so K/V land directly in the frame slots of a KV cache. v_src/v_dst (optional)
- * copy the matching V rows with the same mapping.
+ * copy the matching V rows with the same mapping. K is a multiple of 128.
+ * ss_in (optional, [M] fp32): the row's sum of squares over norm_width >= K
+ * columns, of which this K-wide slice is one part -- a tensor-parallel rank
+ * passes the all-reduced sum of every rank's slice; NULL computes it from the
+ * slice with norm_width = K.
  * Replaces: WanRMSNorm.forward (models.py:424-440) on q and k (models.py:602-604),
  *   rope_apply (models.py:173-214), and the KV-cache torch.cat of
  *   attention.py:1506-1510.
@@ -112,7 +116,35 @@ int srdit_rms_rope(const void* src, long long ld_src, int M, int K, const void* 
                    float eps, void* dst, long long ld_dst, int frame_tokens, int slot0,
                    int n_slots, const double* cos_tab, const double* sin_tab, int tab_rows,
                    int grid_h, int grid_w, int t_offset, const void* v_src, long long ld_vsrc,
-                   void* v_dst, long long ld_vdst, cudaStream_t stream);
+                   void* v_dst, long long ld_vdst, const float* ss_in, int norm_width,
+                   cudaStream_t stream);
+
+#define SRDIT_ROW_SUMSQ 0
+#define SRDIT_ROW_ABSMAX 1
+
+/*
+ * Per-row statistic of a bf16 [M, K] matrix (K multiple of 8): out[m] =
+ * sum_k x^2 (SRDIT_ROW_SUMSQ) or max_k |x| (SRDIT_ROW_ABSMAX), fp32. A
+ * tensor-parallel rank's partial statistic of its column slice, before the
+ * all-reduce that completes the full-row RMSNorm (models.py:437-440) or the
+ * per-token fp8 amax (fp8_linear.py:96-97).
+ */
+int srdit_row_reduce(const void* x, long long ldx, int M, int K, int op, float* out,
+                     cudaStream_t stream);
+
+/*
+ * Residual update after a row-parallel Linear, for [M, N] bf16 x (N multiple of 8):
+ *   y = sum_{s < n_parts} parts[s] + bias          (fp32; parts bf16, part s at
+ *                                                   parts + s * part_stride)
+ *   x = bf16(x + bf16(y) * gate)   (gate [N] fp32 given)
+ *   x = bf16(x + bf16(y))          (gate NULL)
+ * Replaces: the residual updates of models.py:1349-1351 (x + y * e2), :1261
+ *   (x + ffn(...) * e5) and :1257 (x + cross_attn(...)) when the Linear's
+ *   output arrives as per-rank partial products.
+ */
+int srdit_residual(void* x, long long ldx, int M, int N, const void* parts, int n_parts,
+                   long long part_stride, long long ld_part, const void* bias,
+                   const float* gate, cudaStream_t stream);
 
 /* Token grids, strides and frame slots of one window-attention launch. */
 typedef struct srdit_winattn_geom {
