@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--geometry", default="8x8r0", choices=["8x8r0", "4x4r3"])
     ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--tp-comm", default="fused", choices=["fused", "nccl"],
+                    help="TP collectives fused into the kernels over peer memory, or NCCL")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="N > 1: tensor parallelism over one clip (strong scaling, the "
                          "reference's DTensor-style TP) or one clip per GPU (weak scaling)")
@@ -240,7 +242,8 @@ def workload_config(args):
             "model": "SR-DiT 5B (30 blocks, dim 3072, 24x128 heads, ffn 14336)",
             "layers": args.layers, "tokens": 6912, "window": f"3x{bhw[0]}x{bhw[1]} r{rhw}",
             "global_batch": 1 if args.parallel == "tp" else args.gpus, "seq_len": 6912,
-            "parallelism": (f"tp{args.gpus} (sequence-parallel residual stream)"
+            "parallelism": (f"tp{args.gpus} (sequence-parallel residual stream, "
+                            f"{args.tp_comm} collectives)"
                             if args.parallel == "tp" else "replicas") if args.gpus > 1
             else "single",
             "l2": "inputs larger than L2 (5 GB of fp8 weights stream every forward)"}
@@ -313,7 +316,7 @@ def run_gpu_arm(args, rank, world, local):
     tp = world > 1 and args.parallel == "tp"
     if tp:
         tp_mod = import_module("dreamx-creator_b200.tp")
-        model = tp_mod.TPSRDiT.random_init(cfg, dev, seed=0)
+        model = tp_mod.TPSRDiT.random_init(cfg, dev, seed=0, fused=args.tp_comm == "fused")
     else:
         model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
     # tensor parallelism refines one clip on all ranks; replicas one clip each

@@ -40,6 +40,22 @@ class WinattnTiling(ctypes.Structure):
                 ("aboxes_per_tile", c_int), ("has_anchor", c_int)]
 
 
+SRDIT_EPI_PEER = 4
+SRDIT_MAX_RANKS = 8
+SRDIT_RED_SUM, SRDIT_RED_MAX = 0, 1
+
+
+class PeerPtrs(ctypes.Structure):
+    _fields_ = [("p", c_vp * SRDIT_MAX_RANKS)]
+
+
+class TpGemm(ctypes.Structure):
+    _fields_ = [("ag_flags", c_vp), ("ag_expected", ctypes.c_uint32),
+                ("rows_per_rank", c_int), ("rank", c_int), ("world", c_int),
+                ("rs_slot", c_vp * SRDIT_MAX_RANKS), ("ld_rs", c_ll),
+                ("rs_flags", c_vp * SRDIT_MAX_RANKS)]
+
+
 # name -> argtypes (every function returns int)
 SIGNATURES = {
     "srdit_version": [],
@@ -52,6 +68,19 @@ SIGNATURES = {
                        c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_ll,
                        c_vp, c_int, c_vp],
     "srdit_row_reduce": [c_vp, c_ll, c_int, c_int, c_int, c_vp, c_vp],
+    "srdit_fp8_gemm_tp": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
+                          c_int, c_int, c_vp, ctypes.POINTER(TpGemm), c_vp, c_vp],
+    "srdit_fp8_gemm_ctas": [c_int, c_int],
+    "srdit_residual_tp": [c_vp, c_ll, c_int, c_int, c_vp, c_int, c_ll, c_ll, c_vp, c_vp, c_vp,
+                          ctypes.c_uint32, c_vp, c_vp],
+    "srdit_tp_allreduce": [c_vp, c_vp, c_int, c_int, ctypes.POINTER(PeerPtrs),
+                           ctypes.POINTER(PeerPtrs), c_int, c_int, ctypes.c_uint32, c_vp, c_vp],
+    "srdit_tp_push": [c_vp, ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, c_vp,
+                      ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, ctypes.POINTER(PeerPtrs),
+                      c_int, c_int, c_vp],
+    "srdit_ipc_handle": [c_vp, c_vp, ctypes.POINTER(ctypes.c_ulonglong)],
+    "srdit_ipc_open": [c_vp, ctypes.POINTER(c_vp)],
+    "srdit_ipc_close": [c_vp],
     "srdit_residual": [c_vp, c_ll, c_int, c_int, c_vp, c_int, c_ll, c_ll, c_vp, c_vp, c_vp],
     "srdit_winattn_plan": [c_vp, c_int, c_int, c_int, ctypes.POINTER(WinattnTiling)],
     "srdit_winattn_fwd": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
@@ -96,6 +125,11 @@ def lib() -> ctypes.CDLL:
         L.srdit_strerror.restype = ctypes.c_char_p
         _lib = L
         return L
+
+
+def count(name: str, *args) -> int:
+    """Call an entry point that returns a count (not a status)."""
+    return int(getattr(lib(), name)(*args))
 
 
 def check(rc: int, what: str) -> None:

@@ -217,20 +217,35 @@ __global__ void __launch_bounds__(128) row_reduce_kernel(const __nv_bfloat16* __
 // The parts are the bf16 partial products of a row-parallel Linear; the sum is
 // fp32. This is the reference's gated / plain residual after o / cross-o /
 // ffn.2 (models.py:1349-1351, :1257, :1261) applied to a tensor-parallel sum.
+//
+// flags (optional): the parts arrive from peer GPUs; each block first waits
+// (bounded) until flags[s] >= expected for every part s.
 __global__ void __launch_bounds__(256) residual_kernel(
     __nv_bfloat16* __restrict__ x, long long ldx, int M, int N,
     const __nv_bfloat16* __restrict__ parts, int n_parts, long long part_stride,
-    long long ld_part, const __nv_bfloat16* __restrict__ bias, const float* __restrict__ gate) {
+    long long ld_part, const __nv_bfloat16* __restrict__ bias, const float* __restrict__ gate,
+    const uint32_t* flags, uint32_t expected, uint32_t* status) {
+  if (flags) {
+    __shared__ int ready;
+    if (threadIdx.x == 0) {
+      bool ok = true;
+      for (int sp = 0; sp < n_parts && ok; ++sp) ok = flag_wait(flags + sp, expected, status);
+      ready = ok;
+    }
+    __syncthreads();
+    if (!ready) return;
+  }
   const int per_row = N >> 3;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<long long>(M) * per_row) return;
   const int row = static_cast<int>(idx / per_row);
   const int c0 = static_cast<int>(idx % per_row) * 8;
+  // parts may be written by peer GPUs while this kernel waits: coherent loads
   float y[8];
-  unpack8(ld_stream(reinterpret_cast<const uint4*>(parts + row * ld_part + c0)), y);
+  unpack8(*reinterpret_cast<const uint4*>(parts + row * ld_part + c0), y);
   for (int s = 1; s < n_parts; ++s) {
     float t[8];
-    unpack8(ld_stream(reinterpret_cast<const uint4*>(parts + s * part_stride + row * ld_part + c0)), t);
+    unpack8(*reinterpret_cast<const uint4*>(parts + s * part_stride + row * ld_part + c0), t);
 #pragma unroll
     for (int e = 0; e < 8; ++e) y[e] += t[e];
   }
@@ -652,6 +667,14 @@ extern "C" int srdit_row_reduce(const void* x, long long ldx, int M, int K, int 
 extern "C" int srdit_residual(void* x, long long ldx, int M, int N, const void* parts,
                               int n_parts, long long part_stride, long long ld_part,
                               const void* bias, const float* gate, cudaStream_t stream) {
+  return srdit_residual_tp(x, ldx, M, N, parts, n_parts, part_stride, ld_part, bias, gate,
+                           nullptr, 0u, nullptr, stream);
+}
+
+extern "C" int srdit_residual_tp(void* x, long long ldx, int M, int N, const void* parts,
+                                 int n_parts, long long part_stride, long long ld_part,
+                                 const void* bias, const float* gate, const uint32_t* flags,
+                                 uint32_t expected, uint32_t* status, cudaStream_t stream) {
   if (M == 0) return 0;
   if (!x || !parts || M < 0 || N <= 0 || n_parts <= 0) return SRDIT_EINVAL;
   if ((N % 8) || (ldx % 8) || (ld_part % 8) || (part_stride % 8) || !aligned16(x) ||
@@ -661,6 +684,7 @@ extern "C" int srdit_residual(void* x, long long ldx, int M, int N, const void* 
   const unsigned grid = static_cast<unsigned>((work + 255) / 256);
   ew::residual_kernel<<<grid, 256, 0, stream>>>(
       static_cast<__nv_bfloat16*>(x), ldx, M, N, static_cast<const __nv_bfloat16*>(parts),
-      n_parts, part_stride, ld_part, static_cast<const __nv_bfloat16*>(bias), gate);
+      n_parts, part_stride, ld_part, static_cast<const __nv_bfloat16*>(bias), gate, flags,
+      expected, status);
   return static_cast<int>(cudaGetLastError());
 }

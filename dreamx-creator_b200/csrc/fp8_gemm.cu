@@ -29,6 +29,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
+#include <cstring>
+
 namespace srdit {
 namespace gemm {
 
@@ -74,6 +76,29 @@ SRDIT_DEV float tanh_sfu(float x) {
   return y;
 }
 
+// Tensor-parallel extras (zero-filled for a plain launch).
+//  - ag_flags: this rank's all-gather counters; A rows owned by another rank s
+//    (rows [s*rows_per_rank, (s+1)*rows_per_rank)) are complete once
+//    ag_flags[s] reaches ag_expected. The producer waits before loading a
+//    tile's rows and the epilogue before reading their scales; this rank's own
+//    rows were written earlier on the same stream.
+//  - EPI_PEER: output row r belongs to rank r / rows_per_rank; each 32-row box
+//    is stored with that rank's map in `PeerMaps` (its receive slot for this
+//    rank's partial), and once a CTA's stores have landed it adds 1 to
+//    rs_flags[d][rank] on every rank d.
+//  - mt_offset rotates the tile order so the local shard's tiles come first.
+struct TpArgs {
+  const uint32_t* ag_flags;
+  uint32_t ag_expected;
+  int rows_per_rank;
+  int rank, world;
+  int mt_offset;
+  uint32_t* rs_flags[SRDIT_MAX_RANKS];
+};
+struct PeerMaps {
+  CUtensorMap m[SRDIT_MAX_RANKS];
+};
+
 SRDIT_DEV float gelu_tanh(float x) {
   // 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3)))
   const float kBeta = 0.7978845608028654f;
@@ -89,7 +114,8 @@ template <int EPI, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmO, const Params p) {
+                    const __grid_constant__ CUtensorMap tmO, const Params p,
+                    const __grid_constant__ PeerMaps pm, const __grid_constant__ TpArgs tp) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -147,8 +173,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
+      uint32_t ready = 0u;  // owners whose rows this producer already waited for
       for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
-        const int mt = tile / num_n, nt = tile % num_n;
+        const int mt = (tile / num_n + tp.mt_offset) % num_m, nt = tile % num_n;
+        if (tp.ag_flags) {
+          const int r0 = mt * 2 * BM, r1 = min(r0 + 2 * BM, p.M) - 1;
+          for (int o = r0 / tp.rows_per_rank; o <= r1 / tp.rows_per_rank && ok; ++o) {
+            if (o != tp.rank && !((ready >> o) & 1u)) {
+              ok = flag_wait(tp.ag_flags + o, tp.ag_expected, p.status);
+              ready |= 1u << o;
+            }
+          }
+          if (!ok) {
+            *abort_flag = 1u;
+            break;
+          }
+          fence_proxy_async_global();  // the peers' rows, acquired above, feed TMA reads
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, p.status, abort_flag)) {
             ok = false;
@@ -226,7 +267,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     for (int tile = cid; tile < num_tiles; tile += ncl, ++local) {
       const int acc = local & 1;
       const uint32_t aph = static_cast<uint32_t>(local >> 1) & 1u;
-      const int mt = tile / num_n, nt = tile % num_n;
+      const int mt = (tile / num_n + tp.mt_offset) % num_m, nt = tile % num_n;
       const int n0 = nt * BN;
       // column scale and bias of this tile -> shared memory (double-buffered)
       for (int c = ep_tid; c < BN; c += 128) {
@@ -240,7 +281,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM + sub * 32;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
-      const float sa = row_ok ? __ldg(p.a_scale + row) : 0.f;
+      if (tp.ag_flags && row0 < p.M) {  // the scales of gathered rows come from their owner
+        bool got = true;
+        if (lane == 0) {
+          const int o0 = row0 / tp.rows_per_rank;
+          const int o1 = (min(row0 + 32, p.M) - 1) / tp.rows_per_rank;
+          for (int o = o0; o <= o1 && got; ++o)
+            if (o != tp.rank) got = flag_wait(tp.ag_flags + o, tp.ag_expected, p.status);
+        }
+        if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+          *abort_flag = 1u;
+          break;
+        }
+      }
+      const float sa = row_ok ? p.a_scale[row] : 0.f;
       const float* cs = col_s + acc * 256;
       const float* cb = col_b + acc * 256;
       float amax = 0.f;
@@ -319,7 +373,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && row0 < p.M && n0 + ch * 64 < p.N) {  // boxes start inside the tensor
-          tma_store_2d(&tmO, buf, n0 + ch * 64, row0);
+          if constexpr (EPI == EPI_PEER) {
+            const int owner = row0 / tp.rows_per_rank;  // rows_per_rank % 32 == 0
+            tma_store_2d(&pm.m[owner], buf, n0 + ch * 64, row0 - owner * tp.rows_per_rank);
+          } else {
+            tma_store_2d(&tmO, buf, n0 + ch * 64, row0);
+          }
           bulk_commit_group();
         }
         ++stores;
@@ -333,6 +392,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     if (lane == 0) bulk_wait_group_all();
     __syncwarp();
+    if constexpr (EPI == EPI_PEER) {
+      // this CTA's partial tiles have landed in their owners' memory: publish
+      fence_proxy_async_global();
+      __threadfence_system();
+      named_barrier_sync(1, 128);
+      if (ep_tid == 0 && !*abort_flag)
+        for (int d = 0; d < tp.world; ++d) flag_add_release(tp.rs_flags[d] + tp.rank, 1u);
+    }
   }
 
   tc_fence_before();
@@ -345,7 +412,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 template <int EPI, int BN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                  const Params& p, cudaStream_t stream) {
+                  const Params& p, const PeerMaps& pm, const TpArgs& tp, cudaStream_t stream) {
   auto kern = fp8_gemm_kernel<EPI, BN>;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -359,7 +426,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
   const int pairs = num_sms(dev) / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, NUM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, to, p);
+  kern<<<grid, NUM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, to, p, pm, tp);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -382,9 +449,18 @@ static int pick_bn(int M, int N, int pairs) {
 
 template <int EPI>
 static int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const CUtensorMap& to, const Params& p, cudaStream_t stream) {
-  return bn == 256 ? launch<EPI, 256>(ta, tb, to, p, stream)
-                   : launch<EPI, 192>(ta, tb, to, p, stream);
+                     const CUtensorMap& to, const Params& p, const PeerMaps& pm,
+                     const TpArgs& tp, cudaStream_t stream) {
+  return bn == 256 ? launch<EPI, 256>(ta, tb, to, p, pm, tp, stream)
+                   : launch<EPI, 192>(ta, tb, to, p, pm, tp, stream);
+}
+
+// CTAs of one launch (two per output-tile pair, at most one pair per two SMs).
+static int grid_ctas(int M, int N, int dev) {
+  const int pairs = num_sms(dev) / 2;
+  const int bn = pick_bn(M, N, pairs);
+  const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + bn - 1) / bn);
+  return 2 * (tiles < pairs ? tiles : pairs);
 }
 
 }  // namespace gemm
@@ -392,25 +468,55 @@ static int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
 
 using namespace srdit;
 
-extern "C" int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const void* b_fp8,
-                              const float* b_scale, const void* bias, void* out, int M, int N,
-                              int K, int lda, int ldb, int ldo, int epilogue,
-                              const void* residual, int ldr, const float* gate,
-                              float* row_amax, uint32_t* status, cudaStream_t stream) {
+static int fp8_gemm_impl(const void* a_fp8, const float* a_scale, const void* b_fp8,
+                         const float* b_scale, const void* bias, void* out, int M, int N, int K,
+                         int lda, int ldb, int ldo, int epilogue, const void* residual, int ldr,
+                         const float* gate, float* row_amax, uint32_t* status,
+                         const srdit_tp_gemm* tpa, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return (M == 0 || N == 0) ? 0 : SRDIT_EINVAL;
-  if (!a_fp8 || !a_scale || !b_fp8 || !b_scale || !out) return SRDIT_EINVAL;
-  if (lda < K || ldb < K || ldo < N) return SRDIT_EINVAL;
-  if ((lda % 16) || (ldb % 16) || (ldo % 8)) return SRDIT_EALIGN;  // TMA strides: 16 B
+  if (!a_fp8 || !a_scale || !b_fp8 || !b_scale) return SRDIT_EINVAL;
+  if (epilogue != EPI_PEER && !out) return SRDIT_EINVAL;
+  if (lda < K || ldb < K || (epilogue != EPI_PEER && ldo < N)) return SRDIT_EINVAL;
+  if ((lda % 16) || (ldb % 16) || (epilogue != EPI_PEER && (ldo % 8)))
+    return SRDIT_EALIGN;  // TMA strides: 16 B
   if ((reinterpret_cast<uintptr_t>(a_fp8) & 15u) || (reinterpret_cast<uintptr_t>(b_fp8) & 15u) ||
       (reinterpret_cast<uintptr_t>(out) & 15u))
     return SRDIT_EALIGN;
-  if (epilogue < EPI_STORE || epilogue > EPI_RES) return SRDIT_EINVAL;
+  if (epilogue < EPI_STORE || epilogue > EPI_PEER) return SRDIT_EINVAL;
+  if (epilogue == EPI_PEER && !tpa) return SRDIT_EINVAL;
   if (epilogue == EPI_GATED_RES || epilogue == EPI_RES) {
     if (!residual || ldr < N) return SRDIT_EINVAL;
     if ((ldr % 8) || (reinterpret_cast<uintptr_t>(residual) & 15u)) return SRDIT_EALIGN;
   }
   if (epilogue == EPI_GATED_RES && !gate) return SRDIT_EINVAL;
   if (epilogue == EPI_GELU && !row_amax) return SRDIT_EINVAL;
+
+  gemm::TpArgs tp = {};
+  gemm::PeerMaps pm;
+  memset(&pm, 0, sizeof(pm));
+  if (tpa) {
+    if (tpa->world < 1 || tpa->world > SRDIT_MAX_RANKS || tpa->rank < 0 ||
+        tpa->rank >= tpa->world || tpa->rows_per_rank <= 0 ||
+        static_cast<long long>(tpa->rows_per_rank) * tpa->world != M)
+      return SRDIT_EINVAL;
+    tp.ag_flags = tpa->ag_flags;
+    tp.ag_expected = tpa->ag_expected;
+    tp.rows_per_rank = tpa->rows_per_rank;
+    tp.rank = tpa->rank;
+    tp.world = tpa->world;
+    tp.mt_offset = (tpa->rank * tpa->rows_per_rank) / (2 * gemm::BM);
+    if (epilogue == EPI_PEER) {
+      if (tpa->rows_per_rank % 32) return SRDIT_EUNSUPPORTED;  // whole 32-row store boxes
+      if (tpa->ld_rs < N || (tpa->ld_rs % 8)) return SRDIT_EALIGN;
+      for (int d = 0; d < tpa->world; ++d) {
+        if (!tpa->rs_slot[d] || !tpa->rs_flags[d]) return SRDIT_EINVAL;
+        int rc = make_tmap_2d(&pm.m[d], tpa->rs_slot[d], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N,
+                              tpa->rows_per_rank, tpa->ld_rs, 64, 32);
+        if (rc) return rc;
+        tp.rs_flags[d] = tpa->rs_flags[d];
+      }
+    }
+  }
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -421,8 +527,12 @@ extern "C" int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const voi
   if (rc) return rc;
   rc = make_tmap_2d(&tb, b_fp8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldb, gemm::BK, bn / 2);
   if (rc) return rc;
-  rc = make_tmap_2d(&to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldo, 64, 32);
-  if (rc) return rc;
+  if (epilogue == EPI_PEER) {
+    to = pm.m[tp.rank];  // unused by the peer epilogue
+  } else {
+    rc = make_tmap_2d(&to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldo, 64, 32);
+    if (rc) return rc;
+  }
 
   gemm::Params p;
   p.M = M;
@@ -437,9 +547,38 @@ extern "C" int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const voi
   p.row_amax = row_amax;
   p.status = status;
   switch (epilogue) {
-    case EPI_STORE: return gemm::launch_bn<EPI_STORE>(bn, ta, tb, to, p, stream);
-    case EPI_GELU: return gemm::launch_bn<EPI_GELU>(bn, ta, tb, to, p, stream);
-    case EPI_GATED_RES: return gemm::launch_bn<EPI_GATED_RES>(bn, ta, tb, to, p, stream);
-    default: return gemm::launch_bn<EPI_RES>(bn, ta, tb, to, p, stream);
+    case EPI_STORE: return gemm::launch_bn<EPI_STORE>(bn, ta, tb, to, p, pm, tp, stream);
+    case EPI_GELU: return gemm::launch_bn<EPI_GELU>(bn, ta, tb, to, p, pm, tp, stream);
+    case EPI_GATED_RES: return gemm::launch_bn<EPI_GATED_RES>(bn, ta, tb, to, p, pm, tp, stream);
+    case EPI_RES: return gemm::launch_bn<EPI_RES>(bn, ta, tb, to, p, pm, tp, stream);
+    default: return gemm::launch_bn<EPI_PEER>(bn, ta, tb, to, p, pm, tp, stream);
   }
+}
+
+extern "C" int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const void* b_fp8,
+                              const float* b_scale, const void* bias, void* out, int M, int N,
+                              int K, int lda, int ldb, int ldo, int epilogue,
+                              const void* residual, int ldr, const float* gate,
+                              float* row_amax, uint32_t* status, cudaStream_t stream) {
+  if (epilogue == EPI_PEER) return SRDIT_EINVAL;  // the peer epilogue needs srdit_fp8_gemm_tp
+  return fp8_gemm_impl(a_fp8, a_scale, b_fp8, b_scale, bias, out, M, N, K, lda, ldb, ldo,
+                       epilogue, residual, ldr, gate, row_amax, status, nullptr, stream);
+}
+
+extern "C" int srdit_fp8_gemm_tp(const void* a_fp8, const float* a_scale, const void* b_fp8,
+                                 const float* b_scale, const void* bias, void* out, int M, int N,
+                                 int K, int lda, int ldb, int ldo, int epilogue,
+                                 float* row_amax, const srdit_tp_gemm* tp, uint32_t* status,
+                                 cudaStream_t stream) {
+  if (!tp) return SRDIT_EINVAL;
+  if (epilogue == EPI_GATED_RES || epilogue == EPI_RES) return SRDIT_EINVAL;
+  return fp8_gemm_impl(a_fp8, a_scale, b_fp8, b_scale, bias, out, M, N, K, lda, ldb, ldo,
+                       epilogue, nullptr, 0, nullptr, row_amax, status, tp, stream);
+}
+
+extern "C" int srdit_fp8_gemm_ctas(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return gemm::grid_ctas(M, N, dev);
 }

@@ -114,6 +114,41 @@ SRDIT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
   }
 }
 
+// ---------------------------------------------------------------- cross-GPU flags
+// Monotonic uint32 counters in a rank's memory, written by its peers over
+// NVLink. A writer makes its data visible at system scope, then release-adds;
+// a reader acquire-loads until the counter reaches the expected value (compared
+// modulo 2^32, so counters may wrap).
+SRDIT_DEV void flag_add_release(uint32_t* flag, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+SRDIT_DEV uint32_t flag_load_acquire(const uint32_t* flag) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+  return v;
+}
+SRDIT_DEV bool flag_reached(const uint32_t* flag, uint32_t expected) {
+  return static_cast<int32_t>(flag_load_acquire(flag) - expected) >= 0;
+}
+// Bounded wait for flag >= expected. On timeout records kStatusTimeout and
+// returns false (the caller skips its work and exits; nothing hangs).
+SRDIT_DEV bool flag_wait(const uint32_t* flag, uint32_t expected, uint32_t* status) {
+  if (flag_reached(flag, expected)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(100);
+    if (flag_reached(flag, expected)) return true;
+    if (global_timer_ns() - t0 > kWaitBudgetNs) {
+      if (status) atomicOr(status, kStatusTimeout);
+      return false;
+    }
+  }
+}
+// Orders this thread's async-proxy (TMA) global accesses with its generic ones.
+SRDIT_DEV void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 SRDIT_DEV void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

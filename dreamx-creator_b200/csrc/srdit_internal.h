@@ -18,6 +18,7 @@ enum EpiKind : int {
   EPI_GELU = SRDIT_EPI_GELU,
   EPI_GATED_RES = SRDIT_EPI_GATED_RES,
   EPI_RES = SRDIT_EPI_RES,
+  EPI_PEER = SRDIT_EPI_PEER,
 };
 
 // Number of SMs of `dev` (cached).

@@ -205,3 +205,88 @@ def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom,
             int(anchor_mode), ctypes.byref(geom), ctypes.byref(tiling), _ptr(status),
             _stream(q.device), kind="winattn", work=flops)
     return out
+
+
+# --------------------------------------------------------------------------- tensor parallel
+def peer_ptrs(ptrs):
+    """ctypes table of per-rank device addresses (ints)."""
+    t = _lib.PeerPtrs()
+    for i, v in enumerate(ptrs):
+        t.p[i] = int(v)
+    return t
+
+
+def fp8_gemm_ctas(M, N):
+    return _lib.count("srdit_fp8_gemm_ctas", int(M), int(N))
+
+
+def fp8_gemm_tp(a_fp8, a_scale, w_fp8, w_scale, bias=None, out=None, *, tp, epilogue="store",
+                row_amax=None, status=None):
+    """srdit_fp8_gemm_tp: ``tp`` is a filled ``_lib.TpGemm``; epilogue "peer" stores the
+    partial into the owners' receive slots (``out`` unused)."""
+    _need_cuda(a_fp8, a_scale, w_fp8, w_scale, bias, out, row_amax)
+    M, K = a_fp8.shape
+    N = w_fp8.shape[0]
+    code = {"store": _lib.SRDIT_EPI_STORE, "gelu": _lib.SRDIT_EPI_GELU,
+            "peer": _lib.SRDIT_EPI_PEER}[epilogue]
+    ldo = _rows(out) if out is not None else 0
+    _launch("srdit_fp8_gemm_tp", _ptr(a_fp8), _ptr(a_scale), _ptr(w_fp8), _ptr(w_scale),
+            _ptr(bias), _ptr(out), M, N, K, _rows(a_fp8), _rows(w_fp8), ldo, code,
+            _ptr(row_amax), ctypes.byref(tp), _ptr(status), _stream(a_fp8.device),
+            kind="fp8_gemm", work=2 * M * N * K)
+    return out
+
+
+def residual_tp(x, parts, *, bias=None, gate=None, flags, expected, status=None):
+    """srdit_residual_tp over the receive buffer ``parts`` [S, M, N]."""
+    _need_cuda(x, parts, bias, gate)
+    S, M, N = parts.shape
+    _launch("srdit_residual_tp", _ptr(x), _rows(x), M, N, _ptr(parts), S, parts.stride(0),
+            parts.stride(1), _ptr(bias), _ptr(gate), ctypes.c_void_p(int(flags)),
+            int(expected) & 0xffffffff, _ptr(status), _stream(x.device), kind="residual",
+            work=M * N * 2 * (S + 2))
+    return x
+
+
+def tp_allreduce(t, op, *, slots, flags, rank, world, epoch, status=None):
+    """In-place all-reduce (op "sum" / "max") of a contiguous fp32 vector through peer memory."""
+    _need_cuda(t)
+    if t.dtype != torch.float32 or not t.is_contiguous():
+        raise _lib.SrditError("tp_allreduce takes a contiguous float32 vector")
+    code = {"sum": _lib.SRDIT_RED_SUM, "max": _lib.SRDIT_RED_MAX}[op]
+    _launch("srdit_tp_allreduce", _ptr(t), _ptr(t), t.numel(), code, ctypes.byref(slots),
+            ctypes.byref(flags), int(rank), int(world), int(epoch) & 0xffffffff, _ptr(status),
+            _stream(t.device), kind="allreduce", work=t.numel() * 4 * world)
+    return t
+
+
+def tp_push(src, dst, src2, dst2, *, flags, rank, world, stream=None):
+    """srdit_tp_push: copy-engine pushes of src (and src2) to every other rank's
+    dst / dst2 addresses (``peer_ptrs`` tables), then signal ``flags``."""
+    _need_cuda(src, src2)
+    st = ctypes.c_void_p((stream or torch.cuda.current_stream(src.device)).cuda_stream)
+    _lib.call("srdit_tp_push", _ptr(src), ctypes.byref(dst), src.numel() * src.element_size(),
+              _ptr(src2), ctypes.byref(dst2) if dst2 is not None else None,
+              (src2.numel() * src2.element_size()) if src2 is not None else 0,
+              ctypes.byref(flags), int(rank), int(world), st)
+    Stats.launches += 1
+
+
+def ipc_handle(t):
+    """(64-byte CUDA IPC handle, byte offset) of the allocation holding tensor ``t``."""
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_ulonglong(0)
+    _lib.call("srdit_ipc_handle", _ptr(t), h, ctypes.byref(off))
+    return bytes(h.raw), int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a peer's allocation; returns its base address in this process."""
+    buf = ctypes.create_string_buffer(handle, 64)
+    ptr = ctypes.c_void_p()
+    _lib.call("srdit_ipc_open", buf, ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def ipc_close(addr: int) -> None:
+    _lib.call("srdit_ipc_close", ctypes.c_void_p(addr))

@@ -68,6 +68,146 @@ class TPComm:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
 
 
+class PeerComm(TPComm):
+    """``TPComm`` plus symmetric peer buffers for the fused kernels.
+
+    Each rank allocates one region and maps every peer's region (CUDA IPC):
+
+      gather q [M, D] e4m3, gather s [M] fp32   all-gather target: each rank's LN
+                                               kernel writes its own rows, the
+                                               copy engines push them to the peers
+      rs  [P, M/P, D] bf16                     reduce-scatter receive slots, one per
+                                               source rank
+      ar  2 x [P, n_ar] fp32                   all-reduce receive areas (alternating
+                                               between calls)
+      flags 3 x [8] uint32                     counters (gather / rs / ar), one per
+                                               source rank
+
+    Counters only grow; ``expected`` values are tracked here, identically on
+    every rank, since all ranks issue the same kernels in the same order. The
+    buffers are sized on first use for a chunk of M tokens (a collective step:
+    every rank must reach it).
+
+    Reuse is safe with single buffers for gather and rs: a rank writes a peer's
+    gather rows (or rs slot) again only after it consumed that peer's next
+    contribution, which the peer produces only after it finished reading the
+    previous one. The all-reduce has no such step in between, hence two areas.
+    """
+
+    N_FLAG_SETS = 3   # gather, rs, ar
+
+    def __init__(self, group=None):
+        super().__init__(group)
+        self.key = None
+        self.region = None
+        self.peer_bases = []
+
+    def setup(self, M, D, device):
+        key = (M, D)
+        if self.key == key:
+            return
+        if self.key is not None:
+            raise _lib.SrditError("PeerComm buffers are sized for one chunk shape per model")
+        P = self.world
+        if M % P or (M // P) % 32:
+            raise _lib.SrditError(f"fused tensor parallelism needs M/P a multiple of 32 "
+                                  f"(M={M}, P={P})")
+        Ml = M // P
+        self.M, self.D, self.Ml = M, D, Ml
+        self.n_ar = 2 * M + 4096
+        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
+        sizes = [("gq", M * D), ("gs", 4 * M), ("rs", 2 * P * Ml * D),
+                 ("ar0", 4 * P * self.n_ar), ("ar1", 4 * P * self.n_ar),
+                 ("flags", 4 * 8 * self.N_FLAG_SETS)]
+        self.off = {}
+        total = 0
+        for name, n in sizes:
+            self.off[name] = total
+            total += al(n)
+        self.region = torch.zeros(total, dtype=torch.uint8, device=device)
+        handle, offset = ops.ipc_handle(self.region)
+        allh = [None] * P
+        dist.all_gather_object(allh, (handle, offset), group=self.group)
+        bases = []
+        for d, (h, o) in enumerate(allh):
+            if d == self.rank:
+                bases.append(self.region.data_ptr())
+            else:
+                mapped = ops.ipc_open(h)
+                self.peer_bases.append(mapped)
+                bases.append(mapped + o)
+        self.bases = bases
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)   # every region mapped and zeroed before first use
+        r = self.region
+        self.gq = r[self.off["gq"]:self.off["gq"] + M * D].view(torch.float8_e4m3fn).view(M, D)
+        self.gs = r[self.off["gs"]:self.off["gs"] + 4 * M].view(torch.float32)
+        self.rs = r[self.off["rs"]:self.off["rs"] + 2 * P * Ml * D].view(torch.bfloat16) \
+            .view(P, Ml, D)
+        addr = lambda name, extra=0: [b + self.off[name] + extra for b in bases]  # noqa: E731
+        self.t_ar = [ops.peer_ptrs(addr("ar0")), ops.peer_ptrs(addr("ar1"))]
+        self.t_flags = [ops.peer_ptrs(addr("flags", 32 * k)) for k in range(self.N_FLAG_SETS)]
+        self.my_flags = [bases[self.rank] + self.off["flags"] + 32 * k
+                         for k in range(self.N_FLAG_SETS)]
+        self.rs_slot_addrs = [b + self.off["rs"] + self.rank * Ml * D * 2 for b in bases]
+        # this rank's rows inside every rank's gather buffers (push targets)
+        self.t_gq_rows = ops.peer_ptrs(addr("gq", self.rank * Ml * D))
+        self.t_gs_rows = ops.peer_ptrs(addr("gs", self.rank * Ml * 4))
+        self.side = torch.cuda.Stream(device)
+        self.ev_ln = torch.cuda.Event()
+        self.ev_push = torch.cuda.Event()
+        self.ev_push.record(torch.cuda.current_stream(device))
+        self.n_rs = ops.fp8_gemm_ctas(M, D)
+        self.ag_uses = self.rs_uses = self.ar_calls = 0
+        self.key = key
+
+    # ---- fused steps
+    def gather_ln(self, x, eps, **ln):
+        """LN-modulate-quant of this rank's rows into its own gather rows, then the
+        copy engines push them to every other rank on a side stream (the next
+        GEMM starts on the local rows and waits per remote shard)."""
+        main = torch.cuda.current_stream(x.device)
+        main.wait_event(self.ev_push)     # the previous push has read these rows
+        r0, r1 = self.rank * self.Ml, (self.rank + 1) * self.Ml
+        ops.ln_mod_quant(x, eps, q=self.gq[r0:r1], qscale=self.gs[r0:r1], **ln)
+        self.ev_ln.record(main)
+        self.side.wait_event(self.ev_ln)
+        ops.tp_push(self.gq[r0:r1], self.t_gq_rows, self.gs[r0:r1], self.t_gs_rows,
+                    flags=self.t_flags[0], rank=self.rank, world=self.world, stream=self.side)
+        self.ev_push.record(self.side)
+        self.ag_uses += 1
+
+    def tp_gemm(self, *, peer=False):
+        """TpGemm table for a GEMM that reads the gather buffer (waits per remote
+        shard) or stores its partial into the owners' rs slots (peer=True)."""
+        t = _lib.TpGemm()
+        t.rows_per_rank, t.rank, t.world = self.Ml, self.rank, self.world
+        if peer:
+            t.ag_flags = None
+            for d in range(self.world):
+                t.rs_slot[d] = self.rs_slot_addrs[d]
+                t.rs_flags[d] = self.t_flags[1].p[d]
+            t.ld_rs = self.D
+            self.rs_uses += 1
+        else:
+            t.ag_flags = self.my_flags[0]
+            t.ag_expected = self.ag_uses & 0xffffffff   # one push signal per use
+        return t
+
+    def rs_expected(self):
+        return (self.rs_uses * self.n_rs) & 0xffffffff
+
+    def allreduce(self, t, op, status=None):
+        self.ar_calls += 1
+        ops.tp_allreduce(t, op, slots=self.t_ar[self.ar_calls & 1], flags=self.t_flags[2],
+                         rank=self.rank, world=self.world, epoch=self.ar_calls, status=status)
+
+    def close(self):
+        for b in self.peer_bases:
+            ops.ipc_close(b)
+        self.peer_bases = []
+
+
 class _TPLayer:
     """One block's weights for rank r of P."""
 
@@ -121,8 +261,14 @@ class TPSRDiT(SRDiT):
     returns the full refined latent. The K/V ring holds this rank's heads.
     """
 
-    def __init__(self, cfg: SRDiTConfig, sd: dict, device="cuda", comm: TPComm | None = None):
-        self.comm = comm if comm is not None else TPComm()
+    def __init__(self, cfg: SRDiTConfig, sd: dict, device="cuda", comm: TPComm | None = None,
+                 fused: bool = True):
+        """``fused``: collectives fused into the kernels over peer memory
+        (``PeerComm``); False: the same sharding with library (NCCL) collectives."""
+        if comm is None:
+            comm = PeerComm() if fused else TPComm()
+        self.comm = comm
+        self.fused = isinstance(comm, PeerComm)
         P = self.comm.world
         if cfg.num_heads % P or cfg.ffn_dim % P:
             raise _lib.SrditError(f"{P} ranks must divide the {cfg.num_heads} heads and the "
@@ -142,6 +288,11 @@ class TPSRDiT(SRDiT):
                       anchor_kv=None, anchor_align="frame", return_kv=False, ctx_emb=None):
         """``SRDiT.forward_chunk`` on this rank's shard; same arguments and result
         (``anchor_kv`` / the returned K/V hold this rank's heads)."""
+        if self.fused:
+            return self._forward_fused(latent, t, context, cache=cache, t_offset=t_offset,
+                                       update_cache=update_cache, anchor_kv=anchor_kv,
+                                       anchor_align=anchor_align, return_kv=return_kv,
+                                       ctx_emb=ctx_emb)
         c = self.cfg
         P, r = self.world, self.rank
         comm = self.comm
@@ -244,6 +395,117 @@ class TPSRDiT(SRDiT):
             ops.fp8_gemm(hq, hs, ly.w_f2, ly.s_f2, None, part)
             comm.reduce_scatter(y_l, part)
             ops.residual(x, y_l, bias=ly.b_f2, gate=em[5])
+        if update_cache:
+            cache.commit(f)
+        xg = b("tp_xg", (M, D), bf16)
+        comm.all_gather(xg, x)
+        out = self.head(xg, e, grid)
+        return (out, kv_out) if return_kv else out
+
+    def _forward_fused(self, latent, t, context, *, cache, t_offset, update_cache, anchor_kv,
+                       anchor_align, return_kv, ctx_emb):
+        """The sharded block with its collectives fused into the kernels: each
+        rank's LN-quant rows are pushed by the copy engines into every rank's
+        gather buffer and the next GEMM waits per remote shard (all-gather);
+        row-parallel GEMMs store their bf16 partials into the owners' receive
+        slots tile by tile and the owner's residual kernel waits and sums
+        (reduce-scatter); per-token statistics go through the one-block peer
+        all-reduce."""
+        c = self.cfg
+        P, r = self.world, self.rank
+        comm = self.comm
+        D, Dl, Fl = c.dim, c.dim // P, c.ffn_dim // P
+        Hl = c.num_heads // P
+        S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, Hl, Dl)
+        x_full, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
+        f, h, w = grid
+        L, M, Lc = S.L, S.M, S.Lc
+        comm.setup(M, D, self.device)
+        Ml = comm.Ml
+        x = x_full[r * Ml:(r + 1) * Ml].contiguous()
+        dev = self.device
+        bf16, f32, f8 = torch.bfloat16, torch.float32, torch.float8_e4m3fn
+        b = self._buf
+        xq, xs = comm.gq, comm.gs
+        qkv = b("tp_qkv", (M, 3 * Dl), bf16)
+        qb = b("tp_q", (M, Dl), bf16)
+        att = b("tp_att", (M, Dl), bf16)
+        aq, as_ = b("tp_aq", (M, Dl), f8), b("tp_as", (M,), f32)
+        ss = b("tp_ss", (2 * M,), f32)
+        ssc = b("tp_ssc", (M + Lc,), f32)
+        am = b("tp_am", (M,), f32)
+        hbuf = b("tp_h", (M, Fl), bf16)
+        hq, hs = b("tp_hq", (M, Fl), f8), b("tp_hs", (M,), f32)
+        ckv = b("tp_ckv", (Lc, 2 * Dl), bf16)
+        ctxq, ctxs = ops.quant_rowwise(ctx)
+        mods = torch.stack([ly.modulation for ly in self.layers]) + e0[None]
+        kv_out = [] if return_kv else None
+        st = self.status
+        cos, sin = self.rope_cos, self.rope_sin
+        slot_cur = S.slot_cur
+        rs_flags = comm.my_flags[1]
+
+        def rowpar_residual(a_bf16, w_q, w_s, bias, gate):
+            ops.row_reduce(a_bf16, "absmax", out=am)
+            comm.allreduce(am, "max", st)
+            ops.quant_rowwise(a_bf16, amax=am, q=aq, scale=as_)
+            ops.fp8_gemm_tp(aq, as_, w_q, w_s, None, None, tp=comm.tp_gemm(peer=True),
+                            epilogue="peer", status=st)
+            ops.residual_tp(x, comm.rs, bias=bias, gate=gate, flags=rs_flags,
+                            expected=comm.rs_expected(), status=st)
+
+        for li, ly in enumerate(self.layers):
+            em = mods[li]
+            kr, vr = cache.k[li], cache.v[li]
+            # --- self attention
+            comm.gather_ln(x, c.eps, shift=em[0], scale=em[1])
+            ops.fp8_gemm_tp(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv, tp=comm.tp_gemm(),
+                            status=st)
+            ops.row_reduce(qkv[:, :Dl], "sumsq", out=ss[:M])
+            ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
+            comm.allreduce(ss, "sum", st)
+            ops.rms_rope(qkv[:, :Dl], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
+                         grid_h=h, grid_w=w, t_offset=t_offset, ss=ss[:M], norm_width=D)
+            ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
+                         n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
+                         t_offset=t_offset, v_src=qkv[:, 2 * Dl:], v_dst=vr, ss=ss[M:],
+                         norm_width=D)
+            ak = av = None
+            if anchor_kv is not None:
+                ak, av = anchor_kv[li]
+            ops.winattn(qb, kr, vr, att, params_dev=S.params_dev, n_w=S.n_w,
+                        p_stride=int(S.plan["p_stride"]), anchor_mode=S.amode, geom=S.geom,
+                        tiling=S.tiling, k_anchor=ak, v_anchor=av, status=st, flops=S.flops)
+            if return_kv:
+                idx = (torch.arange(f, device=dev) + slot_cur) % cache.cap
+                kv_out.append((kr.view(cache.cap, L, Dl)[idx].reshape(M, Dl).clone(),
+                               vr.view(cache.cap, L, Dl)[idx].reshape(M, Dl).clone()))
+            rowpar_residual(att, ly.w_o, ly.s_o, ly.b_o, em[2])
+            # --- cross attention
+            comm.gather_ln(x, c.eps, ln_weight=ly.n3w, ln_bias=ly.n3b)
+            ops.fp8_gemm_tp(xq, xs, ly.w_cq, ly.s_cq, ly.b_cq, qb, tp=comm.tp_gemm(), status=st)
+            ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
+            ops.row_reduce(qb, "sumsq", out=ssc[:M])
+            ops.row_reduce(ckv[:, :Dl], "sumsq", out=ssc[M:])
+            comm.allreduce(ssc, "sum", st)
+            ops.rms_rope(qb, ly.cnq, c.eps, qb, frame_tokens=M, ss=ssc[:M], norm_width=D)
+            ops.rms_rope(ckv[:, :Dl], ly.cnk, c.eps, ckv[:, :Dl], frame_tokens=Lc,
+                         ss=ssc[M:], norm_width=D)
+            ops.winattn(qb, ckv[:, :Dl], ckv[:, Dl:], att, params_dev=S.cp_params,
+                        n_w=S.cp_nw, p_stride=19, anchor_mode=0, geom=S.cgeom,
+                        tiling=S.cp_tiling, status=st, flops=S.cross_flops)
+            rowpar_residual(att, ly.w_co, ly.s_co, ly.b_co, None)
+            # --- FFN
+            comm.gather_ln(x, c.eps, shift=em[3], scale=em[4])
+            am.zero_()
+            ops.fp8_gemm_tp(xq, xs, ly.w_f0, ly.s_f0, ly.b_f0, hbuf, tp=comm.tp_gemm(),
+                            epilogue="gelu", row_amax=am, status=st)
+            comm.allreduce(am, "max", st)
+            ops.quant_rowwise(hbuf, amax=am, q=hq, scale=hs)
+            ops.fp8_gemm_tp(hq, hs, ly.w_f2, ly.s_f2, None, None, tp=comm.tp_gemm(peer=True),
+                            epilogue="peer", status=st)
+            ops.residual_tp(x, comm.rs, bias=ly.b_f2, gate=em[5], flags=rs_flags,
+                            expected=comm.rs_expected(), status=st)
         if update_cache:
             cache.commit(f)
         xg = b("tp_xg", (M, D), bf16)

@@ -40,6 +40,17 @@ extern "C" {
 #define SRDIT_EPI_GELU 1      /* out = bf16(gelu_tanh(bf16(y))), row_amax[m] = max|out| */
 #define SRDIT_EPI_GATED_RES 2 /* out = bf16(res + bf16(y) * gate[n])   (fp32 math)    */
 #define SRDIT_EPI_RES 3       /* out = bf16(res + bf16(y))                            */
+#define SRDIT_EPI_PEER 4      /* bf16(acc*sa*sb) stored into the row owner's peer slot */
+
+/* tensor parallelism: at most this many ranks; a table of per-rank device pointers
+ * (this process's mapping of each rank's buffer) */
+#define SRDIT_MAX_RANKS 8
+typedef struct srdit_peer_ptrs {
+  void* p[SRDIT_MAX_RANKS];
+} srdit_peer_ptrs;
+
+#define SRDIT_RED_SUM 0
+#define SRDIT_RED_MAX 1
 
 /* window-attention params-row layouts and anchor modes
  * (video_refiner/wan/modules/sr_dit/blockgrid_triton.py:77-80) */
@@ -69,6 +80,49 @@ int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const void* b_fp8,
                    const float* b_scale, const void* bias, void* out, int M, int N, int K,
                    int lda, int ldb, int ldo, int epilogue, const void* residual, int ldr,
                    const float* gate, float* row_amax, uint32_t* status, cudaStream_t stream);
+
+/*
+ * Tensor-parallel form of srdit_fp8_gemm (M = world * rows_per_rank rows).
+ *  - ag_flags (optional): this rank's all-gather counters [world]; the rows of
+ *    A (and a_scale) owned by another rank s are complete once ag_flags[s]
+ *    reaches ag_expected (this rank's own rows are ordered by the stream).
+ *    The kernel waits for each owner before loading its rows, starting with
+ *    this rank's own shard, so the peers' transfers overlap the local tiles'
+ *    math. This fuses the all-gather before a column-parallel Linear (QKV,
+ *    cross q, ffn.0) into its GEMM.
+ *  - epilogue SRDIT_EPI_PEER (row-parallel o / cross o / ffn.2): the bf16
+ *    partial bf16(acc * sa * sb) of output rows owned by rank d is stored into
+ *    rs_slot[d] ([rows_per_rank, N], row stride ld_rs: rank d's receive slot
+ *    for this rank), tile by tile as the math finishes; when a CTA's stores
+ *    have landed it adds 1 to rs_flags[d][rank] on every rank d. This fuses the
+ *    reduce-scatter after a row-parallel Linear into its GEMM; the owner then
+ *    sums the slots (srdit_residual_tp). out / ldo are unused. rows_per_rank
+ *    must be a multiple of 32.
+ *  - other epilogues (SRDIT_EPI_STORE, SRDIT_EPI_GELU) write `out` locally.
+ * Every wait is bounded: a wait that runs out sets SRDIT_STATUS_TIMEOUT.
+ * Replaces: the DTensor all_gather of WanLayerNorm
+ *   (video_refiner/wan/modules/sr_dit/models.py:455-496) and the unfused
+ *   collectives around a sharded Fp8Linear (fp8_linear.py:282-297).
+ */
+typedef struct srdit_tp_gemm {
+  const uint32_t* ag_flags;
+  uint32_t ag_expected;
+  int rows_per_rank;
+  int rank, world;
+  void* rs_slot[SRDIT_MAX_RANKS];
+  long long ld_rs;
+  uint32_t* rs_flags[SRDIT_MAX_RANKS];
+} srdit_tp_gemm;
+
+int srdit_fp8_gemm_tp(const void* a_fp8, const float* a_scale, const void* b_fp8,
+                      const float* b_scale, const void* bias, void* out, int M, int N, int K,
+                      int lda, int ldb, int ldo, int epilogue, float* row_amax,
+                      const srdit_tp_gemm* tp, uint32_t* status, cudaStream_t stream);
+
+/* CTAs of one srdit_fp8_gemm / srdit_fp8_gemm_tp launch for an M x N output
+ * (the number of SRDIT_EPI_PEER signals each rank receives per launch from
+ * each rank). */
+int srdit_fp8_gemm_ctas(int M, int N);
 
 /*
  * Per-row e4m3 quantisation of a bf16 [M, K] matrix (row stride ldx elements):
@@ -145,6 +199,60 @@ int srdit_row_reduce(const void* x, long long ldx, int M, int K, int op, float* 
 int srdit_residual(void* x, long long ldx, int M, int N, const void* parts, int n_parts,
                    long long part_stride, long long ld_part, const void* bias,
                    const float* gate, cudaStream_t stream);
+
+/*
+ * srdit_residual over the parts a row-parallel srdit_fp8_gemm_tp delivered:
+ * parts = this rank's receive buffer ([n_parts slots of M x N]); each thread
+ * block first waits until flags[s] >= expected for every s < n_parts (bounded;
+ * on timeout it sets SRDIT_STATUS_TIMEOUT in *status and skips its rows).
+ */
+int srdit_residual_tp(void* x, long long ldx, int M, int N, const void* parts, int n_parts,
+                      long long part_stride, long long ld_part, const void* bias,
+                      const float* gate, const uint32_t* flags, uint32_t expected,
+                      uint32_t* status, cudaStream_t stream);
+
+/*
+ * out[i] = sum (SRDIT_RED_SUM) or max (SRDIT_RED_MAX) over ranks of in[i], n
+ * fp32 values, through the peers' memory: slots.p[d] is rank d's receive area
+ * (world * n floats, slot s at s * n), flags.p[d] its counters [world]. Every
+ * rank stores its vector into slot `rank` of every rank, adds 1 to
+ * flags.p[d][rank], waits until all its counters reach `epoch` (the number of
+ * calls on these flags so far, this one included, the same on every rank),
+ * then reduces the slots in rank order, so all ranks get identical results.
+ * in and out may alias. Alternate two receive areas between consecutive calls
+ * (a fast rank may store call k + 1 while a slow one still reads call k).
+ * Replaces: the library all-reduce of per-token statistics a sharded
+ *   RMSNorm / fp8 quantiser needs (models.py:437-440, fp8_linear.py:96-97).
+ */
+int srdit_tp_allreduce(const float* in, float* out, int n, int op, const srdit_peer_ptrs* slots,
+                       const srdit_peer_ptrs* flags, int rank, int world, uint32_t epoch,
+                       uint32_t* status, cudaStream_t stream);
+
+/*
+ * All-gather push by the copy engines: copies `bytes` from src to dst.p[d]
+ * (and, when src2 is given, `bytes2` from src2 to dst2.p[d]) for every rank
+ * d != rank, one cudaMemcpyAsync each over NVLink, then a one-thread kernel on
+ * the same stream adds 1 to flags.p[d][rank] on every other rank. Issued on a
+ * side stream after the local rows are written, it overlaps the consuming
+ * GEMM's local-shard tiles (srdit_fp8_gemm_tp waits for each remote shard's
+ * counter).
+ * Replaces: the all_gather of a feature-sharded activation
+ *   (models.py:479-481).
+ */
+int srdit_tp_push(const void* src, const srdit_peer_ptrs* dst, unsigned long long bytes,
+                  const void* src2, const srdit_peer_ptrs* dst2, unsigned long long bytes2,
+                  const srdit_peer_ptrs* flags, int rank, int world, cudaStream_t stream);
+
+/*
+ * Sharing a rank's buffer with the other ranks' processes (CUDA IPC).
+ * srdit_ipc_handle: the 64-byte IPC handle of the allocation holding dev_ptr
+ * and dev_ptr's byte offset inside it. srdit_ipc_open maps a peer's handle
+ * into this process (the mapped allocation base; add the offset);
+ * srdit_ipc_close unmaps it. Neither allocates device memory.
+ */
+int srdit_ipc_handle(const void* dev_ptr, void* handle, unsigned long long* offset);
+int srdit_ipc_open(const void* handle, void** dev_ptr);
+int srdit_ipc_close(void* dev_ptr);
 
 /* Token grids, strides and frame slots of one window-attention launch. */
 typedef struct srdit_winattn_geom {

@@ -1,6 +1,8 @@
 """Tensor-parallel forward (TP=2, NCCL over NVLink) against the single-GPU forward.
 
-Two spawned ranks run the sharded model on one clip: a cache-refresh forward,
+Two spawned ranks run the sharded model on one clip -- with the collectives
+fused into the kernels over peer memory, and with NCCL collectives -- a
+cache-refresh forward,
 then a streaming forward over the ring it filled. Rank 0 also runs the same
 seeded weights unsharded (``SRDiT``, which the other GPU tests pin to the CPU
 oracle) and compares both outputs. What differs between the two is only the
@@ -28,7 +30,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cfg_kw, grid, out_q):
+def _worker(rank, world, port, cfg_kw, grid, fused, out_q):
     import datetime
     sys.path.insert(0, str(ROOT))
     import torch.distributed as dist
@@ -55,7 +57,7 @@ def _worker(rank, world, port, cfg_kw, grid, out_q):
             model.check_status()
             return a.float().cpu(), b.float().cpu()
 
-        tp_out = run(T.TPSRDiT.random_init(cfg, dev, seed=3))
+        tp_out = run(T.TPSRDiT.random_init(cfg, dev, seed=3, fused=fused))
         res = None
         if rank == 0:
             ref_out = run(M.SRDiT.random_init(cfg, dev, seed=3))
@@ -71,11 +73,11 @@ def _worker(rank, world, port, cfg_kw, grid, out_q):
         out_q.put((rank, None, f"{type(e).__name__}: {e}"))
 
 
-def _run_tp(world, cfg_kw, grid):
+def _run_tp(world, cfg_kw, grid, fused):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_kw, grid, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_kw, grid, fused, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -95,11 +97,12 @@ def _run_tp(world, cfg_kw, grid):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("fused", [True, False], ids=["peer-fused", "nccl"])
 @pytest.mark.parametrize("cfg_kw,grid", [
     (dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16, text_dim=64,
-          text_len=16, block_hw=(2, 2), block_radius_hw=(1, 1)), (3, 8, 12)),
+          text_len=16, block_hw=(2, 2), block_radius_hw=(1, 1)), (3, 8, 16)),
     (dict(num_layers=2, block_hw=(8, 8), block_radius_hw=(0, 0)), (3, 36, 64)),
 ], ids=["small", "2K-2layers"])
-def test_tp2_matches_single_gpu(cfg_kw, grid):
-    cos = _run_tp(2, cfg_kw, grid)
+def test_tp2_matches_single_gpu(cfg_kw, grid, fused):
+    cos = _run_tp(2, cfg_kw, grid, fused)
     assert min(cos) >= 0.999, cos
