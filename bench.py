@@ -362,8 +362,10 @@ def run_gpu_arm(args, rank, world, local):
             barrier()
             torch.cuda.nvtx.range_push("srdit_step")
             e0.record()
+            h0 = time.perf_counter()
             for _ in range(args.steps):
                 one_step(noisy)
+            host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # issuing only
             e1.record()
             torch.cuda.nvtx.range_pop()
             barrier()
@@ -437,6 +439,7 @@ def run_gpu_arm(args, rank, world, local):
                 "h2d_bytes_per_step": noisy_host.numel() * 2 + ctx_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2},
         "gpu_launches": launches,
+        "host_ms_per_step": host_ms,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
