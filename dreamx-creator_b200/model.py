@@ -155,10 +155,19 @@ class KVRing:
 
 
 class SRDiT:
-    """The refiner transformer on the B200 kernels (inference only)."""
+    """The refiner transformer on the B200 kernels (inference only).
+
+    ``ops`` is the table of kernel launchers the forward calls (the
+    libsrdit_b200.so wrappers). A test may substitute a table of its own on a
+    subclass to exercise the host-side orchestration without a GPU; the model
+    itself has no other compute path and refuses to build without CUDA.
+    """
+
+    ops = ops
+    require_cuda = True
 
     def __init__(self, cfg: SRDiTConfig, sd: dict, device="cuda"):
-        if not torch.cuda.is_available():
+        if self.require_cuda and not torch.cuda.is_available():
             raise _lib.SrditError("SRDiT needs a CUDA device (there is no CPU path)")
         self.cfg = cfg
         self.device = torch.device(device)
@@ -409,6 +418,7 @@ class SRDiT:
         Returns the refined prediction [C_out, f, H, W] bf16 (and the K/V list).
         """
         c = self.cfg
+        ops = self.ops
         S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb,
                         c.num_heads, c.dim)
         x, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache

@@ -294,6 +294,7 @@ class TPSRDiT(SRDiT):
                                        anchor_align=anchor_align, return_kv=return_kv,
                                        ctx_emb=ctx_emb)
         c = self.cfg
+        ops = self.ops
         P, r = self.world, self.rank
         comm = self.comm
         D, Dl, Fl = c.dim, c.dim // P, c.ffn_dim // P
@@ -412,6 +413,7 @@ class TPSRDiT(SRDiT):
         (reduce-scatter); per-token statistics go through the one-block peer
         all-reduce."""
         c = self.cfg
+        ops = self.ops
         P, r = self.world, self.rank
         comm = self.comm
         D, Dl, Fl = c.dim, c.dim // P, c.ffn_dim // P
