@@ -60,6 +60,9 @@ def parse():
                     help="N > 1: tensor parallelism over one clip (strong scaling, the "
                          "reference's DTensor-style TP) or one clip per GPU (weak scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="issue every kernel from Python instead of replaying the step's "
+                         "CUDA graph")
     ap.add_argument("--micro", default=None, choices=["gemm", "attn", "quant", "ln", "rope"],
                     help="time one kernel in isolation instead of the model step")
     ap.add_argument("--shape", default=None,
@@ -327,7 +330,7 @@ def run_gpu_arm(args, rank, world, local):
     out_host = torch.empty(*LAT_SHAPE, dtype=torch.bfloat16).pin_memory()
     ctx = ctx_host.to(dev)
     noisy = noisy_host.to(dev)
-    stream = pipe_mod.RefinerStream(model, ctx)
+    stream = pipe_mod.RefinerStream(model, ctx, graphs=not args.no_graphs)
     # prefill: the previous chunk's refresh forward leaves a 3-frame cache
     stream.step(prefix_host.to(dev))
     ring = stream.cache
@@ -369,13 +372,17 @@ def run_gpu_arm(args, rank, world, local):
             e1.record()
             torch.cuda.nvtx.range_pop()
             barrier()
-        launches = ops.Stats.launches - l0
+        replayed = ops.Stats.launches - l0   # 0 when the steps replay a graph
         dev_ms = max_over_ranks(e0.elapsed_time(e1))
         model.check_status()
         # ---- attribution pass (outside the timed region): one more step with CUDA
         # events around every launch on the launching stream
         ops.Stats.events = []
+        graphs, stream.graphs = stream.graphs, False
+        l1 = ops.Stats.launches
         one_step(noisy)
+        launches_per_step = ops.Stats.launches - l1
+        stream.graphs = graphs
         torch.cuda.synchronize()
         kinds = {}
         for kind, a, b, work in ops.Stats.events:
@@ -390,14 +397,14 @@ def run_gpu_arm(args, rank, world, local):
         s0.record()
         for _ in range(args.steps):
             c = ctx_host.to(dev, non_blocking=True)
-            stream.context = c
+            stream.set_context(c)
             x = noisy_host.to(dev, non_blocking=True)
             y = one_step(x)
             out_host.copy_(y, non_blocking=True)
         s1.record()
         barrier()
         e2e_ms = max_over_ranks(s0.elapsed_time(s1))
-        stream.context = ctx
+        stream.set_context(ctx)
 
     if rank != 0:
         return
@@ -438,7 +445,8 @@ def run_gpu_arm(args, rank, world, local):
         "e2e": {"value": e2e_val, "unit": UNIT,
                 "h2d_bytes_per_step": noisy_host.numel() * 2 + ctx_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2},
-        "gpu_launches": launches,
+        "gpu_launches": launches_per_step * args.steps,
+        "cuda_graph": stream.graphs and replayed == 0,
         "host_ms_per_step": host_ms,
         "clocks": clk.summary(),
     }

@@ -66,7 +66,7 @@ SIGNATURES = {
                            c_ll, c_vp, c_vp],
     "srdit_rms_rope": [c_vp, c_ll, c_int, c_int, c_vp, c_float, c_vp, c_ll, c_int, c_int,
                        c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_ll,
-                       c_vp, c_int, c_vp],
+                       c_vp, c_int, c_vp, c_vp],
     "srdit_row_reduce": [c_vp, c_ll, c_int, c_int, c_int, c_vp, c_vp],
     "srdit_fp8_gemm_tp": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                           c_int, c_int, c_vp, ctypes.POINTER(TpGemm), c_vp, c_vp],

@@ -401,6 +401,8 @@ struct RopeArgs {
   const double* cos_tab;  // [rows, 64] fp64: table columns for the (t | h | w) axes
   const double* sin_tab;
   int grid_h, grid_w, t_offset;
+  const int* t_offset_dev;  // optional: added to t_offset (a graph replays read it live)
+  int tab_rows;
   float eps;
   const float* ss_in;  // optional per-row sum of squares over norm_width columns
   int norm_width;      // columns the RMS mean is taken over
@@ -466,7 +468,9 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
   // needs only these 4 rotations per row.
   double cr[4], si[4];
   if (a.cos_tab) {
-    const int pos_t = a.t_offset + f;
+    // temporal position, kept inside the table (the host checks the range it knows)
+    const int pos_t =
+        min(a.t_offset + (a.t_offset_dev ? __ldg(a.t_offset_dev) : 0) + f, a.tab_rows - 1);
     const int pos_h = sp / a.grid_w, pos_w = sp % a.grid_w;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
@@ -608,7 +612,7 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
                               int t_offset,
                               const void* v_src, long long ld_vsrc, void* v_dst,
                               long long ld_vdst, const float* ss_in, int norm_width,
-                              cudaStream_t stream) {
+                              const int* t_offset_dev, cudaStream_t stream) {
   if (M == 0) return 0;
   if (!src || !weight || !dst || M < 0 || frame_tokens <= 0 || n_slots <= 0 || slot0 < 0)
     return SRDIT_EINVAL;
@@ -642,6 +646,8 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
   a.grid_h = grid_h;
   a.grid_w = grid_w;
   a.t_offset = t_offset;
+  a.t_offset_dev = t_offset_dev;
+  a.tab_rows = tab_rows;
   a.eps = eps;
   a.ss_in = ss_in;
   a.norm_width = ss_in ? norm_width : K;

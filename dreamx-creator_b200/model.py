@@ -192,7 +192,12 @@ class SRDiT:
         self.rope_cos, self.rope_sin = rope_tables(self.head_dim, cfg.rope_rows, cfg.rope_theta, dev)
         self._bufs = {}
         self._cross_plans = {}
+        self._temb = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.t_offset_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        # True while a caller captures forwards into a CUDA graph: the caller then
+        # sets t_offset_dev itself before every replay
+        self.graph_capture = False
 
     # ------------------------------------------------------------------ construction
     @staticmethod
@@ -318,18 +323,37 @@ class SRDiT:
                                        self.patch_b, stride=c.patch_size)
         f, h, w = x.shape[2:]
         x = x.flatten(2).transpose(1, 2)[0].contiguous()
-        tt = torch.as_tensor([float(t)], device=self.device)
-        e = sinusoidal_embedding_1d(c.freq_dim, tt).float()
-        e = torch.nn.functional.linear(e, *self.tim[0])
-        e = torch.nn.functional.linear(torch.nn.functional.silu(e), *self.tim[1])
-        e0 = torch.nn.functional.linear(torch.nn.functional.silu(e), *self.tproj).view(6, c.dim)
+        e0, e = self._time_embedding(t)
         ctx = context.to(self.device, torch.bfloat16)
         if ctx.shape[0] < c.text_len:
             ctx = torch.cat([ctx, ctx.new_zeros(c.text_len - ctx.shape[0], ctx.shape[1])])
         ctx = torch.nn.functional.linear(ctx, *self.txt[0])
         ctx = torch.nn.functional.gelu(ctx, approximate="tanh")
         ctx = torch.nn.functional.linear(ctx, *self.txt[1]).contiguous()
-        return x, e0.contiguous(), e[0], ctx, (int(f), int(h), int(w))
+        return x, e0, e, ctx, (int(f), int(h), int(w))
+
+    def _time_embedding(self, t):
+        """(e0 [6, D], e [D]) fp32 for timestep t, computed once per t value (the
+        refiner uses two: denoise and refresh), so a forward issues no host-to-
+        device copy and can be captured in a CUDA graph."""
+        key = float(t)
+        hit = self._temb.get(key)
+        if hit is None:
+            c = self.cfg
+            tt = torch.as_tensor([key], device=self.device)
+            e = sinusoidal_embedding_1d(c.freq_dim, tt).float()
+            e = torch.nn.functional.linear(e, *self.tim[0])
+            e = torch.nn.functional.linear(torch.nn.functional.silu(e), *self.tim[1])
+            e0 = torch.nn.functional.linear(torch.nn.functional.silu(e), *self.tproj)
+            hit = self._temb[key] = (e0.view(6, c.dim).contiguous(), e[0].contiguous())
+        return hit
+
+    def set_t_offset(self, t_offset):
+        """The temporal RoPE position of the chunk's first frame, in device memory
+        (read by the kernels when they run)."""
+        if t_offset < 0 or t_offset + self.cfg.chunk_frames > self.cfg.rope_rows:
+            raise _lib.SrditError(f"temporal position {t_offset} outside the RoPE table")
+        self.t_offset_dev.fill_(int(t_offset))
 
     def head(self, x, e, grid):
         """Head (models.py:1357-1384, fp32 as under autocast) + unpatchify (:2234-2257)."""
@@ -419,6 +443,8 @@ class SRDiT:
         """
         c = self.cfg
         ops = self.ops
+        if not self.graph_capture:
+            self.set_t_offset(t_offset)
         S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb,
                         c.num_heads, c.dim)
         x, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
@@ -452,10 +478,10 @@ class SRDiT:
             ops.ln_mod_quant(x, c.eps, shift=em[0], scale=em[1], q=xq, qscale=xs)
             ops.fp8_gemm(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv)
             ops.rms_rope(qkv[:, :D], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
-                         grid_h=h, grid_w=w, t_offset=t_offset)
+                         grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev)
             ops.rms_rope(qkv[:, D:2 * D], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset=t_offset, v_src=qkv[:, 2 * D:], v_dst=vr)
+                         t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * D:], v_dst=vr)
             ak = av = None
             if anchor_kv is not None:
                 ak, av = anchor_kv[li]

@@ -19,17 +19,41 @@ from .model import KVRing, SRDiT
 
 
 class RefinerStream:
+    """Per-chunk refinement over a rolling KV cache.
+
+    ``graphs=True`` replays each step from a CUDA graph: a step is keyed by the
+    ring phase (slot of the oldest cached frame, cached frames) and the chunk
+    shape; the first visit of a key runs eagerly (it also warms up lazily built
+    state), the second captures the two forwards and the flow->x0 update, and
+    later visits replay them. The temporal RoPE position is device-resident
+    (``SRDiT.set_t_offset``), so one graph serves every chunk with the same ring
+    phase -- in the steady state the phases repeat every (kv_len + chunk) /
+    chunk chunks. Steps with an LQ anchor run eagerly.
+    """
+
     def __init__(self, model: SRDiT, context: torch.Tensor, *, denoise_t: float = 625.0,
                  context_noise: float = 0.0, num_train_timesteps: int = 1000,
-                 frame_tokens: int | None = None):
+                 frame_tokens: int | None = None, graphs: bool = False):
         self.model = model
-        self.context = context
         self.denoise_t = float(denoise_t)
         self.context_noise = float(context_noise)
         self.ntt = num_train_timesteps
         self.cache: KVRing | None = None
         self.t_offset = 0
         self._frame_tokens = frame_tokens
+        self.graphs = graphs
+        self._graphs = {}
+        self._seen = set()
+        self.context = context.clone()   # static: graph replays read this buffer
+
+    def set_context(self, context: torch.Tensor):
+        """Replace the text context (copied into the step's static buffer)."""
+        if context.shape != self.context.shape:
+            self.context = context.clone()
+            self._graphs.clear()
+            self._seen.clear()
+        else:
+            self.context.copy_(context)
 
     def reset(self):
         self.cache = None
@@ -52,14 +76,15 @@ class RefinerStream:
                     vs[li].append(v)
         return [(torch.cat(k), torch.cat(v)) for k, v in zip(ks, vs)]
 
-    def step(self, noisy_chunk: torch.Tensor, lq_chunk: torch.Tensor | None = None,
-             anchor_harvest_t: float = 0.0):
-        """Refine one chunk [C, f, H, W] (device, bf16); returns x0 [C, f, H, W] bf16."""
-        m = self.model
+    def _ensure_cache(self, noisy_chunk):
         if self.cache is None:
+            m = self.model
             ph, pw = m.cfg.patch_size[1], m.cfg.patch_size[2]
             L = (noisy_chunk.shape[2] // ph) * (noisy_chunk.shape[3] // pw)
             self.cache = m.new_cache(L)
+
+    def _step_eager(self, noisy_chunk, lq_chunk=None, anchor_harvest_t=0.0):
+        m = self.model
         anchor = self.harvest_anchor(lq_chunk, anchor_harvest_t) if lq_chunk is not None else None
         flow = m.forward_chunk(noisy_chunk, self.denoise_t, self.context, cache=self.cache,
                                t_offset=self.t_offset, anchor_kv=anchor)
@@ -69,3 +94,42 @@ class RefinerStream:
                         t_offset=self.t_offset, update_cache=True)
         self.t_offset += noisy_chunk.shape[1]
         return x0
+
+    def _capture(self, key, noisy_chunk):
+        m = self.model
+        inp = noisy_chunk.clone()
+        saved = (self.cache.start, self.cache.frames, self.t_offset)
+        graph = torch.cuda.CUDAGraph()
+        m.graph_capture = True
+        try:
+            torch.cuda.synchronize(noisy_chunk.device)
+            with torch.cuda.graph(graph):
+                out = self._step_eager(inp)
+        finally:
+            m.graph_capture = False
+            self.cache.start, self.cache.frames, self.t_offset = saved
+        self._graphs[key] = (graph, inp, out)
+        return self._graphs[key]
+
+    def step(self, noisy_chunk: torch.Tensor, lq_chunk: torch.Tensor | None = None,
+             anchor_harvest_t: float = 0.0):
+        """Refine one chunk [C, f, H, W] (device, bf16); returns x0 [C, f, H, W] bf16
+        (with graphs, a buffer the next replay of the same ring phase overwrites)."""
+        self._ensure_cache(noisy_chunk)
+        if not self.graphs or lq_chunk is not None:
+            return self._step_eager(noisy_chunk, lq_chunk, anchor_harvest_t)
+        key = (self.cache.start, self.cache.frames, tuple(noisy_chunk.shape))
+        entry = self._graphs.get(key)
+        if entry is None:
+            if key not in self._seen:
+                self._seen.add(key)
+                return self._step_eager(noisy_chunk)
+            entry = self._capture(key, noisy_chunk)
+        graph, inp, out = entry
+        self.model.set_t_offset(self.t_offset)
+        inp.copy_(noisy_chunk)
+        graph.replay()
+        f = noisy_chunk.shape[1]
+        self.cache.commit(f)
+        self.t_offset += f
+        return out

@@ -156,10 +156,24 @@ class PeerComm(TPComm):
         self.side = torch.cuda.Stream(device)
         self.ev_ln = torch.cuda.Event()
         self.ev_push = torch.cuda.Event()
-        self.ev_push.record(torch.cuda.current_stream(device))
+        self.pushed = False
         self.n_rs = ops.fp8_gemm_ctas(M, D)
+        self.flags_view = r[self.off["flags"]:self.off["flags"] + 4 * 8 * self.N_FLAG_SETS]
+        self.bar = torch.zeros(1, dtype=torch.float32, device=device)
         self.ag_uses = self.rs_uses = self.ar_calls = 0
         self.key = key
+
+    def begin_forward(self):
+        """Start every forward from zeroed counters: zero this rank's counters,
+        then a one-element all-reduce (on the stream, no host wait) as the
+        barrier after which peers may signal again. Every signal of the previous
+        forward was waited for by its receiver inside that forward, so none is
+        lost; and the expected values of a forward are the same every time,
+        which keeps a captured CUDA graph of it valid on replay."""
+        self.flags_view.zero_()
+        dist.all_reduce(self.bar, group=self.group)
+        self.ag_uses = self.rs_uses = self.ar_calls = 0
+        self.pushed = False   # the previous forward's pushes were joined at its end
 
     # ---- fused steps
     def gather_ln(self, x, eps, **ln):
@@ -167,7 +181,8 @@ class PeerComm(TPComm):
         copy engines push them to every other rank on a side stream (the next
         GEMM starts on the local rows and waits per remote shard)."""
         main = torch.cuda.current_stream(x.device)
-        main.wait_event(self.ev_push)     # the previous push has read these rows
+        if self.pushed:
+            main.wait_event(self.ev_push)  # the previous push has read these rows
         r0, r1 = self.rank * self.Ml, (self.rank + 1) * self.Ml
         ops.ln_mod_quant(x, eps, q=self.gq[r0:r1], qscale=self.gs[r0:r1], **ln)
         self.ev_ln.record(main)
@@ -175,6 +190,7 @@ class PeerComm(TPComm):
         ops.tp_push(self.gq[r0:r1], self.t_gq_rows, self.gs[r0:r1], self.t_gs_rows,
                     flags=self.t_flags[0], rank=self.rank, world=self.world, stream=self.side)
         self.ev_push.record(self.side)
+        self.pushed = True
         self.ag_uses += 1
 
     def tp_gemm(self, *, peer=False):
@@ -295,6 +311,8 @@ class TPSRDiT(SRDiT):
                                        ctx_emb=ctx_emb)
         c = self.cfg
         ops = self.ops
+        if not self.graph_capture:
+            self.set_t_offset(t_offset)
         P, r = self.world, self.rank
         comm = self.comm
         D, Dl, Fl = c.dim, c.dim // P, c.ffn_dim // P
@@ -355,10 +373,12 @@ class TPSRDiT(SRDiT):
             ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
             comm.all_reduce_sum(ss)
             ops.rms_rope(qkv[:, :Dl], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
-                         grid_h=h, grid_w=w, t_offset=t_offset, ss=ss[:M], norm_width=D)
+                         grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev, ss=ss[:M],
+                         norm_width=D)
             ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset=t_offset, v_src=qkv[:, 2 * Dl:], v_dst=vr, ss=ss[M:],
+                         t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:], v_dst=vr,
+                         ss=ss[M:],
                          norm_width=D)
             ak = av = None
             if anchor_kv is not None:
@@ -414,6 +434,8 @@ class TPSRDiT(SRDiT):
         all-reduce."""
         c = self.cfg
         ops = self.ops
+        if not self.graph_capture:
+            self.set_t_offset(t_offset)
         P, r = self.world, self.rank
         comm = self.comm
         D, Dl, Fl = c.dim, c.dim // P, c.ffn_dim // P
@@ -423,6 +445,7 @@ class TPSRDiT(SRDiT):
         f, h, w = grid
         L, M, Lc = S.L, S.M, S.Lc
         comm.setup(M, D, self.device)
+        comm.begin_forward()
         Ml = comm.Ml
         x = x_full[r * Ml:(r + 1) * Ml].contiguous()
         dev = self.device
@@ -467,10 +490,12 @@ class TPSRDiT(SRDiT):
             ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
             comm.allreduce(ss, "sum", st)
             ops.rms_rope(qkv[:, :Dl], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
-                         grid_h=h, grid_w=w, t_offset=t_offset, ss=ss[:M], norm_width=D)
+                         grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev, ss=ss[:M],
+                         norm_width=D)
             ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset=t_offset, v_src=qkv[:, 2 * Dl:], v_dst=vr, ss=ss[M:],
+                         t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:], v_dst=vr,
+                         ss=ss[M:],
                          norm_width=D)
             ak = av = None
             if anchor_kv is not None:
@@ -510,6 +535,7 @@ class TPSRDiT(SRDiT):
                             expected=comm.rs_expected(), status=st)
         if update_cache:
             cache.commit(f)
+        torch.cuda.current_stream(dev).wait_event(comm.ev_push)   # side stream rejoins
         xg = b("tp_xg", (M, D), bf16)
         comm.all_gather(xg, x)
         out = self.head(xg, e, grid)

@@ -161,7 +161,10 @@ int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, float eps,
  * ss_in (optional, [M] fp32): the row's sum of squares over norm_width >= K
  * columns, of which this K-wide slice is one part -- a tensor-parallel rank
  * passes the all-reduced sum of every rank's slice; NULL computes it from the
- * slice with norm_width = K.
+ * slice with norm_width = K. t_offset_dev (optional, one device int) is added to
+ * t_offset when the kernel runs, so a captured CUDA graph can be replayed for
+ * later chunks; temporal positions beyond the table are clamped to its last row
+ * (the host range check covers t_offset only).
  * Replaces: WanRMSNorm.forward (models.py:424-440) on q and k (models.py:602-604),
  *   rope_apply (models.py:173-214), and the KV-cache torch.cat of
  *   attention.py:1506-1510.
@@ -171,7 +174,7 @@ int srdit_rms_rope(const void* src, long long ld_src, int M, int K, const void* 
                    int n_slots, const double* cos_tab, const double* sin_tab, int tab_rows,
                    int grid_h, int grid_w, int t_offset, const void* v_src, long long ld_vsrc,
                    void* v_dst, long long ld_vdst, const float* ss_in, int norm_width,
-                   cudaStream_t stream);
+                   const int* t_offset_dev, cudaStream_t stream);
 
 #define SRDIT_ROW_SUMSQ 0
 #define SRDIT_ROW_ABSMAX 1

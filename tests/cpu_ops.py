@@ -82,8 +82,10 @@ def residual(x, parts, bias=None, gate=None):
 
 def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, cos=None,
              sin=None, grid_h=0, grid_w=0, t_offset=0, v_src=None, v_dst=None, ss=None,
-             norm_width=0):
+             norm_width=0, t_offset_dev=None):
     M, K = src.shape
+    if t_offset_dev is not None:
+        t_offset = t_offset + int(t_offset_dev[0])
     xf = src.float()
     if ss is not None:
         r = torch.rsqrt(ss / norm_width + eps)

@@ -30,7 +30,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cfg_kw, grid, fused, out_q):
+def _worker(rank, world, port, cfg_kw, grid, fused, out_q, graphs=False):
     import datetime
     sys.path.insert(0, str(ROOT))
     import torch.distributed as dist
@@ -57,10 +57,23 @@ def _worker(rank, world, port, cfg_kw, grid, fused, out_q):
             model.check_status()
             return a.float().cpu(), b.float().cpu()
 
+        if graphs:
+            # the refiner loop with captured steps: 5 chunks over a 6-slot ring
+            Pm = importlib.import_module("dreamx-creator_b200.pipeline")
+            lat5 = [torch.randn(cfg.in_dim, f, 2 * h, 2 * w, generator=g).to(torch.bfloat16)
+                    .to(dev) for _ in range(5)]
+
+            def run(model, graphed=True):  # noqa: F811
+                stream = Pm.RefinerStream(model, ctx, graphs=graphed)
+                outs = [stream.step(x).float().cpu() for x in lat5]
+                torch.cuda.synchronize()
+                model.check_status()
+                return outs
         tp_out = run(T.TPSRDiT.random_init(cfg, dev, seed=3, fused=fused))
         res = None
         if rank == 0:
-            ref_out = run(M.SRDiT.random_init(cfg, dev, seed=3))
+            ref_model = M.SRDiT.random_init(cfg, dev, seed=3)
+            ref_out = run(ref_model, False) if graphs else run(ref_model)
             cos = []
             for x, y in zip(tp_out, ref_out):
                 x, y = x.double().reshape(-1), y.double().reshape(-1)
@@ -73,11 +86,11 @@ def _worker(rank, world, port, cfg_kw, grid, fused, out_q):
         out_q.put((rank, None, f"{type(e).__name__}: {e}"))
 
 
-def _run_tp(world, cfg_kw, grid, fused):
+def _run_tp(world, cfg_kw, grid, fused, graphs=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_kw, grid, fused, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_kw, grid, fused, q, graphs))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -105,4 +118,15 @@ def _run_tp(world, cfg_kw, grid, fused):
 ], ids=["small", "2K-2layers"])
 def test_tp2_matches_single_gpu(cfg_kw, grid, fused):
     cos = _run_tp(2, cfg_kw, grid, fused)
+    assert min(cos) >= 0.999, cos
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_graph_replay_matches_single_gpu():
+    """The fused TP forward captured in CUDA graphs (peer counters reset per
+    forward, copy-engine pushes and NCCL inside the graph) against the eager
+    single-GPU refiner loop over 5 chunks."""
+    cfg_kw = dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16,
+                  text_dim=64, text_len=16, block_hw=(2, 2), block_radius_hw=(1, 1), kv_len=3)
+    cos = _run_tp(2, cfg_kw, (3, 8, 16), True, graphs=True)
     assert min(cos) >= 0.999, cos
