@@ -154,6 +154,13 @@ class KVRing:
         self.frames = 0
 
 
+@dataclass
+class TextCache:
+    """Text embedding [Lc, D] and per-block cross-attention K | V [Lc, 2 * width]."""
+    ctx_emb: torch.Tensor
+    kv: list
+
+
 class SRDiT:
     """The refiner transformer on the B200 kernels (inference only).
 
@@ -312,10 +319,11 @@ class SRDiT:
             self._cross_plans[key] = (params.to(self.device), tiling, hq, wq, hk, wk)
         return self._cross_plans[key]
 
-    def embed(self, latent, t, context):
+    def embed(self, latent, t, context, ctx_emb=None):
         """Patch, time and text embeddings (models.py:1827-1875) for one sample.
 
-        latent [C, F, H, W] bf16; t scalar timestep; context [Lc, text_dim] bf16.
+        latent [C, F, H, W] bf16; t scalar timestep; context [Lc, text_dim] bf16
+        (or ``ctx_emb``, its text embedding computed earlier).
         Returns x [F*h*w, D] bf16, e0 [6, D] fp32, e [D] fp32, ctx [Lc, D] bf16, (f, h, w).
         """
         c = self.cfg
@@ -324,13 +332,19 @@ class SRDiT:
         f, h, w = x.shape[2:]
         x = x.flatten(2).transpose(1, 2)[0].contiguous()
         e0, e = self._time_embedding(t)
+        if ctx_emb is not None:
+            return x, e0, e, ctx_emb, (int(f), int(h), int(w))
+        return x, e0, e, self.text_embedding(context), (int(f), int(h), int(w))
+
+    def text_embedding(self, context):
+        """text_embedding (Linear -> GELU(tanh) -> Linear) of the padded context."""
+        c = self.cfg
         ctx = context.to(self.device, torch.bfloat16)
         if ctx.shape[0] < c.text_len:
             ctx = torch.cat([ctx, ctx.new_zeros(c.text_len - ctx.shape[0], ctx.shape[1])])
         ctx = torch.nn.functional.linear(ctx, *self.txt[0])
         ctx = torch.nn.functional.gelu(ctx, approximate="tanh")
-        ctx = torch.nn.functional.linear(ctx, *self.txt[1]).contiguous()
-        return x, e0, e, ctx, (int(f), int(h), int(w))
+        return torch.nn.functional.linear(ctx, *self.txt[1]).contiguous()
 
     def _time_embedding(self, t):
         """(e0 [6, D], e [D]) fp32 for timestep t, computed once per t value (the
@@ -375,8 +389,7 @@ class SRDiT:
         tensors this process holds (all heads, or a tensor-parallel slice)."""
         from types import SimpleNamespace
         c = self.cfg
-        x, e0, e, ctx, grid = self.embed(latent, t, context) if ctx_emb is None else \
-            self._embed_with_ctx(latent, t, ctx_emb)
+        x, e0, e, ctx, grid = self.embed(latent, t, context, ctx_emb)
         f, h, w = grid
         L = h * w
         M = f * L
@@ -431,20 +444,24 @@ class SRDiT:
     # ------------------------------------------------------------------ forward
     def forward_chunk(self, latent, t, context, *, cache: KVRing | None = None,
                       t_offset=0, update_cache=False, anchor_kv=None, anchor_align="frame",
-                      return_kv=False, ctx_emb=None):
+                      return_kv=False, ctx_emb=None, text: TextCache | None = None):
         """One streaming forward over a chunk (``_forward_inference`` for one sample).
 
         latent [C_in, f, H, W]; ``cache`` holds the previous chunks' K/V (read in
         place); ``update_cache=True`` makes this the cache-refresh forward (the
         chunk's K/V are kept, the ring advances). ``anchor_kv``: per-layer (K, V)
         [f*h*w, D] bf16 LQ anchor (never cached). ``return_kv`` returns the
-        per-layer roped K / V of this chunk (the anchor harvest).
+        per-layer roped K / V of this chunk (the anchor harvest). ``text``: the
+        context's ``text_cache`` (else the text embedding and cross K/V are
+        computed here, as the reference does every forward).
         Returns the refined prediction [C_out, f, H, W] bf16 (and the K/V list).
         """
         c = self.cfg
         ops = self.ops
         if not self.graph_capture:
             self.set_t_offset(t_offset)
+        if text is not None:
+            ctx_emb = text.ctx_emb
         S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb,
                         c.num_heads, c.dim)
         x, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
@@ -466,7 +483,7 @@ class SRDiT:
         hs = self._buf("hs", (M,), f32)
         amax = self._buf("amax", (M,), f32)
         ckv = self._buf("ckv", (Lc, 2 * D), bf16)
-        ctxq, ctxs = ops.quant_rowwise(ctx)
+        ctxq, ctxs = ops.quant_rowwise(ctx) if text is None else (None, None)
         mods = torch.stack([ly.modulation for ly in self.layers]) + e0[None]   # [layers, 6, D]
         kv_out = [] if return_kv else None
         st = self.status
@@ -500,8 +517,11 @@ class SRDiT:
             ops.ln_mod_quant(x, c.eps, ln_weight=ly.n3w, ln_bias=ly.n3b, q=xq, qscale=xs)
             ops.fp8_gemm(xq, xs, ly.w_cq, ly.s_cq, ly.b_cq, qb)
             ops.rms_rope(qb, ly.cnq, c.eps, qb, frame_tokens=M)
-            ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
-            ops.rms_rope(ckv[:, :D], ly.cnk, c.eps, ckv[:, :D], frame_tokens=Lc)
+            if text is None:
+                ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
+                ops.rms_rope(ckv[:, :D], ly.cnk, c.eps, ckv[:, :D], frame_tokens=Lc)
+            else:
+                ckv = text.kv[li]
             ops.winattn(qb, ckv[:, :D], ckv[:, D:], att, params_dev=cp_params, n_w=cp_nw,
                         p_stride=blockgrid.P_PLAIN, anchor_mode=0, geom=cgeom, tiling=cp_tiling,
                         status=st, flops=S.cross_flops)
@@ -519,10 +539,36 @@ class SRDiT:
         out = self.head(x, e, grid)
         return (out, kv_out) if return_kv else out
 
-    def _embed_with_ctx(self, latent, t, ctx_emb):
-        x, e0, e, _, grid = self.embed(latent, t, torch.zeros(1, self.cfg.text_dim,
-                                                               device=self.device))
-        return x, e0, e, ctx_emb, grid
+    # ------------------------------------------------------------------ text cache
+    def text_cache(self, context, into=None):
+        """The context's text embedding and every block's cross-attention K | V
+        (cross_attn.k / .v, norm_k on K), computed once per context.
+
+        The refiner's text context is fixed for a clip, yet the reference
+        recomputes these in every forward (models.py:1048-1054, :1854-1866); the
+        values are the same, so a forward given the cache skips that work.
+        ``into``: a previous cache to overwrite in place (its buffers stay put,
+        which keeps captured CUDA graphs valid). Returns the cache."""
+        ops = self.ops
+        c = self.cfg
+        ctx = self.text_embedding(context)
+        Lc, W = ctx.shape[0], self.kv_width
+        if into is None:
+            into = TextCache(ctx.clone(), [torch.empty(Lc, 2 * W, dtype=torch.bfloat16,
+                                                       device=self.device)
+                                           for _ in self.layers])
+        else:
+            into.ctx_emb.copy_(ctx)
+        ctxq, ctxs = ops.quant_rowwise(into.ctx_emb)
+        for li, ly in enumerate(self.layers):
+            self._text_kv(ly, ctxq, ctxs, into.kv[li])
+        return into
+
+    def _text_kv(self, ly, ctxq, ctxs, ckv):
+        c = self.cfg
+        W = self.kv_width
+        self.ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
+        self.ops.rms_rope(ckv[:, :W], ly.cnk, c.eps, ckv[:, :W], frame_tokens=ckv.shape[0])
 
     def _scratch_cache(self, L):
         key = ("scratch_cache", L)

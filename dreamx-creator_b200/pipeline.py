@@ -45,15 +45,26 @@ class RefinerStream:
         self._graphs = {}
         self._seen = set()
         self.context = context.clone()   # static: graph replays read this buffer
+        # text embedding + per-block cross K/V of the context, built once per
+        # context (rebuilt in place when set_context changes it)
+        self.text = None
+        self._text_dirty = True
 
     def set_context(self, context: torch.Tensor):
         """Replace the text context (copied into the step's static buffer)."""
         if context.shape != self.context.shape:
             self.context = context.clone()
+            self.text = None
             self._graphs.clear()
             self._seen.clear()
         else:
             self.context.copy_(context)
+        self._text_dirty = True
+
+    def _ensure_text(self):
+        if self._text_dirty:
+            self.text = self.model.text_cache(self.context, into=self.text)
+            self._text_dirty = False
 
     def reset(self):
         self.cache = None
@@ -66,7 +77,7 @@ class RefinerStream:
         for j in range(f):
             _, kv = self.model.forward_chunk(lq_chunk[:, j:j + 1], harvest_t, self.context,
                                              cache=None, t_offset=self.t_offset + j,
-                                             return_kv=True)
+                                             return_kv=True, text=self.text)
             if ks is None:
                 ks = [[k] for k, _ in kv]
                 vs = [[v] for _, v in kv]
@@ -87,11 +98,11 @@ class RefinerStream:
         m = self.model
         anchor = self.harvest_anchor(lq_chunk, anchor_harvest_t) if lq_chunk is not None else None
         flow = m.forward_chunk(noisy_chunk, self.denoise_t, self.context, cache=self.cache,
-                               t_offset=self.t_offset, anchor_kv=anchor)
+                               t_offset=self.t_offset, anchor_kv=anchor, text=self.text)
         sigma = self.denoise_t / self.ntt
         x0 = (noisy_chunk.double() - sigma * flow.double()).to(noisy_chunk.dtype)
         m.forward_chunk(x0, self.context_noise, self.context, cache=self.cache,
-                        t_offset=self.t_offset, update_cache=True)
+                        t_offset=self.t_offset, update_cache=True, text=self.text)
         self.t_offset += noisy_chunk.shape[1]
         return x0
 
@@ -116,6 +127,7 @@ class RefinerStream:
         """Refine one chunk [C, f, H, W] (device, bf16); returns x0 [C, f, H, W] bf16
         (with graphs, a buffer the next replay of the same ring phase overwrites)."""
         self._ensure_cache(noisy_chunk)
+        self._ensure_text()
         if not self.graphs or lq_chunk is not None:
             return self._step_eager(noisy_chunk, lq_chunk, anchor_harvest_t)
         key = (self.cache.start, self.cache.frames, tuple(noisy_chunk.shape))

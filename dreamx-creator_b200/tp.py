@@ -299,16 +299,28 @@ class TPSRDiT(SRDiT):
     def kv_width(self):
         return self.cfg.dim // self.world
 
+    def _text_kv(self, ly, ctxq, ctxs, ckv):
+        """This rank's heads of the text K | V; norm_k over the full width needs
+        the all-reduced sum of squares (a library all-reduce: once per context)."""
+        c = self.cfg
+        Dl = self.kv_width
+        self.ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
+        ss = self.ops.row_reduce(ckv[:, :Dl], "sumsq")
+        self.comm.all_reduce_sum(ss)
+        self.ops.rms_rope(ckv[:, :Dl], ly.cnk, c.eps, ckv[:, :Dl], frame_tokens=ckv.shape[0],
+                          ss=ss, norm_width=c.dim)
+
     # ------------------------------------------------------------------ forward
     def forward_chunk(self, latent, t, context, *, cache=None, t_offset=0, update_cache=False,
-                      anchor_kv=None, anchor_align="frame", return_kv=False, ctx_emb=None):
+                      anchor_kv=None, anchor_align="frame", return_kv=False, ctx_emb=None,
+                      text=None):
         """``SRDiT.forward_chunk`` on this rank's shard; same arguments and result
         (``anchor_kv`` / the returned K/V hold this rank's heads)."""
         if self.fused:
             return self._forward_fused(latent, t, context, cache=cache, t_offset=t_offset,
                                        update_cache=update_cache, anchor_kv=anchor_kv,
                                        anchor_align=anchor_align, return_kv=return_kv,
-                                       ctx_emb=ctx_emb)
+                                       ctx_emb=ctx_emb, text=text)
         c = self.cfg
         ops = self.ops
         if not self.graph_capture:
@@ -317,6 +329,8 @@ class TPSRDiT(SRDiT):
         comm = self.comm
         D, Dl, Fl = c.dim, c.dim // P, c.ffn_dim // P
         Hl = c.num_heads // P
+        if text is not None:
+            ctx_emb = text.ctx_emb
         S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, Hl, Dl)
         x_full, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
         f, h, w = grid
@@ -342,7 +356,7 @@ class TPSRDiT(SRDiT):
         hbuf = b("tp_h", (M, Fl), bf16)
         hq, hs = b("tp_hq", (M, Fl), f8), b("tp_hs", (M,), f32)
         ckv = b("tp_ckv", (Lc, 2 * Dl), bf16)
-        ctxq, ctxs = ops.quant_rowwise(ctx)
+        ctxq, ctxs = ops.quant_rowwise(ctx) if text is None else (None, None)
         mods = torch.stack([ly.modulation for ly in self.layers]) + e0[None]
         kv_out = [] if return_kv else None
         st = self.status
@@ -395,13 +409,17 @@ class TPSRDiT(SRDiT):
             ops.ln_mod_quant(x, c.eps, ln_weight=ly.n3w, ln_bias=ly.n3b, q=xq_l, qscale=xs_l)
             gather_quantised()
             ops.fp8_gemm(xq, xs, ly.w_cq, ly.s_cq, ly.b_cq, qb)
-            ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
             ops.row_reduce(qb, "sumsq", out=ssc[:M])
-            ops.row_reduce(ckv[:, :Dl], "sumsq", out=ssc[M:])
-            comm.all_reduce_sum(ssc)
+            if text is None:
+                ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
+                ops.row_reduce(ckv[:, :Dl], "sumsq", out=ssc[M:])
+                comm.all_reduce_sum(ssc)
+                ops.rms_rope(ckv[:, :Dl], ly.cnk, c.eps, ckv[:, :Dl], frame_tokens=Lc,
+                             ss=ssc[M:], norm_width=D)
+            else:
+                comm.all_reduce_sum(ssc[:M])
+                ckv = text.kv[li]
             ops.rms_rope(qb, ly.cnq, c.eps, qb, frame_tokens=M, ss=ssc[:M], norm_width=D)
-            ops.rms_rope(ckv[:, :Dl], ly.cnk, c.eps, ckv[:, :Dl], frame_tokens=Lc,
-                         ss=ssc[M:], norm_width=D)
             ops.winattn(qb, ckv[:, :Dl], ckv[:, Dl:], att, params_dev=S.cp_params,
                         n_w=S.cp_nw, p_stride=19, anchor_mode=0, geom=S.cgeom,
                         tiling=S.cp_tiling, status=st, flops=S.cross_flops)
@@ -424,7 +442,7 @@ class TPSRDiT(SRDiT):
         return (out, kv_out) if return_kv else out
 
     def _forward_fused(self, latent, t, context, *, cache, t_offset, update_cache, anchor_kv,
-                       anchor_align, return_kv, ctx_emb):
+                       anchor_align, return_kv, ctx_emb, text=None):
         """The sharded block with its collectives fused into the kernels: each
         rank's LN-quant rows are pushed by the copy engines into every rank's
         gather buffer and the next GEMM waits per remote shard (all-gather);
@@ -440,6 +458,8 @@ class TPSRDiT(SRDiT):
         comm = self.comm
         D, Dl, Fl = c.dim, c.dim // P, c.ffn_dim // P
         Hl = c.num_heads // P
+        if text is not None:
+            ctx_emb = text.ctx_emb
         S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, Hl, Dl)
         x_full, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
         f, h, w = grid
@@ -462,7 +482,7 @@ class TPSRDiT(SRDiT):
         hbuf = b("tp_h", (M, Fl), bf16)
         hq, hs = b("tp_hq", (M, Fl), f8), b("tp_hs", (M,), f32)
         ckv = b("tp_ckv", (Lc, 2 * Dl), bf16)
-        ctxq, ctxs = ops.quant_rowwise(ctx)
+        ctxq, ctxs = ops.quant_rowwise(ctx) if text is None else (None, None)
         mods = torch.stack([ly.modulation for ly in self.layers]) + e0[None]
         kv_out = [] if return_kv else None
         st = self.status
@@ -511,13 +531,17 @@ class TPSRDiT(SRDiT):
             # --- cross attention
             comm.gather_ln(x, c.eps, ln_weight=ly.n3w, ln_bias=ly.n3b)
             ops.fp8_gemm_tp(xq, xs, ly.w_cq, ly.s_cq, ly.b_cq, qb, tp=comm.tp_gemm(), status=st)
-            ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
             ops.row_reduce(qb, "sumsq", out=ssc[:M])
-            ops.row_reduce(ckv[:, :Dl], "sumsq", out=ssc[M:])
-            comm.allreduce(ssc, "sum", st)
+            if text is None:
+                ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
+                ops.row_reduce(ckv[:, :Dl], "sumsq", out=ssc[M:])
+                comm.allreduce(ssc, "sum", st)
+                ops.rms_rope(ckv[:, :Dl], ly.cnk, c.eps, ckv[:, :Dl], frame_tokens=Lc,
+                             ss=ssc[M:], norm_width=D)
+            else:
+                comm.allreduce(ssc[:M], "sum", st)
+                ckv = text.kv[li]
             ops.rms_rope(qb, ly.cnq, c.eps, qb, frame_tokens=M, ss=ssc[:M], norm_width=D)
-            ops.rms_rope(ckv[:, :Dl], ly.cnk, c.eps, ckv[:, :Dl], frame_tokens=Lc,
-                         ss=ssc[M:], norm_width=D)
             ops.winattn(qb, ckv[:, :Dl], ckv[:, Dl:], att, params_dev=S.cp_params,
                         n_w=S.cp_nw, p_stride=19, anchor_mode=0, geom=S.cgeom,
                         tiling=S.cp_tiling, status=st, flops=S.cross_flops)

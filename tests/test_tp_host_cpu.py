@@ -33,10 +33,13 @@ GRID = (3, 4, 8)
 
 
 def _run(model, torch, cfg, lat, ctx):
+    """A cache-refresh forward, then a streaming forward that uses the
+    per-context text cache (each rank's share of the cross K / V)."""
     f, h, w = GRID
     ring = model.new_cache(h * w)
     a = model.forward_chunk(lat[0], 0.0, ctx, cache=ring, update_cache=True)
-    b = model.forward_chunk(lat[1], 625.0, ctx, cache=ring, t_offset=f)
+    text = model.text_cache(ctx)
+    b = model.forward_chunk(lat[1], 625.0, ctx, cache=ring, t_offset=f, text=text)
     model.check_status()
     return a.float(), b.float()
 
