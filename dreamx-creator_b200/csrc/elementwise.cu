@@ -98,6 +98,102 @@ SRDIT_DEV float chunk_absmax(const uint4& u) {
                fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(d.x), fabsf(d.y))));
 }
 
+// ---------------------------------------------------------------- packed pairs
+// A bf16x2 word holds element 2i in its low half and 2i+1 in its high half. As
+// an f32 pair ({x, y} = {2i, 2i+1} in one 64-bit register) it feeds sm_100's
+// paired fp32 instructions: one instruction for both elements, each rounded
+// exactly as its scalar form. The row kernels below run their per-element math
+// on pairs, which halves their instruction count: these kernels are
+// issue-bound, not HBM-bound, when written one element at a time.
+SRDIT_DEV uint64_t bf2_unpack(uint32_t w) {
+  // volatile: re-unpacked on every pass instead of cached as floats
+  uint32_t lo, hi;
+  asm volatile("shl.b32 %0, %1, 16;" : "=r"(lo) : "r"(w));
+  asm volatile("and.b32 %0, %1, 0xffff0000;" : "=r"(hi) : "r"(w));
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+SRDIT_DEV uint64_t f2_pack(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+SRDIT_DEV uint64_t u64_of(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+SRDIT_DEV float2 f2_split(uint64_t r) {
+  float2 f;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(r));
+  return f;
+}
+SRDIT_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+SRDIT_DEV uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+SRDIT_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+SRDIT_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// both elements rounded to nearest-even bf16, repacked as a bf16x2 word
+SRDIT_DEV uint32_t f2_to_bf2(uint64_t v) {
+  const float2 f = f2_split(v);
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f.y), "f"(f.x));
+  return d;
+}
+// bf16 x bf16 rounded once to bf16 (the exact product fits in fp32, so this is
+// bf16(float(a) * float(b)) for both halves)
+SRDIT_DEV uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// running per-half max of |w|
+SRDIT_DEV uint32_t bf2_absmax(uint32_t m, uint32_t w) {
+  uint32_t d;
+  asm("{\n\t.reg .b32 t;\n\tand.b32 t, %2, 0x7fff7fff;\n\tmax.bf16x2 %0, %1, t;\n\t}"
+      : "=r"(d)
+      : "r"(m), "r"(w));
+  return d;
+}
+SRDIT_DEV float bf2_hmax(uint32_t m) {
+  const float2 f = f2_split(bf2_unpack(m));
+  return fmaxf(f.x, f.y);
+}
+// x / s for both elements (Markstein's correction, as div_by) -> e4m3 pair,
+// saturated to +-448 (satfinite: the reference's clamp), element 2i in the
+// low byte
+SRDIT_DEV uint32_t f2_quant_e4m3(uint64_t x, uint64_t ns2, uint64_t r2) {
+  const uint64_t q0 = f2_mul(x, r2);
+  const uint64_t e = f2_fma(q0, ns2, x);
+  const float2 q = f2_split(f2_fma(e, r2, q0));
+  uint16_t h;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(h) : "f"(q.y), "f"(q.x));
+  return h;
+}
+// one 16-byte bf16 chunk (8 elements) -> 8 e4m3 bytes
+SRDIT_DEV uint2 chunk_quant(const uint4& u, uint64_t ns2, uint64_t r2) {
+  uint2 o;
+  o.x = f2_quant_e4m3(bf2_unpack(u.x), ns2, r2) | (f2_quant_e4m3(bf2_unpack(u.y), ns2, r2) << 16);
+  o.y = f2_quant_e4m3(bf2_unpack(u.z), ns2, r2) | (f2_quant_e4m3(bf2_unpack(u.w), ns2, r2) << 16);
+  return o;
+}
+
 // ---------------------------------------------------------------- quant_rowwise
 // K = VEC * 256 (VEC <= 16): the row stays in registers, read once.
 // amax_in != null: the per-row amax is already known (accumulated by the
@@ -118,20 +214,20 @@ __global__ void __launch_bounds__(128) quant_rowwise_kernel(
   if (amax_in) {
     amax = __ldg(amax_in + row);
   } else {
-    amax = 0.f;
+    uint32_t m0 = 0u, m1 = 0u;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) amax = fmaxf(amax, chunk_absmax(raw[i]));
-    amax = warp_max(amax);
+    for (int i = 0; i < VEC; ++i) {
+      m0 = bf2_absmax(bf2_absmax(m0, raw[i].x), raw[i].y);
+      m1 = bf2_absmax(bf2_absmax(m1, raw[i].z), raw[i].w);
+    }
+    amax = warp_max(fmaxf(bf2_hmax(m0), bf2_hmax(m1)));
   }
   const float s = scale_of(amax);
   const float rs = __frcp_rn(s);
+  const uint64_t ns2 = f2_pack(-s, -s), r2 = f2_pack(rs, rs);
   uint2* qr = reinterpret_cast<uint2*>(q + row * ldq) + lane;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    float f[8];
-    unpack8(raw[i], f);
-    qr[i * 32] = quant8(f, s, rs);
-  }
+  for (int i = 0; i < VEC; ++i) qr[i * 32] = chunk_quant(raw[i], ns2, r2);
   if (lane == 0) scale_out[row] = s;
 }
 
@@ -318,72 +414,84 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 5 : 3)) ln_mod_quant_kernel(
   uint4 raw[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) raw[i] = ld_stream(xr + i * 32);
-  float sum = 0.f;
+  // mean (two interleaved pair sums), then the centred sum of squares
+  uint64_t sa = f2_pack(0.f, 0.f), sb = sa;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
-    float f[8];
-    unpack8_v(raw[i], f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sum += f[e];
+    sa = f2_add(f2_add(sa, bf2_unpack(raw[i].x)), bf2_unpack(raw[i].y));
+    sb = f2_add(f2_add(sb, bf2_unpack(raw[i].z)), bf2_unpack(raw[i].w));
   }
-  const float mean = warp_sum(sum) / static_cast<float>(K);
-  float sq = 0.f;
+  const float2 ps = f2_split(f2_add(sa, sb));
+  const float mean = warp_sum(ps.x + ps.y) / static_cast<float>(K);
+  const uint64_t mean2 = f2_pack(mean, mean);
+  uint64_t qa = f2_pack(0.f, 0.f), qb = qa;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
-    float f[8];
-    unpack8_v(raw[i], f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float d = f[e] - mean;
-      sq += d * d;
-    }
+    uint64_t d;
+    d = f2_sub(bf2_unpack(raw[i].x), mean2);
+    qa = f2_fma(d, d, qa);
+    d = f2_sub(bf2_unpack(raw[i].y), mean2);
+    qb = f2_fma(d, d, qb);
+    d = f2_sub(bf2_unpack(raw[i].z), mean2);
+    qa = f2_fma(d, d, qa);
+    d = f2_sub(bf2_unpack(raw[i].w), mean2);
+    qb = f2_fma(d, d, qb);
   }
-  const float var = warp_sum(sq) / static_cast<float>(K);
+  const float2 pq = f2_split(f2_add(qa, qb));
+  const float var = warp_sum(pq.x + pq.y) / static_cast<float>(K);
   const float rstd = rsqrtf(var + eps);
-  float amax = 0.f;
+  const uint64_t rstd2 = f2_pack(rstd, rstd);
+  const uint64_t one2 = f2_pack(1.f, 1.f);
+  uint32_t am0 = 0u, am1 = 0u;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
     const int c0 = i * 256 + lane * 8;
-    float v[8];
-    unpack8_v(raw[i], v);
-    float wv[8], bv[8];
-    if (ln_w) unpack8(__ldg(reinterpret_cast<const uint4*>(ln_w + c0)), wv);
-    if (ln_b) unpack8(__ldg(reinterpret_cast<const uint4*>(ln_b + c0)), bv);
-    float sc[8], sh[8];
+    uint4 wv = make_uint4(0u, 0u, 0u, 0u), bv = wv, sa4 = wv, sb4 = wv, ha4 = wv, hb4 = wv;
+    if (ln_w) wv = ldg_inorder(ln_w + c0);
+    if (ln_b) bv = ldg_inorder(ln_b + c0);
     if (scale) {
-      const float4* s4 = reinterpret_cast<const float4*>(scale + c0);
-      const float4* h4 = reinterpret_cast<const float4*>(shift + c0);
-      const float4 s0 = __ldg(s4), s1 = __ldg(s4 + 1), h0 = __ldg(h4), h1 = __ldg(h4 + 1);
-      sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w;
-      sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
-      sh[0] = h0.x; sh[1] = h0.y; sh[2] = h0.z; sh[3] = h0.w;
-      sh[4] = h1.x; sh[5] = h1.y; sh[6] = h1.z; sh[7] = h1.w;
+      sa4 = ldg_inorder(scale + c0);
+      sb4 = ldg_inorder(scale + c0 + 4);
+      ha4 = ldg_inorder(shift + c0);
+      hb4 = ldg_inorder(shift + c0 + 4);
     }
+    uint32_t wr[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+    const uint64_t sc2[4] = {u64_of(sa4.x, sa4.y), u64_of(sa4.z, sa4.w), u64_of(sb4.x, sb4.y),
+                             u64_of(sb4.z, sb4.w)};
+    const uint64_t sh2[4] = {u64_of(ha4.x, ha4.y), u64_of(ha4.z, ha4.w), u64_of(hb4.x, hb4.y),
+                             u64_of(hb4.z, hb4.w)};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float n = (v[e] - mean) * rstd;
-      if (ln_w) n = n * wv[e];
-      if (ln_b) n = n + bv[e];
-      n = bf16_round(n);  // WanLayerNorm returns .type_as(x)
+    for (int k = 0; k < 4; ++k) {
+      uint64_t n = f2_mul(f2_sub(bf2_unpack(wr[k]), mean2), rstd2);
+      if (ln_w && ln_b)
+        n = f2_fma(n, bf2_unpack(ww[k]), bf2_unpack(bw[k]));
+      else if (ln_w)
+        n = f2_mul(n, bf2_unpack(ww[k]));
+      else if (ln_b)
+        n = f2_add(n, bf2_unpack(bw[k]));
+      uint32_t nb = f2_to_bf2(n);  // WanLayerNorm returns .type_as(x)
       if (scale) {
-        const float one_p = __fadd_rn(1.0f, sc[e]);
-        n = bf16_round(__fadd_rn(__fmul_rn(n, one_p), sh[e]));
+        // x * (1 + scale) + shift in fp32 (two roundings), then bf16
+        const uint64_t one_p = f2_add(one2, sc2[k]);
+        nb = f2_to_bf2(f2_add(f2_mul(bf2_unpack(nb), one_p), sh2[k]));
       }
-      v[e] = n;
-      amax = fmaxf(amax, fabsf(n));
+      wr[k] = nb;
+      if (k & 1)
+        am1 = bf2_absmax(am1, nb);
+      else
+        am0 = bf2_absmax(am0, nb);
     }
-    raw[i] = pack8(v);  // exact: every v[e] is already a bf16 value
+    raw[i] = make_uint4(wr[0], wr[1], wr[2], wr[3]);
   }
-  amax = warp_max(amax);
+  const float amax = warp_max(fmaxf(bf2_hmax(am0), bf2_hmax(am1)));
   const float s = scale_of(amax);
   const float rs = __frcp_rn(s);
+  const uint64_t ns2 = f2_pack(-s, -s), r2 = f2_pack(rs, rs);
   uint2* qr = reinterpret_cast<uint2*>(q + row * ldq) + lane;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    float f[8];
-    unpack8_v(raw[i], f);
-    qr[i * 32] = quant8(f, s, rs);
-  }
+  for (int i = 0; i < VEC; ++i) qr[i * 32] = chunk_quant(raw[i], ns2, r2);
   if (lane == 0) qscale[row] = s;
 }
 
@@ -452,17 +560,24 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
   if (a.ss_in) {
     ssum = __ldg(a.ss_in + row);
   } else {
-    float ss = 0.f;
+    uint64_t sa = f2_pack(0.f, 0.f), sb = sa;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
-      float v[8];
-      unpack8_v(raw[i], v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+      uint64_t v;
+      v = bf2_unpack(raw[i].x);
+      sa = f2_fma(v, v, sa);
+      v = bf2_unpack(raw[i].y);
+      sb = f2_fma(v, v, sb);
+      v = bf2_unpack(raw[i].z);
+      sa = f2_fma(v, v, sa);
+      v = bf2_unpack(raw[i].w);
+      sb = f2_fma(v, v, sb);
     }
-    ssum = warp_sum(ss);
+    const float2 ps = f2_split(f2_add(sa, sb));
+    ssum = warp_sum(ps.x + ps.y);
   }
   const float r = rsqrtf(ssum * (1.0f / static_cast<float>(a.norm_width)) + a.eps);
+  const uint64_t r2 = f2_pack(r, r);
   // A lane's columns are lane*8 + 256*i: inside each 128-wide head that is the
   // same 4 complex pairs d = (lane & 15) * 4 + p for every chunk, so the lane
   // needs only these 4 rotations per row.
@@ -485,22 +600,24 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
   for (int i = 0; i < VEC; ++i) {
     if (i == VEC - 1 && !tail_ok) break;
     const int c0 = i * 256 + lane * 8;
-    float v[8], wv[8];
-    unpack8_v(raw[i], v);
-    unpack8(ldg_inorder(a.weight + c0), wv);
-    float o[8];
+    const uint4 wv = ldg_inorder(a.weight + c0);
+    const uint32_t xw[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = bf16_round(bf16_round(v[e] * r) * wv[e]);
-    if (a.cos_tab) {
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const double x0 = static_cast<double>(o[2 * p]);
-        const double x1 = static_cast<double>(o[2 * p + 1]);
-        o[2 * p] = static_cast<float>(x0 * cr[p] - x1 * si[p]);
-        o[2 * p + 1] = static_cast<float>(x0 * si[p] + x1 * cr[p]);
+    for (int p = 0; p < 4; ++p) {
+      // bf16(bf16(x * r) * w): WanRMSNorm's .type_as(x) * weight
+      o[p] = bf2_mul(f2_to_bf2(f2_mul(bf2_unpack(xw[p]), r2)), ww[p]);
+      if (a.cos_tab) {
+        // (x0 + i x1) * (cos + i sin) in fp64, -> fp32 -> bf16
+        const float2 x = f2_split(bf2_unpack(o[p]));
+        const double x0 = static_cast<double>(x.x), x1 = static_cast<double>(x.y);
+        const float y0 = static_cast<float>(x0 * cr[p] - x1 * si[p]);
+        const float y1 = static_cast<float>(x0 * si[p] + x1 * cr[p]);
+        o[p] = f2_to_bf2(f2_pack(y0, y1));
       }
     }
-    dr[i * 32] = pack8(o);
+    dr[i * 32] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

@@ -78,6 +78,19 @@ SRDIT_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of a phase (no suspend): for a thread that polls several
+// barriers in turn.
+SRDIT_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait. Returns false (and records kStatusTimeout) when the budget runs
 // out; callers then skip the rest of their work and exit.
 //
@@ -226,7 +239,21 @@ SRDIT_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int
       "r"(smem_u32(src)), "r"(c0), "r"(c1)
       : "memory");
 }
+// 4-D TMA tile store from shared memory (bulk-group completion). Elements of
+// the box outside the tensor are not written.
+SRDIT_DEV void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 SRDIT_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every committed bulk store has finished reading its shared-memory source
+SRDIT_DEV void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 SRDIT_DEV void bulk_wait_group_read1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }

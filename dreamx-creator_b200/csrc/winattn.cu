@@ -11,18 +11,24 @@
 // d^-0.5 in fp32, natural-exp online softmax with the fully-masked-row guard
 // (:264-268), P rounded to bf16 before P.V, fp32 accumulation, final acc / l.
 //
-// B200 mapping (one CTA = 128 query rows x one head, 192 threads):
-//   warp 0     TMA producer: Q boxes once, then K and V boxes per KV tile
-//              (2-stage ring each). Each box is one frame x bh rows x bw
+// B200 mapping (persistent, one CTA per SM, 320 threads; a work item is 128
+// query rows x one head):
+//   warp 0     producer: resolves each item (params row, KV walk) into a record
+//              that it publishes through a shared-memory ring, loads the item's
+//              Q boxes (double-buffered across items), then K and V boxes per KV
+//              tile (2-stage rings). Each box is one frame x bh rows x bw
 //              columns of the token grid x 64 head dims, read in place from the
 //              token-major [frames, h, w, heads*128] tensor, so nothing is
 //              gathered and the KV cache is never concatenated.
 //   warp 1     tcgen05.mma issuer: S_j = Q.K_j^T into a double-buffered TMEM
-//              score tile, O += P_j.V_j into a TMEM accumulator.
-//   warps 2-5  softmax: one thread per query row. Reads S_j from TMEM, masks
-//              columns outside the window, updates (m, l), rescales O in TMEM
-//              when the row max moves, writes P_j (bf16, 128B-swizzled) to smem.
-//              At the end: O / l -> bf16 -> the row's token in `out`.
+//              score tile, O += P_j.V_j (P read from TMEM) into a double-buffered
+//              TMEM accumulator.
+//   warps 2-9  softmax, two threads per query row: S_j from TMEM, window mask,
+//              online (m, l), P_j (bf16) written back over S_j in TMEM, O
+//              rescaled in TMEM when the row max moves. At the item's end O / l
+//              -> bf16 is staged in the item's Q buffer in the box layout and
+//              written by TMA tile stores (per-thread row stores where a box
+//              would overhang the window inside the tensor).
 #include "sm100.cuh"
 #include "srdit_internal.h"
 
@@ -40,7 +46,11 @@ constexpr int OFF_K = OFF_Q + 2 * QKV_TILE_BYTES;
 constexpr int OFF_V = OFF_K + 2 * QKV_TILE_BYTES;
 constexpr int OFF_BAR = OFF_V + 2 * QKV_TILE_BYTES;
 constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: 768 floats
-constexpr int SMEM_BYTES = OFF_XCH + 768 * 4 + 1024;
+constexpr int REC_SLOTS = 4;            // item-record ring (producer -> MMA, softmax)
+constexpr int REC_BYTES = 160;
+constexpr int OFF_REC = OFF_XCH + 768 * 4;
+constexpr int SMEM_BYTES = OFF_REC + REC_SLOTS * REC_BYTES + 1024;
+constexpr uint32_t kEpiBarrier = 5;     // named barrier of the 256 softmax threads
 constexpr int NUM_SOFTMAX = 256;        // warps 2-9: two threads per query row
 constexpr int NUM_THREADS = 64 + NUM_SOFTMAX;
 // TMEM: S0 @0, S1 @128 (P_g is written back over S_g as packed bf16 in its first
@@ -65,6 +75,7 @@ struct Args {
   int has_anchor;
   __nv_bfloat16* out;
   long long o_stride;
+  int o_tma;  // 1: the tmO tensor map over `out` is valid (TMA tile stores allowed)
   float scale;
   uint32_t* status;
 };
@@ -245,12 +256,45 @@ SRDIT_DEV void item_coords(const Args& a, int item, int& win, int& mt, int& head
   mt = r % a.m_tiles;
 }
 
+// One work item as the producer resolved it (params row, KV walk, store mode).
+// The producer warp publishes these through a shared-memory ring, so the MMA
+// and softmax warps never reload the params row or redo its integer divisions.
+struct ItemRec {
+  Row r;
+  Walk w;
+  int head;
+  int end;     // 1: this CTA has no further items
+  int o_tma;   // 1: O leaves by TMA tile stores (no box element outside the window)
+  int full_k;  // 1: every HR box row and column lies inside the window
+  int full_a;  // same for the anchor boxes
+};
+static_assert(sizeof(ItemRec) <= REC_BYTES, "item record slot");
+
+SRDIT_DEV bool make_rec(const Args& a, int item, ItemRec& o) {
+  int win, mt, head;
+  item_coords(a, item, win, mt, head);
+  o.r = read_row(a.params, win, a.p_stride, a.frame_mode);
+  o.w = make_walk(a, o.r, mt);
+  if (o.w.nqbox <= 0) return false;
+  const Row& r = o.r;
+  o.head = head;
+  o.end = 0;
+  // A TMA store writes whole boxes; elements past the tensor edge are dropped,
+  // so the boxes may only overhang the window where the window ends at the edge.
+  o.o_tma = a.o_tma && min(r.q_w0 + a.bw_q, a.q_w) <= r.q_w0 + r.qwL &&
+            min(r.q_h0 + o.w.hq_chunks * a.bh_q, a.q_h) <= r.q_h0 + r.qhL;
+  o.full_k = (r.kwL == a.bw_k) && (r.khL % a.bh_k == 0);
+  o.full_a = (r.kwL_a == a.bw_a) && (r.khL_a % a.bh_a == 0);
+  return true;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     winattn_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV,
                    const __grid_constant__ CUtensorMap tmKA,
-                   const __grid_constant__ CUtensorMap tmVA, const Args a) {
+                   const __grid_constant__ CUtensorMap tmVA,
+                   const __grid_constant__ CUtensorMap tmO, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -267,10 +311,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* o_empty = bars + 16;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  uint64_t* rec_full = bars + 20;   // [REC_SLOTS]
+  uint64_t* rec_empty = bars + 24;  // [REC_SLOTS]
+  ItemRec* ring = reinterpret_cast<ItemRec*>(smem + OFF_REC);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_items = a.n_w * a.m_tiles * a.n_heads;
+  const uint32_t q_box_bytes = static_cast<uint32_t>(a.bw_q * a.bh_q * 128);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -282,6 +330,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&o_empty[i], NUM_SOFTMAX);
+    }
+    for (int i = 0; i < REC_SLOTS; ++i) {
+      mbar_init(&rec_full[i], 1);
+      mbar_init(&rec_empty[i], NUM_SOFTMAX + 2);  // softmax threads + the two MMA cursors
     }
     mbar_init(p_full, NUM_SOFTMAX);
     mbar_init(o_full, 1);
@@ -313,21 +365,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Resolves each item into a record (published one item ahead, while this
+    // item's loads are in flight), loads the item's Q boxes into the free Q
+    // buffer, then streams its K and V tiles through the 2-stage rings.
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      const uint32_t q_box_bytes = static_cast<uint32_t>(a.bw_q * a.bh_q * 128);
       bool ok = true;
-      int g = 0, it = 0;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        int win, mt, head;
-        item_coords(a, item, win, mt, head);
-        const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
-        const Walk w = make_walk(a, r, mt);
-        if (w.nqbox <= 0) continue;
-        const int b = it & 1;
-        if (!mbar_wait(&q_empty[b], (static_cast<uint32_t>(it >> 1) & 1u) ^ 1u, a.status,
+      int item = blockIdx.x;
+      auto next_rec = [&](ItemRec& o) -> bool {
+        for (; item < n_items; item += gridDim.x) {
+          if (make_rec(a, item, o)) {
+            item += gridDim.x;
+            return true;
+          }
+        }
+        o.end = 1;
+        return false;
+      };
+      auto publish = [&](int n, const ItemRec& o) -> bool {
+        const int s = n % REC_SLOTS;
+        if (!mbar_wait(&rec_empty[s], (static_cast<uint32_t>(n / REC_SLOTS) & 1u) ^ 1u, a.status,
+                       abort_flag))
+          return false;
+        ring[s] = o;
+        mbar_arrive(&rec_full[s]);  // release: the record is visible to the waiters
+        return true;
+      };
+      ItemRec nxt;
+      bool have = next_rec(nxt);
+      ok = publish(0, nxt);
+      int g = 0;
+      for (int n = 0; have && ok; ++n) {
+        const ItemRec cur = nxt;
+        const Row& r = cur.r;
+        const Walk& w = cur.w;
+        const int b = n & 1;
+        if (!mbar_wait(&q_empty[b], (static_cast<uint32_t>(n >> 1) & 1u) ^ 1u, a.status,
                        abort_flag)) {
           ok = false;
           break;
@@ -339,8 +414,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int h = 0; h < 2; ++h)
             tma_load_4d(smem + OFF_Q + b * QKV_TILE_BYTES + h * SLAB +
                             qb * static_cast<int>(q_box_bytes),
-                        &tmQ, &q_full[b], head * D + h * 64, r.q_w0, r.q_h0 + hc * a.bh_q,
+                        &tmQ, &q_full[b], cur.head * D + h * 64, r.q_w0, r.q_h0 + hc * a.bh_q,
                         r.q_t0 + t);
+        }
+        have = next_rec(nxt);
+        if (!publish(n + 1, nxt)) {
+          ok = false;
+          break;
         }
         for (int j = 0; j < w.n_tiles && ok; ++j, ++g) {
           const int st = g & 1;
@@ -375,11 +455,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               }
               for (int h = 0; h < 2; ++h)
                 tma_load_4d(base + h * SLAB + bx * static_cast<int>(box_bytes), map, ful,
-                            head * D + h * 64, c1, c2, c3);
+                            cur.head * D + h * 64, c1, c2, c3);
             }
           }
         }
-        ++it;
       }
       // after giving up, let issued loads land before the CTA exits
       if (!ok)
@@ -390,49 +469,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // Two cursors walk this CTA's flat tile sequence: the S cursor issues
     // S_g = Q.K_g^T (up to two tiles ahead, double-buffered score tile), the PV
     // cursor issues O += P_g.V_g once the softmax published P_g. Whichever is
-    // ready goes first, so a late K tile never holds back the P.V chain.
+    // ready goes first, so a late K tile never holds back the P.V chain. Each
+    // cursor takes its items' walks from the producer's records.
     if (elect_one()) {
       struct Cursor {
-        int item, it, j, g, head;
+        int n, j, g, state;  // state 0: waiting for record n; 1: walking it; 2: done
         Walk w;
-        bool have;
       };
-      auto seek = [&](Cursor& c) {
-        c.have = false;
-        while (c.item < n_items) {
-          int win, mt;
-          item_coords(a, c.item, win, mt, c.head);
-          const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
-          c.w = make_walk(a, r, mt);
-          if (c.w.nqbox > 0) {
-            c.have = true;
-            return;
-          }
-          c.item += gridDim.x;
+      auto poll = [&](Cursor& c) {
+        if (c.state != 0) return;
+        const int s = c.n % REC_SLOTS;
+        if (!mbar_test_wait(&rec_full[s], static_cast<uint32_t>(c.n / REC_SLOTS) & 1u)) return;
+        if (ring[s].end) {
+          c.state = 2;
+        } else {
+          c.w = ring[s].w;
+          c.state = 1;
         }
+        mbar_arrive(&rec_empty[s]);
       };
       auto advance = [&](Cursor& c) {
         ++c.g;
         if (++c.j == c.w.n_tiles) {
           c.j = 0;
-          ++c.it;
-          c.item += gridDim.x;
-          seek(c);
+          ++c.n;
+          c.state = 0;
+          poll(c);
         }
       };
-      Cursor cs{static_cast<int>(blockIdx.x), 0, 0, 0, 0, Walk{}, false};
+      Cursor cs{0, 0, 0, 0, Walk{}};
       Cursor cp = cs;
-      seek(cs);
-      seek(cp);
       auto s_ready = [&]() -> bool {
-        if (!cs.have || cs.g >= cp.g + 2) return false;  // score buffer still in use
+        if (cs.state != 1 || cs.g >= cp.g + 2) return false;  // score buffer still in use
         const int st = cs.g & 1;
-        if (cs.j == 0 && !mbar_try_wait(&q_full[cs.it & 1], static_cast<uint32_t>(cs.it >> 1) & 1u))
+        if (cs.j == 0 && !mbar_try_wait(&q_full[cs.n & 1], static_cast<uint32_t>(cs.n >> 1) & 1u))
           return false;
         return mbar_try_wait(&k_full[st], static_cast<uint32_t>(cs.g >> 1) & 1u);
       };
       auto issue_s = [&]() {
-        const int b = cs.it & 1;
+        const int b = cs.n & 1;
         const int st = cs.g & 1;
         const TileInfo ti = tile_info(a, cs.w, cs.j);
         tc_fence_after();
@@ -448,21 +523,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_commit(&k_empty[st]);
         tc_commit(&s_full[st]);
-        if (cs.j == cs.w.n_tiles - 1) tc_commit(&q_empty[b]);
         advance(cs);
       };
       auto pv_ready = [&]() -> bool {
-        if (!cp.have || cp.g >= cs.g) return false;  // S_g not issued yet
+        if (cp.state != 1 || cp.g >= cs.g) return false;  // S_g not issued yet
         const int st = cp.g & 1;
         if (!mbar_try_wait(p_full, static_cast<uint32_t>(cp.g) & 1u)) return false;
         if (!mbar_try_wait(&v_full[st], static_cast<uint32_t>(cp.g >> 1) & 1u)) return false;
-        if (cp.j == 0 && !mbar_try_wait(&o_empty[cp.it & 1],
-                                        (static_cast<uint32_t>(cp.it >> 1) & 1u) ^ 1u))
+        if (cp.j == 0 && !mbar_try_wait(&o_empty[cp.n & 1],
+                                        (static_cast<uint32_t>(cp.n >> 1) & 1u) ^ 1u))
           return false;
         return true;
       };
       auto issue_pv = [&]() {
-        const int b = cp.it & 1;
+        const int b = cp.n & 1;
         const int st = cp.g & 1;
         const TileInfo ti = tile_info(a, cp.w, cp.j);
         tc_fence_after();
@@ -482,7 +556,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         advance(cp);
       };
       uint64_t idle_since = 0;
-      while (cp.have) {
+      while (cp.state != 2) {
+        poll(cs);
+        poll(cp);
         bool did = false;
         if (pv_ready()) {
           issue_pv();
@@ -499,9 +575,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // softmax is the usual laggard) instead of spinning, so this warp does
           // not take issue slots from the softmax warp sharing its SM
           // sub-partition. The suspend hint bounds the sleep; the loop re-checks.
-          if (cp.have && cp.g < cs.g)
+          if (cp.state == 1 && cp.g < cs.g)
             mbar_try_wait_sleep(p_full, static_cast<uint32_t>(cp.g) & 1u, 1000u);
-          else if (cs.have)
+          else if (cs.state == 1)
             mbar_try_wait_sleep(&k_full[cs.g & 1], static_cast<uint32_t>(cs.g >> 1) & 1u, 1000u);
           const uint64_t now = global_timer_ns();
           if (idle_since == 0) {
@@ -549,51 +625,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       geo_a[qq] = static_cast<uint32_t>(c / ra) | static_cast<uint32_t>((c % ra) / a.bw_a) << 8 |
                   static_cast<uint32_t>((c % ra) % a.bw_a) << 16;
     }
+    // this thread's query row -> (box of the tile, row and column of the box)
+    const int rq = a.bw_q * a.bh_q;
+    const int row_box = row / rq;
+    const int row_h = (row % rq) / a.bw_q;
+    const int row_w = (row % rq) % a.bw_q;
+    // thread 64 issues the O tile stores; the Q buffer they read from is handed
+    // back to the producer once the stores have read it (one item later)
+    int pend_q = -1;
     bool ok = true;
-    int g = 0, it = 0;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      int win, mt, head;
-      item_coords(a, item, win, mt, head);
-      const Row r = read_row(a.params, win, a.p_stride, a.frame_mode);
-      const Walk w = make_walk(a, r, mt);
-      if (w.nqbox <= 0) continue;
-      const int b = it & 1;
-      const int rq = a.bw_q * a.bh_q;
-      const int qb = row / rq, rr = row % rq;
-      const int gq = w.qbox0 + qb;
-      const int t_row = gq / w.hq_chunks;
-      const int hh = (gq % w.hq_chunks) * a.bh_q + rr / a.bw_q;
-      const int ww = rr % a.bw_q;
-      const bool row_ok = qb < w.nqbox && t_row < r.q_tL && hh < r.qhL && ww < r.qwL;
+    int g = 0;
+    for (int n = 0; ok; ++n) {
+      const int s = n % REC_SLOTS;
+      if (!mbar_wait(&rec_full[s], static_cast<uint32_t>(n / REC_SLOTS) & 1u, a.status,
+                     abort_flag))
+        break;
+      // The record stays in its slot until this item is done (rec_empty is
+      // arrived at the end), so its fields are read where they are needed.
+      const ItemRec* rec = ring + s;
+      if (rec->end) break;
+      const int b = n & 1;
+      const int gq = rec->w.qbox0 + row_box;
+      const int hq_chunks = rec->w.hq_chunks;
+      const int t_row = gq / hq_chunks;
+      const int hh = (gq - t_row * hq_chunks) * a.bh_q + row_h;
+      const bool row_ok = row_box < rec->w.nqbox && t_row < rec->r.q_tL && hh < rec->r.qhL &&
+                          row_w < rec->r.qwL;
       // A warp whose rows are all padding keeps the barrier protocol but skips
       // the math (its rows are never stored; the P it leaves in TMEM only feeds
       // its own, never-stored O rows). Both warps of a pair agree on this.
       const bool active = __any_sync(0xffffffffu, row_ok);
       const uint32_t o_tmem =
           tmem_base + t_lane + 256u + static_cast<uint32_t>(b * 128 + half * 64);
+      const int n_tiles = rec->w.n_tiles;
       float m_i = neg_inf, l_i = 0.f;
-      for (int j = 0; j < w.n_tiles; ++j, ++g) {
+      for (int j = 0; j < n_tiles; ++j, ++g) {
         const int st = g & 1;
         const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
-        const TileInfo ti = tile_info(a, w, j);
+        const TileInfo ti = tile_info(a, rec->w, j);
         const int nchunks = (ti.n16 + 31) >> 5;
         // validity of this thread's 64 columns (bit i of vm[qq] = column
         // (2*half + qq)*32 + i); a per-frame anchor tile is invisible to the
         // other frames' rows; columns past the tile's MMA extent are never read
         uint32_t vm[2];
-        const int khl = ti.anchor ? r.khL_a : r.khL;
-        const int kwl = ti.anchor ? r.kwL_a : r.kwL;
-        const bool sees = !(ti.anchor && r.a_per_frame) || (t_row == ti.frame);
-        if (kwl == ti.bw && khl % ti.bh == 0) {
+        const bool sees = !(ti.anchor && rec->r.a_per_frame) || (t_row == ti.frame);
+        if (ti.anchor ? rec->full_a : rec->full_k) {
           // every box row and column lies inside the window: only the tile's
           // row count masks
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
-            const int n = ti.rows - (2 * half + qq) * 32;
-            vm[qq] = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
+            const int nv = ti.rows - (2 * half + qq) * 32;
+            vm[qq] = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
           }
         } else {
-          const int hch = ti.anchor ? w.a_hchunks : w.hr_hchunks;
+          const int khl = ti.anchor ? rec->r.khL_a : rec->r.khL;
+          const int kwl = ti.anchor ? rec->r.kwL_a : rec->r.kwL;
+          const int hch = ti.anchor ? rec->w.a_hchunks : rec->w.hr_hchunks;
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
             const int c = (2 * half + qq) * 32 + lane;
@@ -710,6 +797,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(o_tmem + 32, u1);
             tmem_st_wait();
           }
+        } else if (threadIdx.x == 64 && pend_q >= 0) {
+          // the previous item's O stores have had a tile's time to read their
+          // staging buffer: wait for that, then give the Q buffer back
+          bulk_wait_group_read0();
+          mbar_arrive(&q_empty[pend_q]);
+          pend_q = -1;
         }
         tc_fence_before();
         mbar_arrive(p_full);
@@ -722,16 +815,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float l_tot = l_i + xsum[(half ^ 1) * 128 + row];
       if (!mbar_wait(o_full, static_cast<uint32_t>(g - 1) & 1u, a.status, abort_flag)) break;
       tc_fence_after();
-      const long long tok = static_cast<long long>(r.q_t0 + t_row) * a.q_h * a.q_w +
-                            static_cast<long long>(r.q_h0 + hh) * a.q_w + (r.q_w0 + ww);
-      __nv_bfloat16* orow = a.out + tok * a.o_stride + head * D + half * 64;
       const float inv_l = 1.0f / l_tot;
+      if (rec->o_tma) {
+        // Stage O in this item's Q buffer (its last S.K product is complete:
+        // o_full of the last P.V covers every earlier MMA), in the 128-byte
+        // swizzled box layout the Q boxes were loaded in, and write the boxes
+        // with TMA stores: one row line per thread here, whole boxes to HBM.
+        uint8_t* srow = smem + OFF_Q + b * QKV_TILE_BYTES + half * SLAB + row * 128;
+        const int sw = row & 7;
 #pragma unroll 1
-      for (int q = 0; q < (active ? 2 : 0); ++q) {
-        uint32_t u[32];
-        tmem_ld32(o_tmem + q * 32, u);
-        tmem_ld_wait();
-        if (row_ok) {
+        for (int q = 0; q < (active ? 2 : 0); ++q) {
+          uint32_t u[32];
+          tmem_ld32(o_tmem + q * 32, u);
+          tmem_ld_wait();
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
             uint4 pk;
@@ -742,14 +838,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                                         __uint_as_float(u[v4 * 8 + 2 * h + 1]) * inv_l);
               pw[h] = *reinterpret_cast<uint32_t*>(&b2);
             }
-            *reinterpret_cast<uint4*>(orow + q * 32 + v4 * 8) = pk;
+            *reinterpret_cast<uint4*>(srow + (((q * 4 + v4) ^ sw) << 4)) = pk;
           }
         }
+        fence_proxy_async_smem();
+        named_barrier_sync(kEpiBarrier, NUM_SOFTMAX);
+        if (threadIdx.x == 64) {
+          const int head = rec->head;
+          const int qbox0 = rec->w.qbox0, nqbox = rec->w.nqbox;
+          const int q_t0 = rec->r.q_t0, q_h0 = rec->r.q_h0, q_w0 = rec->r.q_w0;
+          for (int qb = 0; qb < nqbox; ++qb) {
+            const int gq2 = qbox0 + qb;
+            const int t = gq2 / hq_chunks, hc = gq2 - t * hq_chunks;
+            for (int h = 0; h < 2; ++h)
+              tma_store_4d(&tmO, smem + OFF_Q + b * QKV_TILE_BYTES + h * SLAB +
+                                     qb * static_cast<int>(q_box_bytes),
+                           head * D + h * 64, q_w0, q_h0 + hc * a.bh_q, q_t0 + t);
+          }
+          bulk_commit_group();
+          pend_q = b;
+        }
+      } else {
+        const long long tok = static_cast<long long>(rec->r.q_t0 + t_row) * a.q_h * a.q_w +
+                              static_cast<long long>(rec->r.q_h0 + hh) * a.q_w +
+                              (rec->r.q_w0 + row_w);
+        __nv_bfloat16* orow = a.out + tok * a.o_stride + rec->head * D + half * 64;
+#pragma unroll 1
+        for (int q = 0; q < (active ? 2 : 0); ++q) {
+          uint32_t u[32];
+          tmem_ld32(o_tmem + q * 32, u);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 pk;
+              uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(u[v4 * 8 + 2 * h]) * inv_l,
+                                                          __uint_as_float(u[v4 * 8 + 2 * h + 1]) * inv_l);
+                pw[h] = *reinterpret_cast<uint32_t*>(&b2);
+              }
+              *reinterpret_cast<uint4*>(orow + q * 32 + v4 * 8) = pk;
+            }
+          }
+        }
+        // the item's MMAs are complete (o_full above): the Q buffer is free
+        if (threadIdx.x == 64) mbar_arrive(&q_empty[b]);
       }
       tc_fence_before();
       mbar_arrive(&o_empty[b]);
-      ++it;
+      mbar_arrive(&rec_empty[s]);
     }
+    // O stores still reading shared memory finish before the CTA exits
+    if (threadIdx.x == 64) bulk_wait_group_all();
   }
 
   tc_fence_before();
@@ -759,7 +901,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
-
 
 }  // namespace attn
 }  // namespace srdit
@@ -797,7 +938,7 @@ int pick_box(int bw_max, int bh_max, int* bw_out, int* bh_out, int* per_tile_out
 }
 
 struct RowHost {
-  int q_tL, qhL, qwL, khL, kwL, a_frames, khL_a, kwL_a;
+  int q_tL, qhL, qwL, kv_tL, khL, kwL, a_frames, khL_a, kwL_a;
 };
 
 RowHost read_row_host(const int32_t* p, int frame_mode) {
@@ -805,6 +946,7 @@ RowHost read_row_host(const int32_t* p, int frame_mode) {
   if (frame_mode) {
     r.qhL = p[2];
     r.qwL = p[3];
+    r.kv_tL = p[5];
     r.khL = p[7];
     r.kwL = p[9];
     r.q_tL = p[10];
@@ -815,6 +957,7 @@ RowHost read_row_host(const int32_t* p, int frame_mode) {
     r.q_tL = p[1];
     r.qhL = p[4];
     r.qwL = p[5];
+    r.kv_tL = p[7];
     r.khL = p[9];
     r.kwL = p[11];
     r.a_frames = p[12];
@@ -834,7 +977,8 @@ extern "C" int srdit_winattn_plan(const int32_t* params_host, int n_w, int p_str
   int qh = 0, qw = 0, kh = 0, kw = 0, ah = 0, aw = 0, anyA = 0;
   for (int i = 0; i < n_w; ++i) {
     const RowHost r = read_row_host(params_host + static_cast<size_t>(i) * p_stride, frame_mode);
-    if (r.q_tL <= 0 || r.qhL <= 0 || r.qwL <= 0 || r.khL <= 0 || r.kwL <= 0) return SRDIT_EINVAL;
+    if (r.q_tL <= 0 || r.qhL <= 0 || r.qwL <= 0 || r.kv_tL <= 0 || r.khL <= 0 || r.kwL <= 0)
+      return SRDIT_EINVAL;
     qh = r.qhL > qh ? r.qhL : qh;
     qw = r.qwL > qw ? r.qwL : qw;
     kh = r.khL > kh ? r.khL : kh;
@@ -927,6 +1071,21 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
     mka = mk;
     mva = mv;
   }
+  // O boxes leave by TMA stores when `out` admits a tensor map (16-byte aligned
+  // base and row pitch); otherwise every thread stores its own row.
+  CUtensorMap mo;
+  int o_tma = 0;
+  {
+    const long long dims[4] = {C, g->q_w, g->q_h, g->q_frames};
+    const long long st[3] = {g->o_stride * 2, g->o_stride * 2 * g->q_w,
+                             g->o_stride * 2 * g->q_w * g->q_h};
+    const int box[4] = {64, t->bw_q, t->bh_q, 1};
+    if ((reinterpret_cast<uintptr_t>(out) & 15u) == 0 && g->o_stride >= C &&
+        make_tmap_4d(&mo, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, st, box) == 0)
+      o_tma = 1;
+    else
+      mo = mq;  // never read: o_tma = 0
+  }
 
   attn::Args a;
   a.params = params_dev;
@@ -951,6 +1110,7 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
   a.has_anchor = t->has_anchor;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.o_stride = g->o_stride;
+  a.o_tma = o_tma;
   a.scale = g->scale;
   a.status = status;
 
@@ -968,6 +1128,6 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
   const int sms = num_sms(dev);
   dim3 grid(static_cast<unsigned>(items < sms ? items : sms));
   attn::winattn_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(mq, mk, mv, mka,
-                                                                               mva, a);
+                                                                               mva, mo, a);
   return static_cast<int>(cudaGetLastError());
 }
