@@ -2,6 +2,9 @@
 //
 // One warp per token row; each lane owns 8-element (16-byte) chunks strided by
 // 256 elements, so every load and store is a coalesced 512-byte warp access.
+// Per-element math runs on fp32 / bf16 pairs. ln_mod_quant on full-width rows
+// is column-stationary instead (a CTA per row group, per-column operands held
+// in registers).
 //
 //   quant_rowwise   x bf16 -> (e4m3, per-row scale)            fp8_linear.py:93-103
 //   ln_mod_quant    LayerNorm (optionally affine) -> modulate -> e4m3 + scale
@@ -621,6 +624,231 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
   }
 }
 
+// ---------------------------------------------------------------- column-stationary rows
+// For K a multiple of 512 (every full-width row of the model): a CTA of
+// T = K/16 threads covers whole rows, thread t owning the two 8-column chunks
+// t and t + T of every row the CTA processes. Per-column operands (LayerNorm
+// weight and bias, the modulation's scale and shift, the RMSNorm weight) are
+// loaded into registers once per CTA rather than re-read for every row, and
+// each row is read from HBM exactly once, straight into registers. A CTA walks
+// groups of kGroup rows (the next group's loads in flight while it computes
+// one) and reduces each row statistic across its warps once per group.
+constexpr int kGroup = 4;
+constexpr int kCsMaxThreads = 256;  // K <= 4096
+
+// Reduce v[0..3] (one value per group row) over the warp: a butterfly that
+// halves the values each lane carries on the first two steps. Afterwards lane
+// l holds the warp total of row 2 * ((l >> 4) & 1) + ((l >> 3) & 1); lanes 0,
+// 8, 16, 24 hold rows 0, 1, 2, 3.
+template <bool kMax>
+SRDIT_DEV float warp_reduce4(const float (&v)[4]) {
+  const int lane = threadIdx.x & 31;
+  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+  const bool hi = lane & 16;
+  float a0 = hi ? v[2] : v[0], a1 = hi ? v[3] : v[1];
+  const float s0 = hi ? v[0] : v[2], s1 = hi ? v[1] : v[3];
+  a0 = op(a0, __shfl_xor_sync(0xffffffffu, s0, 16));
+  a1 = op(a1, __shfl_xor_sync(0xffffffffu, s1, 16));
+  const bool b8 = lane & 8;
+  float k = b8 ? a1 : a0;
+  const float s = b8 ? a0 : a1;
+  k = op(k, __shfl_xor_sync(0xffffffffu, s, 8));
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) k = op(k, __shfl_xor_sync(0xffffffffu, k, o));
+  return k;
+}
+
+// CTA-wide totals of one statistic for the group's rows: each warp's totals go
+// to part[warp], then every thread combines the warps in the same order.
+template <bool kMax>
+SRDIT_DEV void cta_reduce4(float (&v)[4], float4* part) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float w = warp_reduce4<kMax>(v);
+  if ((lane & 7) == 0) reinterpret_cast<float*>(part + warp)[lane >> 3] = w;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float4 t = part[0];
+  for (int i = 1; i < nw; ++i) {
+    const float4 p = part[i];
+    if (kMax) {
+      t.x = fmaxf(t.x, p.x); t.y = fmaxf(t.y, p.y); t.z = fmaxf(t.z, p.z); t.w = fmaxf(t.w, p.w);
+    } else {
+      t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
+    }
+  }
+  v[0] = t.x;
+  v[1] = t.y;
+  v[2] = t.z;
+  v[3] = t.w;
+}
+
+// the group's rows (zeros past M): chunk ch of row r at d[r][ch]
+SRDIT_DEV void cs_load(uint4 (&d)[kGroup][2], const __nv_bfloat16* x, long long ldx, int M,
+                       int row0, int c0, int c1) {
+#pragma unroll
+  for (int r = 0; r < kGroup; ++r) {
+    if (row0 + r < M) {
+      const __nv_bfloat16* xr = x + static_cast<long long>(row0 + r) * ldx;
+      d[r][0] = ld_stream(reinterpret_cast<const uint4*>(xr + c0));
+      d[r][1] = ld_stream(reinterpret_cast<const uint4*>(xr + c1));
+    } else {
+      d[r][0] = d[r][1] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+SRDIT_DEV uint32_t word(const uint4& u, int k) {
+  return k == 0 ? u.x : (k == 1 ? u.y : (k == 2 ? u.z : u.w));
+}
+
+// Over this thread's 16 elements of a row: the sum (kind 0), the sum of
+// (x - mean)^2 (kind 1) or the sum of x^2 (kind 2).
+template <int kKind>
+SRDIT_DEV float chunk2_sum(const uint4 (&d)[2], uint64_t mean2) {
+  uint64_t a = f2_pack(0.f, 0.f), b = a;
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint64_t v = bf2_unpack(word(d[ch], k));
+      if (kKind == 0) {
+        if (k & 1) b = f2_add(b, v); else a = f2_add(a, v);
+      } else {
+        const uint64_t dd = kKind == 1 ? f2_sub(v, mean2) : v;
+        if (k & 1) b = f2_fma(dd, dd, b); else a = f2_fma(dd, dd, a);
+      }
+    }
+  const float2 s = f2_split(f2_add(a, b));
+  return s.x + s.y;
+}
+
+// MODE bit 0: modulate (x * (1 + scale) + shift); bit 1: LayerNorm affine
+template <int MODE, int kMaxT>
+__global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, int M, float eps,
+    const __nv_bfloat16* __restrict__ ln_w, const __nv_bfloat16* __restrict__ ln_b,
+    const float* __restrict__ shift, const float* __restrict__ scale,
+    uint8_t* __restrict__ q, long long ldq, float* __restrict__ qscale) {
+  constexpr bool kMod = MODE & 1, kAff = MODE & 2;
+  __shared__ float4 part[3][32];
+  const int T = blockDim.x;
+  const int t = threadIdx.x;
+  const int K = T * 16;
+  const int cc[2] = {t * 8, (t + T) * 8};
+  // per-column operands of this thread's 16 columns, as f32 pairs
+  uint64_t one_p[8], sh[8], wt[8], bs[8];
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch) {
+    if (kMod) {
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + cc[ch]));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + cc[ch]) + 1);
+      const float4 h0 = __ldg(reinterpret_cast<const float4*>(shift + cc[ch]));
+      const float4 h1 = __ldg(reinterpret_cast<const float4*>(shift + cc[ch]) + 1);
+      const uint64_t one2 = f2_pack(1.f, 1.f);
+      one_p[ch * 4 + 0] = f2_add(one2, f2_pack(s0.x, s0.y));
+      one_p[ch * 4 + 1] = f2_add(one2, f2_pack(s0.z, s0.w));
+      one_p[ch * 4 + 2] = f2_add(one2, f2_pack(s1.x, s1.y));
+      one_p[ch * 4 + 3] = f2_add(one2, f2_pack(s1.z, s1.w));
+      sh[ch * 4 + 0] = f2_pack(h0.x, h0.y);
+      sh[ch * 4 + 1] = f2_pack(h0.z, h0.w);
+      sh[ch * 4 + 2] = f2_pack(h1.x, h1.y);
+      sh[ch * 4 + 3] = f2_pack(h1.z, h1.w);
+    }
+    if (kAff) {
+      const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(ln_w + cc[ch]));
+      const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(ln_b + cc[ch]));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        wt[ch * 4 + k] = bf2_unpack(word(w4, k));
+        bs[ch * 4 + k] = bf2_unpack(word(b4, k));
+      }
+    }
+  }
+  const int ngroups = (M + kGroup - 1) / kGroup;
+  uint4 cur[kGroup][2], nxt[kGroup][2];
+  int g = blockIdx.x;
+  if (g < ngroups) cs_load(cur, x, ldx, M, g * kGroup, cc[0], cc[1]);
+  for (; g < ngroups; g += gridDim.x) {
+    const int row0 = g * kGroup;
+    if (g + static_cast<int>(gridDim.x) < ngroups)
+      cs_load(nxt, x, ldx, M, (g + gridDim.x) * kGroup, cc[0], cc[1]);
+    float st[4];
+#pragma unroll
+    for (int r = 0; r < kGroup; ++r) st[r] = chunk2_sum<0>(cur[r], 0);
+    cta_reduce4<false>(st, part[0]);
+    uint64_t mean2[kGroup];
+#pragma unroll
+    for (int r = 0; r < kGroup; ++r) {
+      const float mean = st[r] / static_cast<float>(K);
+      mean2[r] = f2_pack(mean, mean);
+    }
+#pragma unroll
+    for (int r = 0; r < kGroup; ++r) st[r] = chunk2_sum<1>(cur[r], mean2[r]);
+    cta_reduce4<false>(st, part[1]);
+    float am[4];
+#pragma unroll
+    for (int r = 0; r < kGroup; ++r) {
+      const float rstd = rsqrtf(st[r] / static_cast<float>(K) + eps);
+      const uint64_t rstd2 = f2_pack(rstd, rstd);
+      uint32_t m0 = 0u, m1 = 0u;
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint64_t n = f2_mul(f2_sub(bf2_unpack(word(cur[r][ch], k)), mean2[r]), rstd2);
+          if (kAff) n = f2_fma(n, wt[ch * 4 + k], bs[ch * 4 + k]);
+          uint32_t nb = f2_to_bf2(n);  // WanLayerNorm returns .type_as(x)
+          if (kMod)  // x * (1 + scale) + shift in fp32 (two roundings), then bf16
+            nb = f2_to_bf2(f2_add(f2_mul(bf2_unpack(nb), one_p[ch * 4 + k]), sh[ch * 4 + k]));
+          o[k] = nb;
+          if (k & 1) m1 = bf2_absmax(m1, nb); else m0 = bf2_absmax(m0, nb);
+        }
+        cur[r][ch] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      am[r] = fmaxf(bf2_hmax(m0), bf2_hmax(m1));
+    }
+    cta_reduce4<true>(am, part[2]);
+#pragma unroll
+    for (int r = 0; r < kGroup; ++r) {
+      if (row0 + r >= M) break;
+      const float sc = scale_of(am[r]);
+      const float rsc = __frcp_rn(sc);
+      const uint64_t ns2 = f2_pack(-sc, -sc), r2 = f2_pack(rsc, rsc);
+      uint8_t* qr = q + static_cast<long long>(row0 + r) * ldq;
+      *reinterpret_cast<uint2*>(qr + cc[0]) = chunk_quant(cur[r][0], ns2, r2);
+      *reinterpret_cast<uint2*>(qr + cc[1]) = chunk_quant(cur[r][1], ns2, r2);
+      if (t == 0) qscale[row0 + r] = sc;
+    }
+#pragma unroll
+    for (int r = 0; r < kGroup; ++r) {
+      cur[r][0] = nxt[r][0];
+      cur[r][1] = nxt[r][1];
+    }
+  }
+  (void)K;
+}
+
+// Persistent grid of a column-stationary kernel: one CTA of `threads` per
+// kGroup rows at most, at most the CTAs resident on the device at once.
+template <auto Kern>
+int cs_grid(int threads, int M, int* grid_out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= kMaxDevices) return SRDIT_EINVAL;
+  static int per_sm[kMaxDevices][kCsMaxThreads / 32 + 1] = {};
+  int& n = per_sm[dev][threads / 32];
+  if (n == 0) {
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, Kern, threads, 0);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (n <= 0) n = 1;
+  }
+  const int need = (M + kGroup - 1) / kGroup;
+  const int cap = n * num_sms(dev);
+  *grid_out = need < cap ? need : cap;
+  return 0;
+}
+
 template <template <int> class Launcher, typename... A>
 int dispatch_vec(int K, A&&... args) {
   switch (K) {
@@ -663,6 +891,39 @@ int rope_launch(const RopeArgs& a, int M, int K, cudaStream_t st) {
   const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
   rms_rope_kernel<VEC><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M, K);
   return static_cast<int>(cudaGetLastError());
+}
+
+template <int MODE, int kMaxT>
+int ln_cs_run_t(const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
+                const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
+                const float* scale, uint8_t* q, long long ldq, float* qs, cudaStream_t st) {
+  int grid = 0;
+  const int rc = cs_grid<ln_mod_quant_cs_kernel<MODE, kMaxT>>(K / 16, M, &grid);
+  if (rc) return rc;
+  ln_mod_quant_cs_kernel<MODE, kMaxT><<<grid, K / 16, 0, st>>>(x, ldx, M, eps, w, b, shift,
+                                                                scale, q, ldq, qs);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int MODE>
+int ln_cs_run(const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
+              const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
+              const float* scale, uint8_t* q, long long ldq, float* qs, cudaStream_t st) {
+  return K / 16 <= 192
+             ? ln_cs_run_t<MODE, 192>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st)
+             : ln_cs_run_t<MODE, 256>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
+}
+
+inline int ln_cs_launch(int mode, const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
+                        const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
+                        const float* scale, uint8_t* q, long long ldq, float* qs,
+                        cudaStream_t st) {
+  switch (mode) {
+    case 0: return ln_cs_run<0>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
+    case 1: return ln_cs_run<1>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
+    case 2: return ln_cs_run<2>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
+    default: return ln_cs_run<3>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
+  }
 }
 
 // K a multiple of 128, ceil(K / 256) chunk slots per lane.
@@ -716,6 +977,14 @@ extern "C" int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, fl
   if ((scale && (!aligned16(scale) || !aligned16(shift))) ||
       (ln_weight && !aligned16(ln_weight)) || (ln_bias && !aligned16(ln_bias)))
     return SRDIT_EALIGN;
+  if (K % 512 == 0 && K / 16 <= ew::kCsMaxThreads) {
+    const int mode = (scale ? 1 : 0) | ((ln_weight || ln_bias) ? 2 : 0);
+    if ((mode & 2) && !(ln_weight && ln_bias)) return SRDIT_EUNSUPPORTED;
+    return ew::ln_cs_launch(mode, static_cast<const __nv_bfloat16*>(x), ldx, M, K, eps,
+                            static_cast<const __nv_bfloat16*>(ln_weight),
+                            static_cast<const __nv_bfloat16*>(ln_bias), shift, scale,
+                            static_cast<uint8_t*>(q), ldq, qscale, stream);
+  }
   return ew::dispatch_vec<ew::LnLaunch>(
       K, static_cast<const __nv_bfloat16*>(x), ldx, M, eps,
       static_cast<const __nv_bfloat16*>(ln_weight), static_cast<const __nv_bfloat16*>(ln_bias),
