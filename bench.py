@@ -38,10 +38,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "2K SR-DiT refine latent-frames/s @1/2/4/8 B200; fp8 GEMM & win-attn % of roofline"
 UNIT = "latent-frames/s"
 FRAMES_PER_STEP = 3
-# DRAM bytes (read + write) per srdit_fp8_gemm launch, averaged over the GEMM
-# launches of one step, from an ncu capture of dram__bytes_read.sum +
-# dram__bytes_write.sum (profiles/fp8_gemm_step_traffic.md); None until captured.
-GEMM_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per srdit_fp8_gemm launch, averaged over the six
+# GEMM launches of one block: ncu dram__bytes_read.sum + dram__bytes_write.sum
+# of one launch of each of the step's four shapes (6912 x {9216, 3072, 14336} x
+# 3072 and 6912 x 3072 x 14336), weighted 1 / 3 / 1 / 1 per block.
+GEMM_TRAFFIC_PER_LAUNCH = 142.0e6
 LAT_SHAPE = (48, 3, 72, 128)
 CTX_SHAPE = (512, 4096)
 
