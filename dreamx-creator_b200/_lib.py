@@ -75,6 +75,9 @@ SIGNATURES = {
                           ctypes.c_uint32, c_vp, c_vp],
     "srdit_tp_allreduce": [c_vp, c_vp, c_int, c_int, ctypes.POINTER(PeerPtrs),
                            ctypes.POINTER(PeerPtrs), c_int, c_int, ctypes.c_uint32, c_vp, c_vp],
+    "srdit_ln_mod_quant_tp": [c_vp, c_ll, c_int, c_int, c_float, c_vp, c_vp, c_vp, c_vp, c_ll,
+                              ctypes.POINTER(PeerPtrs), ctypes.POINTER(PeerPtrs),
+                              ctypes.POINTER(PeerPtrs), c_vp, c_int, c_int, c_vp],
     "srdit_tp_push": [c_vp, ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, c_vp,
                       ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, ctypes.POINTER(PeerPtrs),
                       c_int, c_int, c_vp],

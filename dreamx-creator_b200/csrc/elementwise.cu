@@ -722,13 +722,25 @@ SRDIT_DEV float chunk2_sum(const uint4 (&d)[2], uint64_t mean2) {
   return s.x + s.y;
 }
 
+// Tensor-parallel all-gather fused into the LN epilogue: the rank's e4m3 rows
+// and scales are stored straight into every rank's gather buffer (peer memory
+// over NVLink, this rank's row block), and the last CTA to finish raises this
+// rank's counter at every peer (release at system scope).
+struct LnPeer {
+  uint8_t* q[SRDIT_MAX_RANKS];   // row 0 of this rank's block in rank d's gather buffer
+  float* s[SRDIT_MAX_RANKS];     // the same for the per-row scales
+  uint32_t* flag[SRDIT_MAX_RANKS];  // counter `rank` of rank d
+  uint32_t* done;                // CTAs finished (this rank's memory; reset by the last one)
+  int rank, world;
+};
+
 // MODE bit 0: modulate (x * (1 + scale) + shift); bit 1: LayerNorm affine
-template <int MODE, int kMaxT>
+template <int MODE, int kMaxT, bool kPeer>
 __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_kernel(
     const __nv_bfloat16* __restrict__ x, long long ldx, int M, float eps,
     const __nv_bfloat16* __restrict__ ln_w, const __nv_bfloat16* __restrict__ ln_b,
     const float* __restrict__ shift, const float* __restrict__ scale,
-    uint8_t* __restrict__ q, long long ldq, float* __restrict__ qscale) {
+    uint8_t* __restrict__ q, long long ldq, float* __restrict__ qscale, const LnPeer pe) {
   constexpr bool kMod = MODE & 1, kAff = MODE & 2;
   __shared__ float4 part[3][32];
   const int T = blockDim.x;
@@ -815,15 +827,40 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
       const float sc = scale_of(am[r]);
       const float rsc = __frcp_rn(sc);
       const uint64_t ns2 = f2_pack(-sc, -sc), r2 = f2_pack(rsc, rsc);
-      uint8_t* qr = q + static_cast<long long>(row0 + r) * ldq;
-      *reinterpret_cast<uint2*>(qr + cc[0]) = chunk_quant(cur[r][0], ns2, r2);
-      *reinterpret_cast<uint2*>(qr + cc[1]) = chunk_quant(cur[r][1], ns2, r2);
-      if (t == 0) qscale[row0 + r] = sc;
+      const uint2 v0 = chunk_quant(cur[r][0], ns2, r2);
+      const uint2 v1 = chunk_quant(cur[r][1], ns2, r2);
+      if (kPeer) {
+        for (int d = 0; d < pe.world; ++d) {
+          uint8_t* qr = pe.q[d] + static_cast<long long>(row0 + r) * ldq;
+          *reinterpret_cast<uint2*>(qr + cc[0]) = v0;
+          *reinterpret_cast<uint2*>(qr + cc[1]) = v1;
+          if (t == 0) pe.s[d][row0 + r] = sc;
+        }
+      } else {
+        uint8_t* qr = q + static_cast<long long>(row0 + r) * ldq;
+        *reinterpret_cast<uint2*>(qr + cc[0]) = v0;
+        *reinterpret_cast<uint2*>(qr + cc[1]) = v1;
+        if (t == 0) qscale[row0 + r] = sc;
+      }
     }
 #pragma unroll
     for (int r = 0; r < kGroup; ++r) {
       cur[r][0] = nxt[r][0];
       cur[r][1] = nxt[r][1];
+    }
+  }
+  if (kPeer) {
+    // every thread's peer stores precede thread 0's system-scope fence (the
+    // barrier, then a cumulative fence); the CTA that finishes last signals
+    __syncthreads();
+    if (t == 0) {
+      __threadfence_system();
+      if (atomicAdd(pe.done, 1u) == gridDim.x - 1) {
+        *pe.done = 0u;  // ready for the next launch
+        __threadfence_system();
+        for (int d = 0; d < pe.world; ++d)
+          if (d != pe.rank) flag_add_release(pe.flag[d] + pe.rank, 1u);
+      }
     }
   }
   (void)K;
@@ -893,36 +930,41 @@ int rope_launch(const RopeArgs& a, int M, int K, cudaStream_t st) {
   return static_cast<int>(cudaGetLastError());
 }
 
-template <int MODE, int kMaxT>
+template <int MODE, int kMaxT, bool kPeer>
 int ln_cs_run_t(const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
                 const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
-                const float* scale, uint8_t* q, long long ldq, float* qs, cudaStream_t st) {
+                const float* scale, uint8_t* q, long long ldq, float* qs, const LnPeer& pe,
+                cudaStream_t st) {
   int grid = 0;
-  const int rc = cs_grid<ln_mod_quant_cs_kernel<MODE, kMaxT>>(K / 16, M, &grid);
+  const int rc = cs_grid<ln_mod_quant_cs_kernel<MODE, kMaxT, kPeer>>(K / 16, M, &grid);
   if (rc) return rc;
-  ln_mod_quant_cs_kernel<MODE, kMaxT><<<grid, K / 16, 0, st>>>(x, ldx, M, eps, w, b, shift,
-                                                                scale, q, ldq, qs);
+  ln_mod_quant_cs_kernel<MODE, kMaxT, kPeer><<<grid, K / 16, 0, st>>>(
+      x, ldx, M, eps, w, b, shift, scale, q, ldq, qs, pe);
   return static_cast<int>(cudaGetLastError());
 }
 
-template <int MODE>
+template <int MODE, bool kPeer>
 int ln_cs_run(const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
               const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
-              const float* scale, uint8_t* q, long long ldq, float* qs, cudaStream_t st) {
-  return K / 16 <= 192
-             ? ln_cs_run_t<MODE, 192>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st)
-             : ln_cs_run_t<MODE, 256>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
+              const float* scale, uint8_t* q, long long ldq, float* qs, const LnPeer& pe,
+              cudaStream_t st) {
+  return K / 16 <= 192 ? ln_cs_run_t<MODE, 192, kPeer>(x, ldx, M, K, eps, w, b, shift, scale, q,
+                                                       ldq, qs, pe, st)
+                       : ln_cs_run_t<MODE, 256, kPeer>(x, ldx, M, K, eps, w, b, shift, scale, q,
+                                                       ldq, qs, pe, st);
 }
 
-inline int ln_cs_launch(int mode, const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
-                        const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
-                        const float* scale, uint8_t* q, long long ldq, float* qs,
-                        cudaStream_t st) {
+template <bool kPeer>
+int ln_cs_launch(int mode, const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
+                 const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
+                 const float* scale, uint8_t* q, long long ldq, float* qs, const LnPeer& pe,
+                 cudaStream_t st) {
   switch (mode) {
-    case 0: return ln_cs_run<0>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
-    case 1: return ln_cs_run<1>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
-    case 2: return ln_cs_run<2>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
-    default: return ln_cs_run<3>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, st);
+    case 0: return ln_cs_run<0, kPeer>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, pe, st);
+    case 1: return ln_cs_run<1, kPeer>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, pe, st);
+    case 2: return ln_cs_run<2, kPeer>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, pe, st);
+    default:
+      return ln_cs_run<3, kPeer>(x, ldx, M, K, eps, w, b, shift, scale, q, ldq, qs, pe, st);
   }
 }
 
@@ -980,15 +1022,51 @@ extern "C" int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, fl
   if (K % 512 == 0 && K / 16 <= ew::kCsMaxThreads) {
     const int mode = (scale ? 1 : 0) | ((ln_weight || ln_bias) ? 2 : 0);
     if ((mode & 2) && !(ln_weight && ln_bias)) return SRDIT_EUNSUPPORTED;
-    return ew::ln_cs_launch(mode, static_cast<const __nv_bfloat16*>(x), ldx, M, K, eps,
-                            static_cast<const __nv_bfloat16*>(ln_weight),
-                            static_cast<const __nv_bfloat16*>(ln_bias), shift, scale,
-                            static_cast<uint8_t*>(q), ldq, qscale, stream);
+    ew::LnPeer pe = {};
+    return ew::ln_cs_launch<false>(mode, static_cast<const __nv_bfloat16*>(x), ldx, M, K, eps,
+                                   static_cast<const __nv_bfloat16*>(ln_weight),
+                                   static_cast<const __nv_bfloat16*>(ln_bias), shift, scale,
+                                   static_cast<uint8_t*>(q), ldq, qscale, pe, stream);
   }
   return ew::dispatch_vec<ew::LnLaunch>(
       K, static_cast<const __nv_bfloat16*>(x), ldx, M, eps,
       static_cast<const __nv_bfloat16*>(ln_weight), static_cast<const __nv_bfloat16*>(ln_bias),
       shift, scale, static_cast<uint8_t*>(q), ldq, qscale, stream);
+}
+
+extern "C" int srdit_ln_mod_quant_tp(const void* x, long long ldx, int M, int K, float eps,
+                                     const void* ln_weight, const void* ln_bias,
+                                     const float* shift, const float* scale, long long ldq,
+                                     const srdit_peer_ptrs* q_rows, const srdit_peer_ptrs* s_rows,
+                                     const srdit_peer_ptrs* flags, uint32_t* done, int rank,
+                                     int world, cudaStream_t stream) {
+  if (M == 0) return 0;
+  if (!x || !q_rows || !s_rows || !flags || !done || M < 0) return SRDIT_EINVAL;
+  if (world < 1 || world > SRDIT_MAX_RANKS || rank < 0 || rank >= world) return SRDIT_EINVAL;
+  if ((scale == nullptr) != (shift == nullptr)) return SRDIT_EINVAL;
+  if (K % 512 || K / 16 > ew::kCsMaxThreads) return SRDIT_EUNSUPPORTED;
+  if ((ldx % 8) || (ldq % 16) || !aligned16(x)) return SRDIT_EALIGN;
+  if ((scale && (!aligned16(scale) || !aligned16(shift))) ||
+      (ln_weight && !aligned16(ln_weight)) || (ln_bias && !aligned16(ln_bias)))
+    return SRDIT_EALIGN;
+  const int mode = (scale ? 1 : 0) | ((ln_weight || ln_bias) ? 2 : 0);
+  if ((mode & 2) && !(ln_weight && ln_bias)) return SRDIT_EUNSUPPORTED;
+  ew::LnPeer pe = {};
+  for (int d = 0; d < world; ++d) {
+    if (!q_rows->p[d] || !s_rows->p[d] || !flags->p[d]) return SRDIT_EINVAL;
+    if (!aligned16(q_rows->p[d]) || (reinterpret_cast<uintptr_t>(s_rows->p[d]) & 3u))
+      return SRDIT_EALIGN;
+    pe.q[d] = static_cast<uint8_t*>(q_rows->p[d]);
+    pe.s[d] = static_cast<float*>(s_rows->p[d]);
+    pe.flag[d] = static_cast<uint32_t*>(flags->p[d]);
+  }
+  pe.done = done;
+  pe.rank = rank;
+  pe.world = world;
+  return ew::ln_cs_launch<true>(mode, static_cast<const __nv_bfloat16*>(x), ldx, M, K, eps,
+                                static_cast<const __nv_bfloat16*>(ln_weight),
+                                static_cast<const __nv_bfloat16*>(ln_bias), shift, scale, nullptr,
+                                ldq, nullptr, pe, stream);
 }
 
 extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,

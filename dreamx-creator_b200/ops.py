@@ -261,6 +261,21 @@ def tp_allreduce(t, op, *, slots, flags, rank, world, epoch, status=None):
     return t
 
 
+def ln_mod_quant_tp(x, eps=1e-6, *, ln_weight=None, ln_bias=None, shift=None, scale=None,
+                    q_rows, s_rows, flags, done, rank, world, ldq):
+    """srdit_ln_mod_quant_tp: this rank's LN-modulate-quant rows stored into every
+    rank's gather buffer (``q_rows`` / ``s_rows`` peer tables), then ``flags``
+    signalled; ``done`` is a zeroed uint32 tensor of this rank."""
+    _need_cuda(x, ln_weight, ln_bias, shift, scale, done)
+    if x.dtype != torch.bfloat16:
+        raise _lib.SrditError("ln_mod_quant takes bf16")
+    M, K = x.shape
+    _launch("srdit_ln_mod_quant_tp", _ptr(x), _rows(x), M, K, float(eps), _ptr(ln_weight),
+            _ptr(ln_bias), _ptr(shift), _ptr(scale), int(ldq), ctypes.byref(q_rows),
+            ctypes.byref(s_rows), ctypes.byref(flags), _ptr(done), int(rank), int(world),
+            _stream(x.device), kind="ln_mod_quant", work=M * K * 2 + (M * K + 4 * M) * world)
+
+
 def tp_push(src, dst, src2, dst2, *, flags, rank, world, stream=None):
     """srdit_tp_push: copy-engine pushes of src (and src2) to every other rank's
     dst / dst2 addresses (``peer_ptrs`` tables), then signal ``flags``."""

@@ -96,8 +96,14 @@ class PeerComm(TPComm):
 
     N_FLAG_SETS = 3   # gather, rs, ar
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, push="sm"):
+        """``push``: how a rank's LN rows reach the peers' gather buffers -- "sm":
+        the LN kernel stores them over NVLink itself and its last CTA signals;
+        "ce": the copy engines push them on a side stream (one copy per peer)."""
         super().__init__(group)
+        if push not in ("sm", "ce"):
+            raise ValueError(f"push must be 'sm' or 'ce', not {push!r}")
+        self.push = push
         self.key = None
         self.region = None
         self.peer_bases = []
@@ -157,6 +163,7 @@ class PeerComm(TPComm):
         self.ev_ln = torch.cuda.Event()
         self.ev_push = torch.cuda.Event()
         self.pushed = False
+        self.ln_done = torch.zeros(1, dtype=torch.int32, device=device)  # the LN kernel's CTA count
         self.n_rs = ops.fp8_gemm_ctas(M, D)
         self.flags_view = r[self.off["flags"]:self.off["flags"] + 4 * 8 * self.N_FLAG_SETS]
         self.bar = torch.zeros(1, dtype=torch.float32, device=device)
@@ -177,9 +184,19 @@ class PeerComm(TPComm):
 
     # ---- fused steps
     def gather_ln(self, x, eps, **ln):
-        """LN-modulate-quant of this rank's rows into its own gather rows, then the
-        copy engines push them to every other rank on a side stream (the next
-        GEMM starts on the local rows and waits per remote shard)."""
+        """LN-modulate-quant of this rank's rows into every rank's gather buffer
+        (the next GEMM starts on the local rows and waits per remote shard).
+
+        push "sm": one kernel stores the rows over NVLink and signals (row widths
+        that are a multiple of 512, up to 4096). Otherwise, or with push "ce",
+        the kernel writes this rank's own rows and the copy engines push them to
+        every other rank on a side stream."""
+        if self.push == "sm" and self.D % 512 == 0 and self.D <= 4096:
+            ops.ln_mod_quant_tp(x, eps, q_rows=self.t_gq_rows, s_rows=self.t_gs_rows,
+                                flags=self.t_flags[0], done=self.ln_done, rank=self.rank,
+                                world=self.world, ldq=self.D, **ln)
+            self.ag_uses += 1
+            return
         main = torch.cuda.current_stream(x.device)
         if self.pushed:
             main.wait_event(self.ev_push)  # the previous push has read these rows
@@ -192,6 +209,11 @@ class PeerComm(TPComm):
         self.ev_push.record(self.side)
         self.pushed = True
         self.ag_uses += 1
+
+    def rejoin(self, stream):
+        """Make ``stream`` wait for the side stream's last push (push "ce")."""
+        if self.pushed:
+            stream.wait_event(self.ev_push)
 
     def tp_gemm(self, *, peer=False):
         """TpGemm table for a GEMM that reads the gather buffer (waits per remote
@@ -559,7 +581,7 @@ class TPSRDiT(SRDiT):
                             expected=comm.rs_expected(), status=st)
         if update_cache:
             cache.commit(f)
-        torch.cuda.current_stream(dev).wait_event(comm.ev_push)   # side stream rejoins
+        comm.rejoin(torch.cuda.current_stream(dev))   # a side stream's pushes rejoin
         xg = b("tp_xg", (M, D), bf16)
         comm.all_gather(xg, x)
         out = self.head(xg, e, grid)

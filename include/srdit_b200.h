@@ -232,6 +232,26 @@ int srdit_tp_allreduce(const float* in, float* out, int n, int op, const srdit_p
                        uint32_t* status, cudaStream_t stream);
 
 /*
+ * srdit_ln_mod_quant with the tensor-parallel all-gather fused into its
+ * epilogue: x holds this rank's M rows; the e4m3 rows (row pitch ldq) and
+ * per-row scales are stored straight into every rank's gather buffer, at
+ * q_rows->p[d] / s_rows->p[d] (this rank's row block in rank d's buffers,
+ * d = 0..world-1, this rank included). When every row is stored, counter
+ * `rank` of every other rank (flags->p[d] + rank) is incremented with release
+ * semantics at system scope. `done` is a zero-initialised uint32 in this
+ * rank's memory that the kernel uses to find its last CTA (and leaves at 0).
+ * K must be a multiple of 512 (at most 4096).
+ * Replaces: the all-gather before the column-parallel linears of the sharded
+ * block (the reference's DTensor redistribute of the normed activation,
+ * video_refiner/wan/modules/sr_dit/models.py:455-496).
+ */
+int srdit_ln_mod_quant_tp(const void* x, long long ldx, int M, int K, float eps,
+                          const void* ln_weight, const void* ln_bias, const float* shift,
+                          const float* scale, long long ldq, const srdit_peer_ptrs* q_rows,
+                          const srdit_peer_ptrs* s_rows, const srdit_peer_ptrs* flags,
+                          uint32_t* done, int rank, int world, cudaStream_t stream);
+
+/*
  * All-gather push by the copy engines: copies `bytes` from src to dst.p[d]
  * (and, when src2 is given, `bytes2` from src2 to dst2.p[d]) for every rank
  * d != rank, one cudaMemcpyAsync each over NVLink, then a one-thread kernel on

@@ -1,7 +1,8 @@
-"""Tensor-parallel forward (TP=2, NCCL over NVLink) against the single-GPU forward.
+"""Tensor-parallel forward (TP=2) against the single-GPU forward.
 
 Two spawned ranks run the sharded model on one clip -- with the collectives
-fused into the kernels over peer memory, and with NCCL collectives -- a
+fused into the kernels over peer memory (the all-gather stored by the LN
+kernel itself, or pushed by the copy engines), and with NCCL collectives -- a
 cache-refresh forward,
 then a streaming forward over the ring it filled. Rank 0 also runs the same
 seeded weights unsharded (``SRDiT``, which the other GPU tests pin to the CPU
@@ -69,7 +70,11 @@ def _worker(rank, world, port, cfg_kw, grid, fused, out_q, graphs=False):
                 torch.cuda.synchronize()
                 model.check_status()
                 return outs
-        tp_out = run(T.TPSRDiT.random_init(cfg, dev, seed=3, fused=fused))
+        if fused == "ce":   # peer-fused, all-gather pushed by the copy engines
+            tp_model = T.TPSRDiT.random_init(cfg, dev, seed=3, comm=T.PeerComm(push="ce"))
+        else:
+            tp_model = T.TPSRDiT.random_init(cfg, dev, seed=3, fused=fused)
+        tp_out = run(tp_model)
         res = None
         if rank == 0:
             ref_model = M.SRDiT.random_init(cfg, dev, seed=3)
@@ -110,7 +115,7 @@ def _run_tp(world, cfg_kw, grid, fused, graphs=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("fused", [True, False], ids=["peer-fused", "nccl"])
+@pytest.mark.parametrize("fused", [True, "ce", False], ids=["peer-fused", "peer-ce", "nccl"])
 @pytest.mark.parametrize("cfg_kw,grid", [
     (dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16, text_dim=64,
           text_len=16, block_hw=(2, 2), block_radius_hw=(1, 1)), (3, 8, 16)),
