@@ -115,8 +115,10 @@ SRDIT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    for (int i = 0; i < 8; ++i) {
-      if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    // try_wait without a suspend hint: the hardware's own short suspend, which
+    // wakes as soon as the phase completes (a long hint was seen to wake late)
+    for (int i = 0; i < 16; ++i) {
+      if (mbar_try_wait(bar, parity)) return true;
     }
     if (abort_flag && *abort_flag) return false;
     if (global_timer_ns() - t0 > kWaitBudgetNs) {

@@ -422,12 +422,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
+        // the HR walk's next box, as (h-chunk, ring slot): stepped box by box,
+        // so the producer does no integer division per tile
+        int hr_hc = 0, hr_slot = (a.kv_slot0 + r.kv_t0) % a.kv_slots;
         for (int j = 0; j < w.n_tiles && ok; ++j, ++g) {
           const int st = g & 1;
           const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
           const TileInfo ti = tile_info(a, w, j);
           const uint32_t box_bytes = static_cast<uint32_t>(ti.bw * ti.bh * 128);
           const uint32_t bytes = box_bytes * 2u * static_cast<uint32_t>(ti.nbox);
+          int hc_end = hr_hc, slot_end = hr_slot;
           for (int kv = 0; kv < 2; ++kv) {
             uint64_t* emp = kv ? &v_empty[st] : &k_empty[st];
             uint64_t* ful = kv ? &v_full[st] : &k_full[st];
@@ -437,27 +441,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             mbar_arrive_expect_tx(ful, bytes);
             uint8_t* base = smem + (kv ? OFF_V : OFF_K) + st * QKV_TILE_BYTES;
+            int hc = hr_hc, slot = hr_slot;
             for (int bx = 0; bx < ti.nbox; ++bx) {
-              const int gb = ti.box0 + bx;
               int c1, c2, c3;
               const CUtensorMap* map;
               if (ti.anchor) {
                 c1 = r.kw0_a;
-                c2 = r.kh0_a + gb * ti.bh;
+                c2 = r.kh0_a + (ti.box0 + bx) * ti.bh;
                 c3 = ti.frame;
                 map = kv ? &tmVA : &tmKA;
               } else {
-                const int t = gb / w.hr_hchunks, hc = gb % w.hr_hchunks;
                 c1 = r.kw0;
                 c2 = r.kh0 + hc * ti.bh;
-                c3 = (a.kv_slot0 + r.kv_t0 + t) % a.kv_slots;
+                c3 = slot;
                 map = kv ? &tmV : &tmK;
+                if (++hc == w.hr_hchunks) {
+                  hc = 0;
+                  if (++slot == a.kv_slots) slot = 0;
+                }
               }
               for (int h = 0; h < 2; ++h)
                 tma_load_4d(base + h * SLAB + bx * static_cast<int>(box_bytes), map, ful,
                             cur.head * D + h * 64, c1, c2, c3);
             }
+            hc_end = hc;
+            slot_end = slot;
           }
+          hr_hc = hc_end;
+          hr_slot = slot_end;
         }
       }
       // after giving up, let issued loads land before the CTA exits
@@ -502,9 +513,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       auto s_ready = [&]() -> bool {
         if (cs.state != 1 || cs.g >= cp.g + 2) return false;  // score buffer still in use
         const int st = cs.g & 1;
-        if (cs.j == 0 && !mbar_try_wait(&q_full[cs.n & 1], static_cast<uint32_t>(cs.n >> 1) & 1u))
+        if (cs.j == 0 && !mbar_test_wait(&q_full[cs.n & 1], static_cast<uint32_t>(cs.n >> 1) & 1u))
           return false;
-        return mbar_try_wait(&k_full[st], static_cast<uint32_t>(cs.g >> 1) & 1u);
+        return mbar_test_wait(&k_full[st], static_cast<uint32_t>(cs.g >> 1) & 1u);
       };
       auto issue_s = [&]() {
         const int b = cs.n & 1;
@@ -528,10 +539,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       auto pv_ready = [&]() -> bool {
         if (cp.state != 1 || cp.g >= cs.g) return false;  // S_g not issued yet
         const int st = cp.g & 1;
-        if (!mbar_try_wait(p_full, static_cast<uint32_t>(cp.g) & 1u)) return false;
-        if (!mbar_try_wait(&v_full[st], static_cast<uint32_t>(cp.g >> 1) & 1u)) return false;
-        if (cp.j == 0 && !mbar_try_wait(&o_empty[cp.n & 1],
-                                        (static_cast<uint32_t>(cp.n >> 1) & 1u) ^ 1u))
+        if (!mbar_test_wait(p_full, static_cast<uint32_t>(cp.g) & 1u)) return false;
+        if (!mbar_test_wait(&v_full[st], static_cast<uint32_t>(cp.g >> 1) & 1u)) return false;
+        if (cp.j == 0 && !mbar_test_wait(&o_empty[cp.n & 1],
+                                         (static_cast<uint32_t>(cp.n >> 1) & 1u) ^ 1u))
           return false;
         return true;
       };
@@ -571,14 +582,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (did) {
           idle_since = 0;
         } else {
-          // Nothing issuable: sleep on the barrier the next P.V needs (the
-          // softmax is the usual laggard) instead of spinning, so this warp does
-          // not take issue slots from the softmax warp sharing its SM
-          // sub-partition. The suspend hint bounds the sleep; the loop re-checks.
+          // Nothing issuable: wait (hardware-suspended, no hint, so it wakes as
+          // soon as the phase completes) on the barrier the next P.V needs -- the
+          // softmax is the usual laggard -- instead of spinning, so this warp
+          // does not take issue slots from the softmax warps sharing its SM
+          // sub-partition. The loop re-checks both cursors.
           if (cp.state == 1 && cp.g < cs.g)
-            mbar_try_wait_sleep(p_full, static_cast<uint32_t>(cp.g) & 1u, 1000u);
+            mbar_try_wait(p_full, static_cast<uint32_t>(cp.g) & 1u);
           else if (cs.state == 1)
-            mbar_try_wait_sleep(&k_full[cs.g & 1], static_cast<uint32_t>(cs.g >> 1) & 1u, 1000u);
+            mbar_try_wait(&k_full[cs.g & 1], static_cast<uint32_t>(cs.g >> 1) & 1u);
           const uint64_t now = global_timer_ns();
           if (idle_since == 0) {
             idle_since = now;
