@@ -669,19 +669,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool active = __any_sync(0xffffffffu, row_ok);
       const uint32_t o_tmem =
           tmem_base + t_lane + 256u + static_cast<uint32_t>(b * 128 + half * 64);
-      const int n_tiles = rec->w.n_tiles;
+      // what the tile loop needs of the record, in registers (a shared-memory
+      // re-read after every barrier wait would sit on each tile's critical path)
+      const Walk w = rec->w;
+      const int n_tiles = w.n_tiles;
+      const bool full_k = rec->full_k, full_a = rec->full_a, per_frame = rec->r.a_per_frame;
+      const int khL = rec->r.khL, kwL = rec->r.kwL, khL_a = rec->r.khL_a, kwL_a = rec->r.kwL_a;
       float m_i = neg_inf, l_i = 0.f;
       for (int j = 0; j < n_tiles; ++j, ++g) {
         const int st = g & 1;
         const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
-        const TileInfo ti = tile_info(a, rec->w, j);
+        const TileInfo ti = tile_info(a, w, j);
         const int nchunks = (ti.n16 + 31) >> 5;
         // validity of this thread's 64 columns (bit i of vm[qq] = column
         // (2*half + qq)*32 + i); a per-frame anchor tile is invisible to the
         // other frames' rows; columns past the tile's MMA extent are never read
         uint32_t vm[2];
-        const bool sees = !(ti.anchor && rec->r.a_per_frame) || (t_row == ti.frame);
-        if (ti.anchor ? rec->full_a : rec->full_k) {
+        const bool sees = !(ti.anchor && per_frame) || (t_row == ti.frame);
+        if (ti.anchor ? full_a : full_k) {
           // every box row and column lies inside the window: only the tile's
           // row count masks
 #pragma unroll
@@ -690,9 +695,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             vm[qq] = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
           }
         } else {
-          const int khl = ti.anchor ? rec->r.khL_a : rec->r.khL;
-          const int kwl = ti.anchor ? rec->r.kwL_a : rec->r.kwL;
-          const int hch = ti.anchor ? rec->w.a_hchunks : rec->w.hr_hchunks;
+          const int khl = ti.anchor ? khL_a : khL;
+          const int kwl = ti.anchor ? kwL_a : kwL;
+          const int hch = ti.anchor ? w.a_hchunks : w.hr_hchunks;
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
             const int c = (2 * half + qq) * 32 + lane;

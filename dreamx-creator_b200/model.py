@@ -444,7 +444,8 @@ class SRDiT:
     # ------------------------------------------------------------------ forward
     def forward_chunk(self, latent, t, context, *, cache: KVRing | None = None,
                       t_offset=0, update_cache=False, anchor_kv=None, anchor_align="frame",
-                      return_kv=False, ctx_emb=None, text: TextCache | None = None):
+                      return_kv=False, ctx_emb=None, text: TextCache | None = None,
+                      kv_only=False):
         """One streaming forward over a chunk (``_forward_inference`` for one sample).
 
         latent [C_in, f, H, W]; ``cache`` holds the previous chunks' K/V (read in
@@ -453,9 +454,16 @@ class SRDiT:
         [f*h*w, D] bf16 LQ anchor (never cached). ``return_kv`` returns the
         per-layer roped K / V of this chunk (the anchor harvest). ``text``: the
         context's ``text_cache`` (else the text embedding and cross K/V are
-        computed here, as the reference does every forward).
+        computed here, as the reference does every forward). ``kv_only=True``
+        (a cache-refresh forward whose prediction is discarded, as the refiner's
+        t=0 pass is): the last block stops once its K/V are in the ring, only its
+        k / v columns are projected, and nothing is returned -- the ring ends up
+        exactly as after the full forward.
         Returns the refined prediction [C_out, f, H, W] bf16 (and the K/V list).
         """
+        if kv_only and (return_kv or not update_cache):
+            raise _lib.SrditError("kv_only is for a cache-refresh forward (update_cache=True, "
+                                  "no return_kv)")
         c = self.cfg
         ops = self.ops
         if not self.graph_capture:
@@ -493,6 +501,13 @@ class SRDiT:
             kr, vr = cache.k[li], cache.v[li]
             # --- self attention
             ops.ln_mod_quant(x, c.eps, shift=em[0], scale=em[1], q=xq, qscale=xs)
+            if kv_only and li == len(self.layers) - 1:
+                # the refresh pass's last block: its K / V into the ring, nothing else
+                ops.fp8_gemm(xq, xs, ly.w_qkv[D:], ly.s_qkv[D:], ly.b_qkv[D:], qkv[:, D:])
+                ops.rms_rope(qkv[:, D:2 * D], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
+                             n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
+                             t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * D:], v_dst=vr)
+                break
             ops.fp8_gemm(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv)
             ops.rms_rope(qkv[:, :D], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
                          grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev)
@@ -536,6 +551,8 @@ class SRDiT:
                          gate=em[5])
         if update_cache:
             cache.commit(f)
+        if kv_only:
+            return None
         out = self.head(x, e, grid)
         return (out, kv_out) if return_kv else out
 

@@ -101,8 +101,9 @@ class RefinerStream:
                                t_offset=self.t_offset, anchor_kv=anchor, text=self.text)
         sigma = self.denoise_t / self.ntt
         x0 = (noisy_chunk.double() - sigma * flow.double()).to(noisy_chunk.dtype)
+        # the refresh pass only fills the ring: its prediction is discarded
         m.forward_chunk(x0, self.context_noise, self.context, cache=self.cache,
-                        t_offset=self.t_offset, update_cache=True, text=self.text)
+                        t_offset=self.t_offset, update_cache=True, text=self.text, kv_only=True)
         self.t_offset += noisy_chunk.shape[1]
         return x0
 

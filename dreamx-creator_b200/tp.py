@@ -335,14 +335,17 @@ class TPSRDiT(SRDiT):
     # ------------------------------------------------------------------ forward
     def forward_chunk(self, latent, t, context, *, cache=None, t_offset=0, update_cache=False,
                       anchor_kv=None, anchor_align="frame", return_kv=False, ctx_emb=None,
-                      text=None):
+                      text=None, kv_only=False):
         """``SRDiT.forward_chunk`` on this rank's shard; same arguments and result
         (``anchor_kv`` / the returned K/V hold this rank's heads)."""
+        if kv_only and (return_kv or not update_cache):
+            raise _lib.SrditError("kv_only is for a cache-refresh forward (update_cache=True, "
+                                  "no return_kv)")
         if self.fused:
             return self._forward_fused(latent, t, context, cache=cache, t_offset=t_offset,
                                        update_cache=update_cache, anchor_kv=anchor_kv,
                                        anchor_align=anchor_align, return_kv=return_kv,
-                                       ctx_emb=ctx_emb, text=text)
+                                       ctx_emb=ctx_emb, text=text, kv_only=kv_only)
         c = self.cfg
         ops = self.ops
         if not self.graph_capture:
@@ -404,6 +407,16 @@ class TPSRDiT(SRDiT):
             # --- self attention
             ops.ln_mod_quant(x, c.eps, shift=em[0], scale=em[1], q=xq_l, qscale=xs_l)
             gather_quantised()
+            if kv_only and li == len(self.layers) - 1:
+                # the refresh pass's last block: its K / V into the ring, nothing else
+                ops.fp8_gemm(xq, xs, ly.w_qkv[Dl:], ly.s_qkv[Dl:], ly.b_qkv[Dl:], qkv[:, Dl:])
+                ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
+                comm.all_reduce_sum(ss[M:])
+                ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L,
+                             slot0=slot_cur, n_slots=cache.cap, cos=cos, sin=sin, grid_h=h,
+                             grid_w=w, t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:],
+                             v_dst=vr, ss=ss[M:], norm_width=D)
+                break
             ops.fp8_gemm(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv)
             ops.row_reduce(qkv[:, :Dl], "sumsq", out=ss[:M])
             ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
@@ -458,13 +471,15 @@ class TPSRDiT(SRDiT):
             ops.residual(x, y_l, bias=ly.b_f2, gate=em[5])
         if update_cache:
             cache.commit(f)
+        if kv_only:
+            return None
         xg = b("tp_xg", (M, D), bf16)
         comm.all_gather(xg, x)
         out = self.head(xg, e, grid)
         return (out, kv_out) if return_kv else out
 
     def _forward_fused(self, latent, t, context, *, cache, t_offset, update_cache, anchor_kv,
-                       anchor_align, return_kv, ctx_emb, text=None):
+                       anchor_align, return_kv, ctx_emb, text=None, kv_only=False):
         """The sharded block with its collectives fused into the kernels: each
         rank's LN-quant rows are pushed by the copy engines into every rank's
         gather buffer and the next GEMM waits per remote shard (all-gather);
@@ -526,6 +541,17 @@ class TPSRDiT(SRDiT):
             kr, vr = cache.k[li], cache.v[li]
             # --- self attention
             comm.gather_ln(x, c.eps, shift=em[0], scale=em[1])
+            if kv_only and li == len(self.layers) - 1:
+                # the refresh pass's last block: its K / V into the ring, nothing else
+                ops.fp8_gemm_tp(xq, xs, ly.w_qkv[Dl:], ly.s_qkv[Dl:], ly.b_qkv[Dl:],
+                                qkv[:, Dl:], tp=comm.tp_gemm(), status=st)
+                ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
+                comm.allreduce(ss[M:], "sum", st)
+                ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L,
+                             slot0=slot_cur, n_slots=cache.cap, cos=cos, sin=sin, grid_h=h,
+                             grid_w=w, t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:],
+                             v_dst=vr, ss=ss[M:], norm_width=D)
+                break
             ops.fp8_gemm_tp(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv, tp=comm.tp_gemm(),
                             status=st)
             ops.row_reduce(qkv[:, :Dl], "sumsq", out=ss[:M])
@@ -582,6 +608,8 @@ class TPSRDiT(SRDiT):
         if update_cache:
             cache.commit(f)
         comm.rejoin(torch.cuda.current_stream(dev))   # a side stream's pushes rejoin
+        if kv_only:
+            return None
         xg = b("tp_xg", (M, D), bf16)
         comm.all_gather(xg, x)
         out = self.head(xg, e, grid)

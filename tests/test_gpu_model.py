@@ -127,3 +127,32 @@ def test_graph_replay_matches_eager(srdit, mods, cuda_device):
             assert len(stream._graphs) >= 2   # later chunks really replayed
     for a, b in zip(outs[False], outs[True]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("geom", [dict(), dict(block_hw=(8, 8), block_radius_hw=(0, 0))])
+def test_refresh_kv_only_fills_the_same_ring(srdit, mods, cuda_device, geom):
+    """The refresh pass with kv_only=True (its last block stops after writing
+    K / V, no head) leaves the ring bit-identical to the full refresh forward."""
+    M, _ = mods
+    cfg = small_cfg(M, **geom)
+    sd = random_sd(M, cfg, seed=6)
+    g = torch.Generator().manual_seed(11)
+    ctx = torch.randn(16, 64, generator=g).to(torch.bfloat16).to(cuda_device)
+    hw = (8, 12) if not geom else (16, 24)
+    lats = [torch.randn(16, 3, *hw, generator=g).to(torch.bfloat16).to(cuda_device)
+            for _ in range(2)]
+    rings = []
+    for kv_only in (False, True):
+        model = M.SRDiT.from_state_dict(cfg, sd, cuda_device)
+        ring = model.new_cache(hw[0] * hw[1] // 4)
+        for i, lat in enumerate(lats):   # a second chunk attends the first one's cache
+            out = model.forward_chunk(lat, 0.0, ctx, cache=ring, t_offset=3 * i,
+                                      update_cache=True, kv_only=kv_only)
+            assert (out is None) == kv_only
+        torch.cuda.synchronize()
+        model.check_status()
+        rings.append(ring)
+    a, b = rings
+    assert (a.start, a.frames) == (b.start, b.frames)
+    for la, lb in zip(a.k + a.v, b.k + b.v):
+        assert torch.equal(la, lb)

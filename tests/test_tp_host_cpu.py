@@ -111,6 +111,72 @@ def test_tp2_gloo_matches_one_rank():
     assert min(cos) >= 0.999, cos
 
 
+def _kv_only_worker(rank, world, port, out_q):
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+    try:
+        torch.set_num_threads(2)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=120))
+        importlib.import_module("dreamx-creator_b200")
+        M = importlib.import_module("dreamx-creator_b200.model")
+        T = importlib.import_module("dreamx-creator_b200.tp")
+        from tests import cpu_ops
+
+        class CpuTP(T.TPSRDiT):
+            ops = cpu_ops
+            require_cuda = False
+
+        cfg = M.SRDiTConfig(**CFG)
+        f, h, w = GRID
+        g = torch.Generator().manual_seed(7)
+        ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(torch.bfloat16)
+        lat = torch.randn(cfg.in_dim, f, 2 * h, 2 * w, generator=g).to(torch.bfloat16)
+        sd = M.SRDiT.seeded_state_dict(cfg, "cpu", 3)
+        rings = []
+        for kv_only in (False, True):
+            model = CpuTP(cfg, sd, "cpu", fused=False)
+            ring = model.new_cache(h * w)
+            out = model.forward_chunk(lat, 0.0, ctx, cache=ring, update_cache=True,
+                                      kv_only=kv_only)
+            assert (out is None) == kv_only
+            rings.append(ring)
+        same = all(torch.equal(x, y) for x, y in zip(rings[0].k + rings[0].v,
+                                                       rings[1].k + rings[1].v))
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, same, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        import traceback
+        out_q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+
+
+def test_tp2_refresh_kv_only_fills_the_same_ring():
+    """Two gloo ranks: the kv_only refresh (last block stops after its K / V,
+    no head, no final all-gather) leaves every rank's ring slice equal to the
+    full refresh forward's."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_kv_only_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, same, err = q.get(timeout=300)
+            results[rank] = (same, err)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    errs = [e for _, e in results.values() if e]
+    assert not errs, errs
+    assert all(same for same, _ in results.values()), results
+
+
 def test_single_rank_model_refuses_cpu():
     """Without the test double and without CUDA the model does not build."""
     import torch
