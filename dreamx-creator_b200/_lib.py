@@ -78,6 +78,9 @@ SIGNATURES = {
     "srdit_ln_mod_quant_tp": [c_vp, c_ll, c_int, c_int, c_float, c_vp, c_vp, c_vp, c_vp, c_ll,
                               ctypes.POINTER(PeerPtrs), ctypes.POINTER(PeerPtrs),
                               ctypes.POINTER(PeerPtrs), c_vp, c_int, c_int, c_vp],
+    "srdit_ln_mod_quant_tp_static": [c_vp, c_ll, c_int, c_int, c_float, c_vp, c_vp, c_vp, c_vp,
+                                     c_ll, ctypes.POINTER(PeerPtrs), ctypes.POINTER(PeerPtrs),
+                                     ctypes.POINTER(PeerPtrs), c_int, c_int, c_vp],
     "srdit_tp_push": [c_vp, ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, c_vp,
                       ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, ctypes.POINTER(PeerPtrs),
                       c_int, c_int, c_vp],

@@ -1069,6 +1069,34 @@ extern "C" int srdit_ln_mod_quant_tp(const void* x, long long ldx, int M, int K,
                                 ldq, nullptr, pe, stream);
 }
 
+// The last-CTA counter of srdit_ln_mod_quant_tp_static: a file-scope device
+// array (one instance per device), so that entry point allocates nothing.
+// Element 0 is the counter; the kernel leaves it at 0 after every launch.
+__device__ __align__(256) uint32_t g_ln_tp_done[64];
+
+extern "C" int srdit_ln_mod_quant_tp_static(const void* x, long long ldx, int M, int K,
+                                            float eps, const void* ln_weight, const void* ln_bias,
+                                            const float* shift, const float* scale,
+                                            long long ldq, const srdit_peer_ptrs* q_rows,
+                                            const srdit_peer_ptrs* s_rows,
+                                            const srdit_peer_ptrs* flags, int rank, int world,
+                                            cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices) return SRDIT_EINVAL;
+  // the counter's address on each device, looked up once per device
+  static uint32_t* done_addr[kMaxDevices] = {};
+  if (!done_addr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_ln_tp_done);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    done_addr[dev] = static_cast<uint32_t*>(ptr);
+  }
+  return srdit_ln_mod_quant_tp(x, ldx, M, K, eps, ln_weight, ln_bias, shift, scale, ldq, q_rows,
+                               s_rows, flags, done_addr[dev], rank, world, stream);
+}
+
 extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
                               const void* weight, float eps, void* dst, long long ld_dst,
                               int frame_tokens, int slot0, int n_slots, const double* cos_tab,

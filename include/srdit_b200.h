@@ -252,6 +252,21 @@ int srdit_ln_mod_quant_tp(const void* x, long long ldx, int M, int K, float eps,
                           uint32_t* done, int rank, int world, cudaStream_t stream);
 
 /*
+ * srdit_ln_mod_quant_tp without the `done` argument: the last-CTA counter is a
+ * file-scope device array of the library (one per device, its address looked
+ * up once per device with cudaGetSymbolAddress), so this entry point
+ * allocates nothing and needs no zeroed scratch from the caller. Launches of
+ * it on one device must not overlap (they share the counter); the kernel
+ * leaves the counter at 0 after each launch.
+ */
+int srdit_ln_mod_quant_tp_static(const void* x, long long ldx, int M, int K, float eps,
+                                 const void* ln_weight, const void* ln_bias, const float* shift,
+                                 const float* scale, long long ldq,
+                                 const srdit_peer_ptrs* q_rows, const srdit_peer_ptrs* s_rows,
+                                 const srdit_peer_ptrs* flags, int rank, int world,
+                                 cudaStream_t stream);
+
+/*
  * All-gather push by the copy engines: copies `bytes` from src to dst.p[d]
  * (and, when src2 is given, `bytes2` from src2 to dst2.p[d]) for every rank
  * d != rank, one cudaMemcpyAsync each over NVLink, then a one-thread kernel on
