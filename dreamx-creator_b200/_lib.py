@@ -56,6 +56,11 @@ class TpGemm(ctypes.Structure):
                 ("rs_flags", c_vp * SRDIT_MAX_RANKS)]
 
 
+class VRing(ctypes.Structure):
+    _fields_ = [("ring", c_vp), ("ld", c_ll), ("col0", c_int), ("frame_tokens", c_int),
+                ("slot0", c_int), ("n_slots", c_int)]
+
+
 # name -> argtypes (every function returns int)
 SIGNATURES = {
     "srdit_version": [],
@@ -71,6 +76,8 @@ SIGNATURES = {
     "srdit_fp8_gemm_tp": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                           c_int, c_int, c_vp, ctypes.POINTER(TpGemm), c_vp, c_vp],
     "srdit_fp8_gemm_ctas": [c_int, c_int],
+    "srdit_fp8_gemm_vring": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
+                             c_int, c_int, ctypes.POINTER(VRing), c_vp, c_vp],
     "srdit_residual_tp": [c_vp, c_ll, c_int, c_int, c_vp, c_int, c_ll, c_ll, c_vp, c_vp, c_vp,
                           ctypes.c_uint32, c_vp, c_vp],
     "srdit_tp_allreduce": [c_vp, c_vp, c_int, c_int, ctypes.POINTER(PeerPtrs),

@@ -65,6 +65,10 @@ struct Params {
   const float* gate;
   float* row_amax;
   uint32_t* status;
+  // STORE epilogue, optional (v_col0 >= 0): columns [v_col0, N) go to a frame
+  // ring (tensor map pm.m[0]) instead: output row r = f * v_frame + s lands in
+  // ring row ((v_slot0 + f) % v_nslots) * v_frame + s, column c - v_col0
+  int v_col0, v_frame, v_slot0, v_nslots;
 };
 
 // tanh on the SFU (PTX tanh.approx.f32, max relative error about 2^-11). The
@@ -376,6 +380,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           if constexpr (EPI == EPI_PEER) {
             const int owner = row0 / tp.rows_per_rank;  // rows_per_rank % 32 == 0
             tma_store_2d(&pm.m[owner], buf, n0 + ch * 64, row0 - owner * tp.rows_per_rank);
+          } else if (EPI == EPI_STORE && p.v_col0 >= 0 && n0 + ch * 64 >= p.v_col0) {
+            // a V chunk (v_col0 % 64 == 0, v_frame % 32 == 0): into its ring slot
+            const int f = row0 / p.v_frame, sp = row0 - f * p.v_frame;
+            tma_store_2d(&pm.m[0], buf, n0 + ch * 64 - p.v_col0,
+                         ((p.v_slot0 + f) % p.v_nslots) * p.v_frame + sp);
           } else {
             tma_store_2d(&tmO, buf, n0 + ch * 64, row0);
           }
@@ -472,7 +481,8 @@ static int fp8_gemm_impl(const void* a_fp8, const float* a_scale, const void* b_
                          const float* b_scale, const void* bias, void* out, int M, int N, int K,
                          int lda, int ldb, int ldo, int epilogue, const void* residual, int ldr,
                          const float* gate, float* row_amax, uint32_t* status,
-                         const srdit_tp_gemm* tpa, cudaStream_t stream) {
+                         const srdit_tp_gemm* tpa, cudaStream_t stream,
+                         const srdit_v_ring* vr = nullptr) {
   if (M <= 0 || N <= 0 || K <= 0) return (M == 0 || N == 0) ? 0 : SRDIT_EINVAL;
   if (!a_fp8 || !a_scale || !b_fp8 || !b_scale) return SRDIT_EINVAL;
   if (epilogue != EPI_PEER && !out) return SRDIT_EINVAL;
@@ -535,6 +545,24 @@ static int fp8_gemm_impl(const void* a_fp8, const float* a_scale, const void* b_
   }
 
   gemm::Params p;
+  p.v_col0 = -1;
+  p.v_frame = p.v_slot0 = 0;
+  p.v_nslots = 1;
+  if (vr) {
+    if (epilogue != EPI_STORE || tpa) return SRDIT_EINVAL;
+    if (!vr->ring || vr->col0 < 0 || vr->col0 >= N || (vr->col0 % 64) || vr->frame_tokens <= 0 ||
+        (vr->frame_tokens % 32) || M % vr->frame_tokens || vr->n_slots <= 0 || vr->slot0 < 0 ||
+        vr->ld < N - vr->col0 || (vr->ld % 8) ||
+        static_cast<long long>(M / vr->frame_tokens) > vr->n_slots)
+      return SRDIT_EINVAL;
+    rc = make_tmap_2d(&pm.m[0], vr->ring, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N - vr->col0,
+                      static_cast<long long>(vr->n_slots) * vr->frame_tokens, vr->ld, 64, 32);
+    if (rc) return rc;
+    p.v_col0 = vr->col0;
+    p.v_frame = vr->frame_tokens;
+    p.v_slot0 = vr->slot0;
+    p.v_nslots = vr->n_slots;
+  }
   p.M = M;
   p.N = N;
   p.K = K;
@@ -563,6 +591,16 @@ extern "C" int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const voi
   if (epilogue == EPI_PEER) return SRDIT_EINVAL;  // the peer epilogue needs srdit_fp8_gemm_tp
   return fp8_gemm_impl(a_fp8, a_scale, b_fp8, b_scale, bias, out, M, N, K, lda, ldb, ldo,
                        epilogue, residual, ldr, gate, row_amax, status, nullptr, stream);
+}
+
+extern "C" int srdit_fp8_gemm_vring(const void* a_fp8, const float* a_scale, const void* b_fp8,
+                                    const float* b_scale, const void* bias, void* out, int M,
+                                    int N, int K, int lda, int ldb, int ldo,
+                                    const srdit_v_ring* v_ring, uint32_t* status,
+                                    cudaStream_t stream) {
+  if (!v_ring) return SRDIT_EINVAL;
+  return fp8_gemm_impl(a_fp8, a_scale, b_fp8, b_scale, bias, out, M, N, K, lda, ldb, ldo,
+                       EPI_STORE, nullptr, 0, nullptr, nullptr, status, nullptr, stream, v_ring);
 }
 
 extern "C" int srdit_fp8_gemm_tp(const void* a_fp8, const float* a_scale, const void* b_fp8,

@@ -493,6 +493,7 @@ class SRDiT:
         ckv = self._buf("ckv", (Lc, 2 * D), bf16)
         ctxq, ctxs = ops.quant_rowwise(ctx) if text is None else (None, None)
         mods = torch.stack([ly.modulation for ly in self.layers]) + e0[None]   # [layers, 6, D]
+        v_direct = L % 32 == 0 and D % 64 == 0   # the GEMM can store V into ring slots
         kv_out = [] if return_kv else None
         st = self.status
         cos, sin = self.rope_cos, self.rope_sin
@@ -501,19 +502,21 @@ class SRDiT:
             kr, vr = cache.k[li], cache.v[li]
             # --- self attention
             ops.ln_mod_quant(x, c.eps, shift=em[0], scale=em[1], q=xq, qscale=xs)
-            if kv_only and li == len(self.layers) - 1:
-                # the refresh pass's last block: its K / V into the ring, nothing else
-                ops.fp8_gemm(xq, xs, ly.w_qkv[D:], ly.s_qkv[D:], ly.b_qkv[D:], qkv[:, D:])
-                ops.rms_rope(qkv[:, D:2 * D], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
-                             n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                             t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * D:], v_dst=vr)
-                break
-            ops.fp8_gemm(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv)
-            ops.rms_rope(qkv[:, :D], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
-                         grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev)
+            # q | k | v projection; V goes straight into its ring slot (whole 32-row
+            # store boxes per frame), else the K kernel copies it there
+            last_kv = kv_only and li == len(self.layers) - 1
+            c0 = D if last_kv else 0   # the refresh pass's last block: k | v only
+            v_ring = (vr, 2 * D - c0, L, slot_cur, cache.cap) if v_direct else None
+            ops.fp8_gemm(xq, xs, ly.w_qkv[c0:], ly.s_qkv[c0:], ly.b_qkv[c0:], qkv[:, c0:],
+                         v_ring=v_ring)
+            vcopy = {} if v_direct else dict(v_src=qkv[:, 2 * D:], v_dst=vr)
             ops.rms_rope(qkv[:, D:2 * D], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * D:], v_dst=vr)
+                         t_offset_dev=self.t_offset_dev, **vcopy)
+            if last_kv:
+                break   # its K / V are in the ring: nothing else of the block is used
+            ops.rms_rope(qkv[:, :D], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
+                         grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev)
             ak = av = None
             if anchor_kv is not None:
                 ak, av = anchor_kv[li]

@@ -66,8 +66,12 @@ def _rows(t: torch.Tensor):
 
 
 def fp8_gemm(a_fp8, a_scale, w_fp8, w_scale, bias=None, out=None, *, epilogue="store",
-             residual=None, gate=None, row_amax=None, status=None):
-    """out[M,N] = epilogue(a_fp8 @ w_fp8^T * a_scale[:,None] * w_scale[None,:] + bias)."""
+             residual=None, gate=None, row_amax=None, status=None, v_ring=None):
+    """out[M,N] = epilogue(a_fp8 @ w_fp8^T * a_scale[:,None] * w_scale[None,:] + bias).
+
+    ``v_ring`` (STORE only): (ring [slots*frame_tokens, W] bf16, col0, frame_tokens,
+    slot0, n_slots) -- columns [col0, N) go into the frame ring (output frame f
+    into slot (slot0 + f) % n_slots) instead of ``out``."""
     _need_cuda(a_fp8, a_scale, w_fp8, w_scale, bias, out, residual, gate, row_amax)
     if a_fp8.dtype != torch.float8_e4m3fn or w_fp8.dtype != torch.float8_e4m3fn:
         raise _lib.SrditError("fp8_gemm operands must be float8_e4m3fn")
@@ -83,6 +87,20 @@ def fp8_gemm(a_fp8, a_scale, w_fp8, w_scale, bias=None, out=None, *, epilogue="s
             raise _lib.SrditError(f"{nm} must be contiguous float32")
     if bias is not None and (bias.dtype != torch.bfloat16 or not bias.is_contiguous()):
         raise _lib.SrditError("bias must be contiguous bf16")
+    if v_ring is not None:
+        if epilogue != "store":
+            raise _lib.SrditError("v_ring needs the store epilogue")
+        ring, col0, frame_tokens, slot0, n_slots = v_ring
+        _need_cuda(ring)
+        if ring.dtype != torch.bfloat16:
+            raise _lib.SrditError("the V ring is bf16")
+        vr = _lib.VRing(ctypes.c_void_p(ring.data_ptr()), _rows(ring), int(col0),
+                        int(frame_tokens), int(slot0), int(n_slots))
+        _launch("srdit_fp8_gemm_vring", _ptr(a_fp8), _ptr(a_scale), _ptr(w_fp8), _ptr(w_scale),
+                _ptr(bias), _ptr(out), M, N, K, _rows(a_fp8), _rows(w_fp8), _rows(out),
+                ctypes.byref(vr), _ptr(status), _stream(a_fp8.device), kind="fp8_gemm",
+                work=2 * M * N * K)
+        return out
     ldr = _rows(residual) if residual is not None else 0
     _launch("srdit_fp8_gemm", _ptr(a_fp8), _ptr(a_scale), _ptr(w_fp8), _ptr(w_scale),
             _ptr(bias), _ptr(out), M, N, K, _rows(a_fp8), _rows(w_fp8), _rows(out),

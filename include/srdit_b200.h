@@ -82,6 +82,27 @@ int srdit_fp8_gemm(const void* a_fp8, const float* a_scale, const void* b_fp8,
                    const float* gate, float* row_amax, uint32_t* status, cudaStream_t stream);
 
 /*
+ * srdit_fp8_gemm (STORE epilogue) whose columns [col0, N) are written into a
+ * frame ring instead of `out`: output row r = f * frame_tokens + s (frame f
+ * of the chunk, token s) goes to ring row ((slot0 + f) % n_slots) *
+ * frame_tokens + s, column c - col0 (row stride ld). `out` receives columns
+ * [0, col0). col0 a multiple of 64, frame_tokens a multiple of 32 dividing M.
+ * Used for the fused q|k|v projection: V lands in its KV-cache slot directly.
+ * Replaces: the V half of the reference's cache append
+ * (video_refiner/wan/modules/sr_dit/attention.py:964-974).
+ */
+typedef struct srdit_v_ring {
+  void* ring;          /* bf16 [n_slots * frame_tokens, ld] */
+  long long ld;
+  int col0, frame_tokens, slot0, n_slots;
+} srdit_v_ring;
+
+int srdit_fp8_gemm_vring(const void* a_fp8, const float* a_scale, const void* b_fp8,
+                         const float* b_scale, const void* bias, void* out, int M, int N, int K,
+                         int lda, int ldb, int ldo, const srdit_v_ring* v_ring, uint32_t* status,
+                         cudaStream_t stream);
+
+/*
  * Tensor-parallel form of srdit_fp8_gemm (M = world * rows_per_rank rows).
  *  - ag_flags (optional): this rank's all-gather counters [world]; the rows of
  *    A (and a_scale) owned by another rank s are complete once ag_flags[s]

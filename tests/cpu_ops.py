@@ -41,7 +41,15 @@ def ln_mod_quant(x, eps=1e-6, *, ln_weight=None, ln_bias=None, shift=None, scale
 
 
 def fp8_gemm(a_fp8, a_scale, w_fp8, w_scale, bias=None, out=None, *, epilogue="store",
-             residual=None, gate=None, row_amax=None, status=None):
+             residual=None, gate=None, row_amax=None, status=None, v_ring=None):
+    if v_ring is not None:   # columns [col0, N) into the frame ring, the rest into out
+        ring, col0, ft, slot0, n_slots = v_ring
+        full = fp8_gemm(a_fp8, a_scale, w_fp8, w_scale, bias)
+        out[:, :col0].copy_(full[:, :col0])
+        rows = torch.arange(full.shape[0])
+        f, sp = rows // ft, rows % ft
+        ring[((slot0 + f) % n_slots) * ft + sp] = full[:, col0:]
+        return out
     y = (a_fp8.double() @ w_fp8.double().t()) * a_scale.double()[:, None] * w_scale.double()
     if bias is not None:
         y = y + bias.double()

@@ -238,3 +238,30 @@ def test_winattn_deterministic(srdit, cuda_device):
         pre_cache_k=d(ins["ck"]), pre_cache_v=d(ins["cv"]), attn_impl="b200", block_t=3,
         block_hw=(4, 4), block_radius_hw=(2, 2))[0] for _ in range(2)]
     assert torch.equal(outs[0], outs[1])
+
+
+def test_fp8_gemm_v_ring(srdit, cuda_device):
+    """The q|k|v GEMM with its V columns stored into ring slots: bit-identical to
+    the plain GEMM's columns, frame f in slot (slot0 + f) % n_slots."""
+    M, N, K, ft, cap, slot0 = 3 * 256, 3 * 384, 512, 256, 5, 3
+    g = torch.Generator().manual_seed(12)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    aq, as_ = onum.quantize_rowwise(a)
+    wq, ws = onum.fp8_linear_weights(w)
+    bias = (torch.randn(N, generator=g) * 0.01).to(torch.bfloat16)
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    plain = srdit.ops.fp8_gemm(d(aq), d(as_.reshape(-1).contiguous()), d(wq), d(ws), d(bias))
+    out = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda_device)
+    ring = torch.zeros(cap * ft, N - 2 * 384, dtype=torch.bfloat16, device=cuda_device)
+    srdit.ops.fp8_gemm(d(aq), d(as_.reshape(-1).contiguous()), d(wq), d(ws), d(bias), out,
+                       v_ring=(ring, 2 * 384, ft, slot0, cap))
+    torch.cuda.synchronize()
+    assert torch.equal(out[:, :768], plain[:, :768])
+    assert not bool(out[:, 768:].any())   # V columns never reach out
+    for f in range(M // ft):
+        s = (slot0 + f) % cap
+        assert torch.equal(ring[s * ft:(s + 1) * ft], plain[f * ft:(f + 1) * ft, 768:])
+    used = {(slot0 + f) % cap for f in range(M // ft)}
+    for s in set(range(cap)) - used:
+        assert not bool(ring[s * ft:(s + 1) * ft].any())
