@@ -49,16 +49,16 @@ class PeerPtrs(ctypes.Structure):
     _fields_ = [("p", c_vp * SRDIT_MAX_RANKS)]
 
 
+class VRing(ctypes.Structure):
+    _fields_ = [("ring", c_vp), ("ld", c_ll), ("col0", c_int), ("frame_tokens", c_int),
+                ("slot0", c_int), ("n_slots", c_int)]
+
+
 class TpGemm(ctypes.Structure):
     _fields_ = [("ag_flags", c_vp), ("ag_expected", ctypes.c_uint32),
                 ("rows_per_rank", c_int), ("rank", c_int), ("world", c_int),
                 ("rs_slot", c_vp * SRDIT_MAX_RANKS), ("ld_rs", c_ll),
-                ("rs_flags", c_vp * SRDIT_MAX_RANKS)]
-
-
-class VRing(ctypes.Structure):
-    _fields_ = [("ring", c_vp), ("ld", c_ll), ("col0", c_int), ("frame_tokens", c_int),
-                ("slot0", c_int), ("n_slots", c_int)]
+                ("rs_flags", c_vp * SRDIT_MAX_RANKS), ("v_ring", ctypes.POINTER(VRing))]
 
 
 # name -> argtypes (every function returns int)

@@ -548,8 +548,9 @@ static int fp8_gemm_impl(const void* a_fp8, const float* a_scale, const void* b_
   p.v_col0 = -1;
   p.v_frame = p.v_slot0 = 0;
   p.v_nslots = 1;
+  if (!vr && tpa) vr = tpa->v_ring;
   if (vr) {
-    if (epilogue != EPI_STORE || tpa) return SRDIT_EINVAL;
+    if (epilogue != EPI_STORE) return SRDIT_EINVAL;
     if (!vr->ring || vr->col0 < 0 || vr->col0 >= N || (vr->col0 % 64) || vr->frame_tokens <= 0 ||
         (vr->frame_tokens % 32) || M % vr->frame_tokens || vr->n_slots <= 0 || vr->slot0 < 0 ||
         vr->ld < N - vr->col0 || (vr->ld % 8) ||

@@ -33,6 +33,8 @@ issues the same collectives in the same order.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -215,10 +217,16 @@ class PeerComm(TPComm):
         if self.pushed:
             stream.wait_event(self.ev_push)
 
-    def tp_gemm(self, *, peer=False):
+    def tp_gemm(self, *, peer=False, v_ring=None):
         """TpGemm table for a GEMM that reads the gather buffer (waits per remote
-        shard) or stores its partial into the owners' rs slots (peer=True)."""
+        shard) or stores its partial into the owners' rs slots (peer=True).
+        ``v_ring``: (ring, col0, frame_tokens, slot0, n_slots), columns [col0, N)
+        of a gathered-input GEMM into the frame ring."""
         t = _lib.TpGemm()
+        if v_ring is not None:
+            ring, col0, ft, slot0, n_slots = v_ring
+            t.v_ring = ctypes.pointer(_lib.VRing(ctypes.c_void_p(ring.data_ptr()), ring.stride(0),
+                                                 int(col0), int(ft), int(slot0), int(n_slots)))
         t.rows_per_rank, t.rank, t.world = self.Ml, self.rank, self.world
         if peer:
             t.ag_flags = None
@@ -387,6 +395,7 @@ class TPSRDiT(SRDiT):
         st = self.status
         cos, sin = self.rope_cos, self.rope_sin
         slot_cur = S.slot_cur
+        v_direct = L % 32 == 0 and Dl % 64 == 0   # the GEMM can store V into ring slots
 
         def gather_quantised():
             comm.all_gather(xq, xq_l)
@@ -407,17 +416,21 @@ class TPSRDiT(SRDiT):
             # --- self attention
             ops.ln_mod_quant(x, c.eps, shift=em[0], scale=em[1], q=xq_l, qscale=xs_l)
             gather_quantised()
+            vcopy = {} if v_direct else dict(v_src=qkv[:, 2 * Dl:], v_dst=vr)
             if kv_only and li == len(self.layers) - 1:
                 # the refresh pass's last block: its K / V into the ring, nothing else
-                ops.fp8_gemm(xq, xs, ly.w_qkv[Dl:], ly.s_qkv[Dl:], ly.b_qkv[Dl:], qkv[:, Dl:])
+                ops.fp8_gemm(xq, xs, ly.w_qkv[Dl:], ly.s_qkv[Dl:], ly.b_qkv[Dl:], qkv[:, Dl:],
+                             v_ring=(vr, Dl, L, slot_cur, cache.cap) if v_direct else None)
                 ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
                 comm.all_reduce_sum(ss[M:])
                 ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L,
                              slot0=slot_cur, n_slots=cache.cap, cos=cos, sin=sin, grid_h=h,
-                             grid_w=w, t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:],
-                             v_dst=vr, ss=ss[M:], norm_width=D)
+                             grid_w=w, t_offset_dev=self.t_offset_dev, ss=ss[M:], norm_width=D,
+                             **vcopy)
                 break
-            ops.fp8_gemm(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv)
+            # V goes straight into its ring slot (else the K kernel copies it there)
+            ops.fp8_gemm(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv,
+                         v_ring=(vr, 2 * Dl, L, slot_cur, cache.cap) if v_direct else None)
             ops.row_reduce(qkv[:, :Dl], "sumsq", out=ss[:M])
             ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
             comm.all_reduce_sum(ss)
@@ -426,9 +439,7 @@ class TPSRDiT(SRDiT):
                          norm_width=D)
             ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:], v_dst=vr,
-                         ss=ss[M:],
-                         norm_width=D)
+                         t_offset_dev=self.t_offset_dev, ss=ss[M:], norm_width=D, **vcopy)
             ak = av = None
             if anchor_kv is not None:
                 ak, av = anchor_kv[li]
@@ -525,6 +536,7 @@ class TPSRDiT(SRDiT):
         st = self.status
         cos, sin = self.rope_cos, self.rope_sin
         slot_cur = S.slot_cur
+        v_direct = L % 32 == 0 and Dl % 64 == 0   # the GEMM can store V into ring slots
         rs_flags = comm.my_flags[1]
 
         def rowpar_residual(a_bf16, w_q, w_s, bias, gate):
@@ -541,19 +553,22 @@ class TPSRDiT(SRDiT):
             kr, vr = cache.k[li], cache.v[li]
             # --- self attention
             comm.gather_ln(x, c.eps, shift=em[0], scale=em[1])
+            vcopy = {} if v_direct else dict(v_src=qkv[:, 2 * Dl:], v_dst=vr)
             if kv_only and li == len(self.layers) - 1:
                 # the refresh pass's last block: its K / V into the ring, nothing else
+                vring = (vr, Dl, L, slot_cur, cache.cap) if v_direct else None
                 ops.fp8_gemm_tp(xq, xs, ly.w_qkv[Dl:], ly.s_qkv[Dl:], ly.b_qkv[Dl:],
-                                qkv[:, Dl:], tp=comm.tp_gemm(), status=st)
+                                qkv[:, Dl:], status=st, tp=comm.tp_gemm(v_ring=vring))
                 ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
                 comm.allreduce(ss[M:], "sum", st)
                 ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L,
                              slot0=slot_cur, n_slots=cache.cap, cos=cos, sin=sin, grid_h=h,
-                             grid_w=w, t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:],
-                             v_dst=vr, ss=ss[M:], norm_width=D)
+                             grid_w=w, t_offset_dev=self.t_offset_dev, ss=ss[M:], norm_width=D,
+                             **vcopy)
                 break
-            ops.fp8_gemm_tp(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv, tp=comm.tp_gemm(),
-                            status=st)
+            # V goes straight into its ring slot (else the K kernel copies it there)
+            ops.fp8_gemm_tp(xq, xs, ly.w_qkv, ly.s_qkv, ly.b_qkv, qkv, status=st, tp=comm.tp_gemm(
+                v_ring=(vr, 2 * Dl, L, slot_cur, cache.cap) if v_direct else None))
             ops.row_reduce(qkv[:, :Dl], "sumsq", out=ss[:M])
             ops.row_reduce(qkv[:, Dl:2 * Dl], "sumsq", out=ss[M:])
             comm.allreduce(ss, "sum", st)
@@ -562,9 +577,7 @@ class TPSRDiT(SRDiT):
                          norm_width=D)
             ops.rms_rope(qkv[:, Dl:2 * Dl], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset_dev=self.t_offset_dev, v_src=qkv[:, 2 * Dl:], v_dst=vr,
-                         ss=ss[M:],
-                         norm_width=D)
+                         t_offset_dev=self.t_offset_dev, ss=ss[M:], norm_width=D, **vcopy)
             ak = av = None
             if anchor_kv is not None:
                 ak, av = anchor_kv[li]

@@ -133,6 +133,7 @@ typedef struct srdit_tp_gemm {
   void* rs_slot[SRDIT_MAX_RANKS];
   long long ld_rs;
   uint32_t* rs_flags[SRDIT_MAX_RANKS];
+  const srdit_v_ring* v_ring;  /* optional, STORE epilogue: as srdit_fp8_gemm_vring */
 } srdit_tp_gemm;
 
 int srdit_fp8_gemm_tp(const void* a_fp8, const float* a_scale, const void* b_fp8,
