@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--shape", default=None,
                     help="micro shape: gemm M,N,K | attn f_kv | quant/ln/rope M,K")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--epi", default="store", choices=["store", "gelu", "gated_res", "res"],
+                    help="micro gemm: the epilogue")
     ap.add_argument("--clip", action="store_true",
                     help="BASELINE config 5: a 121-frame clip (33 latent frames, 11 chunks) "
                          "over the rolling KV cache; sustained latent-frames/s and per-chunk "
@@ -108,12 +110,19 @@ def run_micro(args):
         sa, sb = torch.rand(M, device=dev), torch.rand(N, device=dev)
         bias = torch.randn(N, device=dev).to(torch.bfloat16)
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-        ms = timeit(lambda: ops.fp8_gemm(a, sa, w, sb, bias, out))
+        extra = {}
+        if args.epi == "gelu":
+            extra = dict(epilogue="gelu", row_amax=torch.zeros(M, device=dev))
+        elif args.epi in ("gated_res", "res"):
+            extra = dict(epilogue=args.epi, residual=torch.randn(M, N, device=dev).to(torch.bfloat16))
+            if args.epi == "gated_res":
+                extra["gate"] = torch.randn(N, device=dev)
+        ms = timeit(lambda: ops.fp8_gemm(a, sa, w, sb, bias, out, **extra))
         ref = timeit(lambda: torch._scaled_mm(a, w.t(), scale_a=sa.view(-1, 1),
                                               scale_b=sb.view(1, -1), bias=bias,
                                               out_dtype=torch.bfloat16))
         fl = 2 * M * N * K
-        res.update(shape=[M, N, K], ms=ms, tflops=fl / ms / 1e9, cublaslt_ms=ref,
+        res.update(shape=[M, N, K], epilogue=args.epi, ms=ms, tflops=fl / ms / 1e9, cublaslt_ms=ref,
                    cublaslt_tflops=fl / ref / 1e9,
                    frac_of_2x_bf16_burst=fl / ms / 1e9 / (2 * peaks["bf16_tflops"]))
     elif args.micro == "attn":
