@@ -101,83 +101,8 @@ SRDIT_DEV float chunk_absmax(const uint4& u) {
                fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(d.x), fabsf(d.y))));
 }
 
-// ---------------------------------------------------------------- packed pairs
-// A bf16x2 word holds element 2i in its low half and 2i+1 in its high half. As
-// an f32 pair ({x, y} = {2i, 2i+1} in one 64-bit register) it feeds sm_100's
-// paired fp32 instructions: one instruction for both elements, each rounded
-// exactly as its scalar form. The row kernels below run their per-element math
-// on pairs, which halves their instruction count: these kernels are
-// issue-bound, not HBM-bound, when written one element at a time.
-SRDIT_DEV uint64_t bf2_unpack(uint32_t w) {
-  // volatile: re-unpacked on every pass instead of cached as floats
-  uint32_t lo, hi;
-  asm volatile("shl.b32 %0, %1, 16;" : "=r"(lo) : "r"(w));
-  asm volatile("and.b32 %0, %1, 0xffff0000;" : "=r"(hi) : "r"(w));
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-  return r;
-}
-SRDIT_DEV uint64_t f2_pack(float x, float y) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
-  return r;
-}
-SRDIT_DEV uint64_t u64_of(uint32_t lo, uint32_t hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-  return r;
-}
-SRDIT_DEV float2 f2_split(uint64_t r) {
-  float2 f;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(r));
-  return f;
-}
-SRDIT_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-SRDIT_DEV uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-SRDIT_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-SRDIT_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-// both elements rounded to nearest-even bf16, repacked as a bf16x2 word
-SRDIT_DEV uint32_t f2_to_bf2(uint64_t v) {
-  const float2 f = f2_split(v);
-  uint32_t d;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f.y), "f"(f.x));
-  return d;
-}
-// bf16 x bf16 rounded once to bf16 (the exact product fits in fp32, so this is
-// bf16(float(a) * float(b)) for both halves)
-SRDIT_DEV uint32_t bf2_mul(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-// running per-half max of |w|
-SRDIT_DEV uint32_t bf2_absmax(uint32_t m, uint32_t w) {
-  uint32_t d;
-  asm("{\n\t.reg .b32 t;\n\tand.b32 t, %2, 0x7fff7fff;\n\tmax.bf16x2 %0, %1, t;\n\t}"
-      : "=r"(d)
-      : "r"(m), "r"(w));
-  return d;
-}
-SRDIT_DEV float bf2_hmax(uint32_t m) {
-  const float2 f = f2_split(bf2_unpack(m));
-  return fmaxf(f.x, f.y);
-}
+// Paired fp32 / bf16x2 helpers (f2_*, bf2_*): sm100.cuh.
+
 // x / s for both elements (Markstein's correction, as div_by) -> e4m3 pair,
 // saturated to +-448 (satfinite: the reference's clamp), element 2i in the
 // low byte

@@ -49,7 +49,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int OFF_STG = STAGES * STAGE_BYTES;
   static constexpr int OFF_COL = OFF_STG + EPI_WARPS * 2 * STG_BYTES;
-  static constexpr int OFF_BAR = OFF_COL + 2 * 2 * 256 * 4;
+  static constexpr int OFF_BAR = OFF_COL + 3 * 2 * 256 * 4;  // b_scale, bias, gate
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -133,6 +133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   volatile uint32_t* abort_flag = tmem_slot + 1;
   float* col_s = reinterpret_cast<float*>(smem + C::OFF_COL);  // [2][256] b_scale
   float* col_b = col_s + 512;                                  // [2][256] bias
+  float* col_g = col_s + 1024;                                 // [2][256] gate
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -278,6 +279,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const int col = n0 + c;
         col_s[acc * 256 + c] = col < p.N ? __ldg(p.b_scale + col) : 0.f;
         col_b[acc * 256 + c] = (p.bias != nullptr && col < p.N) ? __bfloat162float(p.bias[col]) : 0.f;
+        if constexpr (EPI == EPI_GATED_RES) col_g[acc * 256 + c] = col < p.N ? __ldg(p.gate + col) : 0.f;
       }
       named_barrier_sync(1, 128);
       if (!mbar_wait(&tfull[acc], aph, p.status, abort_flag)) break;
@@ -301,6 +303,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const float sa = row_ok ? p.a_scale[row] : 0.f;
       const float* cs = col_s + acc * 256;
       const float* cb = col_b + acc * 256;
+      const float* cg = col_g + acc * 256;
       float amax = 0.f;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
@@ -331,45 +334,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             }
           }
           tmem_ld_wait();
-          float v[32];
+          // the row's 32 outputs as bf16x2 words, computed on f32 pairs (each
+          // element rounded exactly as its scalar form):
+          //   y = bf16(acc * sa * b_scale + bias)            (STORE / PEER)
+          //   bf16(gelu_tanh(bf16(y)))                       (GELU)
+          //   bf16(res + bf16(y) * gate) / bf16(res + bf16(y))  (GATED_RES / RES)
+          uint32_t pw[16];
+          uint32_t am2 = 0u;
+          const uint64_t sa2 = f2_pack(sa, sa);
+          const uint32_t* rw = reinterpret_cast<const uint32_t*>(rv);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float y = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), sa), cs[c0 + j]);
-            v[j] = __fadd_rn(y, cb[c0 + j]);
-          }
-          if constexpr (EPI == EPI_GELU) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float g = bf16r(gelu_tanh(bf16r(v[j])));
-              v[j] = g;
-              amax = fmaxf(amax, fabsf(g));  // columns past N hold y = 0 -> g = 0
-            }
-          } else if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
-            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(rv);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float y = bf16r(v[j]);
-              const float xr = __bfloat162float(rb[j]);
+          for (int e = 0; e < 16; ++e) {
+            const int j = 2 * e;
+            const uint64_t cs2 = *reinterpret_cast<const uint64_t*>(cs + c0 + j);
+            const uint64_t cb2 = *reinterpret_cast<const uint64_t*>(cb + c0 + j);
+            const uint64_t y = f2_add(f2_mul(f2_mul(u64_of(r[j], r[j + 1]), sa2), cs2), cb2);
+            if constexpr (EPI == EPI_GELU) {
+              // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) on x = bf16(y)
+              const uint64_t x = bf2_unpack(f2_to_bf2(y));
+              const uint64_t x3 = f2_mul(f2_mul(x, x), x);
+              const float2 in = f2_split(f2_mul(f2_pack(0.7978845608028654f, 0.7978845608028654f),
+                                                f2_fma(f2_pack(0.044715f, 0.044715f), x3, x)));
+              const uint64_t t = f2_pack(tanh_sfu(in.x), tanh_sfu(in.y));
+              pw[e] = f2_to_bf2(f2_mul(f2_mul(f2_pack(0.5f, 0.5f), x), f2_add(f2_pack(1.f, 1.f), t)));
+              am2 = bf2_absmax(am2, pw[e]);  // columns past N hold y = 0 -> 0
+            } else if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+              const uint64_t yb = bf2_unpack(f2_to_bf2(y));
+              const uint64_t xr = bf2_unpack(rw[e]);
               if constexpr (EPI == EPI_GATED_RES) {
-                const int col = n0 + c0 + j;
-                const float gt = col < p.N ? __ldg(p.gate + col) : 0.f;
-                v[j] = __fadd_rn(xr, __fmul_rn(y, gt));
+                const uint64_t g2 = *reinterpret_cast<const uint64_t*>(cg + c0 + j);  // 0 past N
+                pw[e] = f2_to_bf2(f2_add(xr, f2_mul(yb, g2)));
               } else {
-                v[j] = __fadd_rn(xr, y);
+                pw[e] = f2_to_bf2(f2_add(xr, yb));
               }
+            } else {
+              pw[e] = f2_to_bf2(y);
             }
           }
+          if constexpr (EPI == EPI_GELU) amax = fmaxf(amax, bf2_hmax(am2));
           // this row's 32 values -> 64 bytes of the 128-byte staging row
           // (16-byte chunk q stored at q ^ (row & 7): the 128B TMA swizzle)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            uint4 pk;
-            uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
-              w[e] = *reinterpret_cast<uint32_t*>(&b2);
-            }
+            const uint4 pk = make_uint4(pw[4 * q], pw[4 * q + 1], pw[4 * q + 2], pw[4 * q + 3]);
             const int chunk = (h * 4 + q) ^ (lane & 7);
             *reinterpret_cast<uint4*>(buf + lane * 128 + chunk * 16) = pk;
           }
