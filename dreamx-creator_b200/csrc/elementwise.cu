@@ -583,28 +583,20 @@ SRDIT_DEV float warp_reduce4(const float (&v)[4]) {
   return k;
 }
 
-// CTA-wide totals of one statistic for the group's rows: each warp's totals go
-// to part[warp], then every thread combines the warps in the same order.
+// CTA-wide total of one statistic for the group's rows: each warp's totals go
+// to part[warp][row]; then lane l combines row l & 3 over the warps, in warp
+// order, so the row's per-row scalar math runs once per warp (lanes 0-3 in
+// parallel) rather than once per thread, and is broadcast by shuffles.
 template <bool kMax>
-SRDIT_DEV void cta_reduce4(float (&v)[4], float4* part) {
+SRDIT_DEV float cta_row_total(const float (&v)[4], float* part) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float w = warp_reduce4<kMax>(v);
-  if ((lane & 7) == 0) reinterpret_cast<float*>(part + warp)[lane >> 3] = w;
+  if ((lane & 7) == 0) part[warp * 4 + (lane >> 3)] = w;
   __syncthreads();
-  const int nw = blockDim.x >> 5;
-  float4 t = part[0];
-  for (int i = 1; i < nw; ++i) {
-    const float4 p = part[i];
-    if (kMax) {
-      t.x = fmaxf(t.x, p.x); t.y = fmaxf(t.y, p.y); t.z = fmaxf(t.z, p.z); t.w = fmaxf(t.w, p.w);
-    } else {
-      t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
-    }
-  }
-  v[0] = t.x;
-  v[1] = t.y;
-  v[2] = t.z;
-  v[3] = t.w;
+  const int nw = blockDim.x >> 5, r = lane & 3;
+  float t = part[r];
+  for (int i = 1; i < nw; ++i) t = kMax ? fmaxf(t, part[i * 4 + r]) : t + part[i * 4 + r];
+  return t;
 }
 
 // the group's rows (zeros past M): chunk ch of row r at d[r][ch]
@@ -626,23 +618,32 @@ SRDIT_DEV uint32_t word(const uint4& u, int k) {
   return k == 0 ? u.x : (k == 1 ? u.y : (k == 2 ? u.z : u.w));
 }
 
-// Over this thread's 16 elements of a row: the sum (kind 0), the sum of
-// (x - mean)^2 (kind 1) or the sum of x^2 (kind 2).
-template <int kKind>
-SRDIT_DEV float chunk2_sum(const uint4 (&d)[2], uint64_t mean2) {
+// Over this thread's 16 elements of a row: the sum (kCentred false) or the sum
+// of (x - mean)^2, on mixed-precision instructions that read the bf16 halves
+// directly (two accumulator pairs, even and odd words).
+template <bool kCentred>
+SRDIT_DEV float chunk2_sum(const uint4 (&d)[2], float mean) {
+  float ax = 0.f, ay = 0.f, bx = 0.f, by = 0.f;
   uint64_t a = f2_pack(0.f, 0.f), b = a;
 #pragma unroll
   for (int ch = 0; ch < 2; ++ch)
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const uint64_t v = bf2_unpack(word(d[ch], k));
-      if (kKind == 0) {
-        if (k & 1) b = f2_add(b, v); else a = f2_add(a, v);
+      const uint32_t w = word(d[ch], k);
+      if (!kCentred) {
+        if (k & 1) {
+          bx = bflo_add(w, bx);
+          by = bfhi_add(w, by);
+        } else {
+          ax = bflo_add(w, ax);
+          ay = bfhi_add(w, ay);
+        }
       } else {
-        const uint64_t dd = kKind == 1 ? f2_sub(v, mean2) : v;
+        const uint64_t dd = bf2_sub_f(w, mean);
         if (k & 1) b = f2_fma(dd, dd, b); else a = f2_fma(dd, dd, a);
       }
     }
+  if (!kCentred) return (ax + bx) + (ay + by);
   const float2 s = f2_split(f2_add(a, b));
   return s.x + s.y;
 }
@@ -667,7 +668,7 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
     const float* __restrict__ shift, const float* __restrict__ scale,
     uint8_t* __restrict__ q, long long ldq, float* __restrict__ qscale, const LnPeer pe) {
   constexpr bool kMod = MODE & 1, kAff = MODE & 2;
-  __shared__ float4 part[3][32];
+  __shared__ float part[3][32 * kGroup];
   const int T = blockDim.x;
   const int t = threadIdx.x;
   const int K = T * 16;
@@ -709,23 +710,22 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
     const int row0 = g * kGroup;
     if (g + static_cast<int>(gridDim.x) < ngroups)
       cs_load(nxt, x, ldx, M, (g + gridDim.x) * kGroup, cc[0], cc[1]);
+    // two-pass statistics; each row's scalars are formed in lane (row) and
+    // broadcast to the warp
     float st[4];
 #pragma unroll
-    for (int r = 0; r < kGroup; ++r) st[r] = chunk2_sum<0>(cur[r], 0);
-    cta_reduce4<false>(st, part[0]);
-    uint64_t mean2[kGroup];
+    for (int r = 0; r < kGroup; ++r) st[r] = chunk2_sum<false>(cur[r], 0.f);
+    const float mean_l = cta_row_total<false>(st, part[0]) / static_cast<float>(K);
+    float mean[kGroup];
 #pragma unroll
-    for (int r = 0; r < kGroup; ++r) {
-      const float mean = st[r] / static_cast<float>(K);
-      mean2[r] = f2_pack(mean, mean);
-    }
+    for (int r = 0; r < kGroup; ++r) mean[r] = __shfl_sync(0xffffffffu, mean_l, r);
 #pragma unroll
-    for (int r = 0; r < kGroup; ++r) st[r] = chunk2_sum<1>(cur[r], mean2[r]);
-    cta_reduce4<false>(st, part[1]);
+    for (int r = 0; r < kGroup; ++r) st[r] = chunk2_sum<true>(cur[r], mean[r]);
+    const float rstd_l = rsqrtf(cta_row_total<false>(st, part[1]) / static_cast<float>(K) + eps);
     float am[4];
 #pragma unroll
     for (int r = 0; r < kGroup; ++r) {
-      const float rstd = rsqrtf(st[r] / static_cast<float>(K) + eps);
+      const float rstd = __shfl_sync(0xffffffffu, rstd_l, r);
       const uint64_t rstd2 = f2_pack(rstd, rstd);
       uint32_t m0 = 0u, m1 = 0u;
 #pragma unroll
@@ -733,7 +733,7 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
         uint32_t o[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          uint64_t n = f2_mul(f2_sub(bf2_unpack(word(cur[r][ch], k)), mean2[r]), rstd2);
+          uint64_t n = f2_mul(bf2_sub_f(word(cur[r][ch], k), mean[r]), rstd2);
           if (kAff) n = f2_fma(n, wt[ch * 4 + k], bs[ch * 4 + k]);
           uint32_t nb = f2_to_bf2(n);  // WanLayerNorm returns .type_as(x)
           if (kMod)  // x * (1 + scale) + shift in fp32 (two roundings), then bf16
@@ -743,14 +743,15 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
         }
         cur[r][ch] = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      am[r] = fmaxf(bf2_hmax(m0), bf2_hmax(m1));
+      am[r] = bf2_hmax(bf2_absmax(m0, m1));
     }
-    cta_reduce4<true>(am, part[2]);
+    const float sc_l = scale_of(cta_row_total<true>(am, part[2]));
+    const float rsc_l = __frcp_rn(sc_l);
 #pragma unroll
     for (int r = 0; r < kGroup; ++r) {
+      const float sc = __shfl_sync(0xffffffffu, sc_l, r);
+      const float rsc = __shfl_sync(0xffffffffu, rsc_l, r);
       if (row0 + r >= M) break;
-      const float sc = scale_of(am[r]);
-      const float rsc = __frcp_rn(sc);
       const uint64_t ns2 = f2_pack(-sc, -sc), r2 = f2_pack(rsc, rsc);
       const uint2 v0 = chunk_quant(cur[r][0], ns2, r2);
       const uint2 v1 = chunk_quant(cur[r][1], ns2, r2);

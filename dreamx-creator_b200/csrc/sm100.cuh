@@ -500,16 +500,52 @@ SRDIT_DEV uint32_t bf2_mul(uint32_t a, uint32_t b) {
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
-// running per-half max of |w|
+// running per-half max of |w|: one max.xorsign.abs (the magnitude is
+// max(|m|, |w|); the sign bit is scrambled, so readers take bf2_hmax)
 SRDIT_DEV uint32_t bf2_absmax(uint32_t m, uint32_t w) {
   uint32_t d;
-  asm("{\n\t.reg .b32 t;\n\tand.b32 t, %2, 0x7fff7fff;\n\tmax.bf16x2 %0, %1, t;\n\t}"
-      : "=r"(d)
-      : "r"(m), "r"(w));
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(m), "r"(w));
   return d;
 }
+// the larger magnitude of the two halves
 SRDIT_DEV float bf2_hmax(uint32_t m) {
   const float2 f = f2_split(bf2_unpack(m));
-  return fmaxf(f.x, f.y);
+  return fmaxf(fabsf(f.x), fabsf(f.y));
 }
+
+// Mixed-precision forms: the low / high bf16 half of w, widened exactly, plus,
+// minus or squared-and-added to an fp32 c -- one FMA-pipe instruction each,
+// with no separate unpack. Same results as widening first.
+SRDIT_DEV float bflo_add(uint32_t w, float c) {
+  float d;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; add.rn.f32.bf16 %0, l, %2;}" : "=f"(d) : "r"(w), "f"(c));
+  return d;
+}
+SRDIT_DEV float bfhi_add(uint32_t w, float c) {
+  float d;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; add.rn.f32.bf16 %0, h, %2;}" : "=f"(d) : "r"(w), "f"(c));
+  return d;
+}
+SRDIT_DEV float bflo_sub(uint32_t w, float c) {  // lo(w) - c
+  float d;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; sub.rn.f32.bf16 %0, l, %2;}" : "=f"(d) : "r"(w), "f"(c));
+  return d;
+}
+SRDIT_DEV float bfhi_sub(uint32_t w, float c) {  // hi(w) - c
+  float d;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; sub.rn.f32.bf16 %0, h, %2;}" : "=f"(d) : "r"(w), "f"(c));
+  return d;
+}
+SRDIT_DEV float bflo_sqadd(uint32_t w, float c) {  // lo(w)^2 + c, one rounding
+  float d;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.bf16 %0, l, l, %2;}" : "=f"(d) : "r"(w), "f"(c));
+  return d;
+}
+SRDIT_DEV float bfhi_sqadd(uint32_t w, float c) {  // hi(w)^2 + c, one rounding
+  float d;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.bf16 %0, h, h, %2;}" : "=f"(d) : "r"(w), "f"(c));
+  return d;
+}
+// (lo(w) - c, hi(w) - c) as an fp32 pair
+SRDIT_DEV uint64_t bf2_sub_f(uint32_t w, float c) { return f2_pack(bflo_sub(w, c), bfhi_sub(w, c)); }
 }  // namespace srdit
