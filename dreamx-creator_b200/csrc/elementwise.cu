@@ -11,7 +11,8 @@
 //                   models.py:497-503 (norm), :1308 / :1258 (x*(1+scale)+shift),
 //                   fp8_linear.py:93-103 (the next Linear's activation quantiser)
 //   rms_rope        RMSNorm over the full row (models.py:437-440) x weight, then
-//                   3-D RoPE per head in fp64 (models.py:173-214), written to the
+//                   3-D RoPE per head in fp64, rounded once to bf16
+//                   (models.py:173-214), written to the
 //                   destination buffers (q buffer, KV-cache frame slots); V rows are
 //                   copied alongside so the cache is filled in the same pass.
 #include "sm100.cuh"
@@ -424,6 +425,14 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 5 : 3)) ln_mod_quant_kernel(
 }
 
 // ---------------------------------------------------------------- rms_rope
+// (lo, hi) rounded to nearest-even bf16 straight from fp64: lo in the low half
+SRDIT_DEV uint32_t f64x2_to_bf2(double lo, double hi) {
+  uint16_t a, b;
+  asm("cvt.rn.bf16.f64 %0, %1;" : "=h"(a) : "d"(lo));
+  asm("cvt.rn.bf16.f64 %0, %1;" : "=h"(b) : "d"(hi));
+  return static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
+}
+
 struct RopeArgs {
   const __nv_bfloat16* src;  // row r at src + r * ld_src
   long long ld_src;
@@ -488,21 +497,21 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
   if (a.ss_in) {
     ssum = __ldg(a.ss_in + row);
   } else {
-    uint64_t sa = f2_pack(0.f, 0.f), sb = sa;
+    // four accumulation chains (low / high halves of the even / odd words) on
+    // mixed-precision square-and-add instructions
+    float ax = 0.f, ay = 0.f, bx = 0.f, by = 0.f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
-      uint64_t v;
-      v = bf2_unpack(raw[i].x);
-      sa = f2_fma(v, v, sa);
-      v = bf2_unpack(raw[i].y);
-      sb = f2_fma(v, v, sb);
-      v = bf2_unpack(raw[i].z);
-      sa = f2_fma(v, v, sa);
-      v = bf2_unpack(raw[i].w);
-      sb = f2_fma(v, v, sb);
+      ax = bflo_sqadd(raw[i].x, ax);
+      ay = bfhi_sqadd(raw[i].x, ay);
+      bx = bflo_sqadd(raw[i].y, bx);
+      by = bfhi_sqadd(raw[i].y, by);
+      ax = bflo_sqadd(raw[i].z, ax);
+      ay = bfhi_sqadd(raw[i].z, ay);
+      bx = bflo_sqadd(raw[i].w, bx);
+      by = bfhi_sqadd(raw[i].w, by);
     }
-    const float2 ps = f2_split(f2_add(sa, sb));
-    ssum = warp_sum(ps.x + ps.y);
+    ssum = warp_sum((ax + bx) + (ay + by));
   }
   const float r = rsqrtf(ssum * (1.0f / static_cast<float>(a.norm_width)) + a.eps);
   const uint64_t r2 = f2_pack(r, r);
@@ -537,12 +546,11 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
       // bf16(bf16(x * r) * w): WanRMSNorm's .type_as(x) * weight
       o[p] = bf2_mul(f2_to_bf2(f2_mul(bf2_unpack(xw[p]), r2)), ww[p]);
       if (a.cos_tab) {
-        // (x0 + i x1) * (cos + i sin) in fp64, -> fp32 -> bf16
+        // (x0 + i x1) * (cos + i sin) in fp64, rounded once from fp64 to bf16
+        // (the reference's .to(x.dtype) on the float64 result)
         const float2 x = f2_split(bf2_unpack(o[p]));
         const double x0 = static_cast<double>(x.x), x1 = static_cast<double>(x.y);
-        const float y0 = static_cast<float>(x0 * cr[p] - x1 * si[p]);
-        const float y1 = static_cast<float>(x0 * si[p] + x1 * cr[p]);
-        o[p] = f2_to_bf2(f2_pack(y0, y1));
+        o[p] = f64x2_to_bf2(x0 * cr[p] - x1 * si[p], x0 * si[p] + x1 * cr[p]);
       }
     }
     dr[i * 32] = make_uint4(o[0], o[1], o[2], o[3]);

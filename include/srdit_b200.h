@@ -173,7 +173,8 @@ int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, float eps,
 
 /*
  * RMSNorm over the K-wide row slice (x * rsqrt(mean(x^2) + eps) -> bf16 -> x
- * weight), then optional 3-D RoPE per 128-wide head in fp64 with the tables
+ * weight), then optional 3-D RoPE per 128-wide head in fp64 (rounded once, fp64
+ * to bf16, as the reference's .to(dtype) of its float64 product) with the tables
  * cos_tab/sin_tab [tab_rows, 64] (columns 0-21 temporal, 22-42 height, 43-63
  * width), token position (t_offset + f, h, w) on the grid_h x grid_w frame grid.
  * Row r = f * frame_tokens + s is written to destination row

@@ -148,6 +148,29 @@ def test_fp8_gemm_residual(srdit, cuda_device, kind):
     assert onum.rel_fro(out.cpu().float(), ref.float()) < 1e-3
 
 
+@pytest.mark.parametrize("kind", ["gated_res", "res"])
+def test_fp8_gemm_residual_in_place_ragged(srdit, cuda_device, kind):
+    """The block's use: the output overwrites the residual stream it reads
+    (out is residual), here with M and N that end inside a 32 x 64 residual box
+    and an output-tile pair; 10 x 8 tiles, so some CTA pairs take two (the
+    residual box of a pair's next tile is loaded during its current one)."""
+    M, N, K = 2536, 1480, 256
+    a, aq, as_, wq, ws, bias = _gemm_inputs(M, N, K, 23)
+    g = torch.Generator().manual_seed(24)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    gate = torch.randn(N, generator=g) * 0.5
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    x = d(res)
+    out = srdit.ops.fp8_gemm(d(aq), d(as_), d(wq), d(ws), d(bias), x, epilogue=kind, residual=x,
+                             gate=d(gate) if kind == "gated_res" else None)
+    assert out.data_ptr() == x.data_ptr()
+    y = onum.fp8_linear(a, wq, ws, bias)
+    ref = (res.float() + y.float() * gate) if kind == "gated_res" else (res.float() + y.float())
+    ref = ref.to(torch.bfloat16)
+    assert onum.rel_fro(x.cpu().float(), ref.float()) < 1e-3
+    assert (x.cpu().view(torch.int16) == ref.view(torch.int16)).float().mean() > 0.99
+
+
 # --------------------------------------------------------------------------- window attention
 def _check_attn(got, ref, max_abs=2e-2, rel=5e-3):
     got = got.float().cpu().double()
