@@ -43,12 +43,15 @@ constexpr int EPI_WARPS = 4;
 constexpr int STG_BYTES = 32 * 128;  // per-warp staging tile: 32 rows x 64 bf16
 constexpr uint32_t TMEM_COLS = 512;
 
-template <int BN>
+// kRes: the residual epilogues also hold two 32-row x 64-column residual
+// boxes per epilogue warp (TMA-loaded one chunk ahead of their use)
+template <int BN, bool kRes = false>
 struct Cfg {
   static constexpr int B_BYTES = (BN / 2) * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int OFF_STG = STAGES * STAGE_BYTES;
-  static constexpr int OFF_COL = OFF_STG + EPI_WARPS * 2 * STG_BYTES;
+  static constexpr int OFF_RES = OFF_STG + EPI_WARPS * 2 * STG_BYTES;
+  static constexpr int OFF_COL = OFF_RES + (kRes ? EPI_WARPS * 2 * STG_BYTES : 0);
   static constexpr int OFF_BAR = OFF_COL + 3 * 2 * 256 * 4;  // b_scale, bias, gate
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
@@ -114,13 +117,19 @@ SRDIT_DEV float gelu_tanh(float x) {
 
 SRDIT_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+template <int EPI>
+constexpr bool has_residual() { return EPI == EPI_GATED_RES || EPI == EPI_RES; }
+
+// pm.m[0] is the residual's tensor map for the residual epilogues (which never
+// run with tensor-parallel peers), and the V ring's for a STORE with v_col0 >= 0
 template <int EPI, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const Params p,
                     const __grid_constant__ PeerMaps pm, const __grid_constant__ TpArgs tp) {
-  using C = Cfg<BN>;
+  constexpr bool kRes = has_residual<EPI>();
+  using C = Cfg<BN, kRes>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -131,6 +140,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tempty = bars + 2 * STAGES + 2;  // [2], in the even CTA, 8 arrivals
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  uint64_t* rbar = bars + 2 * STAGES + 5;    // [EPI_WARPS][2] residual boxes landed
   float* col_s = reinterpret_cast<float*>(smem + C::OFF_COL);  // [2][256] b_scale
   float* col_b = col_s + 512;                                  // [2][256] bias
   float* col_g = col_s + 1024;                                 // [2][256] gate
@@ -154,6 +164,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * EPI_WARPS);
     }
+    if (kRes)
+      for (int i = 0; i < 2 * EPI_WARPS; ++i) mbar_init(&rbar[i], 1);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -267,6 +279,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const int ep_tid = threadIdx.x - 64;    // 0..127
     uint8_t* stg = smem + C::OFF_STG + sub * 2 * STG_BYTES;
     const uint32_t tempty_even = mapa_shared(smem_u32(&tempty[0]), 0);
+    // Residual epilogues: this warp's 32 x 64 residual box of each chunk is
+    // TMA-loaded into rbuf[chunk & 1] one chunk ahead (the next chunk of the
+    // tile, or the first chunk of the warp's next tile), so the global-memory
+    // latency is off the epilogue's path. Boxes wholly past M or N (never
+    // stored) are not loaded.
+    uint8_t* rbuf = smem + C::OFF_RES + sub * 2 * STG_BYTES;
+    uint64_t* rbw = rbar + sub * 2;
+    uint32_t rpend = 0u, rph = 0u;  // bit b: a box in flight into buffer b / its phase
+    auto res_issue = [&](int t, int ch, int b) -> bool {
+      const int mt_ = (t / num_n + tp.mt_offset) % num_m, nt_ = t % num_n;
+      const int r0 = mt_ * 2 * BM + static_cast<int>(rank) * BM + sub * 32;
+      const int c0 = nt_ * BN + ch * 64;
+      if (r0 >= p.M || c0 >= p.N) return false;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&rbw[b], STG_BYTES);
+        tma_load_2d(rbuf + b * STG_BYTES, &pm.m[0], &rbw[b], c0, r0);
+      }
+      return true;
+    };
+    int rseq = 0;  // residual chunks consumed by this warp
+    if (kRes && cid < num_tiles && res_issue(cid, 0, 0)) rpend = 1u;
     int stores = 0;
     int local = 0;
     for (int tile = cid; tile < num_tiles; tile += ncl, ++local) {
@@ -307,6 +340,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       float amax = 0.f;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
+      bool res_ok = true;
 #pragma unroll 1
       for (int ch = 0; ch < BN / 64; ++ch) {
         uint8_t* buf = stg + (stores & 1) * STG_BYTES;
@@ -314,24 +348,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           if (lane == 0) bulk_wait_group_read1();
           __syncwarp();
         }
+        const uint8_t* rcur = rbuf + (rseq & 1) * STG_BYTES;
+        if constexpr (kRes) {
+          // the next box into the other buffer (its last reader, the previous
+          // chunk, finished before that chunk's closing __syncwarp), then wait
+          // for this chunk's box
+          const int nb = (rseq + 1) & 1;
+          bool issued = false;
+          if (ch + 1 < BN / 64) issued = res_issue(tile, ch + 1, nb);
+          else if (tile + ncl < num_tiles) issued = res_issue(tile + ncl, 0, nb);
+          if (issued) rpend |= 1u << nb;
+          const int b = rseq & 1;
+          if ((rpend >> b) & 1u) {
+            if (!mbar_wait(&rbw[b], (rph >> b) & 1u, p.status, abort_flag)) {
+              res_ok = false;
+              break;
+            }
+            rph ^= 1u << b;
+            rpend &= ~(1u << b);
+          }
+          ++rseq;
+        }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c0 = ch * 64 + h * 32;  // column within the tile
           uint32_t r[32];
           tmem_ld32(t_row + c0, r);
           uint4 rv[4];
-          if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
-            const int col = n0 + c0;
-            const __nv_bfloat16* rp = p.res + static_cast<long long>(row) * p.ldr + col;
-            if (row_ok && col + 32 <= p.N) {
+          if constexpr (kRes) {
+            // this row's 32 residual values of half h: 16-byte chunks h*4 + q
+            // of the 128B-swizzled box row (zeros past M / N: TMA fill)
 #pragma unroll
-              for (int q = 0; q < 4; ++q) rv[q] = *reinterpret_cast<const uint4*>(rp + q * 8);
-            } else {
-              __nv_bfloat16* rb = reinterpret_cast<__nv_bfloat16*>(rv);
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                rb[j] = (row_ok && col + j < p.N) ? rp[j] : __float2bfloat16_rn(0.f);
-            }
+            for (int q = 0; q < 4; ++q)
+              rv[q] = *reinterpret_cast<const uint4*>(rcur + lane * 128 +
+                                                      (((h * 4 + q) ^ (lane & 7)) << 4));
           }
           tmem_ld_wait();
           // the row's 32 outputs as bf16x2 words, computed on f32 pairs (each
@@ -399,6 +449,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         ++stores;
       }
+      if (!res_ok) {
+        *abort_flag = 1u;
+        break;
+      }
       if constexpr (EPI == EPI_GELU) {
         if (row_ok) atomicMax(reinterpret_cast<unsigned int*>(p.row_amax + row), __float_as_uint(amax));
       }
@@ -407,6 +461,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive_cluster(tempty_even + 8u * acc);
     }
     if (lane == 0) bulk_wait_group_all();
+    // after an abort, let residual boxes still in flight land before exiting
+    if constexpr (kRes)
+      for (int b = 0; b < 2; ++b)
+        if ((rpend >> b) & 1u) mbar_wait(&rbw[b], (rph >> b) & 1u, p.status, nullptr);
     __syncwarp();
     if constexpr (EPI == EPI_PEER) {
       // this CTA's partial tiles have landed in their owners' memory: publish
@@ -429,20 +487,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 template <int EPI, int BN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                   const Params& p, const PeerMaps& pm, const TpArgs& tp, cudaStream_t stream) {
+  using C = Cfg<BN, has_residual<EPI>()>;
   auto kern = fp8_gemm_kernel<EPI, BN>;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr_done[kMaxDevices] = {};
   if (dev < kMaxDevices && !attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<BN>::SMEM);
+                                         C::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done[dev] = true;
   }
   const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
   const int pairs = num_sms(dev) / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, NUM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, to, p, pm, tp);
+  kern<<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, to, p, pm, tp);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -463,12 +522,20 @@ static int pick_bn(int M, int N, int pairs) {
   return best;
 }
 
+// The residual epilogues run at BN = 192 only (BN = 256 with their residual
+// boxes would not fit in shared memory); the caller picks bn, and sizes the B
+// operand's tensor-map box (bn / 2 rows), accordingly.
 template <int EPI>
 static int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
                      const CUtensorMap& to, const Params& p, const PeerMaps& pm,
                      const TpArgs& tp, cudaStream_t stream) {
-  return bn == 256 ? launch<EPI, 256>(ta, tb, to, p, pm, tp, stream)
-                   : launch<EPI, 192>(ta, tb, to, p, pm, tp, stream);
+  if constexpr (has_residual<EPI>()) {
+    if (bn != 192) return SRDIT_EINVAL;
+    return launch<EPI, 192>(ta, tb, to, p, pm, tp, stream);
+  } else {
+    return bn == 256 ? launch<EPI, 256>(ta, tb, to, p, pm, tp, stream)
+                     : launch<EPI, 192>(ta, tb, to, p, pm, tp, stream);
+  }
 }
 
 // CTAs of one launch (two per output-tile pair, at most one pair per two SMs).
@@ -537,7 +604,8 @@ static int fp8_gemm_impl(const void* a_fp8, const float* a_scale, const void* b_
 
   int dev = 0;
   cudaGetDevice(&dev);
-  const int bn = gemm::pick_bn(M, N, num_sms(dev) / 2);
+  const bool res_epi = epilogue == EPI_GATED_RES || epilogue == EPI_RES;
+  const int bn = res_epi ? 192 : gemm::pick_bn(M, N, num_sms(dev) / 2);
   CUtensorMap ta, tb, to;
   int rc = make_tmap_2d(&ta, a_fp8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, lda, gemm::BK,
                         gemm::BM);
@@ -548,6 +616,11 @@ static int fp8_gemm_impl(const void* a_fp8, const float* a_scale, const void* b_
     to = pm.m[tp.rank];  // unused by the peer epilogue
   } else {
     rc = make_tmap_2d(&to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldo, 64, 32);
+    if (rc) return rc;
+  }
+  if (res_epi) {
+    if (tpa) return SRDIT_EINVAL;  // pm.m[0] carries the residual's map
+    rc = make_tmap_2d(&pm.m[0], residual, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldr, 64, 32);
     if (rc) return rc;
   }
 
