@@ -36,7 +36,6 @@ namespace gemm {
 
 constexpr int BM = 128;  // rows per CTA (256 per pair)
 constexpr int BK = 128;  // bytes == e4m3 elements per stage
-constexpr int STAGES = 5;
 constexpr int A_BYTES = BM * BK;
 constexpr int NUM_THREADS = 192;
 constexpr int EPI_WARPS = 4;
@@ -49,6 +48,9 @@ template <int BN, bool kRes = false>
 struct Cfg {
   static constexpr int B_BYTES = (BN / 2) * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // operand ring depth: 6 stages where shared memory allows (BN = 192 without
+  // residual boxes), 5 otherwise
+  static constexpr int STAGES = (BN == 192 && !kRes) ? 6 : 5;
   static constexpr int OFF_STG = STAGES * STAGE_BYTES;
   static constexpr int OFF_RES = OFF_STG + EPI_WARPS * 2 * STG_BYTES;
   static constexpr int OFF_COL = OFF_RES + (kRes ? EPI_WARPS * 2 * STG_BYTES : 0);
@@ -134,6 +136,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  constexpr int STAGES = C::STAGES;
   uint64_t* full = bars;                     // [STAGES], completed in the even CTA
   uint64_t* empty = bars + STAGES;           // [STAGES], one per CTA
   uint64_t* tfull = bars + 2 * STAGES;       // [2]
