@@ -148,6 +148,31 @@ def cached_plan(spec: blockgrid.WindowSpec, anchor_mode=None) -> dict:
     return plan
 
 
+def frames_plan(spec1: blockgrid.WindowSpec, frames: int) -> dict:
+    """Plan of ``frames`` independent 1-frame samples laid side by side in one
+    chunk: the rows of the 1-frame spec ``spec1`` (no cache, no anchor) repeated
+    once per frame, with the query and KV frame of every row offset by the frame
+    index, so frame j attends to frame j only. This is the anchor harvest's
+    batch of B = frames independent samples (causal_inference.py:456-460) run
+    as one forward; memoised."""
+    key = ("frames", spec1, int(frames))
+    plan = _PLAN_CACHE.get(key)
+    if plan is None:
+        if spec1.f_cur != 1 or spec1.f_kv != 1:
+            raise ValueError("frames_plan needs the spec of a 1-frame sample without a cache")
+        rows, stride, _ = blockgrid.plan_rows(spec1, None)
+        reps = []
+        for j in range(int(frames)):
+            r = rows.clone()
+            r[:, 0] += j  # q_t0
+            r[:, 6] += j  # kv_t0
+            reps.append(r)
+        rows = torch.cat(reps)
+        plan = _PLAN_CACHE[key] = {"params": rows, "n_w": rows.shape[0], "p_stride": stride,
+                                   "hr_base": 0}
+    return plan
+
+
 def install(attention_module) -> None:
     """Route the reference's ``attn_impl="triton"`` launches to the B200 kernel.
 

@@ -382,7 +382,7 @@ class SRDiT:
         return y.to(torch.bfloat16)
 
     def _setup(self, latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, n_heads,
-               width):
+               width, independent_frames=False):
         """Embeddings, the window plan and the attention geometries of one forward.
 
         ``n_heads`` / ``width``: the heads and row width of the q/k/v/out
@@ -401,13 +401,21 @@ class SRDiT:
         if f_kv > cache.cap:
             raise _lib.SrditError(f"chunk of {f} frames does not fit the ring of {cache.cap}")
         slot_cur = (cache.start + cache.frames) % cache.cap
-        spec = blockgrid.make_spec(f_cur=f, f_kv=f_kv, h=h, w=w, block_t=c.block_t,
-                                   block_hw=c.block_hw, block_radius_hw=c.block_radius_hw,
-                                   block_radius_t=c.block_radius_t,
-                                   streaming=cache.frames > 0 or anchor_kv is not None)
         mode = None if anchor_kv is None else anchor_align
-        from .attention import cached_plan, _plan_device_state
-        plan = cached_plan(spec, mode)
+        from .attention import cached_plan, frames_plan, _plan_device_state
+        if independent_frames:
+            if cache.frames or anchor_kv is not None:
+                raise _lib.SrditError("independent_frames: no cache and no anchor")
+            spec1 = blockgrid.make_spec(f_cur=1, f_kv=1, h=h, w=w, block_t=c.block_t,
+                                        block_hw=c.block_hw, block_radius_hw=c.block_radius_hw,
+                                        block_radius_t=c.block_radius_t, streaming=False)
+            plan = frames_plan(spec1, f)
+        else:
+            spec = blockgrid.make_spec(f_cur=f, f_kv=f_kv, h=h, w=w, block_t=c.block_t,
+                                       block_hw=c.block_hw, block_radius_hw=c.block_radius_hw,
+                                       block_radius_t=c.block_radius_t,
+                                       streaming=cache.frames > 0 or anchor_kv is not None)
+            plan = cached_plan(spec, mode)
         fkey = ("flops", n_heads)
         if fkey not in plan:
             plan[fkey] = blockgrid.visible_flops(plan["params"], int(plan["p_stride"]),
@@ -445,7 +453,7 @@ class SRDiT:
     def forward_chunk(self, latent, t, context, *, cache: KVRing | None = None,
                       t_offset=0, update_cache=False, anchor_kv=None, anchor_align="frame",
                       return_kv=False, ctx_emb=None, text: TextCache | None = None,
-                      kv_only=False):
+                      kv_only=False, independent_frames=False):
         """One streaming forward over a chunk (``_forward_inference`` for one sample).
 
         latent [C_in, f, H, W]; ``cache`` holds the previous chunks' K/V (read in
@@ -458,7 +466,10 @@ class SRDiT:
         (a cache-refresh forward whose prediction is discarded, as the refiner's
         t=0 pass is): the last block stops once its K/V are in the ring, only its
         k / v columns are projected, and nothing is returned -- the ring ends up
-        exactly as after the full forward.
+        exactly as after the full forward. ``independent_frames=True`` (no cache,
+        no anchor): the chunk's frames are independent 1-frame samples -- frame j
+        attends to frame j only, at temporal position t_offset + j -- which is the
+        anchor harvest's batch (causal_inference.py:456-460) as one forward.
         Returns the refined prediction [C_out, f, H, W] bf16 (and the K/V list).
         """
         if kv_only and (return_kv or not update_cache):
@@ -471,7 +482,7 @@ class SRDiT:
         if text is not None:
             ctx_emb = text.ctx_emb
         S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb,
-                        c.num_heads, c.dim)
+                        c.num_heads, c.dim, independent_frames)
         x, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
         f, h, w = grid
         L, M, D, Lc = S.L, S.M, c.dim, S.Lc

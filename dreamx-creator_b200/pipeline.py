@@ -71,21 +71,14 @@ class RefinerStream:
         self.t_offset = 0
 
     def harvest_anchor(self, lq_chunk, harvest_t=0.0):
-        """Per-frame anchor K / V (each LR frame an independent 1-frame forward)."""
-        f = lq_chunk.shape[1]
-        ks, vs = None, None
-        for j in range(f):
-            _, kv = self.model.forward_chunk(lq_chunk[:, j:j + 1], harvest_t, self.context,
-                                             cache=None, t_offset=self.t_offset + j,
-                                             return_kv=True, text=self.text)
-            if ks is None:
-                ks = [[k] for k, _ in kv]
-                vs = [[v] for _, v in kv]
-            else:
-                for li, (k, v) in enumerate(kv):
-                    ks[li].append(k)
-                    vs[li].append(v)
-        return [(torch.cat(k), torch.cat(v)) for k, v in zip(ks, vs)]
+        """Per-frame anchor K / V: the LR chunk's frames as independent 1-frame
+        samples (frame j at temporal position t_offset + j, no cache), run as one
+        forward whose self-attention keeps every frame to itself -- the
+        reference's batch of B = f samples (causal_inference.py:456-460)."""
+        _, kv = self.model.forward_chunk(lq_chunk, harvest_t, self.context, cache=None,
+                                         t_offset=self.t_offset, return_kv=True,
+                                         text=self.text, independent_frames=True)
+        return kv
 
     def _ensure_cache(self, noisy_chunk):
         if self.cache is None:

@@ -343,7 +343,7 @@ class TPSRDiT(SRDiT):
     # ------------------------------------------------------------------ forward
     def forward_chunk(self, latent, t, context, *, cache=None, t_offset=0, update_cache=False,
                       anchor_kv=None, anchor_align="frame", return_kv=False, ctx_emb=None,
-                      text=None, kv_only=False):
+                      text=None, kv_only=False, independent_frames=False):
         """``SRDiT.forward_chunk`` on this rank's shard; same arguments and result
         (``anchor_kv`` / the returned K/V hold this rank's heads)."""
         if kv_only and (return_kv or not update_cache):
@@ -353,7 +353,8 @@ class TPSRDiT(SRDiT):
             return self._forward_fused(latent, t, context, cache=cache, t_offset=t_offset,
                                        update_cache=update_cache, anchor_kv=anchor_kv,
                                        anchor_align=anchor_align, return_kv=return_kv,
-                                       ctx_emb=ctx_emb, text=text, kv_only=kv_only)
+                                       ctx_emb=ctx_emb, text=text, kv_only=kv_only,
+                                       independent_frames=independent_frames)
         c = self.cfg
         ops = self.ops
         if not self.graph_capture:
@@ -364,7 +365,8 @@ class TPSRDiT(SRDiT):
         Hl = c.num_heads // P
         if text is not None:
             ctx_emb = text.ctx_emb
-        S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, Hl, Dl)
+        S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, Hl, Dl,
+                        independent_frames)
         x_full, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
         f, h, w = grid
         L, M, Lc = S.L, S.M, S.Lc
@@ -490,7 +492,8 @@ class TPSRDiT(SRDiT):
         return (out, kv_out) if return_kv else out
 
     def _forward_fused(self, latent, t, context, *, cache, t_offset, update_cache, anchor_kv,
-                       anchor_align, return_kv, ctx_emb, text=None, kv_only=False):
+                       anchor_align, return_kv, ctx_emb, text=None, kv_only=False,
+                       independent_frames=False):
         """The sharded block with its collectives fused into the kernels: each
         rank's LN-quant rows are pushed by the copy engines into every rank's
         gather buffer and the next GEMM waits per remote shard (all-gather);
@@ -508,7 +511,8 @@ class TPSRDiT(SRDiT):
         Hl = c.num_heads // P
         if text is not None:
             ctx_emb = text.ctx_emb
-        S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, Hl, Dl)
+        S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, Hl, Dl,
+                        independent_frames)
         x_full, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
         f, h, w = grid
         L, M, Lc = S.L, S.M, S.Lc
