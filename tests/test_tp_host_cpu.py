@@ -187,3 +187,71 @@ def test_single_rank_model_refuses_cpu():
     cfg = M.SRDiTConfig(**CFG)
     with pytest.raises(srdit._lib.SrditError):
         M.SRDiT(cfg, M.SRDiT.seeded_state_dict(cfg, "cpu", 3), "cpu")
+
+
+def _harvest_worker(rank, world, port, out_q):
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+    try:
+        torch.set_num_threads(2)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=120))
+        importlib.import_module("dreamx-creator_b200")
+        M = importlib.import_module("dreamx-creator_b200.model")
+        T = importlib.import_module("dreamx-creator_b200.tp")
+        from tests import cpu_ops
+
+        class CpuTP(T.TPSRDiT):
+            ops = cpu_ops
+            require_cuda = False
+
+        cfg = M.SRDiTConfig(**CFG)
+        f, h, w = GRID
+        g = torch.Generator().manual_seed(21)
+        ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(torch.bfloat16)
+        lq = torch.randn(cfg.in_dim, f, 2 * h, 2 * w, generator=g).to(torch.bfloat16)
+        sd = M.SRDiT.seeded_state_dict(cfg, "cpu", 3)
+        model = CpuTP(cfg, sd, "cpu", fused=False)
+        _, kv = model.forward_chunk(lq, 0.0, ctx, cache=None, t_offset=2, return_kv=True,
+                                    independent_frames=True)
+        per = [model.forward_chunk(lq[:, j:j + 1], 0.0, ctx, cache=None, t_offset=2 + j,
+                                   return_kv=True)[1] for j in range(f)]
+        worst = 1.0
+        for li, (k, v) in enumerate(kv):
+            for got, ref in ((k, torch.cat([p[li][0] for p in per])),
+                             (v, torch.cat([p[li][1] for p in per]))):
+                x, y = got.double().reshape(-1), ref.double().reshape(-1)
+                worst = min(worst, float(torch.dot(x, y) / (x.norm() * y.norm())))
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, worst, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        import traceback
+        out_q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+
+
+def test_tp2_batched_harvest_matches_per_frame_forwards():
+    """Two gloo ranks: each rank's share of the anchor harvest run as one
+    forward over independent frames equals its share from one 1-frame forward
+    per frame (cosine >= 0.9999; the double's float matmul may block rows
+    differently for 1 and 3 frames)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_harvest_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, worst, err = q.get(timeout=300)
+            results[rank] = (worst, err)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    errs = [e for _, e in results.values() if e]
+    assert not errs, errs
+    assert min(w for w, _ in results.values()) >= 0.9999, results
