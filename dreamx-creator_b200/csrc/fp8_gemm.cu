@@ -15,7 +15,7 @@
 //
 // Design: a CTA pair (cluster of 2) computes a 256 x BN output tile with one
 // tcgen05.mma.cta_group::2 per 32-deep K step: each CTA stages its own 128 rows
-// of A and BN/2 rows of B (TMA, 128-byte swizzle, 5-stage ring), the even CTA
+// of A and BN/2 rows of B (TMA, 128-byte swizzle, 5- or 6-stage ring), the even CTA
 // issues the MMAs, and each CTA's TMEM holds its 128 accumulator rows. Per CTA:
 // warp 0 = TMA producer, warp 1 = MMA issuer / TMEM owner, warps 2-5 =
 // epilogue. Two TMEM accumulators let the epilogue of one tile overlap the MMAs
