@@ -300,23 +300,6 @@ __global__ void __launch_bounds__(256) residual_kernel(
 }
 
 // ---------------------------------------------------------------- packed rows
-// ln_mod_quant and rms_rope keep one warp per row, with the row held as packed
-// bf16 (4 registers per 8 values) across the passes. The unpack below is a
-// volatile asm, so the compiler re-unpacks on every pass (two ALU ops per
-// value) instead of caching 8 floats per chunk: a 3072-wide row then costs 48
-// registers, and 24 rows stay in flight per SM.
-SRDIT_DEV void unpack8_v(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t lo, hi;
-    asm volatile("shl.b32 %0, %1, 16;" : "=r"(lo) : "r"(w[i]));
-    asm volatile("and.b32 %0, %1, 0xffff0000;" : "=r"(hi) : "r"(w[i]));
-    f[2 * i] = __uint_as_float(lo);
-    f[2 * i + 1] = __uint_as_float(hi);
-  }
-}
-
 // A read-only 16-byte load that the compiler keeps in program order (volatile
 // asm): used for per-column vectors inside the unrolled row loops, so their
 // loads are not all hoisted ahead of the loop into live registers.

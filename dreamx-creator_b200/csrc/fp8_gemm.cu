@@ -117,8 +117,6 @@ SRDIT_DEV float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanh_sfu(inner));
 }
 
-SRDIT_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
 template <int EPI>
 constexpr bool has_residual() { return EPI == EPI_GATED_RES || EPI == EPI_RES; }
 

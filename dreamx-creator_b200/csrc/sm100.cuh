@@ -36,9 +36,6 @@ SRDIT_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-SRDIT_DEV uint32_t lane_id() { return threadIdx.x & 31u; }
-SRDIT_DEV uint32_t warp_id() { return __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0); }
-
 SRDIT_DEV bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
@@ -96,20 +93,6 @@ SRDIT_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 //
 // `abort_flag` (shared memory, may be null) lets one role that already gave up
 // release the others quickly: every waiter polls it and returns false once set.
-// try_wait that lets the thread sleep (up to `hint_ns`) until the phase completes,
-// instead of re-issuing the poll.
-SRDIT_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
 SRDIT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
                          volatile uint32_t* abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -216,13 +199,6 @@ SRDIT_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
-SRDIT_DEV void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
-  asm volatile(
-      "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
-          cluster_addr),
-      "r"(bytes)
-      : "memory");
-}
 // 2-SM TMA tile load into this CTA's shared memory, completing bytes on an
 // mbarrier that may live in the peer CTA (shared::cluster address).
 SRDIT_DEV void tma_load_2d_2sm(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
@@ -314,16 +290,6 @@ SRDIT_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, ui
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// D(tmem) (+)= A(smem) * B(smem)^T, e4m3/e5m2 inputs, fp32 accumulate.
-SRDIT_DEV void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
 // ---- cta_group::2 forms: a CTA pair shares one MMA (M = 256); both CTAs
 // allocate the same TMEM columns, the even CTA issues the MMAs.
@@ -369,15 +335,6 @@ SRDIT_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
-      : "r"(taddr));
-}
-SRDIT_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
 SRDIT_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
