@@ -255,3 +255,79 @@ def test_tp2_batched_harvest_matches_per_frame_forwards():
     errs = [e for _, e in results.values() if e]
     assert not errs, errs
     assert min(w for w, _ in results.values()) >= 0.9999, results
+
+
+def _anchor_worker(rank, world, port, out_q):
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+    try:
+        torch.set_num_threads(2)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=120))
+        importlib.import_module("dreamx-creator_b200")
+        M = importlib.import_module("dreamx-creator_b200.model")
+        T = importlib.import_module("dreamx-creator_b200.tp")
+        P = importlib.import_module("dreamx-creator_b200.pipeline")
+        from tests import cpu_ops
+
+        class CpuTP(T.TPSRDiT):
+            ops = cpu_ops
+            require_cuda = False
+
+        class CpuOne(M.SRDiT):
+            ops = cpu_ops
+            require_cuda = False
+
+        cfg = M.SRDiTConfig(**CFG)
+        f, h, w = GRID
+        g = torch.Generator().manual_seed(31)
+        ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(torch.bfloat16)
+        lq = torch.randn(cfg.in_dim, f, 2 * h, 2 * w, generator=g).to(torch.bfloat16)
+        x = torch.randn(cfg.in_dim, f, 2 * h, 2 * w, generator=g).to(torch.bfloat16)
+        sd = M.SRDiT.seeded_state_dict(cfg, "cpu", 3)
+
+        def run(model):
+            stream = P.RefinerStream(model, ctx)
+            stream._ensure_text()
+            anchor = stream.harvest_anchor(lq)
+            return model.forward_chunk(x, 625.0, ctx, cache=None, anchor_kv=anchor,
+                                       text=stream.text).float()
+
+        tp_out = run(CpuTP(cfg, sd, "cpu", fused=False))
+        cos = None
+        if rank == 0:
+            ref = run(CpuOne(cfg, sd, "cpu"))
+            a, b = tp_out.double().reshape(-1), ref.double().reshape(-1)
+            cos = float(torch.dot(a, b) / (a.norm() * b.norm()))
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, cos, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        import traceback
+        out_q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+
+
+def test_tp2_anchor_harvest_and_frame_anchor_match_one_rank():
+    """Two gloo ranks: the LQ-anchor path (each rank harvests its heads' share
+    of the anchor in one forward, then a frame-aligned anchored denoise)
+    reproduces one rank's output (cosine >= 0.999)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_anchor_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, cos, err = q.get(timeout=300)
+            results[rank] = (cos, err)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    errs = [e for _, e in results.values() if e]
+    assert not errs, errs
+    assert results[0][0] >= 0.999, results
