@@ -43,12 +43,14 @@ def anchor_stride(h, w, bh, bw, anchor_hw):
         return 1, 1
     h_a, w_a = int(anchor_hw[0]), int(anchor_hw[1])
     if h_a <= 0 or w_a <= 0:
-        raise ValueError(f"anchor_hw must be positive, got {(h_a, w_a)}.")
+        raise ValueError(f"LQ-anchor token grid {(h_a, w_a)}: both sides need at least one token")
     if h % h_a or w % w_a:
-        raise ValueError(f"anchor grid {(h_a, w_a)} must divide the query token grid {(h, w)}.")
+        raise ValueError(f"LQ-anchor token grid {(h_a, w_a)} is not a whole-number thinning of the "
+                         f"{h}x{w} query grid")
     s_h, s_w = h // h_a, w // w_a
     if bh % s_h or bw % s_w:
-        raise ValueError(f"anchor stride {(s_h, s_w)} must divide the query block size {(bh, bw)}.")
+        raise ValueError(f"{bh}x{bw} query blocks cannot be thinned by the anchor step "
+                         f"{(s_h, s_w)}: a block would straddle anchor tokens")
     return s_h, s_w
 
 
@@ -96,8 +98,8 @@ class WindowSpec:
                 runs = [(i * bt, (i + 1) * bt, max(0, i - rt) * bt, (i + 1) * bt)
                         for i in range(f_cur // bt)]
         if sum(b - a for a, b, _, _ in runs) != f_cur or runs[0][0] != 0 or runs[-1][1] != f_cur:
-            raise ValueError(f"temporal runs {runs} do not partition the {f_cur} query frames; "
-                             f"block_t={self.block_t} must divide f_cur.")
+            raise ValueError(f"the {f_cur} query frames do not split into whole temporal blocks of "
+                             f"{self.block_t} (runs {runs})")
         return runs
 
     def anchor_grid(self):
@@ -132,7 +134,8 @@ def plan_rows(spec: WindowSpec, anchor_mode=None):
     rows = []
     if anchor_mode == "frame":
         if len(runs) != 1 or runs[0][:2] != (0, spec.f_cur):
-            raise ValueError(f'anchor_mode="frame" needs one query run [0, {spec.f_cur}), got {runs}.')
+            raise ValueError(f"a frame-aligned anchor pairs query frame t with anchor frame t, which "
+                             f"needs all {spec.f_cur} query frames in one run (got {runs})")
         kv0, kv1 = runs[0][2:]
         for (qh0, qhL, kh0, khL) in hb:
             for (qw0, qwL, kw0, kwL) in wb:

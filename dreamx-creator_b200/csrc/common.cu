@@ -1,6 +1,7 @@
 // common.cu -- host helpers: tensor-map encoding, device caches, version/status.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "srdit_internal.h"
@@ -10,7 +11,7 @@ namespace srdit {
 namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
-int g_sms[kMaxDevices] = {};
+std::atomic<int> g_sms[kMaxDevices] = {};
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   std::call_once(g_encode_once, [] {
@@ -27,12 +28,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 
 int num_sms(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return 148;
-  if (g_sms[dev] == 0) {
+  int v = g_sms[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    g_sms[dev] = n > 0 ? n : 148;
+    v = n > 0 ? n : 148;
+    g_sms[dev].store(v, std::memory_order_relaxed);
   }
-  return g_sms[dev];
+  return v;
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,

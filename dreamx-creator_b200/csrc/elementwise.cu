@@ -15,6 +15,8 @@
 //                   (models.py:173-214), written to the
 //                   destination buffers (q buffer, KV-cache frame slots); V rows are
 //                   copied alongside so the cache is filled in the same pass.
+#include <atomic>
+
 #include "sm100.cuh"
 #include "srdit_internal.h"
 
@@ -790,12 +792,15 @@ int cs_grid(int threads, int M, int* grid_out) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= kMaxDevices) return SRDIT_EINVAL;
-  static int per_sm[kMaxDevices][kCsMaxThreads / 32 + 1] = {};
-  int& n = per_sm[dev][threads / 32];
+  // resident CTAs per SM, per device and block size (computed once; host
+  // threads racing here store the same value)
+  static std::atomic<int> per_sm[kMaxDevices][kCsMaxThreads / 32 + 1] = {};
+  int n = per_sm[dev][threads / 32].load(std::memory_order_relaxed);
   if (n == 0) {
     const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, Kern, threads, 0);
     if (e != cudaSuccess) return static_cast<int>(e);
     if (n <= 0) n = 1;
+    per_sm[dev][threads / 32].store(n, std::memory_order_relaxed);
   }
   const int need = (M + kGroup - 1) / kGroup;
   const int cap = n * num_sms(dev);
@@ -986,10 +991,18 @@ extern "C" int srdit_ln_mod_quant_tp(const void* x, long long ldx, int M, int K,
                                 ldq, nullptr, pe, stream);
 }
 
-// The last-CTA counter of srdit_ln_mod_quant_tp_static: a file-scope device
-// array (one instance per device), so that entry point allocates nothing.
-// Element 0 is the counter; the kernel leaves it at 0 after every launch.
-__device__ __align__(256) uint32_t g_ln_tp_done[64];
+// Scratch of srdit_ln_mod_quant_tp_static, the entry point for callers that
+// cannot allocate device memory: the kernel's last-CTA counter lives in this
+// file-scope device array instead of a caller buffer. The module holds one copy
+// per device for each CUDA context (each process) that loads the library, until
+// the process exits. Element 0 is the only word; the kernel's last CTA resets
+// it to 0 before it signals the peers, so every launch starts from 0.
+static __device__ __align__(256) uint32_t g_ln_tp_done[1];
+
+// Its address on each device, looked up on the first call made with that device
+// current (cudaGetSymbolAddress, checked) and reused afterwards. Host threads
+// that race on the first call store the same address.
+static std::atomic<uint32_t*> g_ln_tp_done_addr[kMaxDevices] = {};
 
 extern "C" int srdit_ln_mod_quant_tp_static(const void* x, long long ldx, int M, int K,
                                             float eps, const void* ln_weight, const void* ln_bias,
@@ -1002,16 +1015,16 @@ extern "C" int srdit_ln_mod_quant_tp_static(const void* x, long long ldx, int M,
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
   if (dev < 0 || dev >= kMaxDevices) return SRDIT_EINVAL;
-  // the counter's address on each device, looked up once per device
-  static uint32_t* done_addr[kMaxDevices] = {};
-  if (!done_addr[dev]) {
+  uint32_t* done = g_ln_tp_done_addr[dev].load(std::memory_order_acquire);
+  if (!done) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_ln_tp_done);
     if (e != cudaSuccess) return static_cast<int>(e);
-    done_addr[dev] = static_cast<uint32_t*>(ptr);
+    done = static_cast<uint32_t*>(ptr);
+    g_ln_tp_done_addr[dev].store(done, std::memory_order_release);
   }
   return srdit_ln_mod_quant_tp(x, ldx, M, K, eps, ln_weight, ln_bias, shift, scale, ldq, q_rows,
-                               s_rows, flags, done_addr[dev], rank, world, stream);
+                               s_rows, flags, done, rank, world, stream);
 }
 
 extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,

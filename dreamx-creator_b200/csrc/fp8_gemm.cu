@@ -23,6 +23,7 @@
 // stages bf16 rows in a swizzled buffer and writes them with TMA tile stores
 // (which also clip the M / N edges). The kernel is persistent: one pair per two
 // SMs walks the tile list.
+#include <atomic>
 #include "sm100.cuh"
 #include "srdit_internal.h"
 
@@ -492,12 +493,14 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   auto kern = fp8_gemm_kernel<EPI, BN>;
   int dev = 0;
   cudaGetDevice(&dev);
-  static bool attr_done[kMaxDevices] = {};
-  if (dev < kMaxDevices && !attr_done[dev]) {
+  // per device: set the shared-memory attribute once (host threads may race
+  // here; setting it twice is harmless)
+  static std::atomic<bool> attr_done[kMaxDevices] = {};
+  if (dev < kMaxDevices && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
   const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
   const int pairs = num_sms(dev) / 2;

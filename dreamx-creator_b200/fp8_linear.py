@@ -1,14 +1,18 @@
 """Drop-in ``Fp8Linear`` on the B200 e4m3 GEMM.
 
-Mirrors the reference module (video_refiner/wan/modules/sr_dit/fp8_linear.py:214-354):
-the weight is quantised once, per output channel, to e4m3 with the reference's
-row-wise rule; each call quantises the activation per token and runs the
-row-wise scaled GEMM with the bias in the epilogue, returning bf16. The module
-swap ``convert_linears_to_fp8`` and the ``weight`` stand-in that keeps
-``self.o.weight.dtype`` working are the reference's interface.
+Interface of the reference module (video_refiner/wan/modules/sr_dit/fp8_linear.py:
+214-354): ``Fp8Linear(weight, bias)`` / ``Fp8Linear.from_linear(lin)``, the
+buffers ``weight_fp8`` (e4m3 [N, K]), ``weight_scale`` (fp32 [1, N]), ``bias``
+(bf16 [N]) and the zero-element ``weight`` stand-in that keeps
+``self.o.weight.dtype`` working (models.py:673, :1013), ``forward(x[..., K]) ->
+[..., N]`` in x's dtype, ``TARGETS_ALL`` and ``convert_linears_to_fp8(model,
+targets, skip_first, skip_last, blocks_attr)``.
 
-The per-call path is two kernels of libsrdit_b200.so (row-wise quantiser +
-tcgen05 GEMM); there is no torch._scaled_mm or CPU path.
+The weight is quantised once, per output channel, with the reference's
+row-wise rule (fp8_linear.py:93-103); every call quantises the activation per
+token (``srdit_quant_rowwise``) and runs the row-wise scaled tcgen05 GEMM with
+the bias in its epilogue (``srdit_fp8_gemm``). There is no torch._scaled_mm or
+CPU path: without the library or a GPU, the call raises.
 """
 from __future__ import annotations
 
@@ -49,89 +53,102 @@ def quantize_weight(weight: torch.Tensor):
 class Fp8Linear(nn.Module):
     """Frozen inference Linear computed as a row-wise scaled e4m3 GEMM."""
 
+    # buffers whose dtype is part of their meaning: a module-wide dtype cast
+    # (``.to(torch.bfloat16)``, ``.half()``, ``.float()``) must only move them
+    _FIXED_DTYPE = {"weight_fp8": FP8_DTYPE, "weight_scale": torch.float32,
+                    "bias": torch.bfloat16}
+
     def __init__(self, weight, bias=None):
         super().__init__()
         if weight.dim() != 2:
-            raise ValueError(f"expected a 2D weight, got {tuple(weight.shape)}")
-        self.out_features, self.in_features = weight.shape
-        w_fp8, w_scale = quantize_weight(weight)
-        self.register_buffer("weight_fp8", w_fp8.contiguous(), persistent=False)
-        self.register_buffer("weight_scale", w_scale.reshape(1, -1).contiguous().float(),
+            raise ValueError(f"Fp8Linear needs a 2-D [out, in] weight, got {tuple(weight.shape)}")
+        n_out, n_in = (int(v) for v in weight.shape)
+        self.out_features, self.in_features = n_out, n_in
+        q, s = quantize_weight(weight)
+        self.register_buffer("weight_fp8", q.contiguous(), persistent=False)
+        self.register_buffer("weight_scale", s.float().view(1, n_out).contiguous(),
                              persistent=False)
-        if bias is None:
-            self.bias = None
-        else:
-            b = bias.detach().clone()
-            if b.dtype != torch.bfloat16:
-                b = b.to(torch.bfloat16)
-            self.register_buffer("bias", b.contiguous(), persistent=False)
-        self.register_buffer("weight", torch.empty(0, dtype=weight.dtype, device=weight.device),
+        # the GEMM epilogue adds a bf16 bias to the fp32 accumulator
+        self.register_buffer("bias", None if bias is None else
+                             bias.detach().to(torch.bfloat16).clone().contiguous(),
                              persistent=False)
+        # zero-element stand-in: callers read .weight.dtype; any use as a real
+        # weight fails on its shape instead of computing with stale values
+        self.register_buffer("weight", weight.new_empty(0), persistent=False)
 
     @classmethod
-    def from_linear(cls, lin):
+    def from_linear(cls, lin: nn.Linear) -> "Fp8Linear":
         return cls(lin.weight, lin.bias).to(lin.weight.device)
 
     def _apply(self, fn, recurse=True):
-        saved = {n: b for n, b in self._buffers.items()
-                 if n in ("weight_fp8", "weight_scale", "bias") and b is not None}
-        out = super()._apply(fn, recurse)
-        for name, old in saved.items():
-            new = out._buffers[name]
-            if new is not None and new.dtype != old.dtype:
-                out._buffers[name] = old.to(device=new.device)
-        return out
+        """Module-wide conversions move the fixed-dtype buffers, never cast them.
 
-    def forward(self, x):
-        out_dtype = x.dtype
-        lead = x.shape[:-1]
-        x2 = x.reshape(-1, self.in_features)
-        if x2.dtype != torch.bfloat16:
-            x2 = x2.to(torch.bfloat16)
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
-        xq, xs = ops.quant_rowwise(x2)
-        out = ops.fp8_gemm(xq, xs, self.weight_fp8, self.weight_scale.reshape(-1), self.bias)
-        if out_dtype is not torch.bfloat16:
-            out = out.to(out_dtype)
-        return out.reshape(*lead, self.out_features)
+        The fixed buffers are hidden from ``fn`` while the base class converts
+        the rest; ``fn`` is then applied to an empty probe tensor to learn the
+        device it sends tensors to, and the original buffers are moved there
+        unchanged (a bf16 round trip of the fp32 scales, or fp8 codes cast as
+        numbers, would silently change the product)."""
+        fixed = {}
+        for name in self._FIXED_DTYPE:
+            buf = self._buffers.get(name)
+            if buf is not None:
+                fixed[name] = buf
+                self._buffers[name] = None
+        try:
+            super()._apply(fn, recurse)
+        finally:
+            if fixed:
+                home = next(iter(fixed.values())).device
+                dest = fn(torch.empty(0, device=home)).device
+                for name, buf in fixed.items():
+                    self._buffers[name] = buf if buf.device == dest else buf.to(dest)
+        return self
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x [..., in_features] -> [..., out_features] in x's dtype (computed from
+        x rounded to bf16, the quantiser's input type)."""
+        if x.shape[-1] != self.in_features:
+            raise ValueError(f"Fp8Linear expects {self.in_features} input features, "
+                             f"got {x.shape[-1]}")
+        rows = x.reshape(-1, self.in_features)
+        rows = rows.to(torch.bfloat16).contiguous()  # a view when x is contiguous bf16
+        xq, xs = ops.quant_rowwise(rows)
+        y = ops.fp8_gemm(xq, xs, self.weight_fp8, self.weight_scale.view(-1), self.bias)
+        return y.to(x.dtype).view(*x.shape[:-1], self.out_features)
 
     def extra_repr(self):
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"bias={self.bias is not None}, fp8=e4m3-rowwise, backend=b200")
 
 
-def convert_linears_to_fp8(model, targets=TARGETS_ALL, skip_first=0, skip_last=0,
+def convert_linears_to_fp8(model: nn.Module, targets=TARGETS_ALL, skip_first=0, skip_last=0,
                            blocks_attr="blocks"):
-    """Swap the target Linears inside ``model.blocks`` for Fp8Linear, in place
-    (fp8_linear.py:313-354). Returns the converted qualified names."""
+    """Replace the ``targets`` Linears of ``model.<blocks_attr>[i]`` by Fp8Linear,
+    in place, for block indices skip_first <= i < len(blocks) - skip_last.
+
+    Targets are dotted paths inside a block (``"self_attn.q"``, ``"ffn.0"``).
+    A missing path, or one that is not an ``nn.Linear`` (for instance an
+    Fp8Linear from an earlier call), is left alone, so the call is idempotent.
+    Returns the qualified names converted, e.g. ``"blocks.3.ffn.0"``.
+    """
     if not torch.cuda.is_available():
         raise _lib.SrditError("Fp8Linear needs a CUDA device (there is no CPU path)")
     blocks = getattr(model, blocks_attr, None)
     if blocks is None:
         return []
-    n = len(blocks)
-    lo, hi = int(skip_first), n - int(skip_last)
+    chosen = range(int(skip_first), len(blocks) - int(skip_last))
     converted = []
-    for i, block in enumerate(blocks):
-        if not (lo <= i < hi):
-            continue
-        for suffix in targets:
-            *path, leaf = suffix.split(".")
-            parent = block
-            for p in path:
-                parent = getattr(parent, p, None) if not p.isdigit() else parent[int(p)]
-                if parent is None:
-                    break
-            if parent is None:
+    for idx in chosen:
+        block = blocks[idx]
+        for path in targets:
+            try:
+                lin = block.get_submodule(path)
+            except AttributeError:
                 continue
-            cur = parent[int(leaf)] if leaf.isdigit() else getattr(parent, leaf, None)
-            if not isinstance(cur, nn.Linear):
+            if not isinstance(lin, nn.Linear):
                 continue
-            new = Fp8Linear.from_linear(cur)
-            if leaf.isdigit():
-                parent[int(leaf)] = new
-            else:
-                setattr(parent, leaf, new)
-            converted.append(f"{blocks_attr}.{i}.{suffix}")
+            owner_path, _, leaf = path.rpartition(".")
+            owner = block.get_submodule(owner_path) if owner_path else block
+            owner.add_module(leaf, Fp8Linear.from_linear(lin))
+            converted.append(f"{blocks_attr}.{idx}.{path}")
     return converted

@@ -26,9 +26,11 @@ Per block the work is 10 launches of libsrdit_b200.so kernels, in this order:
   quant_rowwise(h, amax)             -> h_q
   fp8_gemm(h_q, W_ffn2, gated_res e5)-> x              x + ffn.2(h) * e5
 
-The per-layer text K/V (cross_attn.k/v over the 512 text tokens) is computed
-by the same GEMM + RMSNorm kernels once per forward, as the reference does
-(models.py:1048-1054).
+The per-layer text K/V (cross_attn.k/v over the 512 text tokens) comes from
+``SRDiT.text_cache``: the same GEMM + RMSNorm kernels run once per text context
+(the reference recomputes them in every forward, models.py:1048-1054; the
+values do not change within a clip). A forward given no cache computes them
+inline.
 
 The KV cache is a per-layer ring of ``kv_len + chunk`` frame slots: the current
 chunk's roped K and V are written straight into their slots by ``rms_rope`` and
@@ -453,7 +455,7 @@ class SRDiT:
     def forward_chunk(self, latent, t, context, *, cache: KVRing | None = None,
                       t_offset=0, update_cache=False, anchor_kv=None, anchor_align="frame",
                       return_kv=False, ctx_emb=None, text: TextCache | None = None,
-                      kv_only=False, independent_frames=False):
+                      kv_only=False, independent_frames=False, block_outputs=None):
         """One streaming forward over a chunk (``_forward_inference`` for one sample).
 
         latent [C_in, f, H, W]; ``cache`` holds the previous chunks' K/V (read in
@@ -470,6 +472,8 @@ class SRDiT:
         no anchor): the chunk's frames are independent 1-frame samples -- frame j
         attends to frame j only, at temporal position t_offset + j -- which is the
         anchor harvest's batch (causal_inference.py:456-460) as one forward.
+        ``block_outputs`` (a list, optional): every block's output hidden state
+        [M, D] bf16 is appended to it (a copy; for parity checks per block).
         Returns the refined prediction [C_out, f, H, W] bf16 (and the K/V list).
         """
         if kv_only and (return_kv or not update_cache):
@@ -563,6 +567,8 @@ class SRDiT:
             ops.quant_rowwise(hbuf, amax=amax, q=hq, scale=hs)
             ops.fp8_gemm(hq, hs, ly.w_f2, ly.s_f2, ly.b_f2, x, epilogue="gated_res", residual=x,
                          gate=em[5])
+            if block_outputs is not None:
+                block_outputs.append(x.clone())
         if update_cache:
             cache.commit(f)
         if kv_only:

@@ -275,12 +275,29 @@ int srdit_ln_mod_quant_tp(const void* x, long long ldx, int M, int K, float eps,
                           uint32_t* done, int rank, int world, cudaStream_t stream);
 
 /*
- * srdit_ln_mod_quant_tp without the `done` argument: the last-CTA counter is a
- * file-scope device array of the library (one per device, its address looked
- * up once per device with cudaGetSymbolAddress), so this entry point
- * allocates nothing and needs no zeroed scratch from the caller. Launches of
- * it on one device must not overlap (they share the counter); the kernel
- * leaves the counter at 0 after each launch.
+ * srdit_ln_mod_quant_tp without the `done` argument, for callers that cannot
+ * allocate device memory: a host runtime that owns a fixed pool handed out
+ * before the first step and refuses allocations later (a serving process with
+ * a static memory plan), or code running between a CUDA-graph capture's
+ * begin and end, where a cudaMalloc would break the capture. Such a caller
+ * has no way to provide the zeroed `done` word.
+ *
+ * The last-CTA counter is instead a one-word file-scope device array of the
+ * library (4 bytes, 256-byte aligned), held by every GPU that loads the
+ * library until the process exits. The entry point calls no cudaMalloc,
+ * cudaFree or allocating routine. Its first call on a device looks the array's
+ * address up with cudaGetSymbolAddress (with that device current) and keeps
+ * it; make that first call before any stream capture, and make no call after
+ * a cudaDeviceReset in the same process. The array is per CUDA context, i.e.
+ * per process and device: two processes on one GPU each have their own.
+ * Every launch on one device shares the word, so launches that overlap on the
+ * GPU (two streams, or two threads' streams) race on it and must not be
+ * issued; the kernel's last CTA resets it to 0, so each launch starts from 0.
+ * With world > 1 the caller must still keep the peers' flag words and gather
+ * buffers for one launch out of use by any other launch in flight. K must be a
+ * multiple of 512 and at most 4096 (the same limits as srdit_ln_mod_quant_tp;
+ * larger widths return SRDIT_EUNSUPPORTED). There is no counterpart in the
+ * reference: it adds a no-allocation variant of the entry point above.
  */
 int srdit_ln_mod_quant_tp_static(const void* x, long long ldx, int M, int K, float eps,
                                  const void* ln_weight, const void* ln_bias, const float* shift,

@@ -23,8 +23,10 @@ def sinusoidal(dim, position):
 
 
 def forward_chunk(sd, cfg, latent, t, context, *, caches=None, t_offset=0, kv_len=9,
-                  linear="fp8", fp8caches=None, anchor=None, anchor_align="frame"):
-    """Returns (out [C_out, f, H, W] bf16, new per-layer caches [(K, V)])."""
+                  linear="fp8", fp8caches=None, anchor=None, anchor_align="frame",
+                  block_outputs=None):
+    """Returns (out [C_out, f, H, W] bf16, new per-layer caches [(K, V)]).
+    ``block_outputs`` (a list, optional) receives every block's output [L, dim]."""
     bf = lambda n: sd[n].to(torch.bfloat16)  # noqa: E731
     f32 = lambda n: sd[n].float()  # noqa: E731
     D = cfg.dim
@@ -63,6 +65,8 @@ def forward_chunk(sd, cfg, latent, t, context, *, caches=None, t_offset=0, kv_le
             block_t=cfg.block_t, heads=cfg.num_heads, eps=cfg.eps, linear=linear,
             fp8cache=fp8caches[i])
         new.append((nk, nv))
+        if block_outputs is not None:
+            block_outputs.append(x)
     mod = f32("head.modulation").reshape(2, D) + e
     n = onum.layer_norm(x, cfg.eps)
     y = torch.nn.functional.linear(n.float() * (1 + mod[1]) + mod[0], f32("head.head.weight"),

@@ -18,6 +18,12 @@ Files:
   quant.npz     ``_quantize_rowwise_impl`` outputs
   norms.npz     ``WanLayerNorm`` / ``WanRMSNorm`` outputs
   block.npz     one ``WanAttentionBlock`` streaming forward (bf16, window attn)
+  model.npz     two streaming chunks of a small ``WanModel`` (``_forward_inference``:
+                patch / time / text embeddings, window-attention blocks, ``Head``,
+                ``unpatchify``), the second over the first chunk's KV cache
+
+The only argument is the path of the reference checkout; nothing here assumes
+where it lives.
 """
 from __future__ import annotations
 
@@ -263,9 +269,67 @@ def gen_block(models):
     print("block ok")
 
 
+def gen_model(models):
+    """A small WanModel (2 blocks, dim 128, 2 heads of 64, window attention 2x2
+    radius 1 on the sdpa backend), seeded weights; two 3-frame chunks through its
+    streaming ``forward`` -> ``_forward_inference`` (models.py:1877-2002), the second
+    at temporal offset 3 over the first chunk's returned KV cache. The time
+    embedding, time projection and head are kept in fp32 (what the CUDA fp32
+    autocast around them gives on the GPU; the CPU autocast is a no-op), the rest
+    in bf16."""
+    dim, ffn, heads, layers, c_in, c_out, text_dim, text_len = 128, 256, 2, 2, 16, 16, 32, 8
+    f, H, W = 3, 8, 12
+    torch.manual_seed(7)
+    m = models.WanModel(model_type="t2v", patch_size=(1, 2, 2), text_len=text_len, in_dim=c_in,
+                        dim=dim, ffn_dim=ffn, freq_dim=256, text_dim=text_dim, out_dim=c_out,
+                        num_heads=heads, num_layers=layers, qk_norm=True, cross_attn_norm=True,
+                        eps=1e-6, stream_chunk_size=3)
+    m.enable_window_attention(window_block_hw=(2, 2), window_block_radius_hw=(1, 1),
+                              window_attn_impl="sdpa")
+    g = torch.Generator().manual_seed(8)
+    with torch.no_grad():
+        for name, p in sorted(m.named_parameters()):
+            if name.endswith("modulation"):
+                p.copy_(torch.randn(p.shape, generator=g) / dim ** 0.5)
+            elif name.endswith("bias"):
+                p.copy_(torch.randn(p.shape, generator=g) * 0.01)
+            elif "norm" in name:
+                p.copy_(1 + 0.1 * torch.randn(p.shape, generator=g))
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.05)
+    m = m.to(torch.bfloat16)
+    for sub in (m.time_embedding, m.time_projection, m.head):
+        sub.float()
+    for blk in m.blocks:
+        blk.modulation.data = blk.modulation.data.float()
+    m.eval()
+    lat = [torch.randn(c_in, f, H, W, generator=g).to(torch.bfloat16) for _ in range(2)]
+    ctx = torch.randn(text_len - 2, text_dim, generator=g).to(torch.bfloat16)  # padded by the model
+    L = f * (H // 2) * (W // 2)
+    outs, caches = [], None
+    with torch.no_grad():
+        for i, x in enumerate(lat):
+            o, caches = m(x=[x], t=torch.tensor([625.0]), context=[ctx], seq_len=L,
+                          temporal_offset=3 * i, kv_caches=caches, kv_len=9, is_stream=True)
+            outs.append(o[0])
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).numpy()
+    sd = {f"w.{k}": (bits(v) if v.dtype == torch.bfloat16 else v.numpy())
+          for k, v in m.state_dict().items()}
+    np.savez_compressed(HERE / "model.npz", lat0=bits(lat[0]), lat1=bits(lat[1]), ctx=bits(ctx),
+                        out0=bits(outs[0]), out1=bits(outs[1]),
+                        k1_layer1=bits(caches[1][0][0]), v1_layer1=bits(caches[1][1][0]),
+                        dims=np.asarray([dim, ffn, heads, layers, c_in, c_out, text_dim,
+                                         text_len, f, H, W]), **sd)
+    print("model ok")
+
+
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-    attention, bgt, fp8, models = load_reference(root)
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/gen_golden.py <path of the reference "
+                         "checkout> [writes the .npz files beside this script]")
+    attention, bgt, fp8, models = load_reference(sys.argv[1])
     torch.set_num_threads(8)
     gen_plans(attention, bgt)
     gen_quant(fp8)
@@ -273,6 +337,7 @@ def main():
     gen_rope(models)
     gen_winattn(attention, models)
     gen_block(models)
+    gen_model(models)
 
 
 if __name__ == "__main__":

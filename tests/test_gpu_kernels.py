@@ -1,4 +1,6 @@
 """Parity of the sm_100a kernels with the CPU oracle (GPU required)."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -48,13 +50,16 @@ def test_ln_mod_quant(srdit, cuda_device, affine, modulate):
     if modulate:
         n = (n.float() * (1 + scale) + shift).to(torch.bfloat16)
     qo, so = onum.quantize_rowwise(n)
-    # LayerNorm statistics are reduced in a different order than torch's: allow
-    # the rare bf16 tie to round the other way, nothing more.
+    # LayerNorm statistics are reduced in a different order than torch's CPU
+    # kernel, so a bf16 tie can round the other way before quantisation. Measured
+    # on B200 (this test's inputs and 6912 x 3072, 4096 x 4096, 2000 x 1024 with
+    # each mode): 0 to 1.6e-6 of the e4m3 bytes differ, every row scale is
+    # bit-identical; the bounds below keep an order of magnitude of margin.
     deq = q.float().cpu() * qs.cpu()[:, None]
     deq_o = qo.float() * so
-    assert onum.rel_fro(deq, deq_o) < 2e-3
-    assert (q.view(torch.uint8).cpu() == qo.view(torch.uint8)).float().mean() > 0.995
-    np.testing.assert_allclose(qs.cpu().numpy(), so.reshape(-1).numpy(), rtol=1e-2)
+    assert onum.rel_fro(deq, deq_o) < 1e-4
+    assert (q.view(torch.uint8).cpu() != qo.view(torch.uint8)).float().mean() <= 1e-5
+    np.testing.assert_array_equal(qs.cpu().numpy(), so.reshape(-1).numpy())
 
 
 def test_rms_rope_matches_reference_math(srdit, cuda_device):
@@ -288,3 +293,59 @@ def test_fp8_gemm_v_ring(srdit, cuda_device):
     used = {(slot0 + f) % cap for f in range(M // ft)}
     for s in set(range(cap)) - used:
         assert not bool(ring[s * ft:(s + 1) * ft].any())
+
+
+# --------------------------------------------------------------------------- bounded waits
+def test_residual_wait_times_out_into_the_status_word(srdit, cuda_device):
+    """A peer flag that nothing raises: srdit_residual_tp's bounded wait runs out
+    (2 s of %globaltimer), the kernel ORs SRDIT_STATUS_TIMEOUT into the status word,
+    skips its rows and returns -- no hang, no trap. The context stays usable: the
+    same launch with the flag raised then completes and updates x."""
+    M, N = 32, 64   # one thread block
+    g = torch.Generator().manual_seed(31)
+    x0 = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    parts = torch.randn(1, M, N, generator=g).to(torch.bfloat16).to(cuda_device)
+    flags = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    x = x0.to(cuda_device)
+    srdit.ops.residual_tp(x, parts, flags=flags.data_ptr(), expected=1, status=status)
+    torch.cuda.synchronize(cuda_device)
+    assert int(status.item()) == srdit._lib.SRDIT_STATUS_TIMEOUT
+    assert torch.equal(x.cpu(), x0)            # its rows were skipped
+    flags.fill_(1)
+    status.zero_()
+    srdit.ops.residual_tp(x, parts, flags=flags.data_ptr(), expected=1, status=status)
+    torch.cuda.synchronize(cuda_device)
+    assert int(status.item()) == 0
+    ref = (x0.float() + parts[0].cpu().float()).to(torch.bfloat16)
+    assert torch.equal(x.cpu(), ref)
+
+
+def test_allreduce_wait_times_out_into_the_status_word(srdit, cuda_device):
+    """srdit_tp_allreduce with one rank asked for epoch 2 after its first signal:
+    its own counter reaches only 1, the bounded wait runs out, the status word
+    says so and ``out`` is left untouched. A second call (the counter then
+    reaches 2) completes and reduces."""
+    n = 1000
+    vals = torch.randn(n, generator=torch.Generator().manual_seed(32)).to(cuda_device)
+    t = vals.clone()
+    slots = torch.zeros(n, dtype=torch.float32, device=cuda_device)
+    flags = torch.zeros(8, dtype=torch.int32, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    st = srdit.ops.peer_ptrs([slots.data_ptr()])
+    ft = srdit.ops.peer_ptrs([flags.data_ptr()])
+    out = torch.full((n,), -7.0, device=cuda_device)
+    L = srdit._lib.lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    args = (ctypes.c_void_p(t.data_ptr()), ctypes.c_void_p(out.data_ptr()), n,
+            srdit._lib.SRDIT_RED_SUM, ctypes.byref(st), ctypes.byref(ft), 0, 1, 2,
+            ctypes.c_void_p(status.data_ptr()), stream)
+    assert L.srdit_tp_allreduce(*args) == 0
+    torch.cuda.synchronize(cuda_device)
+    assert int(status.item()) == srdit._lib.SRDIT_STATUS_TIMEOUT
+    assert bool((out == -7.0).all())
+    status.zero_()
+    assert L.srdit_tp_allreduce(*args) == 0
+    torch.cuda.synchronize(cuda_device)
+    assert int(status.item()) == 0 and int(flags[0].item()) == 2
+    assert torch.equal(out, vals)

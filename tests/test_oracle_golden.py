@@ -127,3 +127,41 @@ def test_oracle_block_matches_reference_block(golden):
     assert onum.cosine(y.float(), ref.float()) > 0.99999
     assert (y.float() - ref.float()).abs().max() < 0.05
     assert torch.equal(nk, t["nk"][0]) and torch.equal(nv, t["nv"][0])
+
+
+def test_oracle_model_matches_reference_wanmodel(golden):
+    """oracle.model (embeddings, blocks with bf16 Linears, Head, unpatchify) vs two
+    streaming chunks of the reference's own WanModel._forward_inference, the second
+    over the first chunk's KV cache (tests/golden/gen_golden.py, gen_model)."""
+    from types import SimpleNamespace
+
+    from oracle import model as omodel
+    g = golden("model")
+    dim, ffn, heads, layers, c_in, c_out, text_dim, text_len, f, H, W = (int(v) for v in g["dims"])
+    sd = {}
+    for k, v in g.items():
+        if k.startswith("w."):
+            t = torch.from_numpy(v)
+            sd[k[2:]] = t.view(torch.bfloat16) if t.dtype == torch.int16 else t
+    cfg = SimpleNamespace(dim=dim, num_heads=heads, num_layers=layers, patch_size=(1, 2, 2),
+                          freq_dim=256, text_len=text_len, eps=1e-6, rope_rows=1024,
+                          block_hw=(2, 2), block_radius_hw=(1, 1), block_t=3, out_dim=c_out)
+    ctx = bf16(g["ctx"])
+    caches = None
+    for i in range(2):
+        out, caches = omodel.forward_chunk(sd, cfg, bf16(g[f"lat{i}"]), 625.0, ctx, caches=caches,
+                                           t_offset=3 * i, kv_len=9, linear="bf16")
+        ref = bf16(g[f"out{i}"])
+        assert out.shape == ref.shape == (c_out, f, H, W)
+        assert onum.cosine(out.float(), ref.float()) > 0.99999, i
+        assert (out.float() - ref.float()).abs().max() < 0.05, i
+    # the second layer's cache after the second chunk (roped K, raw V, 6 frames).
+    # Layer 1's input already carries layer 0's bf16 rounding differences (the
+    # reference's CPU attention and Linears accumulate in other orders), so about
+    # 30% of its values sit an ulp or so away: compared by cosine, not bits
+    nk, nv = caches[1]
+    L = f * (H // 2) * (W // 2)
+    assert nk.shape[0] == 2 * L
+    for got, key in ((nk, "k1_layer1"), (nv, "v1_layer1")):
+        ref = bf16(g[key]).reshape(got.shape)
+        assert onum.cosine(got.float(), ref.float()) > 0.99999, key
