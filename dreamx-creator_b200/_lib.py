@@ -19,6 +19,7 @@ SRDIT_EPI_STORE, SRDIT_EPI_GELU, SRDIT_EPI_GATED_RES, SRDIT_EPI_RES = 0, 1, 2, 3
 SRDIT_P_FRAME, SRDIT_P_PLAIN = 17, 19
 SRDIT_ANCHOR_NONE, SRDIT_ANCHOR_CHUNK, SRDIT_ANCHOR_FRAME = 0, 1, 2
 SRDIT_STATUS_TIMEOUT = 1
+SRDIT_SPLIT_FIELDS = 9
 SRDIT_ROW_SUMSQ, SRDIT_ROW_ABSMAX = 0, 1
 
 c_int, c_ll, c_float, c_vp = ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_void_p
@@ -30,7 +31,7 @@ class WinattnGeom(ctypes.Structure):
                 ("a_frames", c_int), ("a_h", c_int), ("a_w", c_int),
                 ("n_heads", c_int), ("head_dim", c_int),
                 ("q_stride", c_ll), ("kv_stride", c_ll), ("a_stride", c_ll),
-                ("o_stride", c_ll), ("scale", c_float)]
+                ("o_stride", c_ll), ("scale", c_float), ("col_split", c_vp)]
 
 
 class WinattnTiling(ctypes.Structure):
@@ -71,7 +72,7 @@ SIGNATURES = {
                            c_ll, c_vp, c_vp],
     "srdit_rms_rope": [c_vp, c_ll, c_int, c_int, c_vp, c_float, c_vp, c_ll, c_int, c_int,
                        c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_ll,
-                       c_vp, c_int, c_vp, c_vp],
+                       c_vp, c_int, c_vp, c_int, c_vp],
     "srdit_row_reduce": [c_vp, c_ll, c_int, c_int, c_int, c_vp, c_vp],
     "srdit_fp8_gemm_tp": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                           c_int, c_int, c_vp, ctypes.POINTER(TpGemm), c_vp, c_vp],

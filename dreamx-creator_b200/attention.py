@@ -56,9 +56,22 @@ def check_rows(params: torch.Tensor, p_stride: int, *, f_cur, h, w, kv_frames, a
             raise ValueError("a window params row addresses anchor tokens outside the anchor")
 
 
+# Merge horizontally adjacent windows into one launch row when that cuts the
+# kernel's (query tile, KV tile) pairs below this fraction of the unmerged count
+PAIR_GAIN = 0.85
+
+
 def _plan_device_state(plan: dict, device: torch.device, anchor_mode, check_key, check_kw):
-    """Device params + kernel tiling, cached inside the plan dict per device; the
-    rows are bounds-checked once per (device, tensor geometry)."""
+    """Device params + kernel tiling (+ the window-pair records), cached inside the
+    plan dict per device; the rows are bounds-checked once per (device, tensor
+    geometry). Returns (params_dev, tiling, n_rows, anchor mode, split_dev or None).
+
+    Windows narrower than a query tile (the shipped 3x4x4 windows hold 48
+    queries, 37% of a 128-row tile) run two at a time: the rows of two
+    horizontally adjacent windows merge into one row over the union of their
+    KV columns, and the kernel masks each query row to its own window's columns
+    (``blockgrid.pair_rows``). The merge is used when it cuts the kernel's tile
+    pairs enough; every query row still sees exactly its own window's keys."""
     key = ("b200", device)
     st = plan.get(key)
     if st is None:
@@ -66,13 +79,23 @@ def _plan_device_state(plan: dict, device: torch.device, anchor_mode, check_key,
         if not torch.is_tensor(params):
             params = torch.as_tensor(params)
         params = params.to(torch.int32).contiguous().cpu()
+        stride = int(plan["p_stride"])
         mode = blockgrid.ANCHOR_MODES[anchor_mode]
-        tiling = ops.winattn_plan(params, int(plan["p_stride"]), mode)
-        st = plan[key] = (params.to(device), tiling, params.shape[0], mode, params, set())
-    if check_key not in st[5]:
-        check_rows(st[4], int(plan["p_stride"]), **check_kw)
-        st[5].add(check_key)
-    return st[:4]
+        tiling = ops.winattn_plan(params, stride, mode)
+        split_dev = None
+        rows_p, split = blockgrid.pair_rows(params, stride)
+        if rows_p.shape[0] < params.shape[0]:
+            tiling_p = ops.winattn_plan(rows_p, stride, mode)
+            if (blockgrid.tile_pairs(rows_p, stride, tiling_p)
+                    < PAIR_GAIN * blockgrid.tile_pairs(params, stride, tiling)):
+                params, tiling = rows_p, tiling_p
+                split_dev = split.to(device)
+        st = plan[key] = (params.to(device), tiling, params.shape[0], mode, split_dev, params,
+                          set())
+    if check_key not in st[6]:
+        check_rows(st[5], int(plan["p_stride"]), **check_kw)
+        st[6].add(check_key)
+    return st[:5]
 
 
 def _geom(q, k_hr, *, f_cur, h, w, n, d, kv_frames, kv_slot0=0, anchor=None, a_hw=None):
@@ -123,11 +146,12 @@ def run_blockgrid_b200(q, k_ext, v_ext, out, *, plan, f_cur, h, w, n, d, anchor_
         p0 = plan["params"][0]
         a_hw = (int(p0[-2]), int(p0[-1]))
         a_frames = hr_base // (a_hw[0] * a_hw[1])
-    params_dev, tiling, n_w, mode = _plan_device_state(
+    params_dev, tiling, n_w, mode, split_dev = _plan_device_state(
         plan, q.device, anchor_mode, (f_cur, h, w, kv_frames, a_hw, a_frames),
         dict(f_cur=f_cur, h=h, w=w, kv_frames=kv_frames, a_hw=a_hw, a_frames=a_frames))
     g = _geom(qf, k_hr, f_cur=f_cur, h=h, w=w, n=n, d=d, kv_frames=kv_frames, anchor=ka, a_hw=a_hw)
     g.o_stride = of.stride(0)
+    g.col_split = None if split_dev is None else split_dev.data_ptr()
     ops.winattn(qf, k_hr, v_hr, of, params_dev=params_dev, n_w=n_w,
                 p_stride=int(plan["p_stride"]), anchor_mode=mode, geom=g, tiling=tiling,
                 k_anchor=ka, v_anchor=va, status=status)

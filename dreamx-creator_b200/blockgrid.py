@@ -169,3 +169,97 @@ def visible_flops(params: torch.Tensor, p_stride: int, n_heads: int, head_dim: i
             qL, qhL, qwL, kvL, khL, kwL, af, khLa, kwLa = r[1], r[4], r[5], r[7], r[9], r[11], r[12], r[14], r[16]
             tot += qL * qhL * qwL * (kvL * khL * kwL + af * khLa * kwLa)
     return 4 * head_dim * n_heads * tot
+
+
+# Params-row columns of the fields a window pair merges, per row layout:
+# (q_w0, qwL, kw0, kwL, kw0_a, kwL_a, anchor frames); the others must agree.
+_PAIR_COLS = {P_PLAIN: (3, 5, 10, 11, 15, 16, 12), P_FRAME: (1, 3, 8, 9, 13, 14, 10)}
+SPLIT_FIELDS = 9
+
+
+def pair_rows(params: torch.Tensor, p_stride: int):
+    """Merge horizontally adjacent windows into one row each: (rows, split).
+
+    Rows i and i + 1 merge when window B = row i + 1 starts where window A =
+    row i ends (B.q_w0 == A.q_w0 + A.qwL) and everything but their column
+    extents agrees (query frames and rows, KV frames and rows, anchor frames
+    and rows). The merged row is A's with the query columns of both and the
+    union of their KV (and anchor) columns; ``split`` [n, SPLIT_FIELDS] int32
+    records, per merged row, {q_split, hr_lo_a, hr_hi_a, hr_lo_b, hr_hi_b,
+    an_lo_a, an_hi_a, an_lo_b, an_hi_b}: query columns [0, q_split) are A's,
+    and each window keeps seeing only its own KV / anchor columns (relative to
+    the merged row's kw0 / kw0_a). Rows that do not merge keep q_split 0.
+    The merged rows are rows of the same layout and cover the same tokens, so
+    they pass the same bounds checks; the kernel masks per query row.
+    """
+    qw0, qwl, kw0, kwl, kw0a, kwla, _ = _PAIR_COLS[p_stride]
+    rows = params.to(torch.int64).tolist()
+    keep = [i for i in range(p_stride) if i not in (qw0, qwl, kw0, kwl, kw0a, kwla)]
+    out, split = [], []
+    i = 0
+    while i < len(rows):
+        a = rows[i]
+        b = rows[i + 1] if i + 1 < len(rows) else None
+        ok = (b is not None and b[qw0] == a[qw0] + a[qwl] and b[kw0] >= a[kw0]
+              and b[kw0] + b[kwl] >= a[kw0] + a[kwl] and all(a[k] == b[k] for k in keep))
+        # the anchor columns merge the same way (the reference fills them in
+        # rows without an anchor too, so the merge stays exactly invertible)
+        if ok:
+            ok = b[kw0a] >= a[kw0a] and b[kw0a] + b[kwla] >= a[kw0a] + a[kwla]
+        if not ok:
+            out.append(a)
+            split.append([0] * SPLIT_FIELDS)
+            i += 1
+            continue
+        u = list(a)
+        u[qwl] = a[qwl] + b[qwl]
+        u[kwl] = b[kw0] + b[kwl] - a[kw0]
+        u[kwla] = b[kw0a] + b[kwla] - a[kw0a]
+        rec = [a[qwl], 0, a[kwl], b[kw0] - a[kw0], b[kw0] - a[kw0] + b[kwl],
+               0, a[kwla], b[kw0a] - a[kw0a], b[kw0a] - a[kw0a] + b[kwla]]
+        out.append(u)
+        split.append(rec)
+        i += 2
+    return (torch.tensor(out, dtype=torch.int32).reshape(-1, p_stride),
+            torch.tensor(split, dtype=torch.int32).reshape(-1, SPLIT_FIELDS))
+
+
+def tile_pairs(params: torch.Tensor, p_stride: int, tiling) -> int:
+    """(query tile, KV tile) pairs the window kernel walks for these rows with
+    this tiling: its work in units of the per-tile softmax + MMA step."""
+    frame = p_stride == P_FRAME
+    total = 0
+    for r in params.to(torch.int64).tolist():
+        if frame:
+            q_tL, qhL, kv_tL, khL, a_f, khL_a = r[10], r[2], r[5], r[7], r[10], r[12]
+        else:
+            q_tL, qhL, kv_tL, khL, a_f, khL_a = r[1], r[4], r[7], r[9], r[12], r[14]
+        hq = -(-qhL // tiling.bh_q)
+        m_tiles = -(-(q_tL * hq) // tiling.qboxes_per_tile)
+        kv = -(-(kv_tL * -(-khL // tiling.bh_k)) // tiling.kboxes_per_tile)
+        if tiling.has_anchor and a_f > 0:
+            per_frame = -(-(-(-khL_a // tiling.bh_a)) // tiling.aboxes_per_tile)
+            # a frame-aligned anchor: each query tile sees the anchor frames of
+            # its own query frames; a chunk anchor: every anchor frame
+            kv += per_frame * (min(a_f, -(-tiling.qboxes_per_tile // hq)) if frame else a_f)
+        total += m_tiles * kv
+    return total
+
+
+def unpair_rows(rows: torch.Tensor, split: torch.Tensor, p_stride: int) -> torch.Tensor:
+    """The per-window rows that ``pair_rows`` merged (its inverse)."""
+    qw0, qwl, kw0, kwl, kw0a, kwla, _ = _PAIR_COLS[p_stride]
+    out = []
+    for u, rec in zip(rows.to(torch.int64).tolist(), split.to(torch.int64).tolist()):
+        if rec[0] == 0:
+            out.append(u)
+            continue
+        a, b = list(u), list(u)
+        a[qwl] = rec[0]
+        b[qw0], b[qwl] = u[qw0] + rec[0], u[qwl] - rec[0]
+        a[kw0], a[kwl] = u[kw0] + rec[1], rec[2] - rec[1]
+        b[kw0], b[kwl] = u[kw0] + rec[3], rec[4] - rec[3]
+        a[kw0a], a[kwla] = u[kw0a] + rec[5], rec[6] - rec[5]
+        b[kw0a], b[kwla] = u[kw0a] + rec[7], rec[8] - rec[7]
+        out += [a, b]
+    return torch.tensor(out, dtype=torch.int32).reshape(-1, p_stride)

@@ -47,7 +47,7 @@ constexpr int OFF_V = OFF_K + 2 * QKV_TILE_BYTES;
 constexpr int OFF_BAR = OFF_V + 2 * QKV_TILE_BYTES;
 constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: 768 floats
 constexpr int REC_SLOTS = 4;            // item-record ring (producer -> MMA, softmax)
-constexpr int REC_BYTES = 160;
+constexpr int REC_BYTES = 192;
 constexpr int OFF_REC = OFF_XCH + 768 * 4;
 constexpr int SMEM_BYTES = OFF_REC + REC_SLOTS * REC_BYTES + 1024;
 constexpr uint32_t kEpiBarrier = 5;     // named barrier of the 256 softmax threads
@@ -78,6 +78,7 @@ struct Args {
   int o_tma;  // 1: the tmO tensor map over `out` is valid (TMA tile stores allowed)
   float scale;
   uint32_t* status;
+  const int32_t* split;  // optional [n_w, SRDIT_SPLIT_FIELDS]: rows that pair two windows
 };
 
 struct Row {
@@ -267,6 +268,9 @@ struct ItemRec {
   int o_tma;   // 1: O leaves by TMA tile stores (no box element outside the window)
   int full_k;  // 1: every HR box row and column lies inside the window
   int full_a;  // same for the anchor boxes
+  // a row that pairs windows A | B: {q_split, hr_lo_a, hr_hi_a, hr_lo_b, hr_hi_b,
+  // an_lo_a, an_hi_a, an_lo_b, an_hi_b}; q_split 0: one window
+  int sp[SRDIT_SPLIT_FIELDS];
 };
 static_assert(sizeof(ItemRec) <= REC_BYTES, "item record slot");
 
@@ -285,6 +289,9 @@ SRDIT_DEV bool make_rec(const Args& a, int item, ItemRec& o) {
             min(r.q_h0 + o.w.hq_chunks * a.bh_q, a.q_h) <= r.q_h0 + r.qhL;
   o.full_k = (r.kwL == a.bw_k) && (r.khL % a.bh_k == 0);
   o.full_a = (r.kwL_a == a.bw_a) && (r.khL_a % a.bh_a == 0);
+#pragma unroll
+  for (int i = 0; i < SRDIT_SPLIT_FIELDS; ++i)
+    o.sp[i] = a.split ? __ldg(a.split + static_cast<size_t>(win) * SRDIT_SPLIT_FIELDS + i) : 0;
   return true;
 }
 
@@ -674,6 +681,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const Walk w = rec->w;
       const int n_tiles = w.n_tiles;
       const bool full_k = rec->full_k, full_a = rec->full_a, per_frame = rec->r.a_per_frame;
+      // a row pairing windows A | B: this row's side, and each side's visible KV
+      // columns (HR and anchor, relative to the row's KV cuboid)
+      const int q_split = rec->sp[0];
+      const bool paired = q_split > 0;
+      const bool side_b = paired && row_w >= q_split;
+      const int hr_lo_a = rec->sp[1], hr_hi_a = rec->sp[2], hr_lo_b = rec->sp[3],
+                hr_hi_b = rec->sp[4];
+      const int an_lo_a = rec->sp[5], an_hi_a = rec->sp[6], an_lo_b = rec->sp[7],
+                an_hi_b = rec->sp[8];
       const int khL = rec->r.khL, kwL = rec->r.kwL, khL_a = rec->r.khL_a, kwL_a = rec->r.kwL_a;
       float m_i = neg_inf, l_i = 0.f;
       for (int j = 0; j < n_tiles; ++j, ++g) {
@@ -708,6 +724,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int hc = (ti.box0 + bi) % hch;
             const bool v = (c < ti.rows) && (hc * ti.bh + hr < khl) && (cw < kwl);
             vm[qq] = __ballot_sync(0xffffffffu, v);
+          }
+        }
+        if (paired) {
+          // columns outside this row's own window: masked, per side
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            const int cw = static_cast<int>((ti.anchor ? geo_a[qq] : geo_k[qq]) >> 16);
+            const int lo_a = ti.anchor ? an_lo_a : hr_lo_a, hi_a = ti.anchor ? an_hi_a : hr_hi_a;
+            const int lo_b = ti.anchor ? an_lo_b : hr_lo_b, hi_b = ti.anchor ? an_hi_b : hr_hi_b;
+            const uint32_t m_a = __ballot_sync(0xffffffffu, cw >= lo_a && cw < hi_a);
+            const uint32_t m_b = __ballot_sync(0xffffffffu, cw >= lo_b && cw < hi_b);
+            vm[qq] &= side_b ? m_b : m_a;
           }
         }
         const int my_chunks = min(max(nchunks - 2 * half, 0), 2);  // warp-uniform
@@ -1130,6 +1158,7 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
   a.o_tma = o_tma;
   a.scale = g->scale;
   a.status = status;
+  a.split = g->col_split;
 
   int dev = 0;
   cudaGetDevice(&dev);

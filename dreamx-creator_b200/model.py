@@ -207,6 +207,9 @@ class SRDiT:
         # True while a caller captures forwards into a CUDA graph: the caller then
         # sets t_offset_dev itself before every replay
         self.graph_capture = False
+        # width position of the token grid's column 0: 0, or a strip's first
+        # column when this process refines one strip of a wider grid
+        self.rope_w0 = 0
 
     # ------------------------------------------------------------------ construction
     @staticmethod
@@ -423,7 +426,7 @@ class SRDiT:
             plan[fkey] = blockgrid.visible_flops(plan["params"], int(plan["p_stride"]),
                                                  n_heads, 128)
         a_hw = (h, w) if anchor_kv is not None else None
-        params_dev, tiling, n_w, amode = _plan_device_state(
+        params_dev, tiling, n_w, amode, split_dev = _plan_device_state(
             plan, dev, mode, (f, h, w, f_kv, a_hw, f if a_hw else 0),
             dict(f_cur=f, h=h, w=w, kv_frames=f_kv, a_hw=a_hw, a_frames=f if a_hw else 0))
         geom = _lib.WinattnGeom()
@@ -432,6 +435,7 @@ class SRDiT:
         geom.n_heads, geom.head_dim = n_heads, 128
         geom.q_stride = geom.kv_stride = geom.o_stride = width
         geom.scale = 128 ** -0.5
+        geom.col_split = None if split_dev is None else split_dev.data_ptr()
         if anchor_kv is not None:
             geom.a_frames, geom.a_h, geom.a_w, geom.a_stride = f, h, w, width
 
@@ -527,11 +531,12 @@ class SRDiT:
             vcopy = {} if v_direct else dict(v_src=qkv[:, 2 * D:], v_dst=vr)
             ops.rms_rope(qkv[:, D:2 * D], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset_dev=self.t_offset_dev, **vcopy)
+                         t_offset_dev=self.t_offset_dev, w_offset=self.rope_w0, **vcopy)
             if last_kv:
                 break   # its K / V are in the ring: nothing else of the block is used
             ops.rms_rope(qkv[:, :D], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
-                         grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev)
+                         grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev,
+                         w_offset=self.rope_w0)
             ak = av = None
             if anchor_kv is not None:
                 ak, av = anchor_kv[li]

@@ -187,7 +187,8 @@ int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, float eps,
  * slice with norm_width = K. t_offset_dev (optional, one device int) is added to
  * t_offset when the kernel runs, so a captured CUDA graph can be replayed for
  * later chunks; temporal positions beyond the table are clamped to its last row
- * (the host range check covers t_offset only).
+ * (the host range check covers t_offset only). w_offset: the width position of
+ * the grid's column 0, for a strip of a wider token grid (0 otherwise).
  * Replaces: WanRMSNorm.forward (models.py:424-440) on q and k (models.py:602-604),
  *   rope_apply (models.py:173-214), and the KV-cache torch.cat of
  *   attention.py:1506-1510.
@@ -197,7 +198,7 @@ int srdit_rms_rope(const void* src, long long ld_src, int M, int K, const void* 
                    int n_slots, const double* cos_tab, const double* sin_tab, int tab_rows,
                    int grid_h, int grid_w, int t_offset, const void* v_src, long long ld_vsrc,
                    void* v_dst, long long ld_vdst, const float* ss_in, int norm_width,
-                   const int* t_offset_dev, cudaStream_t stream);
+                   const int* t_offset_dev, int w_offset, cudaStream_t stream);
 
 #define SRDIT_ROW_SUMSQ 0
 #define SRDIT_ROW_ABSMAX 1
@@ -342,7 +343,19 @@ typedef struct srdit_winattn_geom {
   int n_heads, head_dim;      /* head_dim must be 128                                   */
   long long q_stride, kv_stride, a_stride, o_stride; /* elements between tokens        */
   float scale;                /* softmax scale, head_dim^-0.5                           */
+  /* optional (NULL: every row is one window): int32 [n_w, SRDIT_SPLIT_FIELDS],
+   * one record per params row, for rows that are the union of two horizontally
+   * adjacent windows A | B of the same frames and rows (same KV frames and KV
+   * rows). Record: {q_split, hr_lo_a, hr_hi_a, hr_lo_b, hr_hi_b, an_lo_a,
+   * an_hi_a, an_lo_b, an_hi_b}: query columns [0, q_split) of the row's cuboid
+   * are window A's, the rest B's; window A sees HR KV columns [hr_lo_a,
+   * hr_hi_a) of the row's KV cuboid (relative to its kw0) and anchor columns
+   * [an_lo_a, an_hi_a) (relative to kw0_a), B likewise. q_split 0: an
+   * ordinary (unpaired) row. */
+  const int32_t* col_split;
 } srdit_winattn_geom;
+
+#define SRDIT_SPLIT_FIELDS 9
 
 /* TMA box tiling derived once per plan by srdit_winattn_plan. */
 typedef struct srdit_winattn_tiling {

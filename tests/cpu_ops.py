@@ -90,7 +90,7 @@ def residual(x, parts, bias=None, gate=None):
 
 def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, cos=None,
              sin=None, grid_h=0, grid_w=0, t_offset=0, v_src=None, v_dst=None, ss=None,
-             norm_width=0, t_offset_dev=None):
+             norm_width=0, t_offset_dev=None, w_offset=0):
     M, K = src.shape
     if t_offset_dev is not None:
         t_offset = t_offset + int(t_offset_dev[0])
@@ -105,7 +105,8 @@ def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, c
     if cos is not None:
         d = torch.arange(K // 2) % 64
         pos = torch.where(d[None] < 22, (t_offset + f)[:, None],
-                          torch.where(d[None] < 43, (sp // grid_w)[:, None], (sp % grid_w)[:, None]))
+                          torch.where(d[None] < 43, (sp // grid_w)[:, None],
+                                      (sp % grid_w + w_offset)[:, None]))
         c, s = cos[pos, d[None]], sin[pos, d[None]]
         x2 = o.double().view(M, K // 2, 2)
         o = torch.stack([x2[..., 0] * c - x2[..., 1] * s, x2[..., 0] * s + x2[..., 1] * c],
@@ -132,7 +133,17 @@ def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom,
         return out
     f, h, w = geom.q_frames, geom.q_h, geom.q_w
     L = h * w
-    params = params_dev.cpu().numpy()
+    params = params_dev.cpu()
+    if geom.col_split:
+        # rows that pair two windows: the double attends each window on its own
+        import ctypes
+        import importlib
+        bg = importlib.import_module("dreamx-creator_b200.blockgrid")
+        n_rows = params.shape[0]
+        raw = (ctypes.c_int32 * (n_rows * bg.SPLIT_FIELDS)).from_address(int(geom.col_split))
+        split = torch.tensor(list(raw), dtype=torch.int32).view(n_rows, bg.SPLIT_FIELDS)
+        params = bg.unpair_rows(params, split, p_stride)
+    params = params.numpy()
     if p_stride == 17:
         f_kv = int((params[:, 4] + params[:, 5]).max())
     else:

@@ -138,3 +138,30 @@ def test_rows_outside_the_grid_are_rejected(srdit, golden):
     params[7, 10] = 64 - params[7, 11] + 1
     with pytest.raises(ValueError):
         srdit.attention.check_rows(params, 19, f_cur=3, h=36, w=64, kv_frames=6)
+
+
+@pytest.mark.parametrize("name", ["2k_4x4_r3_f6", "2k_4x4_r3_f12_frame", "2k_4x4_r3_f6_chunk",
+                                  "odd_frame", "2k_8x8_r0_f6", "cfg1_4x4_r3"])
+def test_window_pairs_round_trip_and_cover_the_same_pairs(srdit, golden, name):
+    """Merging adjacent windows (pair_rows) keeps every window's visible set:
+    unpair_rows restores the reference's rows exactly, the merged rows stay
+    inside the grids, and the kernel's tile-pair count drops where it pays."""
+    import importlib
+    from tests.golden_cases import spec_fields
+    bg = importlib.import_module("dreamx-creator_b200.blockgrid")
+    attn = importlib.import_module("dreamx-creator_b200.attention")
+    g = golden("plans")
+    vals, mode = spec_fields(g, name)
+    rows = torch.from_numpy(g[f"{name}.params"]).to(torch.int32)
+    stride = int(g[f"{name}.meta"][5])
+    merged, split = bg.pair_rows(rows, stride)
+    assert torch.equal(bg.unpair_rows(merged, split, stride), rows)
+    a_hw = vals["anchor_hw"] or (vals["h"], vals["w"]) if mode else None
+    attn.check_rows(merged, stride, f_cur=vals["f_cur"], h=vals["h"], w=vals["w"],
+                    kv_frames=vals["f_kv"], a_hw=a_hw, a_frames=vals["f_cur"] if mode else 0)
+    if name.startswith("2k_4x4") or name == "cfg1_4x4_r3":
+        assert merged.shape[0] * 2 == rows.shape[0]
+        code = {None: 0, "chunk": 1, "frame": 2}[mode]
+        t0 = srdit.ops.winattn_plan(rows, stride, code)
+        t1 = srdit.ops.winattn_plan(merged, stride, code)
+        assert bg.tile_pairs(merged, stride, t1) < 0.7 * bg.tile_pairs(rows, stride, t0)
