@@ -10,8 +10,17 @@ Mirrors ``CausalInferencePipeline.inference_sr``'s hot loop
      x0 = x_t - (t/1000) * flow in fp64 (utils/sr_dit_wrapper.py:551-558);
   3. KV refresh: one forward over x0 at t = context_noise (0) that writes the
      chunk's K / V into the cache, which keeps the newest ``kv_len`` frames.
+
+The harvest of chunk i + 1 reads only chunk i + 1's LR frames (and the text
+context), not the cache, so ``step(..., next_lq_chunk=...)`` starts it on a
+side stream before chunk i's forwards and the next step picks its K / V up:
+on one GPU it fills the gaps between chunk i's kernels, and its result is the
+one a serial harvest would give (its own scratch buffers, its own temporal
+position word).
 """
 from __future__ import annotations
+
+import copy
 
 import torch
 
@@ -49,6 +58,10 @@ class RefinerStream:
         # context (rebuilt in place when set_context changes it)
         self.text = None
         self._text_dirty = True
+        # anchor harvest of the next chunk, started ahead on a side stream
+        self._harvester = None
+        self._side = None
+        self._pending = None   # (t_offset, per-layer K / V, completion event or None)
 
     def set_context(self, context: torch.Tensor):
         """Replace the text context (copied into the step's static buffer)."""
@@ -69,6 +82,7 @@ class RefinerStream:
     def reset(self):
         self.cache = None
         self.t_offset = 0
+        self._pending = None
 
     def harvest_anchor(self, lq_chunk, harvest_t=0.0):
         """Per-frame anchor K / V: the LR chunk's frames as independent 1-frame
@@ -80,6 +94,78 @@ class RefinerStream:
                                          text=self.text, independent_frames=True)
         return kv
 
+    def _harvest_model(self):
+        """The model with its own scratch buffers, temporal-position word, status
+        word and per-shape caches (weights, RoPE tables and the text cache are
+        shared), so a harvest on the side stream never touches a buffer that
+        the main stream's forwards use."""
+        if self._harvester is None:
+            h = copy.copy(self.model)
+            h._bufs = {}
+            h._cross_plans = {}
+            h._temb = {}
+            h.status = torch.zeros_like(self.model.status)
+            h.t_offset_dev = torch.zeros_like(self.model.t_offset_dev)
+            h.graph_capture = False
+            self._harvester = h
+        return self._harvester
+
+    def prefetch_anchor(self, lq_chunk, t_offset, harvest_t=0.0):
+        """Start the anchor harvest of the chunk at temporal position ``t_offset``
+        (its LR frames ``lq_chunk``) on a side stream; the ``step`` of that chunk
+        takes the result (``causal_inference.py:878-899`` harvests each chunk
+        from its LR frames alone). On a CPU model it runs at once."""
+        self._ensure_text()
+        dev = self.model.device
+        if getattr(self.model, "world", 1) > 1:
+            # a sharded model's harvest runs collectives, which every rank must
+            # issue in one order on one stream: harvest in line instead
+            self._pending = (t_offset, self.model.forward_chunk(
+                lq_chunk, harvest_t, self.context, cache=None, t_offset=t_offset,
+                return_kv=True, text=self.text, independent_frames=True)[1], None)
+            return
+        h = self._harvest_model()
+        if dev.type != "cuda":
+            _, kv = h.forward_chunk(lq_chunk, harvest_t, self.context, cache=None,
+                                    t_offset=t_offset, return_kv=True, text=self.text,
+                                    independent_frames=True)
+            self._pending = (t_offset, kv, None)
+            return
+        main = torch.cuda.current_stream(dev)
+        if self._side is None:
+            self._side = torch.cuda.Stream(dev)
+        side = self._side
+        side.wait_stream(main)          # the LR frames, the text cache are ready
+        lq_chunk.record_stream(side)    # the caller may drop it before the side reads it
+        with torch.cuda.stream(side):
+            _, kv = h.forward_chunk(lq_chunk, harvest_t, self.context, cache=None,
+                                    t_offset=t_offset, return_kv=True, text=self.text,
+                                    independent_frames=True)
+            done = torch.cuda.Event()
+            done.record(side)
+        self._pending = (t_offset, kv, done)
+
+    def _take_anchor(self, lq_chunk, harvest_t):
+        """This chunk's anchor: the prefetched harvest if one was started for this
+        temporal position, else a harvest now, on the main stream."""
+        pend, self._pending = self._pending, None
+        if pend is not None and pend[0] == self.t_offset:
+            _, kv, done = pend
+            if done is not None:
+                main = torch.cuda.current_stream(self.model.device)
+                main.wait_event(done)
+                for k, v in kv:   # made on the side stream, read and freed on main
+                    k.record_stream(main)
+                    v.record_stream(main)
+            return kv
+        return self.harvest_anchor(lq_chunk, harvest_t)
+
+    def check_status(self):
+        """Raise if a kernel of the main or the harvest stream gave up on a wait."""
+        self.model.check_status()
+        if self._harvester is not None:
+            self._harvester.check_status()
+
     def _ensure_cache(self, noisy_chunk):
         if self.cache is None:
             m = self.model
@@ -87,9 +173,10 @@ class RefinerStream:
             L = (noisy_chunk.shape[2] // ph) * (noisy_chunk.shape[3] // pw)
             self.cache = m.new_cache(L)
 
-    def _step_eager(self, noisy_chunk, lq_chunk=None, anchor_harvest_t=0.0):
+    def _step_eager(self, noisy_chunk, lq_chunk=None, anchor_harvest_t=0.0, anchor=None):
         m = self.model
-        anchor = self.harvest_anchor(lq_chunk, anchor_harvest_t) if lq_chunk is not None else None
+        if anchor is None and lq_chunk is not None:
+            anchor = self.harvest_anchor(lq_chunk, anchor_harvest_t)
         flow = m.forward_chunk(noisy_chunk, self.denoise_t, self.context, cache=self.cache,
                                t_offset=self.t_offset, anchor_kv=anchor, text=self.text)
         sigma = self.denoise_t / self.ntt
@@ -117,13 +204,24 @@ class RefinerStream:
         return self._graphs[key]
 
     def step(self, noisy_chunk: torch.Tensor, lq_chunk: torch.Tensor | None = None,
-             anchor_harvest_t: float = 0.0):
+             anchor_harvest_t: float = 0.0, next_lq_chunk: torch.Tensor | None = None,
+             next_t_offset: int | None = None):
         """Refine one chunk [C, f, H, W] (device, bf16); returns x0 [C, f, H, W] bf16
-        (with graphs, a buffer the next replay of the same ring phase overwrites)."""
+        (with graphs, a buffer the next replay of the same ring phase overwrites).
+
+        ``lq_chunk``: this chunk's LR frames, for the LQ anchor (harvested now
+        unless a previous step prefetched it). ``next_lq_chunk``: the next
+        chunk's LR frames; their harvest starts on the side stream before this
+        chunk's forwards, for temporal position ``next_t_offset`` (default: right
+        after this chunk)."""
         self._ensure_cache(noisy_chunk)
         self._ensure_text()
-        if not self.graphs or lq_chunk is not None:
-            return self._step_eager(noisy_chunk, lq_chunk, anchor_harvest_t)
+        anchor = self._take_anchor(lq_chunk, anchor_harvest_t) if lq_chunk is not None else None
+        if next_lq_chunk is not None:
+            nt = self.t_offset + noisy_chunk.shape[1] if next_t_offset is None else next_t_offset
+            self.prefetch_anchor(next_lq_chunk, nt, anchor_harvest_t)
+        if not self.graphs or anchor is not None:
+            return self._step_eager(noisy_chunk, anchor=anchor)
         key = (self.cache.start, self.cache.frames, tuple(noisy_chunk.shape))
         entry = self._graphs.get(key)
         if entry is None:

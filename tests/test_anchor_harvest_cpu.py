@@ -83,3 +83,29 @@ def test_independent_frames_refuses_a_cache_or_an_anchor():
     model.forward_chunk(lq, 0.0, ctx, cache=ring, update_cache=True)
     with pytest.raises(M._lib.SrditError):
         model.forward_chunk(lq, 0.0, ctx, cache=ring, t_offset=3, independent_frames=True)
+
+
+def test_prefetched_harvest_gives_the_serial_stream():
+    """RefinerStream.step(..., next_lq_chunk=...) harvests the next chunk's anchor
+    ahead (a side stream on the GPU; at once on this CPU double) with its own
+    scratch; three anchored chunks must come out exactly as with the harvest
+    done inside each step."""
+    M, cfg, model = _model()
+    P = importlib.import_module("dreamx-creator_b200.pipeline")
+    g = torch.Generator().manual_seed(14)
+    ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(torch.bfloat16)
+    noisy = [torch.randn(cfg.in_dim, 3, 8, 16, generator=g).to(torch.bfloat16) for _ in range(3)]
+    lq = [torch.randn(cfg.in_dim, 3, 8, 16, generator=g).to(torch.bfloat16) for _ in range(3)]
+    outs = {}
+    for prefetch in (False, True):
+        stream = P.RefinerStream(model, ctx)
+        res = []
+        for i in range(3):
+            nxt = lq[i + 1] if prefetch and i + 1 < 3 else None
+            res.append(stream.step(noisy[i], lq_chunk=lq[i], next_lq_chunk=nxt).clone())
+            if prefetch and nxt is not None:
+                assert stream._pending is not None and stream._pending[0] == 3 * (i + 1)
+        stream.check_status()
+        outs[prefetch] = res
+    for a, b in zip(outs[False], outs[True]):
+        assert torch.equal(a, b)

@@ -183,3 +183,32 @@ def test_refresh_kv_only_fills_the_same_ring(srdit, mods, cuda_device, geom):
     assert (a.start, a.frames) == (b.start, b.frames)
     for la, lb in zip(a.k + a.v, b.k + b.v):
         assert torch.equal(la, lb)
+
+
+def test_side_stream_harvest_matches_serial_stream(srdit, mods, cuda_device):
+    """Anchored chunks with the next chunk's harvest started on a side stream
+    (RefinerStream.step(..., next_lq_chunk=...)) against the harvest done in
+    line: the side stream's forward has its own scratch, so every chunk must be
+    bit-identical while the two streams run side by side."""
+    M, P = mods
+    cfg = small_cfg(M)
+    sd = random_sd(M, cfg, seed=8)
+    g = torch.Generator().manual_seed(15)
+    ctx = torch.randn(16, 64, generator=g).to(torch.bfloat16).to(cuda_device)
+    noisy = [torch.randn(16, 3, 8, 16, generator=g).to(torch.bfloat16).to(cuda_device)
+             for _ in range(4)]
+    lq = [torch.randn(16, 3, 8, 16, generator=g).to(torch.bfloat16).to(cuda_device)
+          for _ in range(4)]
+    outs = {}
+    for overlap in (False, True):
+        model = M.SRDiT.from_state_dict(cfg, sd, cuda_device)
+        stream = P.RefinerStream(model, ctx)
+        res = []
+        for i in range(4):
+            nxt = lq[i + 1] if overlap and i + 1 < 4 else None
+            res.append(stream.step(noisy[i], lq_chunk=lq[i], next_lq_chunk=nxt).clone())
+        torch.cuda.synchronize()
+        stream.check_status()
+        outs[overlap] = res
+    for a, b in zip(outs[False], outs[True]):
+        assert torch.equal(a, b)
