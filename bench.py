@@ -57,9 +57,11 @@ def parse():
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--tp-comm", default="fused", choices=["fused", "nccl"],
                     help="TP collectives fused into the kernels over peer memory, or NCCL")
-    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+    ap.add_argument("--parallel", default="tp", choices=["tp", "spatial", "replicas"],
                     help="N > 1: tensor parallelism over one clip (strong scaling, the "
-                         "reference's DTensor-style TP) or one clip per GPU (weak scaling)")
+                         "reference's DTensor-style TP), the spatial partition of one clip "
+                         "(each GPU refines a strip of token columns with the full model; "
+                         "radius-0 windows), or one clip per GPU (weak scaling)")
     ap.add_argument("--anchor", default="none", choices=["none", "serial", "overlap"],
                     help="LQ-anchor steps (the shipped default denoise): every step also "
                          "harvests an anchor from a 3-frame LR chunk and denoises frame-"
@@ -268,10 +270,12 @@ def workload_config(args):
                         "3 latent frames 36x64 tokens, 3-frame KV prefix, 512 text tokens",
             "model": "SR-DiT 5B (30 blocks, dim 3072, 24x128 heads, ffn 14336)",
             "layers": args.layers, "tokens": 6912, "window": f"3x{bhw[0]}x{bhw[1]} r{rhw}",
-            "global_batch": 1 if args.parallel == "tp" else args.gpus, "seq_len": 6912,
-            "parallelism": (f"tp{args.gpus} (sequence-parallel residual stream, "
-                            f"{args.tp_comm} collectives)"
-                            if args.parallel == "tp" else "replicas") if args.gpus > 1
+            "global_batch": args.gpus if args.parallel == "replicas" else 1, "seq_len": 6912,
+            "parallelism": ({"tp": f"tp{args.gpus} (sequence-parallel residual stream, "
+                                   f"{args.tp_comm} collectives)",
+                             "spatial": f"spatial{args.gpus} (w-strips of whole windows, "
+                                        f"full model per GPU, one all-gather per forward)",
+                             "replicas": "replicas"}[args.parallel]) if args.gpus > 1
             else "single",
             "l2": "inputs larger than L2 (5 GB of fp8 weights stream every forward)",
             "lq_anchor": {"none": "off",
@@ -344,10 +348,13 @@ def run_gpu_arm(args, rank, world, local):
     torch.cuda.set_device(dev)
     bhw, rhw = geometry(args.geometry)
     cfg = model_mod.SRDiTConfig(num_layers=args.layers, block_hw=bhw, block_radius_hw=rhw)
-    tp = world > 1 and args.parallel == "tp"
-    if tp:
+    tp = world > 1 and args.parallel in ("tp", "spatial")   # one clip over all ranks
+    if world > 1 and args.parallel == "tp":
         tp_mod = import_module("dreamx-creator_b200.tp")
         model = tp_mod.TPSRDiT.random_init(cfg, dev, seed=0, fused=args.tp_comm == "fused")
+    elif world > 1 and args.parallel == "spatial":
+        sp_mod = import_module("dreamx-creator_b200.spatial")
+        model = sp_mod.SpatialSRDiT.random_init(cfg, dev, seed=0)
     else:
         model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
     # tensor parallelism refines one clip on all ranks; replicas one clip each
@@ -514,10 +521,13 @@ def run_clip(args, rank, world, local):
     torch.cuda.set_device(dev)
     bhw, rhw = geometry(args.geometry)
     cfg = model_mod.SRDiTConfig(num_layers=args.layers, block_hw=bhw, block_radius_hw=rhw)
-    tp = world > 1 and args.parallel == "tp"
-    if tp:
+    tp = world > 1 and args.parallel in ("tp", "spatial")   # one clip over all ranks
+    if world > 1 and args.parallel == "tp":
         tp_mod = import_module("dreamx-creator_b200.tp")
         model = tp_mod.TPSRDiT.random_init(cfg, dev, seed=0, fused=args.tp_comm == "fused")
+    elif world > 1 and args.parallel == "spatial":
+        sp_mod = import_module("dreamx-creator_b200.spatial")
+        model = sp_mod.SpatialSRDiT.random_init(cfg, dev, seed=0)
     else:
         model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
     n_chunks, f = 11, 3

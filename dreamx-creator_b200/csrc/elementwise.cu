@@ -431,6 +431,7 @@ struct RopeArgs {
   const double* cos_tab;  // [rows, 64] fp64: table columns for the (t | h | w) axes
   const double* sin_tab;
   int grid_h, grid_w, t_offset;
+  int w_offset;             // width position of the grid's column 0 (a strip of a wider grid)
   const int* t_offset_dev;  // optional: added to t_offset (a graph replays read it live)
   int tab_rows;
   float eps;
@@ -508,7 +509,7 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
     // temporal position, kept inside the table (the host checks the range it knows)
     const int pos_t =
         min(a.t_offset + (a.t_offset_dev ? __ldg(a.t_offset_dev) : 0) + f, a.tab_rows - 1);
-    const int pos_h = sp / a.grid_w, pos_w = sp % a.grid_w;
+    const int pos_h = sp / a.grid_w, pos_w = sp % a.grid_w + a.w_offset;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const int d = (lane & 15) * 4 + p;
@@ -1034,7 +1035,7 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
                               int t_offset,
                               const void* v_src, long long ld_vsrc, void* v_dst,
                               long long ld_vdst, const float* ss_in, int norm_width,
-                              const int* t_offset_dev, cudaStream_t stream) {
+                              const int* t_offset_dev, int w_offset, cudaStream_t stream) {
   if (M == 0) return 0;
   if (!src || !weight || !dst || M < 0 || frame_tokens <= 0 || n_slots <= 0 || slot0 < 0)
     return SRDIT_EINVAL;
@@ -1047,7 +1048,7 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
     const int frames = (M + frame_tokens - 1) / frame_tokens;
     if (grid_w <= 0 || grid_h <= 0 || grid_h * grid_w != frame_tokens ||
         t_offset < 0 || tab_rows <= 0 || t_offset + frames > tab_rows || grid_h > tab_rows ||
-        grid_w > tab_rows)
+        w_offset < 0 || grid_w + w_offset > tab_rows)
       return SRDIT_EINVAL;
   }
   if ((v_src == nullptr) != (v_dst == nullptr)) return SRDIT_EINVAL;
@@ -1068,6 +1069,7 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
   a.grid_h = grid_h;
   a.grid_w = grid_w;
   a.t_offset = t_offset;
+  a.w_offset = w_offset;
   a.t_offset_dev = t_offset_dev;
   a.tab_rows = tab_rows;
   a.eps = eps;
