@@ -38,12 +38,13 @@ class WinattnTiling(ctypes.Structure):
     _fields_ = [("bw_q", c_int), ("bh_q", c_int), ("qboxes_per_tile", c_int),
                 ("m_tiles", c_int), ("bw_k", c_int), ("bh_k", c_int),
                 ("kboxes_per_tile", c_int), ("bw_a", c_int), ("bh_a", c_int),
-                ("aboxes_per_tile", c_int), ("has_anchor", c_int)]
+                ("aboxes_per_tile", c_int), ("has_anchor", c_int), ("split_kv", c_int)]
 
 
 SRDIT_EPI_PEER = 4
 SRDIT_MAX_RANKS = 8
 SRDIT_RED_SUM, SRDIT_RED_MAX = 0, 1
+SRDIT_AR_BLOCKS = 16
 
 
 class PeerPtrs(ctypes.Structure):

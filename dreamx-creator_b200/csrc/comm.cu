@@ -5,11 +5,11 @@
 //       IPC; the buffer may sit inside a larger caching-allocator block, so the
 //       handle names the enclosing allocation and the offset travels with it).
 //   srdit_tp_allreduce
-//       one-block all-reduce (sum or max) of a short fp32 vector through the
-//       peers' memory: every rank stores its vector into slot `rank` of every
-//       rank's receive area, release-adds a counter there, waits for all
-//       counters, then reduces the slots in rank order -- so every rank gets
-//       bit-identical results. Used for the per-token RMSNorm sums and fp8 amax
+//       all-reduce (sum or max) of a short fp32 vector through the peers'
+//       memory, SRDIT_AR_BLOCKS blocks each owning a share: every rank stores
+//       its share into slot `rank` of every rank's receive area, release-adds a
+//       counter there, waits for all counters, then reduces the slots in rank
+//       order -- so every rank gets bit-identical results. Used for the per-token RMSNorm sums and fp8 amax
 //       values the sharded block needs (a few thousand floats).
 //   srdit_tp_push
 //       all-gather by the copy engines: cudaMemcpyAsync of this rank's rows into
@@ -33,13 +33,20 @@ struct Ptrs {
   void* p[SRDIT_MAX_RANKS];
 };
 
-__global__ void __launch_bounds__(1024) tp_allreduce_kernel(const float* __restrict__ in,
-                                                            float* __restrict__ out, int n,
-                                                            int op, Ptrs slots, Ptrs flags,
-                                                            int rank, int world, uint32_t epoch,
-                                                            uint32_t* status) {
+// SRDIT_AR_BLOCKS blocks; block b owns elements [b * share, (b + 1) * share).
+// Every block stores its share into slot `rank` of every rank, then adds 1 to
+// counter `rank` at every rank (so one call adds SRDIT_AR_BLOCKS there), waits
+// until every counter of its own rank reaches epoch * SRDIT_AR_BLOCKS -- all
+// blocks of all ranks have stored -- and reduces its share in rank order.
+__global__ void __launch_bounds__(256) tp_allreduce_kernel(const float* __restrict__ in,
+                                                           float* __restrict__ out, int n,
+                                                           int op, Ptrs slots, Ptrs flags,
+                                                           int rank, int world, uint32_t epoch,
+                                                           uint32_t* status) {
   __shared__ int ok;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  const int share = (n + gridDim.x - 1) / gridDim.x;
+  const int i0 = blockIdx.x * share, i1 = min(n, i0 + share);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     const float v = in[i];
     for (int d = 0; d < world; ++d) static_cast<float*>(slots.p[d])[rank * n + i] = v;
   }
@@ -49,14 +56,15 @@ __global__ void __launch_bounds__(1024) tp_allreduce_kernel(const float* __restr
     for (int d = 0; d < world; ++d)
       flag_add_release(static_cast<uint32_t*>(flags.p[d]) + rank, 1u);
     const uint32_t* mine = static_cast<const uint32_t*>(flags.p[rank]);
+    const uint32_t target = epoch * static_cast<uint32_t>(gridDim.x);
     bool good = true;
-    for (int s = 0; s < world && good; ++s) good = flag_wait(mine + s, epoch, status);
+    for (int s = 0; s < world && good; ++s) good = flag_wait(mine + s, target, status);
     ok = good;
   }
   __syncthreads();
   if (!ok) return;
   const float* slot = static_cast<const float*>(slots.p[rank]);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     float acc = slot[i];
     for (int s = 1; s < world; ++s) {
       const float v = slot[s * n + i];
@@ -136,8 +144,8 @@ extern "C" int srdit_tp_allreduce(const float* in, float* out, int n, int op,
     f.p[i] = i < world ? flags->p[i] : nullptr;
     if (i < world && (!s.p[i] || !f.p[i])) return SRDIT_EINVAL;
   }
-  comm::tp_allreduce_kernel<<<1, 1024, 0, stream>>>(in, out, n, op, s, f, rank, world, epoch,
-                                                   status);
+  comm::tp_allreduce_kernel<<<SRDIT_AR_BLOCKS, 256, 0, stream>>>(in, out, n, op, s, f, rank,
+                                                                world, epoch, status);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -23,10 +23,17 @@ Per block, per rank (Dl = D/P, Fl = F/P):
 Row-parallel weights are quantised per output channel over the FULL input
 width before slicing, so every rank uses the reference's per-channel scales;
 column-parallel weights are sliced by output rows, which keeps theirs exact.
-The per-token activation scales are the full-row ones (all-reduced amax), so
-each partial product is the TP=1 product restricted to a K slice; what
-differs from one GPU is the fp32 summation order and the bf16 rounding of
-each rank's partial before the sum.
+The e4m3 inputs of the row-parallel Linears (attention outputs, the FFN
+hidden) are scaled per token over the rank's own column slice
+(``local_scales=True``, the default): each partial product is then exactly
+the product of its own quantised slice, and the reduce-scatter sums them as
+before, with no all-reduce of a per-token max in between (three of the five
+per-block synchronisation points). The scale is finer-grained than one GPU's
+full-row scale, never coarser. ``local_scales=False`` all-reduces the max so
+each partial is the one-GPU product restricted to a K slice. What differs
+from one GPU either way is the fp32 summation order, the bf16 rounding of each
+rank's partial before the sum and, with local scales, the quantisation grid of
+the row-parallel inputs.
 
 Collectives go through ``TPComm`` (NCCL via torch.distributed). Every rank
 issues the same collectives in the same order.
@@ -308,9 +315,12 @@ class TPSRDiT(SRDiT):
     """
 
     def __init__(self, cfg: SRDiTConfig, sd: dict, device="cuda", comm: TPComm | None = None,
-                 fused: bool = True):
+                 fused: bool = True, local_scales: bool = True):
         """``fused``: collectives fused into the kernels over peer memory
-        (``PeerComm``); False: the same sharding with library (NCCL) collectives."""
+        (``PeerComm``); False: the same sharding with library (NCCL) collectives.
+        ``local_scales``: per-token e4m3 scales of the row-parallel inputs over this
+        rank's slice (no all-reduce); False: over the full row (all-reduced max)."""
+        self.local_scales = local_scales
         if comm is None:
             comm = PeerComm() if fused else TPComm()
         self.comm = comm
@@ -404,10 +414,12 @@ class TPSRDiT(SRDiT):
             comm.all_gather(xs, xs_l)
 
         def rowpar_residual(a_bf16, w_q, w_s, bias, gate):
-            # per-token scale over the full row: all-reduce the slices' max |a|
-            ops.row_reduce(a_bf16, "absmax", out=am)
-            comm.all_reduce_max(am)
-            ops.quant_rowwise(a_bf16, amax=am, q=aq, scale=as_)
+            if self.local_scales:   # per-token scale over this rank's slice
+                ops.quant_rowwise(a_bf16, q=aq, scale=as_)
+            else:                   # over the full row: all-reduce the slices' max |a|
+                ops.row_reduce(a_bf16, "absmax", out=am)
+                comm.all_reduce_max(am)
+                ops.quant_rowwise(a_bf16, amax=am, q=aq, scale=as_)
             ops.fp8_gemm(aq, as_, w_q, w_s, None, part)          # bf16(acc * sa * sb)
             comm.reduce_scatter(y_l, part)
             ops.residual(x, y_l, bias=bias, gate=gate)
@@ -477,7 +489,8 @@ class TPSRDiT(SRDiT):
             gather_quantised()
             am.zero_()
             ops.fp8_gemm(xq, xs, ly.w_f0, ly.s_f0, ly.b_f0, hbuf, epilogue="gelu", row_amax=am)
-            comm.all_reduce_max(am)
+            if not self.local_scales:
+                comm.all_reduce_max(am)
             ops.quant_rowwise(hbuf, amax=am, q=hq, scale=hs)
             ops.fp8_gemm(hq, hs, ly.w_f2, ly.s_f2, None, part)
             comm.reduce_scatter(y_l, part)
@@ -544,9 +557,12 @@ class TPSRDiT(SRDiT):
         rs_flags = comm.my_flags[1]
 
         def rowpar_residual(a_bf16, w_q, w_s, bias, gate):
-            ops.row_reduce(a_bf16, "absmax", out=am)
-            comm.allreduce(am, "max", st)
-            ops.quant_rowwise(a_bf16, amax=am, q=aq, scale=as_)
+            if self.local_scales:   # per-token scale over this rank's slice
+                ops.quant_rowwise(a_bf16, q=aq, scale=as_)
+            else:
+                ops.row_reduce(a_bf16, "absmax", out=am)
+                comm.allreduce(am, "max", st)
+                ops.quant_rowwise(a_bf16, amax=am, q=aq, scale=as_)
             ops.fp8_gemm_tp(aq, as_, w_q, w_s, None, None, tp=comm.tp_gemm(peer=True),
                             epilogue="peer", status=st)
             ops.residual_tp(x, comm.rs, bias=bias, gate=gate, flags=rs_flags,
@@ -616,7 +632,8 @@ class TPSRDiT(SRDiT):
             am.zero_()
             ops.fp8_gemm_tp(xq, xs, ly.w_f0, ly.s_f0, ly.b_f0, hbuf, tp=comm.tp_gemm(),
                             epilogue="gelu", row_amax=am, status=st)
-            comm.allreduce(am, "max", st)
+            if not self.local_scales:
+                comm.allreduce(am, "max", st)
             ops.quant_rowwise(hbuf, amax=am, q=hq, scale=hs)
             ops.fp8_gemm_tp(hq, hs, ly.w_f2, ly.s_f2, None, None, tp=comm.tp_gemm(peer=True),
                             epilogue="peer", status=st)

@@ -51,6 +51,7 @@ typedef struct srdit_peer_ptrs {
 
 #define SRDIT_RED_SUM 0
 #define SRDIT_RED_MAX 1
+#define SRDIT_AR_BLOCKS 16  /* blocks of one srdit_tp_allreduce launch */
 
 /* window-attention params-row layouts and anchor modes
  * (video_refiner/wan/modules/sr_dit/blockgrid_triton.py:77-80) */
@@ -241,11 +242,14 @@ int srdit_residual_tp(void* x, long long ldx, int M, int N, const void* parts, i
 /*
  * out[i] = sum (SRDIT_RED_SUM) or max (SRDIT_RED_MAX) over ranks of in[i], n
  * fp32 values, through the peers' memory: slots.p[d] is rank d's receive area
- * (world * n floats, slot s at s * n), flags.p[d] its counters [world]. Every
- * rank stores its vector into slot `rank` of every rank, adds 1 to
- * flags.p[d][rank], waits until all its counters reach `epoch` (the number of
- * calls on these flags so far, this one included, the same on every rank),
- * then reduces the slots in rank order, so all ranks get identical results.
+ * (world * n floats, slot s at s * n), flags.p[d] its counters [world]. The
+ * launch has SRDIT_AR_BLOCKS blocks, each owning a share of the vector: every
+ * block stores its share into slot `rank` of every rank and adds 1 to
+ * flags.p[d][rank] (one call adds SRDIT_AR_BLOCKS to each counter), waits
+ * until all its rank's counters reach epoch * SRDIT_AR_BLOCKS (`epoch`: the
+ * number of calls on these flags so far, this one included, the same on every
+ * rank), then reduces its share in rank order, so all ranks get identical
+ * results.
  * in and out may alias. Alternate two receive areas between consecutive calls
  * (a fast rank may store call k + 1 while a slow one still reads call k).
  * Replaces: the library all-reduce of per-token statistics a sharded
@@ -363,6 +367,8 @@ typedef struct srdit_winattn_tiling {
   int bw_k, bh_k, kboxes_per_tile;
   int bw_a, bh_a, aboxes_per_tile;
   int has_anchor;
+  int split_kv;  /* 1: two softmax groups take alternate KV tiles of an item (items of
+                    6 KV tiles or more on average); 0: both work on every tile */
 } srdit_winattn_tiling;
 
 /*

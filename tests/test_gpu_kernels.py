@@ -322,10 +322,11 @@ def test_residual_wait_times_out_into_the_status_word(srdit, cuda_device):
 
 
 def test_allreduce_wait_times_out_into_the_status_word(srdit, cuda_device):
-    """srdit_tp_allreduce with one rank asked for epoch 2 after its first signal:
-    its own counter reaches only 1, the bounded wait runs out, the status word
-    says so and ``out`` is left untouched. A second call (the counter then
-    reaches 2) completes and reduces."""
+    """srdit_tp_allreduce with one rank asked for epoch 2 after its first call:
+    its own counter reaches only SRDIT_AR_BLOCKS (one per block), the bounded
+    waits run out, the status word says so and ``out`` is left untouched. A
+    second call (the counter then reaches 2 * SRDIT_AR_BLOCKS) completes and
+    reduces."""
     n = 1000
     vals = torch.randn(n, generator=torch.Generator().manual_seed(32)).to(cuda_device)
     t = vals.clone()
@@ -347,5 +348,5 @@ def test_allreduce_wait_times_out_into_the_status_word(srdit, cuda_device):
     status.zero_()
     assert L.srdit_tp_allreduce(*args) == 0
     torch.cuda.synchronize(cuda_device)
-    assert int(status.item()) == 0 and int(flags[0].item()) == 2
+    assert int(status.item()) == 0 and int(flags[0].item()) == 2 * srdit._lib.SRDIT_AR_BLOCKS
     assert torch.equal(out, vals)

@@ -70,7 +70,10 @@ def _worker(rank, world, port, cfg_kw, grid, fused, out_q, graphs=False):
                 torch.cuda.synchronize()
                 model.check_status()
                 return outs
-        if fused == "ce":   # peer-fused, all-gather pushed by the copy engines
+        if fused == "spatial":   # the window-strip partition instead of TP
+            S = importlib.import_module("dreamx-creator_b200.spatial")
+            tp_model = S.SpatialSRDiT.random_init(cfg, dev, seed=3)
+        elif fused == "ce":   # peer-fused, all-gather pushed by the copy engines
             tp_model = T.TPSRDiT.random_init(cfg, dev, seed=3, comm=T.PeerComm(push="ce"))
         else:
             tp_model = T.TPSRDiT.random_init(cfg, dev, seed=3, fused=fused)
@@ -134,4 +137,19 @@ def test_tp2_graph_replay_matches_single_gpu():
     cfg_kw = dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16,
                   text_dim=64, text_len=16, block_hw=(2, 2), block_radius_hw=(1, 1), kv_len=3)
     cos = _run_tp(2, cfg_kw, (3, 8, 16), True, graphs=True)
+    assert min(cos) >= 0.999, cos
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "graphs"])
+@pytest.mark.parametrize("cfg_kw,grid", [
+    (dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16, text_dim=64,
+          text_len=16, block_hw=(2, 4), block_radius_hw=(1, 0), kv_len=3), (3, 8, 16)),
+    (dict(num_layers=2, block_hw=(8, 8), block_radius_hw=(0, 0)), (3, 36, 64)),
+], ids=["small", "2K-2layers"])
+def test_spatial2_matches_single_gpu(cfg_kw, grid, graphs):
+    """The window-strip partition on two GPUs (each refines half of the token
+    columns with the full model, one all-gather per forward; eager and in
+    captured CUDA graphs) against the single-GPU forward."""
+    cos = _run_tp(2, cfg_kw, grid, "spatial", graphs=graphs)
     assert min(cos) >= 0.999, cos
