@@ -666,7 +666,10 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
   const int T = blockDim.x;
   const int t = threadIdx.x;
   const int K = T * 16;
-  const int cc[2] = {t * 8, (t + T) * 8};
+  // this thread's 16 consecutive columns, as two 8-column chunks: its e4m3 row
+  // segment leaves as one 16-byte store (to every rank's gather buffer, over
+  // NVLink, in the tensor-parallel form)
+  const int cc[2] = {t * 16, t * 16 + 8};
   // per-column operands of this thread's 16 columns, as f32 pairs
   uint64_t one_p[8], sh[8], wt[8], bs[8];
 #pragma unroll
@@ -752,14 +755,12 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
       if (kPeer) {
         for (int d = 0; d < pe.world; ++d) {
           uint8_t* qr = pe.q[d] + static_cast<long long>(row0 + r) * ldq;
-          *reinterpret_cast<uint2*>(qr + cc[0]) = v0;
-          *reinterpret_cast<uint2*>(qr + cc[1]) = v1;
+          *reinterpret_cast<uint4*>(qr + cc[0]) = make_uint4(v0.x, v0.y, v1.x, v1.y);
           if (t == 0) pe.s[d][row0 + r] = sc;
         }
       } else {
         uint8_t* qr = q + static_cast<long long>(row0 + r) * ldq;
-        *reinterpret_cast<uint2*>(qr + cc[0]) = v0;
-        *reinterpret_cast<uint2*>(qr + cc[1]) = v1;
+        *reinterpret_cast<uint4*>(qr + cc[0]) = make_uint4(v0.x, v0.y, v1.x, v1.y);
         if (t == 0) qscale[row0 + r] = sc;
       }
     }

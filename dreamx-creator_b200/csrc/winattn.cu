@@ -29,6 +29,8 @@
 //              -> bf16 is staged in the item's Q buffer in the box layout and
 //              written by TMA tile stores (per-thread row stores where a box
 //              would overhang the window inside the tensor).
+#include <atomic>
+
 #include "sm100.cuh"
 #include "srdit_internal.h"
 
@@ -45,10 +47,11 @@ constexpr int OFF_Q = 0;  // two Q buffers (the next item's Q loads during this 
 constexpr int OFF_K = OFF_Q + 2 * QKV_TILE_BYTES;
 constexpr int OFF_V = OFF_K + 2 * QKV_TILE_BYTES;
 constexpr int OFF_BAR = OFF_V + 2 * QKV_TILE_BYTES;
-constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: 768 floats
+constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: 1024 floats
 constexpr int REC_SLOTS = 4;            // item-record ring (producer -> MMA, softmax)
 constexpr int REC_BYTES = 192;
-constexpr int OFF_REC = OFF_XCH + 768 * 4;
+constexpr int OFF_PAIR = OFF_XCH + 1024 * 4;  // split KV: 4 pair mbarriers (one per lane quarter)
+constexpr int OFF_REC = OFF_PAIR + 64;
 constexpr int SMEM_BYTES = OFF_REC + REC_SLOTS * REC_BYTES + 1024;
 constexpr uint32_t kEpiBarrier = 5;     // named barrier of the 256 softmax threads
 constexpr int NUM_SOFTMAX = 256;        // warps 2-9: two threads per query row
@@ -295,6 +298,9 @@ SRDIT_DEV bool make_rec(const Args& a, int item, ItemRec& o) {
   return true;
 }
 
+// kSplit: the split-KV schedule (two softmax groups take alternate KV tiles of
+// an item, each with its own O accumulator; for items with many KV tiles).
+template <bool kSplit>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     winattn_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmK,
@@ -320,6 +326,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   volatile uint32_t* abort_flag = tmem_slot + 1;
   uint64_t* rec_full = bars + 20;   // [REC_SLOTS]
   uint64_t* rec_empty = bars + 24;  // [REC_SLOTS]
+  // split-KV schedule: P_g published by one group (128 threads) and P.V_g
+  // completion, one barrier per score / O buffer (g & 1)
+  uint64_t* p_full_g = bars + 28;  // [2]
+  uint64_t* o_full_g = bars + 30;  // [2]
+  static_assert(32 * 8 <= OFF_XCH - OFF_BAR, "barrier area");
+  uint64_t* pair_full = reinterpret_cast<uint64_t*>(smem + OFF_PAIR);  // [4]
   ItemRec* ring = reinterpret_cast<ItemRec*>(smem + OFF_REC);
 
   const int warp = threadIdx.x >> 5;
@@ -344,6 +356,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(p_full, NUM_SOFTMAX);
     mbar_init(o_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full_g[i], NUM_SOFTMAX / 2);
+      mbar_init(&o_full_g[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_full[i], 64);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -546,11 +563,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       auto pv_ready = [&]() -> bool {
         if (cp.state != 1 || cp.g >= cs.g) return false;  // S_g not issued yet
         const int st = cp.g & 1;
-        if (!mbar_test_wait(p_full, static_cast<uint32_t>(cp.g) & 1u)) return false;
+        if (kSplit) {
+          if (!mbar_test_wait(&p_full_g[st], static_cast<uint32_t>(cp.g >> 1) & 1u)) return false;
+        } else {
+          if (!mbar_test_wait(p_full, static_cast<uint32_t>(cp.g) & 1u)) return false;
+        }
         if (!mbar_test_wait(&v_full[st], static_cast<uint32_t>(cp.g >> 1) & 1u)) return false;
-        if (cp.j == 0 && !mbar_test_wait(&o_empty[cp.n & 1],
-                                         (static_cast<uint32_t>(cp.n >> 1) & 1u) ^ 1u))
+        if (kSplit) {
+          // both O buffers belong to every item: the previous item's epilogue
+          // must have read them before this item's first P.V
+          const uint32_t par = (static_cast<uint32_t>(cp.n) & 1u) ^ 1u;
+          if (cp.j == 0 && (!mbar_test_wait(&o_empty[0], par) || !mbar_test_wait(&o_empty[1], par)))
+            return false;
+        } else if (cp.j == 0 && !mbar_test_wait(&o_empty[cp.n & 1],
+                                                (static_cast<uint32_t>(cp.n >> 1) & 1u) ^ 1u)) {
           return false;
+        }
         return true;
       };
       auto issue_pv = [&]() {
@@ -560,17 +588,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + OFF_V + st * QKV_TILE_BYTES);
         const uint32_t idesc = idesc_make(1u, 1u, 0u, 1u, 128u, 128u);
-        const uint32_t o_tmem = tmem_base + 256u + static_cast<uint32_t>(b * 128);
+        // split-KV: tile g accumulates into its group's O (buffer g & 1), fresh
+        // at the group's first tile of the item (j 0 or 1)
+        const uint32_t o_tmem = tmem_base + 256u + static_cast<uint32_t>((kSplit ? st : b) * 128);
         const uint32_t p_tmem = tmem_base + static_cast<uint32_t>(st * 128);
+        const bool acc0 = kSplit ? cp.j >= 2 : cp.j > 0;
         const int ksteps = ti.n16 / 16;
         for (int k = 0; k < ksteps; ++k) {
           const uint32_t voff = static_cast<uint32_t>(k * 16 * 128);
           mma_bf16_ts(o_tmem, p_tmem + static_cast<uint32_t>(k * 8),
                       sdesc_sw128(v_addr + voff, SLAB, 1024), idesc,
-                      (cp.j > 0 || k > 0) ? 1u : 0u);
+                      (acc0 || k > 0) ? 1u : 0u);
         }
         tc_commit(&v_empty[st]);
-        tc_commit(o_full);
+        tc_commit(kSplit ? &o_full_g[st] : o_full);
         advance(cp);
       };
       uint64_t idle_since = 0;
@@ -594,8 +625,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // softmax is the usual laggard -- instead of spinning, so this warp
           // does not take issue slots from the softmax warps sharing its SM
           // sub-partition. The loop re-checks both cursors.
-          if (cp.state == 1 && cp.g < cs.g)
-            mbar_try_wait(p_full, static_cast<uint32_t>(cp.g) & 1u);
+          if (cp.state == 1 && cp.g < cs.g) {
+            if (kSplit)
+              mbar_try_wait(&p_full_g[cp.g & 1], static_cast<uint32_t>(cp.g >> 1) & 1u);
+            else
+              mbar_try_wait(p_full, static_cast<uint32_t>(cp.g) & 1u);
+          }
           else if (cs.state == 1)
             mbar_try_wait(&k_full[cs.g & 1], static_cast<uint32_t>(cs.g >> 1) & 1u);
           const uint64_t now = global_timer_ns();
@@ -609,6 +644,330 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+  } else if (kSplit) {
+    // ------------------------------------------------------------ softmax, split KV
+    // Two groups of four warps, one thread per query row each: group 0 (warps
+    // 2-5) takes the KV tiles of even global index g, group 1 (warps 6-9) the
+    // odd ones, each with its own running (max, sum) and its own O in TMEM (the
+    // P.V of tile g accumulates into O buffer g & 1). The groups' softmax steps
+    // run side by side on different tiles, so on an SM sub-partition one
+    // group's exp2 work overlaps the other's TMEM loads and stores, and no
+    // per-tile row-max exchange is needed. At the item's end the two threads of
+    // a row (warps w and w + 4, one lane quarter) combine the partial results:
+    // O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)).
+    const int sub = warp & 3;
+    const int grp = (warp - 2) >> 2;
+    const int row = sub * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(sub * 32) << 16;
+    // [item parity][group][row] partial max and sum (parity: the partner reads
+    // item n's values before either thread can pass item n + 1's barrier)
+    float* xm = reinterpret_cast<float*>(smem + OFF_XCH);
+    float* xl = xm + 512;
+    const float neg_inf = -__int_as_float(0x7f800000);
+    const float c_scale = a.scale * kLog2e;
+    const uint64_t c_scale2 = pack_f2(c_scale, c_scale);
+    const float kRescale = 8.0f;
+    uint32_t geo_k[4], geo_a[4];
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) {
+      const int c = qq * 32 + lane;
+      const int rk = a.bw_k * a.bh_k, ra = a.bw_a * a.bh_a;
+      geo_k[qq] = static_cast<uint32_t>(c / rk) | static_cast<uint32_t>((c % rk) / a.bw_k) << 8 |
+                  static_cast<uint32_t>((c % rk) % a.bw_k) << 16;
+      geo_a[qq] = static_cast<uint32_t>(c / ra) | static_cast<uint32_t>((c % ra) / a.bw_a) << 8 |
+                  static_cast<uint32_t>((c % ra) % a.bw_a) << 16;
+    }
+    const int rq = a.bw_q * a.bh_q;
+    const int row_box = row / rq;
+    const int row_h = (row % rq) / a.bw_q;
+    const int row_w = (row % rq) % a.bw_q;
+    int pend_q = -1;
+    bool ok = true;
+    int g = 0;
+    for (int n = 0; ok; ++n) {
+      const int s = n % REC_SLOTS;
+      if (!mbar_wait(&rec_full[s], static_cast<uint32_t>(n / REC_SLOTS) & 1u, a.status,
+                     abort_flag))
+        break;
+      const ItemRec* rec = ring + s;
+      if (rec->end) break;
+      const int b = n & 1;
+      const int gq = rec->w.qbox0 + row_box;
+      const int hq_chunks = rec->w.hq_chunks;
+      const int t_row = gq / hq_chunks;
+      const int hh = (gq - t_row * hq_chunks) * a.bh_q + row_h;
+      const bool row_ok = row_box < rec->w.nqbox && t_row < rec->r.q_tL && hh < rec->r.qhL &&
+                          row_w < rec->r.qwL;
+      const bool active = __any_sync(0xffffffffu, row_ok);
+      const Walk& w = rec->w;  // read from the record in shared memory where used
+      const int n_tiles = w.n_tiles;
+      const bool full_k = rec->full_k, full_a = rec->full_a, per_frame = rec->r.a_per_frame;
+      // (the record stays in shared memory until the item ends: the rarely used
+      // fields are read from there, which keeps registers for the scores)
+      const bool paired = rec->sp[0] > 0;
+      const bool side_b = paired && row_w >= rec->sp[0];
+      const int g0 = g;
+      const uint32_t o_tmem = tmem_base + t_lane + 256u + static_cast<uint32_t>(grp * 128);
+      float m_i = neg_inf, l_i = 0.f;
+      int mine = 0;  // this group's tiles of the item so far
+      for (int j = 0; j < n_tiles; ++j, ++g) {
+        if ((g & 1) != grp) continue;
+        const int st = grp;
+        const uint32_t ph = static_cast<uint32_t>(g >> 1) & 1u;
+        const TileInfo ti = tile_info(a, w, j);
+        const int nchunks = (ti.n16 + 31) >> 5;  // warp-uniform, 1..4
+        uint32_t vm[4];
+        const bool sees = !(ti.anchor && per_frame) || (t_row == ti.frame);
+        if (ti.anchor ? full_a : full_k) {
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int nv = ti.rows - qq * 32;
+            vm[qq] = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
+          }
+        } else {
+          const int khl = ti.anchor ? rec->r.khL_a : rec->r.khL;
+          const int kwl = ti.anchor ? rec->r.kwL_a : rec->r.kwL;
+          const int hch = ti.anchor ? w.a_hchunks : w.hr_hchunks;
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int c = qq * 32 + lane;
+            const uint32_t geo = ti.anchor ? geo_a[qq] : geo_k[qq];
+            const int bi = static_cast<int>(geo & 0xffu);
+            const int hr = static_cast<int>((geo >> 8) & 0xffu);
+            const int cw = static_cast<int>(geo >> 16);
+            const int hc = (ti.box0 + bi) % hch;
+            const bool v = (c < ti.rows) && (hc * ti.bh + hr < khl) && (cw < kwl);
+            vm[qq] = __ballot_sync(0xffffffffu, v);
+          }
+        }
+        if (paired) {
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int cw = static_cast<int>((ti.anchor ? geo_a[qq] : geo_k[qq]) >> 16);
+            const int* rg = rec->sp + (ti.anchor ? 5 : 1);  // {lo_a, hi_a, lo_b, hi_b}
+            const int lo_a = rg[0], hi_a = rg[1], lo_b = rg[2], hi_b = rg[3];
+            const uint32_t m_a = __ballot_sync(0xffffffffu, cw >= lo_a && cw < hi_a);
+            const uint32_t m_b = __ballot_sync(0xffffffffu, cw >= lo_b && cw < hi_b);
+            vm[qq] &= side_b ? m_b : m_a;
+          }
+        }
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) vm[qq] = (sees && qq < nchunks) ? vm[qq] : 0u;
+        if (!mbar_wait(&s_full[st], ph, a.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t s_tmem = tmem_base + t_lane + static_cast<uint32_t>(st * 128);
+        // Two passes over the score row, 32 columns at a time (the whole row
+        // would not fit the registers of a 10-warp CTA): the row max, then the
+        // scores again for exp2. Masked columns (and columns past the tile's MMA
+        // extent, never loaded) count as -inf.
+        float pmax = neg_inf;
+        if (active) {
+          float m0 = neg_inf, m1 = neg_inf;
+#pragma unroll 1
+          for (int qq = 0; qq < 4; ++qq) {
+            if (qq >= nchunks) break;  // warp-uniform
+            uint32_t u[32];
+            tmem_ld32(s_tmem + qq * 32, u);
+            tmem_ld_wait();
+            const uint32_t m = qq == 0 ? vm[0] : qq == 1 ? vm[1] : qq == 2 ? vm[2] : vm[3];
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              m0 = max3f(m0, ((m >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf,
+                         ((m >> (i + 1)) & 1u) ? __uint_as_float(u[i + 1]) : neg_inf);
+              m1 = max3f(m1, ((m >> (i + 2)) & 1u) ? __uint_as_float(u[i + 2]) : neg_inf,
+                         ((m >> (i + 3)) & 1u) ? __uint_as_float(u[i + 3]) : neg_inf);
+            }
+          }
+          pmax = fmaxf(m0, m1);
+        }
+        const float tmax = pmax * c_scale;
+        const bool row_valid = tmax != neg_inf;
+        const bool raise = row_valid && (tmax > m_i + kRescale || m_i == neg_inf);
+        const float m_new = raise ? tmax : m_i;
+        const float alpha = raise ? ex2_approx(m_i - m_new) : 1.f;
+        const float neg_m = row_valid ? -m_new : 0.f;
+        const uint64_t neg_m2 = pack_f2(neg_m, neg_m);
+        uint64_t sum2 = pack_f2(0.f, 0.f);
+        if (active) {
+          // P = exp2(s*c - m) -> bf16 pairs, 32 scores at a time; chunk qq's 16
+          // words go over score columns [16 qq, 16 qq + 16), already read
+#pragma unroll 1
+          for (int qq = 0; qq < 4; ++qq) {
+            uint32_t u[32], pw[16];
+            if (qq < nchunks) {  // warp-uniform
+              tmem_ld32(s_tmem + qq * 32, u);
+              tmem_ld_wait();
+            }
+            const uint32_t m = qq == 0 ? vm[0] : qq == 1 ? vm[1] : qq == 2 ? vm[2] : vm[3];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float s0 = ((m >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf;
+              const float s1 = ((m >> (i + 1)) & 1u) ? __uint_as_float(u[i + 1]) : neg_inf;
+              const float2 x = unpack_f2(fma_f2(pack_f2(s0, s1), c_scale2, neg_m2));
+              const float p0 = ex2_approx(x.x);
+              const float p1 = ex2_approx(x.y);
+              sum2 = add_f2(sum2, pack_f2(p0, p1));
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+              pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            tmem_st16(s_tmem + qq * 16, pw);
+          }
+          tmem_st_wait();
+        }
+        const float2 sp = unpack_f2(sum2);
+        l_i = alpha * l_i + (sp.x + sp.y);
+        m_i = m_new;
+        // P.V of this group's previous tile (g - 2) is complete: S_g, which this
+        // thread waited for, ran after it on the tensor pipe. Waited here once,
+        // in tile order, so this group's O barrier is never two phases ahead.
+        if (g >= 2 && !mbar_wait(&o_full_g[st], static_cast<uint32_t>((g - 2) >> 1) & 1u, a.status,
+                                 abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (mine > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int qq = 0; qq < 4; ++qq) {
+            uint32_t o[32];
+            tmem_ld32(o_tmem + qq * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_tmem + qq * 32, o);
+          }
+          tmem_st_wait();
+        } else if (mine == 0 && threadIdx.x == 64 && pend_q >= 0) {
+          // the previous item's O stores have had this tile's time to read their
+          // staging buffer: wait for that, then give the Q buffer back
+          bulk_wait_group_read0();
+          mbar_arrive(&q_empty[pend_q]);
+          pend_q = -1;
+        }
+        tc_fence_before();
+        mbar_arrive(&p_full_g[st]);
+        ++mine;
+      }
+      if (!ok) break;
+      // item done: this group's last P.V, then the pair's combine
+      const int g_last = g0 + n_tiles - 1;
+      const int my_last = ((g_last & 1) == grp) ? g_last : g_last - 1;
+      if (mine > 0 && !mbar_wait(&o_full_g[grp], static_cast<uint32_t>(my_last >> 1) & 1u,
+                                 a.status, abort_flag))
+        break;
+      const bool has0 = n_tiles >= 2 || (g0 & 1) == 0;   // group 0 had a tile
+      const bool has1 = n_tiles >= 2 || (g0 & 1) == 1;
+      float* xmb = xm + (n & 1) * 256;
+      float* xlb = xl + (n & 1) * 256;
+      xmb[grp * 128 + row] = m_i;
+      xlb[grp * 128 + row] = l_i;
+      // the row pair's exchange: an mbarrier of the lane quarter (64 threads,
+      // one phase per item) with a bounded wait, so a partner that gave up on
+      // an earlier wait cannot leave this thread blocked
+      tc_fence_before();
+      mbar_arrive(&pair_full[sub]);
+      if (!mbar_wait(&pair_full[sub], static_cast<uint32_t>(n) & 1u, a.status, abort_flag)) break;
+      tc_fence_after();
+      const float ma = xmb[row], mb = xmb[128 + row];
+      const float la = xlb[row], lb = xlb[128 + row];
+      const float mm = fmaxf(ma, mb);
+      const float fa = (has0 && ma != neg_inf) ? ex2_approx(ma - mm) : 0.f;
+      const float fb = (has1 && mb != neg_inf) ? ex2_approx(mb - mm) : 0.f;
+      const float inv_l = 1.0f / (la * fa + lb * fb);
+      const float wa = fa * inv_l, wb = fb * inv_l;
+      // this thread's 64 output columns: [grp * 64, grp * 64 + 64) of both O's
+      const uint32_t oa = tmem_base + t_lane + 256u + static_cast<uint32_t>(grp * 64);
+      const uint32_t ob = oa + 128u;
+      auto out_chunk = [&](int q, uint32_t (&res)[16]) {
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        uint32_t x[32];
+        if (has0) {
+          tmem_ld32(oa + q * 32, x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(x[i]) * wa;
+        }
+        if (has1) {
+          tmem_ld32(ob + q * 32, x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(x[i]), wb, acc[i]);
+        }
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * h], acc[2 * h + 1]);
+          res[h] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+      };
+      if (rec->o_tma) {
+        uint8_t* srow = smem + OFF_Q + b * QKV_TILE_BYTES + grp * SLAB + row * 128;
+        const int sw = row & 7;
+#pragma unroll 1
+        for (int q = 0; q < (active ? 2 : 0); ++q) {
+          uint32_t res[16];
+          out_chunk(q, res);
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4)
+            *reinterpret_cast<uint4*>(srow + (((q * 4 + v4) ^ sw) << 4)) =
+                make_uint4(res[4 * v4], res[4 * v4 + 1], res[4 * v4 + 2], res[4 * v4 + 3]);
+        }
+        fence_proxy_async_smem();
+        named_barrier_sync(kEpiBarrier, NUM_SOFTMAX);
+        if (threadIdx.x == 64) {
+          if (pend_q >= 0) {  // an earlier item's Q buffer not handed back yet
+            bulk_wait_group_read0();
+            mbar_arrive(&q_empty[pend_q]);
+          }
+          const int head = rec->head;
+          const int qbox0 = rec->w.qbox0, nqbox = rec->w.nqbox;
+          const int q_t0 = rec->r.q_t0, q_h0 = rec->r.q_h0, q_w0 = rec->r.q_w0;
+          for (int qb = 0; qb < nqbox; ++qb) {
+            const int gq2 = qbox0 + qb;
+            const int t = gq2 / hq_chunks, hc = gq2 - t * hq_chunks;
+            for (int h = 0; h < 2; ++h)
+              tma_store_4d(&tmO, smem + OFF_Q + b * QKV_TILE_BYTES + h * SLAB +
+                                     qb * static_cast<int>(q_box_bytes),
+                           head * D + h * 64, q_w0, q_h0 + hc * a.bh_q, q_t0 + t);
+          }
+          bulk_commit_group();
+          pend_q = b;
+        }
+      } else {
+        const long long tok = static_cast<long long>(rec->r.q_t0 + t_row) * a.q_h * a.q_w +
+                              static_cast<long long>(rec->r.q_h0 + hh) * a.q_w +
+                              (rec->r.q_w0 + row_w);
+        __nv_bfloat16* orow = a.out + tok * a.o_stride + rec->head * D + grp * 64;
+#pragma unroll 1
+        for (int q = 0; q < (active ? 2 : 0); ++q) {
+          uint32_t res[16];
+          out_chunk(q, res);
+          if (row_ok) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4)
+              *reinterpret_cast<uint4*>(orow + q * 32 + v4 * 8) =
+                  make_uint4(res[4 * v4], res[4 * v4 + 1], res[4 * v4 + 2], res[4 * v4 + 3]);
+          }
+        }
+        if (threadIdx.x == 64) {
+          if (pend_q >= 0) {
+            bulk_wait_group_read0();
+            mbar_arrive(&q_empty[pend_q]);
+            pend_q = -1;
+          }
+          mbar_arrive(&q_empty[b]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&o_empty[0]);
+      mbar_arrive(&o_empty[1]);
+      mbar_arrive(&rec_empty[s]);
+    }
+    if (threadIdx.x == 64) bulk_wait_group_all();
   } else {
     // ------------------------------------------------------------ softmax
     // Two threads per query row: warps 2-5 own score columns 0-63 and warps 6-9
@@ -1055,6 +1414,22 @@ extern "C" int srdit_winattn_plan(const int32_t* params_host, int n_w, int p_str
   }
   out->m_tiles = m_tiles;
   out->has_anchor = anyA;
+  // The split-KV schedule is used for long items only: its end-of-item combine
+  // and the O buffers it no longer double-buffers across items cost about a
+  // tile per item. Measured on B200 (f_kv 6 / 12): 4x4 radius-3 window pairs
+  // (~30 tiles per item) 0.771 -> 0.755 ms; 8x8 windows at f_kv 12 (6 tiles)
+  // 0.159 -> 0.177 ms, slower. So items of 12 tiles or more on average.
+  long long kv_tiles = 0;
+  for (int i = 0; i < n_w; ++i) {
+    const RowHost r = read_row_host(params_host + static_cast<size_t>(i) * p_stride, frame_mode);
+    kv_tiles += (r.kv_tL * ((r.khL + out->bh_k - 1) / out->bh_k) + out->kboxes_per_tile - 1) /
+                out->kboxes_per_tile;
+    if (anyA && r.a_frames > 0)
+      kv_tiles += static_cast<long long>(frame_mode ? 1 : r.a_frames) *
+                  ((((r.khL_a + out->bh_a - 1) / out->bh_a) + out->aboxes_per_tile - 1) /
+                   out->aboxes_per_tile);
+  }
+  out->split_kv = kv_tiles >= 12LL * n_w;
   return 0;
 }
 
@@ -1162,18 +1537,28 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
 
   int dev = 0;
   cudaGetDevice(&dev);
-  static bool attr_done[kMaxDevices] = {};
-  if (dev < kMaxDevices && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn::winattn_kernel,
+  // per device: the shared-memory attribute of both schedules, set once (host
+  // threads racing here set it twice, which is harmless)
+  static std::atomic<bool> attr_done[kMaxDevices] = {};
+  if (dev < kMaxDevices && !attr_done[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(attn::winattn_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         attn::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn::winattn_kernel<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attn::SMEM_BYTES);
     if (e != cudaSuccess) return static_cast<int>(e);
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
   const long long items = static_cast<long long>(n_w) * t->m_tiles * g->n_heads;
   const int sms = num_sms(dev);
   dim3 grid(static_cast<unsigned>(items < sms ? items : sms));
-  attn::winattn_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(mq, mk, mv, mka,
-                                                                               mva, mo, a);
+  if (t->split_kv)
+    attn::winattn_kernel<true><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(
+        mq, mk, mv, mka, mva, mo, a);
+  else
+    attn::winattn_kernel<false><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(
+        mq, mk, mv, mka, mva, mo, a);
   return static_cast<int>(cudaGetLastError());
 }

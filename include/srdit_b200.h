@@ -368,7 +368,7 @@ typedef struct srdit_winattn_tiling {
   int bw_a, bh_a, aboxes_per_tile;
   int has_anchor;
   int split_kv;  /* 1: two softmax groups take alternate KV tiles of an item (items of
-                    6 KV tiles or more on average); 0: both work on every tile */
+                    12 KV tiles or more on average); 0: both work on every tile */
 } srdit_winattn_tiling;
 
 /*

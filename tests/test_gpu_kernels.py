@@ -350,3 +350,41 @@ def test_allreduce_wait_times_out_into_the_status_word(srdit, cuda_device):
     torch.cuda.synchronize(cuda_device)
     assert int(status.item()) == 0 and int(flags[0].item()) == 2 * srdit._lib.SRDIT_AR_BLOCKS
     assert torch.equal(out, vals)
+
+
+@pytest.mark.parametrize("f_cur,f_kv,bhw,rhw,anchor", [
+    (1, 1, (8, 8), (0, 0), None),      # one KV tile per item: one group has none
+    (3, 3, (8, 8), (0, 0), None),      # two tiles per item
+    (3, 6, (4, 4), (1, 1), "frame"),   # many tiles, per-frame anchor tiles, window pairs
+])
+def test_winattn_split_kv_schedule_forced(srdit, cuda_device, f_cur, f_kv, bhw, rhw, anchor):
+    """The split-KV schedule (two softmax groups on alternate KV tiles, each with
+    its own O, combined at the item's end) forced onto plans the planner would
+    run on the other schedule, including items whose single KV tile leaves one
+    group without work; against the oracle and the other schedule."""
+    h, w, n = 8, 16, 2
+    L = h * w
+    gen = torch.Generator().manual_seed(41 + f_cur + f_kv)
+    q = torch.randn(f_cur * L, n, 128, generator=gen).to(torch.bfloat16)
+    a_tok = f_cur * L if anchor else 0
+    k = torch.randn(a_tok + f_kv * L, n, 128, generator=gen).to(torch.bfloat16)
+    v = torch.randn(a_tok + f_kv * L, n, 128, generator=gen).to(torch.bfloat16)
+    spec = obg.make_spec(f_cur, f_kv, h, w, block_t=3, block_hw=bhw, block_radius_hw=rhw,
+                         streaming=f_kv > f_cur or anchor is not None)
+    oplan = obg.build_plan(spec, anchor)
+    ref = owa.run_plan(q, k, v, oplan, f_cur=f_cur, h=h, w=w)
+    outs = []
+    for split in (0, 1):
+        plan = {"params": torch.as_tensor(oplan["params"]), "n_w": oplan["n_w"],
+                "p_stride": oplan["p_stride"], "hr_base": oplan["hr_base"]}
+        out = torch.empty_like(q, device=cuda_device)
+        d = lambda t: t.to(cuda_device)  # noqa: E731
+        srdit.attention.run_blockgrid_b200(d(q), d(k), d(v), out, plan=plan, f_cur=f_cur, h=h,
+                                           w=w, n=n, d=128, anchor_mode=anchor)
+        plan[("b200", out.device)][1].split_kv = split   # the launch's tiling record
+        srdit.attention.run_blockgrid_b200(d(q), d(k), d(v), out, plan=plan, f_cur=f_cur, h=h,
+                                           w=w, n=n, d=128, anchor_mode=anchor)
+        torch.cuda.synchronize(cuda_device)
+        _check_attn(out, ref)
+        outs.append(out.float())
+    assert onum.rel_fro(outs[1], outs[0]) < 5e-3

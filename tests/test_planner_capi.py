@@ -165,3 +165,17 @@ def test_window_pairs_round_trip_and_cover_the_same_pairs(srdit, golden, name):
         t0 = srdit.ops.winattn_plan(rows, stride, code)
         t1 = srdit.ops.winattn_plan(merged, stride, code)
         assert bg.tile_pairs(merged, stride, t1) < 0.7 * bg.tile_pairs(rows, stride, t0)
+
+
+@pytest.mark.parametrize("name,split", [("2k_4x4_r3_f6", 1), ("2k_4x4_r3_f12_frame", 1),
+                                        ("2k_8x8_r0_f6", 0), ("cfg1_8x8_r0", 0)])
+def test_split_kv_schedule_choice(srdit, golden, name, split):
+    """The planner picks the split-KV schedule for items that average 12 KV
+    tiles or more (the shipped 4x4 radius-3 windows, about 30), not for
+    BASELINE's 8x8 windows (3 to 6 tiles per item)."""
+    g = golden("plans")
+    params = torch.from_numpy(g[f"{name}.params"])
+    mode = spec_fields(g, name)[1]
+    t = srdit.ops.winattn_plan(params, int(g[f"{name}.meta"][5]),
+                               srdit.blockgrid.ANCHOR_MODES[mode])
+    assert t.split_kv == split
