@@ -762,24 +762,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Two passes over the score row, 32 columns at a time (the whole row
         // would not fit the registers of a 10-warp CTA): the row max, then the
         // scores again for exp2. Masked columns (and columns past the tile's MMA
-        // extent, never loaded) count as -inf.
+        // extent, never loaded) count as -inf. Each pass keeps the next chunk's
+        // TMEM load in flight while it works on the current one (two buffers).
         float pmax = neg_inf;
-        if (active) {
-          float m0 = neg_inf, m1 = neg_inf;
-#pragma unroll 1
-          for (int qq = 0; qq < 4; ++qq) {
-            if (qq >= nchunks) break;  // warp-uniform
-            uint32_t u[32];
-            tmem_ld32(s_tmem + qq * 32, u);
-            tmem_ld_wait();
-            const uint32_t m = qq == 0 ? vm[0] : qq == 1 ? vm[1] : qq == 2 ? vm[2] : vm[3];
+        float m0 = neg_inf, m1 = neg_inf;
+        auto chunk_max = [&](const uint32_t (&u)[32], uint32_t m) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              m0 = max3f(m0, ((m >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf,
-                         ((m >> (i + 1)) & 1u) ? __uint_as_float(u[i + 1]) : neg_inf);
-              m1 = max3f(m1, ((m >> (i + 2)) & 1u) ? __uint_as_float(u[i + 2]) : neg_inf,
-                         ((m >> (i + 3)) & 1u) ? __uint_as_float(u[i + 3]) : neg_inf);
-            }
+          for (int i = 0; i < 32; i += 4) {
+            m0 = max3f(m0, ((m >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf,
+                       ((m >> (i + 1)) & 1u) ? __uint_as_float(u[i + 1]) : neg_inf);
+            m1 = max3f(m1, ((m >> (i + 2)) & 1u) ? __uint_as_float(u[i + 2]) : neg_inf,
+                       ((m >> (i + 3)) & 1u) ? __uint_as_float(u[i + 3]) : neg_inf);
+          }
+        };
+        if (active) {  // nchunks is warp-uniform (tcgen05.ld is warp-collective)
+          uint32_t ua[32], ub[32];
+          tmem_ld32(s_tmem, ua);
+          tmem_ld_wait();
+          if (nchunks > 1) tmem_ld32(s_tmem + 32, ub);
+          chunk_max(ua, vm[0]);
+          if (nchunks > 1) {
+            tmem_ld_wait();
+            if (nchunks > 2) tmem_ld32(s_tmem + 64, ua);
+            chunk_max(ub, vm[1]);
+          }
+          if (nchunks > 2) {
+            tmem_ld_wait();
+            if (nchunks > 3) tmem_ld32(s_tmem + 96, ub);
+            chunk_max(ua, vm[2]);
+          }
+          if (nchunks > 3) {
+            tmem_ld_wait();
+            chunk_max(ub, vm[3]);
           }
           pmax = fmaxf(m0, m1);
         }
@@ -791,29 +805,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float neg_m = row_valid ? -m_new : 0.f;
         const uint64_t neg_m2 = pack_f2(neg_m, neg_m);
         uint64_t sum2 = pack_f2(0.f, 0.f);
-        if (active) {
-          // P = exp2(s*c - m) -> bf16 pairs, 32 scores at a time; chunk qq's 16
-          // words go over score columns [16 qq, 16 qq + 16), already read
-#pragma unroll 1
-          for (int qq = 0; qq < 4; ++qq) {
-            uint32_t u[32], pw[16];
-            if (qq < nchunks) {  // warp-uniform
-              tmem_ld32(s_tmem + qq * 32, u);
-              tmem_ld_wait();
-            }
-            const uint32_t m = qq == 0 ? vm[0] : qq == 1 ? vm[1] : qq == 2 ? vm[2] : vm[3];
+        // P = exp2(s*c - m) -> bf16 pairs; chunk qq's 16 words go over score
+        // columns [16 qq, 16 qq + 16), which this pass has already read
+        auto chunk_exp = [&](const uint32_t (&u)[32], uint32_t m, int qq) {
+          uint32_t pw[16];
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float s0 = ((m >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf;
-              const float s1 = ((m >> (i + 1)) & 1u) ? __uint_as_float(u[i + 1]) : neg_inf;
-              const float2 x = unpack_f2(fma_f2(pack_f2(s0, s1), c_scale2, neg_m2));
-              const float p0 = ex2_approx(x.x);
-              const float p1 = ex2_approx(x.y);
-              sum2 = add_f2(sum2, pack_f2(p0, p1));
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-              pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
-            }
-            tmem_st16(s_tmem + qq * 16, pw);
+          for (int i = 0; i < 32; i += 2) {
+            const float s0 = ((m >> i) & 1u) ? __uint_as_float(u[i]) : neg_inf;
+            const float s1 = ((m >> (i + 1)) & 1u) ? __uint_as_float(u[i + 1]) : neg_inf;
+            const float2 x = unpack_f2(fma_f2(pack_f2(s0, s1), c_scale2, neg_m2));
+            const float p0 = ex2_approx(x.x);
+            const float p1 = ex2_approx(x.y);
+            sum2 = add_f2(sum2, pack_f2(p0, p1));
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+            pw[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          tmem_st16(s_tmem + qq * 16, pw);
+        };
+        if (active) {
+          uint32_t ua[32], ub[32];
+          tmem_ld32(s_tmem, ua);
+          tmem_ld_wait();
+          if (nchunks > 1) tmem_ld32(s_tmem + 32, ub);
+          chunk_exp(ua, vm[0], 0);
+          if (nchunks > 1) {
+            tmem_ld_wait();
+            if (nchunks > 2) tmem_ld32(s_tmem + 64, ua);
+            chunk_exp(ub, vm[1], 1);
+          } else {
+            chunk_exp(ub, 0u, 1);  // columns past the tile: P = 0 (masks are all off)
+          }
+          if (nchunks > 2) {
+            tmem_ld_wait();
+            if (nchunks > 3) tmem_ld32(s_tmem + 96, ub);
+            chunk_exp(ua, vm[2], 2);
+          } else {
+            chunk_exp(ua, 0u, 2);
+          }
+          if (nchunks > 3) {
+            tmem_ld_wait();
+            chunk_exp(ub, vm[3], 3);
+          } else {
+            chunk_exp(ub, 0u, 3);
           }
           tmem_st_wait();
         }
