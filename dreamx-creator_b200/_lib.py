@@ -63,6 +63,12 @@ class TpGemm(ctypes.Structure):
                 ("rs_flags", c_vp * SRDIT_MAX_RANKS), ("v_ring", ctypes.POINTER(VRing))]
 
 
+class RopeHalo(ctypes.Structure):
+    _fields_ = [("k", c_vp * 2), ("v", c_vp * 2), ("grid_w", c_int * 2), ("w0", c_int * 2),
+                ("col_lo", c_int * 2), ("col_hi", c_int * 2), ("flag", c_vp * 2),
+                ("done", c_vp)]
+
+
 # name -> argtypes (every function returns int)
 SIGNATURES = {
     "srdit_version": [],
@@ -73,7 +79,8 @@ SIGNATURES = {
                            c_ll, c_vp, c_vp],
     "srdit_rms_rope": [c_vp, c_ll, c_int, c_int, c_vp, c_float, c_vp, c_ll, c_int, c_int,
                        c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_ll,
-                       c_vp, c_int, c_vp, c_int, c_vp],
+                       c_vp, c_int, c_vp, c_int, c_int, c_int, ctypes.POINTER(RopeHalo),
+                       c_vp],
     "srdit_row_reduce": [c_vp, c_ll, c_int, c_int, c_int, c_vp, c_vp],
     "srdit_fp8_gemm_tp": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                           c_int, c_int, c_vp, ctypes.POINTER(TpGemm), c_vp, c_vp],
@@ -93,6 +100,7 @@ SIGNATURES = {
     "srdit_tp_push": [c_vp, ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, c_vp,
                       ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, ctypes.POINTER(PeerPtrs),
                       c_int, c_int, c_vp],
+    "srdit_wait_counters": [c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp],
     "srdit_ipc_handle": [c_vp, c_vp, ctypes.POINTER(ctypes.c_ulonglong)],
     "srdit_ipc_open": [c_vp, ctypes.POINTER(c_vp)],
     "srdit_ipc_close": [c_vp],

@@ -25,12 +25,14 @@ BLOCKGRID_IMPLS = ("b200",)
 
 
 def check_rows(params: torch.Tensor, p_stride: int, *, f_cur, h, w, kv_frames, a_hw=None,
-               a_frames=0) -> None:
+               a_frames=0, kv_w=None) -> None:
     """Every cuboid a params row addresses lies inside its tensor.
 
     The kernel addresses tokens straight from the rows, so this is the check that
-    keeps a malformed plan from turning into an out-of-bounds store.
+    keeps a malformed plan from turning into an out-of-bounds store. ``kv_w``:
+    the K/V frames' width when it differs from the query grid's ``w``.
     """
+    kv_w = w if kv_w is None else kv_w
     p = params.to(torch.int64)
     if p.dim() != 2 or p.shape[1] != p_stride:
         raise ValueError(f"params rows must be [n_w, {p_stride}], got {tuple(p.shape)}")
@@ -45,7 +47,7 @@ def check_rows(params: torch.Tensor, p_stride: int, *, f_cur, h, w, kv_frames, a
     ok = ((q_t0 >= 0) & (q_tL > 0) & (q_t0 + q_tL <= f_cur) & (q_h0 >= 0) & (qhL > 0)
           & (q_h0 + qhL <= h) & (q_w0 >= 0) & (qwL > 0) & (q_w0 + qwL <= w)
           & (kv0 >= 0) & (kvL > 0) & (kv0 + kvL <= kv_frames) & (kh0 >= 0) & (khL > 0)
-          & (kh0 + khL <= h) & (kw0 >= 0) & (kwL > 0) & (kw0 + kwL <= w))
+          & (kh0 + khL <= h) & (kw0 >= 0) & (kwL > 0) & (kw0 + kwL <= kv_w))
     if not bool(ok.all()):
         raise ValueError("a window params row addresses tokens outside the q/KV grids")
     if a_hw is not None:

@@ -246,6 +246,35 @@ def tile_pairs(params: torch.Tensor, p_stride: int, tiling) -> int:
     return total
 
 
+def strip_rows(params: torch.Tensor, p_stride: int, w_lo: int, w_hi: int, kv_lo: int,
+               kv_w: int) -> torch.Tensor:
+    """The rows of the windows whose query columns lie in [w_lo, w_hi) of the full
+    grid, in the coordinates of a strip that holds those query columns and the
+    K/V (and anchor) columns [kv_lo, kv_lo + kv_w): query column c becomes
+    c - w_lo, KV and anchor columns c - kv_lo, and the anchor grid is kv_w wide.
+
+    Every window must lie wholly inside or outside the strip, every kept row's
+    KV columns inside [kv_lo, kv_lo + kv_w), and the anchor on the query's own
+    token grid (anchor step 1, so its columns are the KV columns' numbering)."""
+    qw0, qwl, kw0, kwl, kw0a, kwla, _ = _PAIR_COLS[p_stride]
+    wa = p_stride - 1   # the anchor grid's width, last field of both layouts
+    p = params.to(torch.int64)
+    if p.numel() and not (torch.equal(p[:, kw0a], p[:, kw0]) and torch.equal(p[:, kwla], p[:, kwl])):
+        raise ValueError("a strip's rows need the anchor on the query token grid (step 1)")
+    inside = (p[:, qw0] >= w_lo) & (p[:, qw0] + p[:, qwl] <= w_hi)
+    touches = (p[:, qw0] < w_hi) & (p[:, qw0] + p[:, qwl] > w_lo)
+    if bool((touches & ~inside).any()):
+        raise ValueError(f"a window crosses the edge of the strip [{w_lo}, {w_hi})")
+    r = p[inside].clone()
+    r[:, qw0] -= w_lo
+    r[:, kw0] -= kv_lo
+    r[:, kw0a] -= kv_lo
+    r[:, wa] = kv_w
+    if bool(((r[:, kw0] < 0) | (r[:, kw0] + r[:, kwl] > kv_w)).any()):
+        raise ValueError(f"a window of the strip sees columns outside [{kv_lo}, {kv_lo + kv_w})")
+    return r.to(torch.int32)
+
+
 def unpair_rows(rows: torch.Tensor, split: torch.Tensor, p_stride: int) -> torch.Tensor:
     """The per-window rows that ``pair_rows`` merged (its inverse)."""
     qw0, qwl, kw0, kwl, kw0a, kwla, _ = _PAIR_COLS[p_stride]

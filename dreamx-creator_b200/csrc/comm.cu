@@ -11,6 +11,9 @@
 //       counter there, waits for all counters, then reduces the slots in rank
 //       order -- so every rank gets bit-identical results. Used for the per-token RMSNorm sums and fp8 amax
 //       values the sharded block needs (a few thousand floats).
+//   srdit_wait_counters
+//       one-thread bounded wait on counters other ranks release-add (the K/V
+//       halo signals of the spatial partition).
 //   srdit_tp_push
 //       all-gather by the copy engines: cudaMemcpyAsync of this rank's rows into
 //       every other rank's gather buffer, then a one-thread kernel that
@@ -82,6 +85,16 @@ __global__ void tp_signal_kernel(Ptrs flags, int rank, int world) {
     if (d != rank) flag_add_release(static_cast<uint32_t*>(flags.p[d]) + rank, 1u);
 }
 
+// One thread: bounded wait until counters[s] >= expected for every bit s of
+// mask. A later kernel of the stream then sees what the signalling ranks
+// stored before their release-adds.
+__global__ void wait_counters_kernel(const uint32_t* counters, uint32_t mask, uint32_t expected,
+                                     uint32_t* status) {
+  for (int s = 0; s < 32; ++s)
+    if ((mask >> s) & 1u)
+      if (!flag_wait(counters + s, expected, status)) return;
+}
+
 PFN_cuMemGetAddressRange_v3020 g_range = nullptr;
 std::once_flag g_range_once;
 
@@ -146,6 +159,14 @@ extern "C" int srdit_tp_allreduce(const float* in, float* out, int n, int op,
   }
   comm::tp_allreduce_kernel<<<SRDIT_AR_BLOCKS, 256, 0, stream>>>(in, out, n, op, s, f, rank,
                                                                 world, epoch, status);
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int srdit_wait_counters(const uint32_t* counters, uint32_t mask, uint32_t expected,
+                                   uint32_t* status, cudaStream_t stream) {
+  if (!counters) return SRDIT_EINVAL;
+  if (!mask) return 0;
+  comm::wait_counters_kernel<<<1, 1, 0, stream>>>(counters, mask, expected, status);
   return static_cast<int>(cudaGetLastError());
 }
 

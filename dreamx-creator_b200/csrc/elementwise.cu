@@ -418,6 +418,19 @@ SRDIT_DEV uint32_t f64x2_to_bf2(double lo, double hi) {
   return static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
 }
 
+// Where a strip's edge rows also go: up to two peers' K/V rings (the K/V halo
+// of a spatial partition), peer j taking this grid's columns [col_lo, col_hi)
+// at column (c + w0) of its grid_h x grid_w frames, same slots and row pitch.
+// When every row is stored, the kernel's last CTA release-adds 1 to each
+// peer's counter flag[j] (the counter of this rank in the peer's memory).
+struct RopeHalo {
+  __nv_bfloat16* k[2];  // null: no peer on that side
+  __nv_bfloat16* v[2];
+  int grid_w[2], w0[2], col_lo[2], col_hi[2];
+  uint32_t* flag[2];
+  uint32_t* done;  // CTAs finished (this rank's memory; reset by the last one)
+};
+
 struct RopeArgs {
   const __nv_bfloat16* src;  // row r at src + r * ld_src
   long long ld_src;
@@ -425,8 +438,11 @@ struct RopeArgs {
   __nv_bfloat16* dst;           // destination row address computed by dst_row()
   long long ld_dst;
   // destination frame mapping: token r = f * frame_tokens + s goes to
-  // dst + (((slot0 + f) % n_slots) * frame_tokens + s) * ld_dst
+  // dst + (((slot0 + f) % n_slots) * frame_tokens + s) * ld_dst, or, with
+  // dst_grid_w > 0 (a strip written into a wider frame grid), to frame row
+  // (s / grid_w) and column (s % grid_w) + dst_w0 of a grid_h x dst_grid_w frame
   int frame_tokens, slot0, n_slots;
+  int dst_grid_w, dst_w0;
   // RoPE (cos_t / sin_t null -> no rotation)
   const double* cos_tab;  // [rows, 64] fp64: table columns for the (t | h | w) axes
   const double* sin_tab;
@@ -442,6 +458,7 @@ struct RopeArgs {
   long long ld_vsrc;
   __nv_bfloat16* v_dst;
   long long ld_vdst;
+  RopeHalo halo;  // read only by the kHalo instantiation
 };
 
 // VEC chunk slots of 256 columns per row; the last slot is partial when K is an
@@ -449,11 +466,8 @@ struct RopeArgs {
 // sum of squares over the full norm width (norm_width columns, of which this
 // row slice is a part) is given, as a tensor-parallel rank has it after the
 // all-reduce of its partial sums.
-template <int VEC>
-__global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(RopeArgs a, int M, int K) {
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= M) return;
+template <int VEC, bool kHalo>
+SRDIT_DEV void rope_row(const RopeArgs& a, int row, int lane, int K) {
   const bool tail_ok = (VEC - 1) * 256 + lane * 8 < K;  // this lane has the last chunk
   const uint4* xr = reinterpret_cast<const uint4*>(a.src + row * a.ld_src) + lane;
   uint4 raw[VEC];
@@ -461,8 +475,28 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
   for (int i = 0; i < VEC; ++i)
     raw[i] = (i < VEC - 1 || tail_ok) ? ld_stream(xr + i * 32) : make_uint4(0u, 0u, 0u, 0u);
   const int f = row / a.frame_tokens, sp = row % a.frame_tokens;
-  const long long drow =
-      static_cast<long long>((a.slot0 + f) % a.n_slots) * a.frame_tokens + sp;
+  const long long slot = (a.slot0 + f) % a.n_slots;
+  long long drow;
+  if (a.dst_grid_w > 0) {
+    const int hh = sp / a.grid_w, ww = sp - hh * a.grid_w;
+    drow = (slot * a.grid_h + hh) * a.dst_grid_w + ww + a.dst_w0;
+  } else {
+    drow = slot * a.frame_tokens + sp;
+  }
+  // peer copies of this row (edge columns of a strip)
+  __nv_bfloat16* pk[2] = {nullptr, nullptr};
+  __nv_bfloat16* pv[2] = {nullptr, nullptr};
+  if constexpr (kHalo) {
+    const int hh = sp / a.grid_w, ww = sp - hh * a.grid_w;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (a.halo.k[j] && ww >= a.halo.col_lo[j] && ww < a.halo.col_hi[j]) {
+        const long long prow = (slot * a.grid_h + hh) * a.halo.grid_w[j] + ww + a.halo.w0[j];
+        pk[j] = a.halo.k[j] + prow * a.ld_dst;
+        if (a.v_src) pv[j] = a.halo.v[j] + prow * a.ld_vdst;
+      }
+    }
+  }
   // The V copy is independent of the norm: issue it first so its traffic
   // overlaps the reduction (4 chunks at a time, to bound the registers it holds).
   if (a.v_src) {
@@ -476,7 +510,14 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
         if (i0 + u < VEC && (i0 + u < VEC - 1 || tail_ok)) t[u] = ldg_inorder(vr + (i0 + u) * 32);
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        if (i0 + u < VEC && (i0 + u < VEC - 1 || tail_ok)) vd[(i0 + u) * 32] = t[u];
+        if (i0 + u < VEC && (i0 + u < VEC - 1 || tail_ok)) {
+          vd[(i0 + u) * 32] = t[u];
+          if constexpr (kHalo) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              if (pv[j]) (reinterpret_cast<uint4*>(pv[j]) + lane)[(i0 + u) * 32] = t[u];
+          }
+        }
     }
   }
   float ssum;
@@ -539,7 +580,35 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(Rope
         o[p] = f64x2_to_bf2(x0 * cr[p] - x1 * si[p], x0 * si[p] + x1 * cr[p]);
       }
     }
-    dr[i * 32] = make_uint4(o[0], o[1], o[2], o[3]);
+    const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+    dr[i * 32] = ov;
+    if constexpr (kHalo) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (pk[j]) (reinterpret_cast<uint4*>(pk[j]) + lane)[i * 32] = ov;
+    }
+  }
+}
+
+template <int VEC, bool kHalo>
+__global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(RopeArgs a, int M, int K) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row < M) rope_row<VEC, kHalo>(a, row, lane, K);
+  if constexpr (kHalo) {
+    // every thread's peer stores precede thread 0's system-scope fence (the
+    // barrier, then a cumulative fence); the CTA that finishes last signals
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      if (atomicAdd(a.halo.done, 1u) == gridDim.x - 1) {
+        *a.halo.done = 0u;  // ready for the next launch
+        __threadfence_system();
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          if (a.halo.k[j]) flag_add_release(a.halo.flag[j], 1u);
+      }
+    }
   }
 }
 
@@ -850,7 +919,10 @@ struct LnLaunch {
 template <int VEC>
 int rope_launch(const RopeArgs& a, int M, int K, cudaStream_t st) {
   const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
-  rms_rope_kernel<VEC><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M, K);
+  if (a.halo.done)
+    rms_rope_kernel<VEC, true><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M, K);
+  else
+    rms_rope_kernel<VEC, false><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M, K);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -1036,9 +1108,12 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
                               int t_offset,
                               const void* v_src, long long ld_vsrc, void* v_dst,
                               long long ld_vdst, const float* ss_in, int norm_width,
-                              const int* t_offset_dev, int w_offset, cudaStream_t stream) {
-  if (M == 0) return 0;
-  if (!src || !weight || !dst || M < 0 || frame_tokens <= 0 || n_slots <= 0 || slot0 < 0)
+                              const int* t_offset_dev, int w_offset, int dst_grid_w,
+                              int dst_w0, const srdit_rope_halo* halo, cudaStream_t stream) {
+  if (M == 0 && !halo) return 0;
+  // with a halo the peers count this launch's signal: it needs rows to launch a grid
+  if (!src || !weight || !dst || M < 0 || (halo && M == 0) || frame_tokens <= 0 ||
+      n_slots <= 0 || slot0 < 0)
     return SRDIT_EINVAL;
   if (K <= 0 || K % 128) return SRDIT_EUNSUPPORTED;
   if (ss_in && norm_width < K) return SRDIT_EINVAL;
@@ -1053,6 +1128,21 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
       return SRDIT_EINVAL;
   }
   if ((v_src == nullptr) != (v_dst == nullptr)) return SRDIT_EINVAL;
+  if (dst_grid_w > 0 && (grid_w <= 0 || grid_h <= 0 || grid_h * grid_w != frame_tokens ||
+                         dst_w0 < 0 || dst_w0 + grid_w > dst_grid_w))
+    return SRDIT_EINVAL;
+  if (halo) {
+    // peers' rows are addressed through the strip's grid: the grid mapping is required
+    if (dst_grid_w <= 0 || !halo->done) return SRDIT_EINVAL;
+    for (int j = 0; j < 2; ++j) {
+      if (!halo->k[j]) continue;
+      const int lo = halo->col_lo[j], hi = halo->col_hi[j];
+      if (!halo->flag[j] || (v_src == nullptr) != (halo->v[j] == nullptr) || lo < 0 ||
+          hi <= lo || hi > grid_w || lo + halo->w0[j] < 0 || hi + halo->w0[j] > halo->grid_w[j])
+        return SRDIT_EINVAL;
+      if (!aligned16(halo->k[j]) || (halo->v[j] && !aligned16(halo->v[j]))) return SRDIT_EALIGN;
+    }
+  }
   if ((ld_src % 8) || (ld_dst % 8) || !aligned16(src) || !aligned16(dst)) return SRDIT_EALIGN;
   if (v_src && ((ld_vsrc % 8) || (ld_vdst % 8) || !aligned16(v_src) || !aligned16(v_dst)))
     return SRDIT_EALIGN;
@@ -1063,6 +1153,8 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
   a.dst = static_cast<__nv_bfloat16*>(dst);
   a.ld_dst = ld_dst;
   a.frame_tokens = frame_tokens;
+  a.dst_grid_w = dst_grid_w > 0 ? dst_grid_w : 0;
+  a.dst_w0 = dst_w0;
   a.slot0 = slot0;
   a.n_slots = n_slots;
   a.cos_tab = cos_tab;
@@ -1080,6 +1172,20 @@ extern "C" int srdit_rms_rope(const void* src, long long ld_src, int M, int K,
   a.ld_vsrc = ld_vsrc;
   a.v_dst = static_cast<__nv_bfloat16*>(v_dst);
   a.ld_vdst = ld_vdst;
+  a.halo = ew::RopeHalo{};
+  if (halo) {
+    for (int j = 0; j < 2; ++j) {
+      if (!halo->k[j]) continue;
+      a.halo.k[j] = static_cast<__nv_bfloat16*>(halo->k[j]);
+      a.halo.v[j] = static_cast<__nv_bfloat16*>(halo->v[j]);
+      a.halo.grid_w[j] = halo->grid_w[j];
+      a.halo.w0[j] = halo->w0[j];
+      a.halo.col_lo[j] = halo->col_lo[j];
+      a.halo.col_hi[j] = halo->col_hi[j];
+      a.halo.flag[j] = halo->flag[j];
+    }
+    a.halo.done = halo->done;
+  }
   return ew::rope_dispatch(a, M, K, stream);
 }
 

@@ -297,8 +297,10 @@ class SRDiT:
             t = self._bufs[name] = torch.empty(shape, dtype=dtype, device=self.device)
         return t
 
-    def new_cache(self, frame_tokens):
-        """K/V ring for this model's heads (all heads; a tensor-parallel rank's slice)."""
+    def new_cache(self, frame_tokens, grid_hw=None):
+        """K/V ring for this model's heads (all heads; a tensor-parallel rank's slice)
+        for frames of ``frame_tokens`` tokens (``grid_hw``: their (h, w) token grid,
+        which a spatially partitioned model needs)."""
         c = self.cfg
         return KVRing(c.num_layers, frame_tokens, self.kv_width, c.kv_len, c.chunk_frames,
                       self.device)
@@ -386,6 +388,36 @@ class SRDiT:
         y = torch.einsum("fhwpqrc->cfphqwr", y).reshape(c.out_dim, f * p[0], h * p[1], w * p[2])
         return y.to(torch.bfloat16)
 
+    def _window_plan(self, f, f_kv, h, w, streaming, mode, independent_frames):
+        """The window plan dict of a chunk of f frames on an h x w token grid over
+        f_kv visible frames (``independent_frames``: f separate 1-frame samples)."""
+        from .attention import cached_plan, frames_plan
+        c = self.cfg
+        if independent_frames:
+            spec1 = blockgrid.make_spec(f_cur=1, f_kv=1, h=h, w=w, block_t=c.block_t,
+                                        block_hw=c.block_hw, block_radius_hw=c.block_radius_hw,
+                                        block_radius_t=c.block_radius_t, streaming=False)
+            return frames_plan(spec1, f)
+        spec = blockgrid.make_spec(f_cur=f, f_kv=f_kv, h=h, w=w, block_t=c.block_t,
+                                   block_hw=c.block_hw, block_radius_hw=c.block_radius_hw,
+                                   block_radius_t=c.block_radius_t, streaming=streaming)
+        return cached_plan(spec, mode)
+
+    def _kv_width(self, w):
+        """Token columns of the K/V ring's (and the anchor's) frames for a chunk w
+        tokens wide: the chunk's own."""
+        return w
+
+    def _begin_forward(self):
+        """Called at the start of every forward (a sharded model's per-forward setup)."""
+
+    def _ring_kw(self, li, cache, w):
+        """Extra ``rms_rope`` arguments of the K/V ring write of block ``li``."""
+        return {}
+
+    def _kv_sync(self, li, cache, slot_cur, f):
+        """Called between block ``li``'s K/V ring write and its attention."""
+
     def _setup(self, latent, t, context, cache, anchor_kv, anchor_align, ctx_emb, n_heads,
                width, independent_frames=False):
         """Embeddings, the window plan and the attention geometries of one forward.
@@ -400,44 +432,37 @@ class SRDiT:
         M = f * L
         dev = self.device
         if cache is None:
-            cache = self._scratch_cache(L)
+            cache = self._scratch_cache(L, (h, w))
             cache.reset()
         f_kv = cache.frames + f
         if f_kv > cache.cap:
             raise _lib.SrditError(f"chunk of {f} frames does not fit the ring of {cache.cap}")
         slot_cur = (cache.start + cache.frames) % cache.cap
         mode = None if anchor_kv is None else anchor_align
-        from .attention import cached_plan, frames_plan, _plan_device_state
-        if independent_frames:
-            if cache.frames or anchor_kv is not None:
-                raise _lib.SrditError("independent_frames: no cache and no anchor")
-            spec1 = blockgrid.make_spec(f_cur=1, f_kv=1, h=h, w=w, block_t=c.block_t,
-                                        block_hw=c.block_hw, block_radius_hw=c.block_radius_hw,
-                                        block_radius_t=c.block_radius_t, streaming=False)
-            plan = frames_plan(spec1, f)
-        else:
-            spec = blockgrid.make_spec(f_cur=f, f_kv=f_kv, h=h, w=w, block_t=c.block_t,
-                                       block_hw=c.block_hw, block_radius_hw=c.block_radius_hw,
-                                       block_radius_t=c.block_radius_t,
-                                       streaming=cache.frames > 0 or anchor_kv is not None)
-            plan = cached_plan(spec, mode)
+        from .attention import _plan_device_state
+        if independent_frames and (cache.frames or anchor_kv is not None):
+            raise _lib.SrditError("independent_frames: no cache and no anchor")
+        plan = self._window_plan(f, f_kv, h, w, cache.frames > 0 or anchor_kv is not None, mode,
+                                 independent_frames)
+        kv_w = self._kv_width(w)
         fkey = ("flops", n_heads)
         if fkey not in plan:
             plan[fkey] = blockgrid.visible_flops(plan["params"], int(plan["p_stride"]),
                                                  n_heads, 128)
-        a_hw = (h, w) if anchor_kv is not None else None
+        a_hw = (h, kv_w) if anchor_kv is not None else None
         params_dev, tiling, n_w, amode, split_dev = _plan_device_state(
-            plan, dev, mode, (f, h, w, f_kv, a_hw, f if a_hw else 0),
-            dict(f_cur=f, h=h, w=w, kv_frames=f_kv, a_hw=a_hw, a_frames=f if a_hw else 0))
+            plan, dev, mode, (f, h, w, f_kv, a_hw, f if a_hw else 0, kv_w),
+            dict(f_cur=f, h=h, w=w, kv_frames=f_kv, a_hw=a_hw, a_frames=f if a_hw else 0,
+                 kv_w=kv_w))
         geom = _lib.WinattnGeom()
         geom.q_frames, geom.q_h, geom.q_w = f, h, w
-        geom.kv_h, geom.kv_w, geom.kv_slots, geom.kv_slot0 = h, w, cache.cap, cache.start
+        geom.kv_h, geom.kv_w, geom.kv_slots, geom.kv_slot0 = h, kv_w, cache.cap, cache.start
         geom.n_heads, geom.head_dim = n_heads, 128
         geom.q_stride = geom.kv_stride = geom.o_stride = width
         geom.scale = 128 ** -0.5
         geom.col_split = None if split_dev is None else split_dev.data_ptr()
         if anchor_kv is not None:
-            geom.a_frames, geom.a_h, geom.a_w, geom.a_stride = f, h, w, width
+            geom.a_frames, geom.a_h, geom.a_w, geom.a_stride = f, h, kv_w, width
 
         Lc = ctx.shape[0]
         cp_params, cp_tiling, cp_nw, cwq, chk, cwk = self._cross_plan(M, Lc)
@@ -491,6 +516,7 @@ class SRDiT:
             ctx_emb = text.ctx_emb
         S = self._setup(latent, t, context, cache, anchor_kv, anchor_align, ctx_emb,
                         c.num_heads, c.dim, independent_frames)
+        self._begin_forward()
         x, e0, e, ctx, grid, cache = S.x, S.e0, S.e, S.ctx, S.grid, S.cache
         f, h, w = grid
         L, M, D, Lc = S.L, S.M, c.dim, S.Lc
@@ -512,7 +538,9 @@ class SRDiT:
         ckv = self._buf("ckv", (Lc, 2 * D), bf16)
         ctxq, ctxs = ops.quant_rowwise(ctx) if text is None else (None, None)
         mods = torch.stack([ly.modulation for ly in self.layers]) + e0[None]   # [layers, 6, D]
-        v_direct = L % 32 == 0 and D % 64 == 0   # the GEMM can store V into ring slots
+        # the GEMM can store V into ring slots (whole 32-row boxes of frames the
+        # chunk's own size)
+        v_direct = L % 32 == 0 and D % 64 == 0 and cache.frame_tokens == L
         kv_out = [] if return_kv else None
         st = self.status
         cos, sin = self.rope_cos, self.rope_sin
@@ -531,12 +559,15 @@ class SRDiT:
             vcopy = {} if v_direct else dict(v_src=qkv[:, 2 * D:], v_dst=vr)
             ops.rms_rope(qkv[:, D:2 * D], ly.nk, c.eps, kr, frame_tokens=L, slot0=slot_cur,
                          n_slots=cache.cap, cos=cos, sin=sin, grid_h=h, grid_w=w,
-                         t_offset_dev=self.t_offset_dev, w_offset=self.rope_w0, **vcopy)
+                         t_offset_dev=self.t_offset_dev, w_offset=self.rope_w0, **vcopy,
+                         **self._ring_kw(li, cache, w))
             if last_kv:
+                self._kv_sync(li, cache, slot_cur, f)
                 break   # its K / V are in the ring: nothing else of the block is used
             ops.rms_rope(qkv[:, :D], ly.nq, c.eps, qb, frame_tokens=L, cos=cos, sin=sin,
                          grid_h=h, grid_w=w, t_offset_dev=self.t_offset_dev,
                          w_offset=self.rope_w0)
+            self._kv_sync(li, cache, slot_cur, f)
             ak = av = None
             if anchor_kv is not None:
                 ak, av = anchor_kv[li]
@@ -546,8 +577,9 @@ class SRDiT:
                         flops=S.flops)
             if return_kv:
                 idx = (torch.arange(f, device=dev) + slot_cur) % cache.cap
-                kv_out.append((kr.view(cache.cap, L, D)[idx].reshape(M, D).clone(),
-                               vr.view(cache.cap, L, D)[idx].reshape(M, D).clone()))
+                Lr = cache.frame_tokens
+                kv_out.append((kr.view(cache.cap, Lr, D)[idx].reshape(f * Lr, D).clone(),
+                               vr.view(cache.cap, Lr, D)[idx].reshape(f * Lr, D).clone()))
             ops.quant_rowwise(att, q=xq, scale=xs)
             ops.fp8_gemm(xq, xs, ly.w_o, ly.s_o, ly.b_o, x, epilogue="gated_res", residual=x,
                          gate=em[2])
@@ -612,7 +644,7 @@ class SRDiT:
         self.ops.fp8_gemm(ctxq, ctxs, ly.w_ckv, ly.s_ckv, ly.b_ckv, ckv)
         self.ops.rms_rope(ckv[:, :W], ly.cnk, c.eps, ckv[:, :W], frame_tokens=ckv.shape[0])
 
-    def _scratch_cache(self, L):
+    def _scratch_cache(self, L, grid_hw=None):
         key = ("scratch_cache", L)
         if key not in self._bufs:
             self._bufs[key] = self.new_cache(L)

@@ -144,13 +144,16 @@ def ln_mod_quant(x, eps=1e-6, *, ln_weight=None, ln_bias=None, shift=None, scale
 
 def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, cos=None,
              sin=None, grid_h=0, grid_w=0, t_offset=0, v_src=None, v_dst=None, ss=None,
-             norm_width=0, t_offset_dev=None, w_offset=0):
+             norm_width=0, t_offset_dev=None, w_offset=0, dst_grid_w=0, dst_w0=0, halo=None):
     """RMSNorm(src) * weight [-> 3-D RoPE] -> dst frame slots (+ V copy).
 
     ``ss`` ([M] fp32, optional): per-row sum of squares over ``norm_width``
     columns (a tensor-parallel slice's all-reduced statistic). ``t_offset_dev``
     (optional int32 [1] on the device): added to ``t_offset`` at run time.
-    ``w_offset``: width position of the grid's column 0 (a strip of a wider grid)."""
+    ``w_offset``: width position of the grid's column 0 (a strip of a wider grid).
+    ``dst_grid_w`` > 0: destination frames of grid_h x dst_grid_w tokens, the
+    grid's column c written to column c + ``dst_w0``. ``halo`` (a ``_lib.RopeHalo``):
+    the strip's edge columns also stored into the neighbours' rings, then signalled."""
     _need_cuda(src, weight, dst, cos, sin, v_src, v_dst, ss)
     if ss is not None and (ss.dtype != torch.float32 or not ss.is_contiguous()):
         raise _lib.SrditError("ss must be contiguous float32")
@@ -165,7 +168,9 @@ def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, c
             _ptr(sin), int(tab_rows), int(grid_h), int(grid_w), int(t_offset), _ptr(v_src),
             _rows(v_src) if v_src is not None else 0, _ptr(v_dst),
             _rows(v_dst) if v_dst is not None else 0, _ptr(ss), int(norm_width),
-            _ptr(t_offset_dev), int(w_offset), _stream(src.device), kind="rms_rope",
+            _ptr(t_offset_dev), int(w_offset), int(dst_grid_w), int(dst_w0),
+            ctypes.byref(halo) if halo is not None else None,
+            _stream(src.device), kind="rms_rope",
             work=M * K * 2 * (4 if v_src is not None else 2))
     return dst
 
@@ -278,6 +283,14 @@ def tp_allreduce(t, op, *, slots, flags, rank, world, epoch, status=None):
             ctypes.byref(flags), int(rank), int(world), int(epoch) & 0xffffffff, _ptr(status),
             _stream(t.device), kind="allreduce", work=t.numel() * 4 * world)
     return t
+
+
+def wait_counters(counters: int, mask: int, expected: int, *, status=None, device=None):
+    """srdit_wait_counters: the stream waits (bounded) until the uint32 counters at
+    device address ``counters`` selected by ``mask`` reach ``expected``."""
+    _need_cuda(status)
+    _launch("srdit_wait_counters", ctypes.c_void_p(int(counters)), int(mask) & 0xffffffff,
+            int(expected) & 0xffffffff, _ptr(status), _stream(device), kind="wait")
 
 
 def ln_mod_quant_tp(x, eps=1e-6, *, ln_weight=None, ln_bias=None, shift=None, scale=None,

@@ -170,8 +170,8 @@ class RefinerStream:
         if self.cache is None:
             m = self.model
             ph, pw = m.cfg.patch_size[1], m.cfg.patch_size[2]
-            L = (noisy_chunk.shape[2] // ph) * (noisy_chunk.shape[3] // pw)
-            self.cache = m.new_cache(L)
+            h, w = noisy_chunk.shape[2] // ph, noisy_chunk.shape[3] // pw
+            self.cache = m.new_cache(h * w, grid_hw=(h, w))
 
     def _step_eager(self, noisy_chunk, lq_chunk=None, anchor_harvest_t=0.0, anchor=None):
         m = self.model

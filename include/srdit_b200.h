@@ -172,6 +172,18 @@ int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, float eps,
                        const float* scale, void* q, long long ldq, float* qscale,
                        cudaStream_t stream);
 
+/* Peer destinations of a strip's edge rows (srdit_rms_rope). */
+typedef struct srdit_rope_halo {
+  void* k[2];         /* peer's K ring (slot 0 of the layer), NULL: no peer */
+  void* v[2];         /* peer's V ring, with v_src */
+  int grid_w[2];      /* the peer's frame width in tokens */
+  int w0[2];          /* column of this grid's column 0 in the peer's frame (may be < 0) */
+  int col_lo[2];      /* columns [col_lo, col_hi) of this grid go to the peer */
+  int col_hi[2];
+  uint32_t* flag[2];  /* this rank's counter in the peer's memory */
+  uint32_t* done;     /* zeroed word of this rank (last-CTA detection) */
+} srdit_rope_halo;
+
 /*
  * RMSNorm over the K-wide row slice (x * rsqrt(mean(x^2) + eps) -> bf16 -> x
  * weight), then optional 3-D RoPE per 128-wide head in fp64 (rounded once, fp64
@@ -190,6 +202,20 @@ int srdit_ln_mod_quant(const void* x, long long ldx, int M, int K, float eps,
  * later chunks; temporal positions beyond the table are clamped to its last row
  * (the host range check covers t_offset only). w_offset: the width position of
  * the grid's column 0, for a strip of a wider token grid (0 otherwise).
+ * dst_grid_w > 0: the destination frames are grid_h x dst_grid_w tokens and
+ * token s of a frame (row s / grid_w, column s % grid_w) goes to column
+ * (s % grid_w) + dst_w0 of its row -- a strip's rows written inside a ring that
+ * also holds neighbouring columns (the K/V halo of a spatial partition);
+ * 0: the destination frames are the source frames.
+ * halo (optional; needs dst_grid_w > 0): the strip's edge columns also go to up
+ * to two other ranks' rings over peer memory -- the K/V halo a neighbouring
+ * strip's windows read. Peer j (k[j] non-NULL) takes columns [col_lo[j],
+ * col_hi[j]) of this grid, stored at column c + w0[j] of its grid_h x grid_w[j]
+ * frames (same slots, same row pitches; v[j] with v_src). When every row is
+ * stored, the launch's last CTA release-adds 1 (system scope) to *flag[j], this
+ * rank's counter in peer j's memory; `done` is a zeroed uint32 of this rank
+ * that the kernel uses to find its last CTA (and leaves at 0). The peer waits
+ * for the counter (srdit_wait_counters) before reading its halo columns.
  * Replaces: WanRMSNorm.forward (models.py:424-440) on q and k (models.py:602-604),
  *   rope_apply (models.py:173-214), and the KV-cache torch.cat of
  *   attention.py:1506-1510.
@@ -199,7 +225,8 @@ int srdit_rms_rope(const void* src, long long ld_src, int M, int K, const void* 
                    int n_slots, const double* cos_tab, const double* sin_tab, int tab_rows,
                    int grid_h, int grid_w, int t_offset, const void* v_src, long long ld_vsrc,
                    void* v_dst, long long ld_vdst, const float* ss_in, int norm_width,
-                   const int* t_offset_dev, int w_offset, cudaStream_t stream);
+                   const int* t_offset_dev, int w_offset, int dst_grid_w, int dst_w0,
+                   const srdit_rope_halo* halo, cudaStream_t stream);
 
 #define SRDIT_ROW_SUMSQ 0
 #define SRDIT_ROW_ABSMAX 1
@@ -310,6 +337,17 @@ int srdit_ln_mod_quant_tp_static(const void* x, long long ldx, int M, int K, flo
                                  const srdit_peer_ptrs* q_rows, const srdit_peer_ptrs* s_rows,
                                  const srdit_peer_ptrs* flags, int rank, int world,
                                  cudaStream_t stream);
+
+/*
+ * One-thread wait, bounded like every cross-GPU wait of the library: until
+ * counters[s] >= expected for every bit s of `mask` (counters other ranks
+ * release-add, e.g. srdit_rms_rope's halo signal). On timeout it records
+ * SRDIT_STATUS_TIMEOUT in *status (when given) and returns. Later kernels of
+ * the stream see the stores the signalling ranks made before their adds.
+ * Replaces: nothing in the reference, which does not shard the refiner.
+ */
+int srdit_wait_counters(const uint32_t* counters, uint32_t mask, uint32_t expected,
+                        uint32_t* status, cudaStream_t stream);
 
 /*
  * All-gather push by the copy engines: copies `bytes` from src to dst.p[d]

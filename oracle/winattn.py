@@ -22,10 +22,12 @@ def _cuboid(t0, tL, h0, hL, w0, wL, H, W, base=0):
     return (base + t * (H * W) + h * W + w).reshape(-1)
 
 
-def window_index_sets(plan, f_cur, h, w):
+def window_index_sets(plan, f_cur, h, w, kv_w=None):
     """Yield (q_idx, kv_idx_list) per window: kv_idx_list is one index array per
     query sub-group (all query rows for plain rows; one per frame for frame rows),
-    with its query index array. Indices address cat([anchor, HR])."""
+    with its query index array. Indices address cat([anchor, HR]); the HR frames
+    are h x kv_w tokens (default kv_w = w)."""
+    kv_w = w if kv_w is None else kv_w
     params = np.asarray(plan["params"])
     hr_base = int(plan["hr_base"])
     frame = int(plan["p_stride"]) == 17
@@ -33,7 +35,7 @@ def window_index_sets(plan, f_cur, h, w):
         if frame:
             (qh0, qw0, qhL, qwL, kv0, kvL, kh0, khL, kw0, kwL, fc,
              kh0a, khLa, kw0a, kwLa, Ha, Wa) = row
-            hr = _cuboid(kv0, kvL, kh0, khL, kw0, kwL, h, w, base=hr_base)
+            hr = _cuboid(kv0, kvL, kh0, khL, kw0, kwL, h, kv_w, base=hr_base)
             groups = []
             for t in range(fc):
                 q = _cuboid(t, 1, qh0, qhL, qw0, qwL, h, w)
@@ -44,7 +46,7 @@ def window_index_sets(plan, f_cur, h, w):
             (q0, qL, qh0, qw0, qhL, qwL, kv0, kvL, kh0, khL, kw0, kwL, af,
              kh0a, khLa, kw0a, kwLa, Ha, Wa) = row
             q = _cuboid(q0, qL, qh0, qhL, qw0, qwL, h, w)
-            hr = _cuboid(kv0, kvL, kh0, khL, kw0, kwL, h, w, base=hr_base)
+            hr = _cuboid(kv0, kvL, kh0, khL, kw0, kwL, h, kv_w, base=hr_base)
             if af > 0:
                 a = _cuboid(0, af, kh0a, khLa, kw0a, kwLa, Ha, Wa)
                 kv = np.concatenate([a, hr])
@@ -53,7 +55,7 @@ def window_index_sets(plan, f_cur, h, w):
             yield [(q, kv)]
 
 
-def run_plan(q, k_ext, v_ext, plan, *, f_cur, h, w, dtype=torch.float64):
+def run_plan(q, k_ext, v_ext, plan, *, f_cur, h, w, dtype=torch.float64, kv_w=None):
     """out[token] = softmax(q k^T * d^-0.5) v over each window's visible set.
 
     q: [f_cur*h*w, n, d]; k_ext/v_ext: [anchor + HR tokens, n, d] (torch CPU).
@@ -65,7 +67,7 @@ def run_plan(q, k_ext, v_ext, plan, *, f_cur, h, w, dtype=torch.float64):
     n, d = q.shape[1], q.shape[2]
     out = torch.zeros(q.shape, dtype=dtype)
     scale = d ** -0.5
-    for groups in window_index_sets(plan, f_cur, h, w):
+    for groups in window_index_sets(plan, f_cur, h, w, kv_w):
         for qi, kvi in groups:
             qi_t = torch.from_numpy(qi)
             kvi_t = torch.from_numpy(kvi)

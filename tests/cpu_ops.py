@@ -90,7 +90,9 @@ def residual(x, parts, bias=None, gate=None):
 
 def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, cos=None,
              sin=None, grid_h=0, grid_w=0, t_offset=0, v_src=None, v_dst=None, ss=None,
-             norm_width=0, t_offset_dev=None, w_offset=0):
+             norm_width=0, t_offset_dev=None, w_offset=0, dst_grid_w=0, dst_w0=0, halo=None):
+    if halo is not None:
+        raise NotImplementedError("the CPU double has no peer memory")
     M, K = src.shape
     if t_offset_dev is not None:
         t_offset = t_offset + int(t_offset_dev[0])
@@ -111,7 +113,10 @@ def rms_rope(src, weight, eps, dst, *, frame_tokens, slot0=0, n_slots=1 << 30, c
         x2 = o.double().view(M, K // 2, 2)
         o = torch.stack([x2[..., 0] * c - x2[..., 1] * s, x2[..., 0] * s + x2[..., 1] * c],
                         -1).view(M, K).to(BF16)
-    drow = ((slot0 + f) % n_slots) * frame_tokens + sp
+    if dst_grid_w:
+        drow = (((slot0 + f) % n_slots) * grid_h + sp // grid_w) * dst_grid_w + sp % grid_w + dst_w0
+    else:
+        drow = ((slot0 + f) % n_slots) * frame_tokens + sp
     res = o.clone()
     dst[drow] = res
     if v_src is not None:
@@ -123,8 +128,9 @@ def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom,
             k_anchor=None, v_anchor=None, status=None, flops=0):
     n = geom.n_heads
     scale = geom.scale
-    if (geom.kv_h, geom.kv_w) != (geom.q_h, geom.q_w) or geom.q_frames == 1 and geom.kv_slots == 1:
-        # dense attention over every key (the cross-attention "window")
+    if geom.q_frames == 1 and geom.kv_slots == 1:
+        # dense attention over every key (the cross-attention "window"; a
+        # self-attention ring has at least two slots)
         qh = q.double().view(q.shape[0], n, 128)
         kh = k_hr.double().reshape(k_hr.shape[0], n, 128)
         vh = v_hr.double().reshape(v_hr.shape[0], n, 128)
@@ -132,7 +138,7 @@ def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom,
         out.copy_(torch.einsum("nqk,knd->qnd", att, vh).reshape(out.shape).to(BF16))
         return out
     f, h, w = geom.q_frames, geom.q_h, geom.q_w
-    L = h * w
+    L = geom.kv_h * geom.kv_w
     params = params_dev.cpu()
     if geom.col_split:
         # rows that pair two windows: the double attends each window on its own
@@ -158,6 +164,7 @@ def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom,
         vf = torch.cat([v_anchor, vf])
     plan = {"params": params, "hr_base": hr_base, "p_stride": p_stride}
     o = owa.run_plan(q.reshape(q.shape[0], n, 128), kf.reshape(kf.shape[0], n, 128),
-                     vf.reshape(vf.shape[0], n, 128), plan, f_cur=f, h=h, w=w)
+                     vf.reshape(vf.shape[0], n, 128), plan, f_cur=f, h=h, w=w,
+                     kv_w=geom.kv_w)
     out.copy_(o.reshape(out.shape).to(BF16))
     return out

@@ -51,7 +51,7 @@ def _worker(rank, world, port, cfg_kw, grid, fused, out_q, graphs=False):
                for _ in range(2)]
 
         def run(model):
-            ring = model.new_cache(h * w)
+            ring = model.new_cache(h * w, grid_hw=(h, w))
             a = model.forward_chunk(lat[0], 0.0, ctx, cache=ring, update_cache=True)
             b = model.forward_chunk(lat[1], 625.0, ctx, cache=ring, t_offset=f)
             torch.cuda.synchronize()
@@ -67,12 +67,15 @@ def _worker(rank, world, port, cfg_kw, grid, fused, out_q, graphs=False):
             def run(model, graphed=True):  # noqa: F811
                 stream = Pm.RefinerStream(model, ctx, graphs=graphed)
                 outs = [stream.step(x).float().cpu() for x in lat5]
+                # an anchored step: the LR frames' harvest, then the anchor's columns
+                outs.append(stream.step(lat5[0], lq_chunk=lat5[1]).float().cpu())
                 torch.cuda.synchronize()
                 model.check_status()
                 return outs
-        if fused == "spatial":   # the window-strip partition instead of TP
+        if str(fused).startswith("spatial"):   # the window-strip partition instead of TP
             S = importlib.import_module("dreamx-creator_b200.spatial")
-            tp_model = S.SpatialSRDiT.random_init(cfg, dev, seed=3)
+            halo = fused.split(":")[1] if ":" in fused else "peer"
+            tp_model = S.SpatialSRDiT.random_init(cfg, dev, seed=3, halo=halo)
         elif fused == "ce":   # peer-fused, all-gather pushed by the copy engines
             tp_model = T.TPSRDiT.random_init(cfg, dev, seed=3, comm=T.PeerComm(push="ce"))
         else:
@@ -140,16 +143,26 @@ def test_tp2_graph_replay_matches_single_gpu():
     assert min(cos) >= 0.999, cos
 
 
+_SMALL = dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16,
+              text_dim=64, text_len=16, block_hw=(2, 4), kv_len=3)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("graphs", [False, True], ids=["eager", "graphs"])
-@pytest.mark.parametrize("cfg_kw,grid", [
-    (dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, in_dim=16, out_dim=16, text_dim=64,
-          text_len=16, block_hw=(2, 4), block_radius_hw=(1, 0), kv_len=3), (3, 8, 16)),
-    (dict(num_layers=2, block_hw=(8, 8), block_radius_hw=(0, 0)), (3, 36, 64)),
-], ids=["small", "2K-2layers"])
-def test_spatial2_matches_single_gpu(cfg_kw, grid, graphs):
+@pytest.mark.parametrize("cfg_kw,grid,halo", [
+    (dict(_SMALL, block_radius_hw=(1, 0)), (3, 8, 16), "peer"),
+    (dict(num_layers=2, block_hw=(8, 8), block_radius_hw=(0, 0)), (3, 36, 64), "peer"),
+    (dict(_SMALL, block_radius_hw=(1, 1)), (3, 8, 16), "peer"),
+    (dict(_SMALL, block_radius_hw=(1, 1)), (3, 8, 16), "collective"),
+    (dict(num_layers=2, block_hw=(4, 4), block_radius_hw=(3, 3)), (3, 36, 64), "peer"),
+], ids=["small", "2K-8x8r0-2layers", "small-halo-peer", "small-halo-nccl",
+        "2K-4x4r3-2layers-halo-peer"])
+def test_spatial2_matches_single_gpu(cfg_kw, grid, halo, graphs):
     """The window-strip partition on two GPUs (each refines half of the token
     columns with the full model, one all-gather per forward; eager and in
-    captured CUDA graphs) against the single-GPU forward."""
-    cos = _run_tp(2, cfg_kw, grid, "spatial", graphs=graphs)
+    captured CUDA graphs, with an anchored step) against the single-GPU
+    forward. With radius > 0 along w the strips' K/V halo columns cross GPUs
+    every block: stored into the neighbour's ring by the ring-write kernel
+    ("peer") or sent with NCCL point-to-point calls ("nccl")."""
+    cos = _run_tp(2, cfg_kw, grid, "spatial:" + halo, graphs=graphs)
     assert min(cos) >= 0.999, cos

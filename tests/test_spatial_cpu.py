@@ -3,7 +3,9 @@ double of the kernel launchers: each rank refines half of the token columns,
 and the gathered prediction must match the one-rank forward over the whole
 grid -- chunks over a refreshed cache (RoPE at the strip's true width
 positions, the strip's own ring) and an anchored chunk (the harvest on each
-strip)."""
+strip). With windows that see neighbouring columns (radius 1 along w) the
+strips exchange their K/V halo columns every block (torch.distributed
+point-to-point over gloo: the "collective" halo)."""
 import datetime
 import importlib
 import pathlib
@@ -37,7 +39,7 @@ def _stream_outputs(P, model, torch, cfg):
     return res
 
 
-def _worker(rank, world, port, out_q):
+def _worker(rank, world, port, out_q, radius_w):
     sys.path.insert(0, str(ROOT))
     import torch
     import torch.distributed as dist
@@ -59,9 +61,9 @@ def _worker(rank, world, port, out_q):
             ops = cpu_ops
             require_cuda = False
 
-        cfg = M.SRDiTConfig(**CFG)
+        cfg = M.SRDiTConfig(**{**CFG, "block_radius_hw": (1, radius_w)})
         sd = M.SRDiT.seeded_state_dict(cfg, "cpu", 3)
-        got = _stream_outputs(P, CpuSpatial(cfg, sd, "cpu"), torch, cfg)
+        got = _stream_outputs(P, CpuSpatial(cfg, sd, "cpu", halo="collective"), torch, cfg)
         res = None
         if rank == 0:
             ref = _stream_outputs(P, CpuOne(cfg, sd, "cpu"), torch, cfg)
@@ -78,11 +80,12 @@ def _worker(rank, world, port, out_q):
         out_q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
 
 
-def test_two_strips_match_one_rank():
+@pytest.mark.parametrize("radius_w", [0, 1], ids=["radius0", "halo"])
+def test_two_strips_match_one_rank(radius_w):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, radius_w)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
@@ -101,14 +104,42 @@ def test_two_strips_match_one_rank():
     assert len(cos) == 3 and min(cos) > 0.9999, cos
 
 
-def test_radius_along_w_is_refused(monkeypatch):
-    import torch.distributed as dist
+def test_strips_narrower_than_the_halo_are_refused():
+    """The halo comes from the adjacent strips only: a strip must be at least
+    radius_w x block_w columns wide."""
     importlib.import_module("dreamx-creator_b200")
     S = importlib.import_module("dreamx-creator_b200.spatial")
     M = importlib.import_module("dreamx-creator_b200.model")
-    monkeypatch.setattr(dist, "is_initialized", lambda: True)
-    monkeypatch.setattr(dist, "get_world_size", lambda g=None: 2)
-    monkeypatch.setattr(dist, "get_rank", lambda g=None: 0)
-    cfg = M.SRDiTConfig(**{**CFG, "block_radius_hw": (1, 1)})
-    with pytest.raises(M._lib.SrditError, match="radius 0 along w"):
-        S.SpatialSRDiT(cfg, {}, "cpu")
+    m = object.__new__(S.SpatialSRDiT)
+    m.cfg = M.SRDiTConfig(**{**CFG, "block_radius_hw": (1, 3)})
+    m.world, m.rank, m.R = 2, 0, 3 * 4
+    assert m.strip(32) == (0, 16) and m._ext_of(0, 32) == (0, 28)
+    assert m._ext_of(1, 32) == (4, 32)
+    with pytest.raises(M._lib.SrditError, match="narrower than the 12-column"):
+        m.strip(16)
+
+
+def test_strip_rows_keep_each_windows_keys():
+    """A strip's rows (blockgrid.strip_rows) address, in the strip's K/V frame
+    coordinates, exactly the full plan's query and key columns of its windows."""
+    import torch
+    importlib.import_module("dreamx-creator_b200")
+    bg = importlib.import_module("dreamx-creator_b200.blockgrid")
+    for mode in (None, "chunk", "frame"):
+        spec = bg.make_spec(f_cur=3, f_kv=6, h=8, w=32, block_t=3, block_hw=(4, 4),
+                            block_radius_hw=(1, 2), streaming=True)
+        rows, stride, _ = bg.plan_rows(spec, mode)
+        qw0, qwl, kw0, kwl, kw0a, kwla, _ = bg._PAIR_COLS[stride]
+        seen = []
+        for r, (w0, w1, e0, e1) in enumerate([(0, 16, 0, 24), (16, 32, 8, 32)]):
+            sr = bg.strip_rows(rows, stride, w0, w1, e0, e1 - e0)
+            back = sr.to(torch.int64).clone()
+            back[:, qw0] += w0
+            back[:, kw0] += e0
+            back[:, kw0a] += e0
+            back[:, stride - 1] = 32
+            seen.append(back)
+        got = sorted(map(tuple, torch.cat(seen).tolist()))
+        assert got == sorted(map(tuple, rows.to(torch.int64).tolist())), mode
+    with pytest.raises(ValueError, match="outside"):
+        bg.strip_rows(rows, stride, 0, 16, 0, 16)   # no room for the halo
