@@ -71,10 +71,13 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true",
                     help="issue every kernel from Python instead of replaying the step's "
                          "CUDA graph")
-    ap.add_argument("--micro", default=None, choices=["gemm", "attn", "quant", "ln", "rope"],
-                    help="time one kernel in isolation instead of the model step")
+    ap.add_argument("--micro", default=None,
+                    choices=["gemm", "attn", "quant", "ln", "rope", "conv", "upsampler"],
+                    help="time one kernel (or the latent upsampler) in isolation instead of "
+                         "the model step")
     ap.add_argument("--shape", default=None,
-                    help="micro shape: gemm M,N,K | attn f_kv | quant/ln/rope M,K")
+                    help="micro shape: gemm M,N,K | attn f_kv | quant/ln/rope M,K | "
+                         "conv F,H,W,cin,n_src,cout | upsampler T,H,W (LR latent)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--epi", default="store", choices=["store", "gelu", "gated_res", "res"],
                     help="micro gemm: the epilogue")
@@ -147,6 +150,29 @@ def run_micro(args):
         fl = srdit.blockgrid.visible_flops(plan["params"], plan["p_stride"], 24, 128)
         res.update(geometry=args.geometry, f_kv=fkv, ms=ms, gflop=fl / 1e9,
                    tflops=fl / ms / 1e9, frac_of_bf16_burst=fl / ms / 1e9 / peaks["bf16_tflops"])
+    elif args.micro == "conv":
+        F, H, W, cin, n_src, cout = (int(v) for v in (args.shape or "33,72,128,128,2,128")
+                                     .split(","))
+        x = torch.randn(F, H, W, cin, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(cout, n_src * cin, 3, 3, device=dev, generator=g) * 0.02)
+        w = w.to(torch.bfloat16)
+        b = torch.randn(cout, device=dev, generator=g).to(torch.bfloat16)
+        w2, b2 = ops.conv_weight(w, n_src=n_src), ops.conv_bias(b)
+        out = torch.empty(F, H, W, cout, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda: ops.conv3x3(x, w2, b2, frames_per_clip=F, n_src=n_src, relu=True,
+                                        out=out))
+        # cuDNN: the reference's bf16 nn.Conv2d on NCHW frames (the cat of the
+        # block's two sources made once, outside the timing)
+        xn = x.permute(0, 3, 1, 2).contiguous()
+        if n_src == 2:
+            xn = torch.cat([xn, torch.cat([xn[:1], xn[:-1]])], 1)
+        ref = timeit(lambda: torch.relu(torch.nn.functional.conv2d(xn, w, b, padding=1)))
+        fl = 2 * F * H * W * cout * 9 * cin * n_src
+        res.update(shape=[F, H, W, cin, n_src, cout], ms=ms, tflops=fl / ms / 1e9,
+                   cudnn_ms=ref, cudnn_tflops=fl / ref / 1e9,
+                   frac_of_bf16_burst=fl / ms / 1e9 / peaks["bf16_tflops"])
+    elif args.micro == "upsampler":
+        res.update(run_upsampler_micro(args, dev, timeit, peaks))
     else:
         M, K = (int(v) for v in (args.shape or "6912,3072").split(","))
         x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
@@ -171,6 +197,62 @@ def run_micro(args):
                    frac_of_hbm=byts / ms / 1e6 / peaks["hbm_gbs"])
     res["peaks"] = kind
     print(json.dumps(res), flush=True)
+
+
+def cudnn_upsampler(sd, x, *, num_blocks, scale):
+    """The reference FlashLatentUpsampler's parallel forward (flash_latent_up.py:
+    453-495; replicate memory, no residual) as its bf16 torch ops: cuDNN convs on
+    NCHW frames, PixelShuffle, ReLU, the cat with the previous frames -- the
+    reference's own execution path, for timing beside the B200 kernels."""
+    B, C, T, H, W = x.shape
+    h = x.permute(0, 2, 1, 3, 4).reshape(B * T, C, H, W)
+    h = torch.nn.functional.conv2d(h, sd["pre_shuffle.0.weight"], sd["pre_shuffle.0.bias"],
+                                   padding=1)
+    h = torch.relu(torch.nn.functional.pixel_shuffle(h, scale))
+    for i in range(num_blocks):
+        hb = h.reshape(B, T, *h.shape[1:])
+        past = torch.cat([hb[:, :1], hb[:, :-1]], 1).reshape(h.shape)
+        p = f"blocks.{i}.conv"
+        t = torch.relu(torch.nn.functional.conv2d(torch.cat([h, past], 1), sd[p + ".0.weight"],
+                                                  sd[p + ".0.bias"], padding=1))
+        t = torch.relu(torch.nn.functional.conv2d(t, sd[p + ".2.weight"], sd[p + ".2.bias"],
+                                                  padding=1))
+        t = torch.nn.functional.conv2d(t, sd[p + ".4.weight"], sd[p + ".4.bias"], padding=1)
+        h = torch.relu(t + h)
+    h = torch.nn.functional.conv2d(h, sd["final.weight"], sd["final.bias"], padding=1)
+    return h.reshape(B, T, *h.shape[1:]).permute(0, 2, 1, 3, 4)
+
+
+def run_upsampler_micro(args, dev, timeit, peaks):
+    """The shipped latent upsampler (configs/latent_upsampler_flash.yaml: 48
+    channels, mid 128, 8 blocks, x2, replicate memory) on a 2K clip's LR latent
+    (33 frames of 36 x 64 -> 72 x 128), seeded weights: the B200 forward against
+    the reference's ops on cuDNN, same box, L2 flushed between runs."""
+    up = importlib.import_module("dreamx-creator_b200.upsampler")
+    T, H, W = (int(v) for v in (args.shape or "33,36,64").split(","))
+    kw = dict(in_channels=48, out_channels=48, mid_channels=128, num_blocks=8, upsample_scale=2)
+    sd = up.FlashLatentUpsampler.seeded_state_dict(**kw, seed=0)
+    m = up.FlashLatentUpsampler(sd, **kw, memory_init="replicate", device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(1, 48, T, H, W, device=dev, generator=g).to(torch.bfloat16)
+    ms = timeit(lambda: m(x))
+    sdd = {k: v.to(dev) for k, v in sd.items()}
+    ref = timeit(lambda: cudnn_upsampler(sdd, x, num_blocks=8, scale=2))
+    a, b = m(x).float(), cudnn_upsampler(sdd, x, num_blocks=8, scale=2).float()
+    fl = m.flops(T, H, W)
+    srdit_ops = importlib.import_module("dreamx-creator_b200.ops")
+    srdit_ops.Stats.events = []
+    m(x)
+    torch.cuda.synchronize()
+    evs, srdit_ops.Stats.events = srdit_ops.Stats.events, None
+    conv_ms = sum(e0.elapsed_time(e1) for _, e0, e1, _ in evs)
+    return {"workload": "FlashLatentUpsampler x2 (48 ch, mid 128, 8 blocks, replicate), "
+                        f"LR latent 1 x 48 x {T} x {H} x {W}", "ms": ms,
+            "latent_frames_per_s": T / ms * 1e3, "tflops": fl / ms / 1e9,
+            "conv_launches": len(evs), "conv_ms": conv_ms, "conv_tflops": fl / conv_ms / 1e9,
+            "frac_of_bf16_burst": fl / conv_ms / 1e9 / peaks["bf16_tflops"],
+            "cudnn_ms": ref, "cudnn_tflops": fl / ref / 1e9, "speedup_vs_cudnn": ref / ms,
+            "rel_fro_vs_cudnn": float((a - b).norm() / b.norm())}
 
 
 def dist_setup(n):

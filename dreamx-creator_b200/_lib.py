@@ -100,6 +100,8 @@ SIGNATURES = {
     "srdit_tp_push": [c_vp, ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, c_vp,
                       ctypes.POINTER(PeerPtrs), ctypes.c_ulonglong, ctypes.POINTER(PeerPtrs),
                       c_int, c_int, c_vp],
+    "srdit_conv3x3": [c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int,
+                      c_vp, c_float, c_int, c_int, c_vp, c_vp, c_vp],
     "srdit_wait_counters": [c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp],
     "srdit_ipc_handle": [c_vp, c_vp, ctypes.POINTER(ctypes.c_ulonglong)],
     "srdit_ipc_open": [c_vp, ctypes.POINTER(c_vp)],

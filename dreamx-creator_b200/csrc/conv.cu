@@ -1,0 +1,404 @@
+// conv.cu -- 3x3 convolution of channels-last bf16 frames on the tensor cores
+// (sm_100a), for the latent upsampler (FlashLatentUpsampler,
+// video_refiner/wan/modules/latent_upsampler/flash_latent_up.py:326-570).
+//
+//   out[f, h, w, n] = epilogue( bias[n] + sum_{s, dy, dx, c} in_s[f_s, h+dy-1, w+dx-1, c]
+//                                                          * W[n, s, dy, dx, c] )
+//
+// in_0 is the frame itself and, for the memory blocks, in_1 its previous frame
+// of the same clip (the block's torch.cat([x, past], 1), flash_latent_up.py:
+// 320 and :452-476): the first frame of a clip sees itself ("replicate") or
+// zeros. Taps outside the frame read zeros (padding=1).
+//
+// Implicit GEMM: a CTA pair computes a 256-pixel x 128-channel output tile
+// with one tcgen05.mma.cta_group::2 (kind::f16, bf16 in, fp32 accumulate in
+// TMEM) per 16 deep K step. Each CTA owns 128 pixels: a bh x bw block of one
+// frame (bh * bw = 128), whose 64-channel slices for each tap and source are
+// 4-D TMA boxes [1 frame, bh, bw, 64 channels] at the tap's offset -- the box
+// lands as 128 rows of 128 bytes in the 128-byte swizzled K-major layout the
+// MMA reads, and the tensor map's zero fill at the frame edges is the conv's
+// zero padding. The weights are a K-major [Cout, sources * 9 * Cin] matrix;
+// each CTA stages half of a stage's 128 output channels. Per CTA: warp 0 =
+// TMA producer (8-stage ring), warp 1 = MMA issuer (even CTA) / TMEM owner,
+// warps 2-5 = epilogue, which reads its 32 pixels x 128 fp32 accumulators
+// from TMEM (two accumulators, so the epilogue of one tile overlaps the MMAs
+// of the next), adds the bias, rounds to bf16, optionally adds a residual
+// (times a scale) and applies ReLU, and stores -- at the pixel-shuffled
+// position when the conv feeds a PixelShuffle(r) (output channel g * Cg + c
+// goes to channel c of sub-pixel (g / r, g % r); the host orders the weight
+// rows that way). Persistent: one pair per two SMs walks the tile list.
+#include <atomic>
+
+#include "sm100.cuh"
+#include "srdit_internal.h"
+
+#include <cuda_bf16.h>
+
+namespace srdit {
+namespace conv {
+
+constexpr int BM = 128;            // pixels per CTA (256 per pair)
+constexpr int BN = 128;            // output channels per pair tile
+constexpr int BK = 64;             // input channels (bf16) per stage: one 128-byte row
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = (BN / 2) * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int STAGES = 8;
+constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 4;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr int OFF_BIAS = STAGES * STAGE_BYTES;
+constexpr int OFF_BAR = OFF_BIAS + 2 * BN * 4;
+constexpr int SMEM = OFF_BAR + 256 + 1024;
+static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1024-byte aligned");
+static_assert(SMEM <= 232448, "shared memory budget");
+
+struct Params {
+  int F, H, W;          // frames (clips x frames per clip), frame height, width
+  int T;                // frames per clip (the previous-frame source stays inside a clip)
+  int cin_slices;       // input channels / 64 per source
+  int n_src;            // 1, or 2 with the previous frame
+  int replicate;        // a clip's first frame is its own previous frame (else zeros)
+  int cout;             // output channels stored
+  int n_tiles;          // ceil(cout / 128)
+  int bh, bw;           // pixel block of one CTA (bh * bw = 128)
+  int tiles_h, tiles_w;
+  int pix_tiles;        // F * tiles_h * tiles_w
+  int pair_tiles;       // ceil(pix_tiles / 2)
+  const float* bias;    // [cout] fp32
+  const __nv_bfloat16* res;  // optional residual [F, H, W, cout]
+  float res_scale;
+  int relu;
+  int shuffle;          // PixelShuffle factor r (1: none); cout = r * r * cg
+  int cg;
+  __nv_bfloat16* out;   // [F, H, W, cout], or [F, r H, r W, cg] with a shuffle
+  uint32_t* status;
+};
+
+SRDIT_DEV uint32_t bf2_relu(uint32_t w) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(w), "r"(0u));
+  return d;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    conv3x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = bars;                     // [STAGES], completed in the even CTA
+  uint64_t* empty = bars + STAGES;           // [STAGES], one per CTA
+  uint64_t* tfull = bars + 2 * STAGES;       // [2]
+  uint64_t* tempty = bars + 2 * STAGES + 2;  // [2], in the even CTA, 8 arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+  float* bias_s = reinterpret_cast<float*>(smem + OFF_BIAS);  // [2][BN]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int num_tiles = p.pair_tiles * p.n_tiles;
+  const int num_kb = p.n_src * 9 * p.cin_slices;
+  const int cid = static_cast<int>(cluster_id_x());
+  const int ncl = static_cast<int>(num_clusters_x());
+  const int per_frame = p.tiles_h * p.tiles_w;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);
+    }
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_2sm(tmem_slot, TMEM_COLS);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (elect_one()) {
+      const uint32_t full_even = mapa_shared(smem_u32(&full[0]), 0);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
+        const int pt = tile / p.n_tiles, nt = tile - pt * p.n_tiles;
+        const int px = 2 * pt + static_cast<int>(rank);
+        // a missing last pixel tile reads frame F (outside the tensor: zeros)
+        int f = p.F, h0 = 0, w0 = 0;
+        if (px < p.pix_tiles) {
+          f = px / per_frame;
+          const int r = px - f * per_frame;
+          h0 = (r / p.tiles_w) * p.bh;
+          w0 = (r % p.tiles_w) * p.bw;
+        }
+        const int t = f % p.T;
+        // previous frame of the clip; the clip's first frame: itself, or frame -1
+        // (outside the tensor: zeros)
+        const int f_prev = t > 0 ? f - 1 : (p.replicate ? f : -1);
+        int kb = 0;
+        for (int src = 0; src < p.n_src && ok; ++src) {
+          const int fs = src == 0 ? f : f_prev;
+          for (int tap = 0; tap < 9 && ok; ++tap) {
+            const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+            for (int cs = 0; cs < p.cin_slices; ++cs, ++kb) {
+              if (!mbar_wait(&empty[s], ph ^ 1u, p.status, abort_flag)) {
+                ok = false;
+                break;
+              }
+              if (rank == 0) mbar_arrive_expect_tx(&full[s], 2u * STAGE_BYTES);
+              uint8_t* st = smem + s * STAGE_BYTES;
+              tma_load_4d_2sm(st, &tmA, full_even + 8u * s, cs * BK, w0 + dx, h0 + dy, fs);
+              tma_load_2d_2sm(st + A_BYTES, &tmB, full_even + 8u * s, kb * BK,
+                              nt * BN + static_cast<int>(rank) * (BN / 2));
+              if (++s == STAGES) {
+                s = 0;
+                ph ^= 1u;
+              }
+            }
+          }
+        }
+      }
+      // after giving up, let the loads already issued land before the CTA exits
+      if (!ok)
+        for (int i = 0; i < 200; ++i) __nanosleep(1000);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (rank == 0 && elect_one()) {
+      const uint32_t idesc = idesc_make(1u, 1u, 0u, 0u, 2 * BM, BN);
+      const uint32_t empty_own = mapa_shared(smem_u32(&empty[0]), 0);
+      const uint32_t empty_peer = mapa_shared(smem_u32(&empty[0]), 1);
+      const uint32_t tfull_own = mapa_shared(smem_u32(&tfull[0]), 0);
+      const uint32_t tfull_peer = mapa_shared(smem_u32(&tfull[0]), 1);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = cid; tile < num_tiles && ok; tile += ncl, ++local) {
+        const int acc = local & 1;
+        const uint32_t aph = static_cast<uint32_t>(local >> 1) & 1u;
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, p.status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[s], ph, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            mma_bf16_ss_2sm(d_tmem, sdesc_sw128(a_addr + k * 32, 16, 1024),
+                            sdesc_sw128(b_addr + k * 32, 16, 1024), idesc,
+                            (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit_2sm(empty_own + 8u * s);
+          tc_commit_2sm(empty_peer + 8u * s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) {
+          tc_commit_2sm(tfull_own + 8u * acc);
+          tc_commit_2sm(tfull_peer + 8u * acc);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int sub = warp & 3;             // TMEM lane quarter of this warp
+    const int ep_tid = threadIdx.x - 64;  // 0..127
+    const uint32_t tempty_even = mapa_shared(smem_u32(&tempty[0]), 0);
+    const int r = p.shuffle;
+    const uint64_t scale2 = f2_pack(p.res_scale, p.res_scale);
+    int local = 0;
+    for (int tile = cid; tile < num_tiles; tile += ncl, ++local) {
+      const int acc = local & 1;
+      const uint32_t aph = static_cast<uint32_t>(local >> 1) & 1u;
+      const int pt = tile / p.n_tiles, nt = tile - pt * p.n_tiles;
+      const int n0 = nt * BN;
+      for (int c = ep_tid; c < BN; c += 128)
+        bias_s[acc * BN + c] = n0 + c < p.cout ? __ldg(p.bias + n0 + c) : 0.f;
+      named_barrier_sync(1, 128);
+      if (!mbar_wait(&tfull[acc], aph, p.status, abort_flag)) break;
+      tc_fence_after();
+      // this thread's pixel: row sub * 32 + lane of the CTA's bh x bw block
+      const int px = 2 * pt + static_cast<int>(rank);
+      const int row = sub * 32 + lane;
+      bool pix_ok = px < p.pix_tiles;
+      int f = 0, h = 0, w = 0;
+      if (pix_ok) {
+        f = px / per_frame;
+        const int rr = px - f * per_frame;
+        h = (rr / p.tiles_w) * p.bh + row / p.bw;
+        w = (rr % p.tiles_w) * p.bw + row % p.bw;
+        pix_ok = h < p.H && w < p.W;
+      }
+      const long long pix = (static_cast<long long>(f) * p.H + h) * p.W + w;
+      const float* bs = bias_s + acc * BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t v[32];
+        tmem_ld32(t_row + ch * 32, v);
+        tmem_ld_wait();
+        if (!pix_ok) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // 8 output channels = one 16-byte store
+          const int n = n0 + ch * 32 + q * 8;
+          if (n >= p.cout) break;
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = ch * 32 + q * 8 + 2 * e;  // column within the tile
+            const uint64_t y = f2_add(u64_of(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]),
+                                      *reinterpret_cast<const uint64_t*>(bs + j));
+            o[e] = f2_to_bf2(y);
+          }
+          if (p.res) {
+            const uint4 rv =
+                *reinterpret_cast<const uint4*>(p.res + pix * p.cout + n);
+            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint64_t yb = bf2_unpack(o[e]);
+              if (p.res_scale != 1.0f) yb = bf2_unpack(f2_to_bf2(f2_mul(yb, scale2)));
+              o[e] = f2_to_bf2(f2_add(bf2_unpack(rw[e]), yb));
+            }
+          }
+          if (p.relu) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] = bf2_relu(o[e]);
+          }
+          __nv_bfloat16* dst;
+          if (r > 1) {
+            const int g = n / p.cg, c = n - g * p.cg;
+            const int i = g / r, jj = g - i * r;
+            const long long opix =
+                (static_cast<long long>(f) * r * p.H + r * h + i) * (r * p.W) + r * w + jj;
+            dst = p.out + opix * p.cg + c;
+          } else {
+            dst = p.out + pix * p.cout + n;
+          }
+          *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_even + 8u * acc);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_2sm(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace conv
+}  // namespace srdit
+
+using namespace srdit;
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W,
+                             int cin, int n_src, int replicate, const void* weight,
+                             const float* bias, int cout, const void* residual, float res_scale,
+                             int relu, int shuffle, void* out, uint32_t* status,
+                             cudaStream_t stream) {
+  if (frames == 0) return 0;
+  if (!x || !weight || !bias || !out || frames < 0 || frames_per_clip <= 0 ||
+      frames % frames_per_clip || H <= 0 || W <= 0 || cout <= 0 || (n_src != 1 && n_src != 2) ||
+      shuffle < 1 || shuffle > 4)
+    return SRDIT_EINVAL;
+  if (cin <= 0 || cin % conv::BK) return SRDIT_EUNSUPPORTED;  // 64-channel slices
+  const int cg = cout / (shuffle * shuffle);
+  if (cg * shuffle * shuffle != cout || cg % 8 || cout % 8) return SRDIT_EUNSUPPORTED;
+  if (residual && shuffle != 1) return SRDIT_EINVAL;
+  if (!al16(x) || !al16(weight) || !al16(out) || (residual && !al16(residual)) ||
+      (reinterpret_cast<uintptr_t>(bias) & 3u))
+    return SRDIT_EALIGN;
+  // pixel block of a CTA: a whole row segment of up to 128 columns, stacked rows
+  // when the frame is narrower (bw a power of two, bh * bw = 128)
+  int bw = 128;
+  while (bw > 1 && bw / 2 >= W) bw /= 2;
+  const int bh = conv::BM / bw;
+  const int n_tiles = (cout + conv::BN - 1) / conv::BN;
+  const long long kcols = static_cast<long long>(n_src) * 9 * cin;
+
+  CUtensorMap ta, tb;
+  const long long dims[4] = {cin, W, H, frames};
+  const long long strides[3] = {static_cast<long long>(cin) * 2, static_cast<long long>(W) * cin * 2,
+                                static_cast<long long>(H) * W * cin * 2};
+  const int box[4] = {conv::BK, bw, bh, 1};
+  int rc = make_tmap_4d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, strides, box);
+  if (rc) return rc;
+  // weights [cout rows, kcols], K-major (the boxes' rows past cout read zeros)
+  rc = make_tmap_2d(&tb, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<int>(kcols),
+                    cout, kcols, conv::BK, conv::BN / 2);
+  if (rc) return rc;
+
+  conv::Params p;
+  p.F = frames;
+  p.H = H;
+  p.W = W;
+  p.T = frames_per_clip;
+  p.cin_slices = cin / conv::BK;
+  p.n_src = n_src;
+  p.replicate = replicate ? 1 : 0;
+  p.cout = cout;
+  p.n_tiles = n_tiles;
+  p.bh = bh;
+  p.bw = bw;
+  p.tiles_h = (H + bh - 1) / bh;
+  p.tiles_w = (W + bw - 1) / bw;
+  p.pix_tiles = frames * p.tiles_h * p.tiles_w;
+  p.pair_tiles = (p.pix_tiles + 1) / 2;
+  p.bias = bias;
+  p.res = static_cast<const __nv_bfloat16*>(residual);
+  p.res_scale = res_scale;
+  p.relu = relu ? 1 : 0;
+  p.shuffle = shuffle;
+  p.cg = cg;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.status = status;
+
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<bool> attr_done[kMaxDevices] = {};
+  if (dev < kMaxDevices && !attr_done[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(conv::conv3x3_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, conv::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_done[dev].store(true, std::memory_order_release);
+  }
+  const int tiles = p.pair_tiles * n_tiles;
+  const int pairs = num_sms(dev) / 2;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  conv::conv3x3_kernel<<<grid, conv::NUM_THREADS, conv::SMEM, stream>>>(ta, tb, p);
+  return static_cast<int>(cudaGetLastError());
+}

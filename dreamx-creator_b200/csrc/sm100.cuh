@@ -209,6 +209,16 @@ SRDIT_DEV void tma_load_2d_2sm(void* dst, const CUtensorMap* map, uint32_t bar_c
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
       : "memory");
 }
+// 2-SM 4-D TMA tile load into this CTA's shared memory (barrier as above).
+SRDIT_DEV void tma_load_4d_2sm(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                               int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3)
+      : "memory");
+}
 // TMA tile store from shared memory (bulk-group completion).
 SRDIT_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile(
@@ -318,6 +328,16 @@ SRDIT_DEV void mma_f8_ss_2sm(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, 
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+SRDIT_DEV void mma_bf16_ss_2sm(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

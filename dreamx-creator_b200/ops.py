@@ -285,6 +285,70 @@ def tp_allreduce(t, op, *, slots, flags, rank, world, epoch, status=None):
     return t
 
 
+def conv3x3(x, weight, bias, *, frames_per_clip, n_src=1, replicate=True, residual=None,
+            res_scale=1.0, relu=False, shuffle=1, out=None, status=None):
+    """srdit_conv3x3 of channels-last frames x [F, H, W, cin] bf16 (cin a multiple of
+    64) with ``weight`` [cout, n_src * 9 * cin] bf16 (``conv_weight`` builds it) and
+    fp32 ``bias`` [cout]; returns out [F, H, W, cout], or [F, r H, r W, cout / r^2]
+    with ``shuffle`` = r."""
+    _need_cuda(x, weight, bias, residual, out, status)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or bias.dtype != torch.float32:
+        raise _lib.SrditError("conv3x3 takes bf16 frames and weights and fp32 bias")
+    if x.dim() != 4 or not x.is_contiguous() or not weight.is_contiguous():
+        raise _lib.SrditError("conv3x3 takes contiguous [F, H, W, C] frames")
+    F, H, W, cin = x.shape
+    cout = weight.shape[0]
+    if weight.shape[1] != n_src * 9 * cin or bias.shape != (cout,):
+        raise _lib.SrditError(f"weight {tuple(weight.shape)} / bias {tuple(bias.shape)} do not "
+                              f"match {n_src} source(s) of {cin} channels")
+    r = int(shuffle)
+    shape = (F, H, W, cout) if r == 1 else (F, r * H, r * W, cout // (r * r))
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
+    elif tuple(out.shape) != shape or not out.is_contiguous() or out.dtype != torch.bfloat16:
+        raise _lib.SrditError(f"out must be a contiguous bf16 {shape}")
+    if residual is not None and (tuple(residual.shape) != (F, H, W, cout)
+                                 or not residual.is_contiguous()
+                                 or residual.dtype != torch.bfloat16):
+        raise _lib.SrditError(f"residual must be a contiguous bf16 {(F, H, W, cout)}")
+    _launch("srdit_conv3x3", _ptr(x), F, int(frames_per_clip), H, W, cin, int(n_src),
+            int(bool(replicate)), _ptr(weight), _ptr(bias), cout, _ptr(residual),
+            float(res_scale), int(bool(relu)), r, _ptr(out), _ptr(status), _stream(x.device),
+            kind="conv3x3", work=2 * F * H * W * cout * n_src * 9 * cin)
+    return out
+
+
+def conv_weight(w, *, n_src=1, cin_pad=None, shuffle=1):
+    """An nn.Conv2d weight [cout, n_src * cin, 3, 3] as srdit_conv3x3's K-major
+    [cout, n_src * 9 * cin_pad] bf16 matrix (column (s * 9 + ky * 3 + kx) * cin_pad
+    + c; channels past cin zero). With ``shuffle`` = r the rows are reordered
+    so that row g * cg + c holds output channel c * r^2 + g -- PixelShuffle(r)'s
+    channel for sub-pixel g -- as the kernel's shuffled store expects."""
+    cout, cin_all, kh, kw = w.shape
+    if (kh, kw) != (3, 3) or cin_all % n_src:
+        raise _lib.SrditError(f"not a 3x3 conv weight of {n_src} source(s): {tuple(w.shape)}")
+    cin = cin_all // n_src
+    cin_pad = cin if cin_pad is None else int(cin_pad)
+    t = w.detach().to(torch.float32).reshape(cout, n_src, cin, 3, 3).permute(0, 1, 3, 4, 2)
+    if cin_pad != cin:
+        t = torch.nn.functional.pad(t, (0, cin_pad - cin))
+    t = t.reshape(cout, n_src * 9 * cin_pad)
+    r = int(shuffle)
+    if r > 1:
+        cg = cout // (r * r)
+        t = t.reshape(cg, r * r, -1).transpose(0, 1).reshape(cout, -1)
+    return t.to(torch.bfloat16).contiguous()
+
+
+def conv_bias(b, *, shuffle=1):
+    """The conv's bias [cout] as fp32, in ``conv_weight``'s row order."""
+    t = b.detach().to(torch.float32)
+    r = int(shuffle)
+    if r > 1:
+        t = t.reshape(-1, r * r).t().reshape(-1)
+    return t.contiguous()
+
+
 def wait_counters(counters: int, mask: int, expected: int, *, status=None, device=None):
     """srdit_wait_counters: the stream waits (bounded) until the uint32 counters at
     device address ``counters`` selected by ``mask`` reach ``expected``."""

@@ -339,6 +339,33 @@ int srdit_ln_mod_quant_tp_static(const void* x, long long ldx, int M, int K, flo
                                  cudaStream_t stream);
 
 /*
+ * 3x3 convolution (stride 1, zero padding 1) of channels-last bf16 frames on
+ * the tensor cores, fp32 accumulation:
+ *   y[f, h, w, n] = bias[n] + sum_{s, ky, kx, c} in_s[f_s, h + ky - 1, w + kx - 1, c]
+ *                                                * weight[n, (s * 9 + ky * 3 + kx) * cin + c]
+ * x: [frames, H, W, cin] bf16, cin a multiple of 64 (zero-pad narrower inputs
+ * and their weight columns). Source s = 0 is the frame itself; with n_src = 2,
+ * source 1 is the previous frame of the same clip (clips of frames_per_clip
+ * frames; the first frame of a clip sees itself when `replicate`, else zeros)
+ * -- the conv of torch.cat([x, past], 1). weight: [cout, n_src * 9 * cin] bf16
+ * (K-major); bias: [cout] fp32. Epilogue per output: bf16(y); then, with a
+ * residual [frames, H, W, cout] bf16, bf16(res + bf16(y * res_scale)) (the
+ * multiply skipped when res_scale is 1); then ReLU when `relu`. shuffle = r > 1:
+ * the output feeds a PixelShuffle(r) -- channel g * cg + c (cout = r * r * cg,
+ * g = i * r + j) is stored at [f, r h + i, r w + j, c] of out [frames, r H, r W,
+ * cg] (order the weight rows so; no residual then). cout and cg multiples of 8.
+ * Replaces: the bf16 nn.Conv2d(3x3, padding=1) calls of FlashLatentUpsampler
+ *   (flash_latent_up.py:12-13, the memory block :311-325 with its
+ *   torch.cat([x, past]) :323 and the past frames of :452-476, the
+ *   PixelShuffle heads :141-180, the final projection :386) and the ReLU /
+ *   residual adds that follow them.
+ */
+int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W, int cin,
+                  int n_src, int replicate, const void* weight, const float* bias, int cout,
+                  const void* residual, float res_scale, int relu, int shuffle, void* out,
+                  uint32_t* status, cudaStream_t stream);
+
+/*
  * One-thread wait, bounded like every cross-GPU wait of the library: until
  * counters[s] >= expected for every bit s of `mask` (counters other ranks
  * release-add, e.g. srdit_rms_rope's halo signal). On timeout it records

@@ -21,6 +21,10 @@ Files:
   model.npz     two streaming chunks of a small ``WanModel`` (``_forward_inference``:
                 patch / time / text embeddings, window-attention blocks, ``Head``,
                 ``unpatchify``), the second over the first chunk's KV cache
+  upsampler.npz ``FlashLatentUpsampler`` forwards (bf16 and fp32) of two small
+                configurations: the shipped one's structure (x2, replicate
+                memory, no residual) and a x4 two-stage head with the residual
+                skip head and zero memory
 
 The only argument is the path of the reference checkout; nothing here assumes
 where it lives.
@@ -325,19 +329,72 @@ def gen_model(models):
     print("model ok")
 
 
+# (name, constructor arguments, (B, T, H, W))
+UPSAMPLER_CASES = [
+    ("x2_replicate", dict(in_channels=16, out_channels=16, mid_channels=64, num_blocks=2,
+                          upsample_scale=2, residual=False, memory_init="replicate"),
+     (2, 3, 6, 10)),
+    ("x4_residual", dict(in_channels=16, out_channels=16, mid_channels=64, num_blocks=1,
+                         upsample_scale=4, residual=True, residual_scale=0.5,
+                         memory_init="zero"),
+     (1, 2, 5, 6)),
+]
+
+
+def gen_upsampler(root: str):
+    import importlib.util
+    path = (pathlib.Path(root) / "video_refiner" / "wan" / "modules" / "latent_upsampler"
+            / "flash_latent_up.py")
+    spec = importlib.util.spec_from_file_location("flash_latent_up", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    out = {}
+    for i, (name, kw, (B, T, H, W)) in enumerate(UPSAMPLER_CASES):
+        torch.manual_seed(100 + i)
+        # PyTorch's default conv init (random weights), the final projection kept
+        m = mod.FlashLatentUpsampler(**kw, init_mode="default", zero_init_final=False).eval()
+        m = m.to(torch.bfloat16)
+        x = torch.randn(B, kw["in_channels"], T, H, W).to(torch.bfloat16)
+        with torch.no_grad():
+            y = m(x)
+            y32 = m.float()(x.float())
+        for k, v in m.state_dict().items():
+            out[f"{name}.sd.{k}"] = v.to(torch.bfloat16).view(torch.int16).numpy()
+        out[f"{name}.x"] = x.view(torch.int16).numpy()
+        out[f"{name}.y"] = y.view(torch.int16).numpy()
+        out[f"{name}.y32"] = y32.numpy()
+    np.savez_compressed(HERE / "upsampler.npz", **out)
+    print("upsampler ok")
+
+
+GENERATORS = ("plans", "quant", "norms", "rope", "winattn", "block", "model", "upsampler")
+
+
 def main():
-    if len(sys.argv) != 2:
+    if len(sys.argv) < 2 or any(a not in GENERATORS for a in sys.argv[2:]):
         raise SystemExit("usage: python tests/golden/gen_golden.py <path of the reference "
-                         "checkout> [writes the .npz files beside this script]")
-    attention, bgt, fp8, models = load_reference(sys.argv[1])
+                         "checkout> [" + " | ".join(GENERATORS) + " ...] (writes the .npz "
+                         "files beside this script; all of them by default)")
+    which = set(sys.argv[2:]) or set(GENERATORS)
     torch.set_num_threads(8)
-    gen_plans(attention, bgt)
-    gen_quant(fp8)
-    gen_norms(models)
-    gen_rope(models)
-    gen_winattn(attention, models)
-    gen_block(models)
-    gen_model(models)
+    if which - {"upsampler"}:
+        attention, bgt, fp8, models = load_reference(sys.argv[1])
+    if "plans" in which:
+        gen_plans(attention, bgt)
+    if "quant" in which:
+        gen_quant(fp8)
+    if "norms" in which:
+        gen_norms(models)
+    if "rope" in which:
+        gen_rope(models)
+    if "winattn" in which:
+        gen_winattn(attention, models)
+    if "block" in which:
+        gen_block(models)
+    if "model" in which:
+        gen_model(models)
+    if "upsampler" in which:
+        gen_upsampler(sys.argv[1])
 
 
 if __name__ == "__main__":

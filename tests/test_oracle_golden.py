@@ -165,3 +165,37 @@ def test_oracle_model_matches_reference_wanmodel(golden):
     for got, key in ((nk, "k1_layer1"), (nv, "v1_layer1")):
         ref = bf16(g[key]).reshape(got.shape)
         assert onum.cosine(got.float(), ref.float()) > 0.99999, key
+
+
+UPSAMPLER_CASES = {
+    "x2_replicate": dict(num_blocks=2, upsample_scale=2, residual=False,
+                         memory_init="replicate"),
+    "x4_residual": dict(num_blocks=1, upsample_scale=4, residual=True, residual_scale=0.5,
+                        memory_init="zero"),
+}
+
+
+def upsampler_case(g, name):
+    """(state dict, bf16 input, bf16 reference output, fp32 reference output) of a
+    golden FlashLatentUpsampler case."""
+    pre = name + ".sd."
+    sd = {k[len(pre):]: torch.from_numpy(g[k]).view(torch.bfloat16) for k in g
+          if k.startswith(pre)}
+    return (sd, torch.from_numpy(g[name + ".x"]).view(torch.bfloat16),
+            torch.from_numpy(g[name + ".y"]).view(torch.bfloat16),
+            torch.from_numpy(g[name + ".y32"]))
+
+
+@pytest.mark.parametrize("name", sorted(UPSAMPLER_CASES))
+def test_oracle_upsampler_matches_reference(golden, name):
+    """The oracle's latent upsampler against the reference FlashLatentUpsampler run
+    in bf16 (the pipeline's precision) and in fp32: bf16-rounded at the same
+    points, it sits about 10x closer to the bf16 run (only accumulation order
+    differs; ~98% of the values bit-equal) than either does to fp32."""
+    from oracle import upsampler as ou
+    sd, x, y, y32 = upsampler_case(golden("upsampler"), name)
+    out = ou.upsample(sd, x, **UPSAMPLER_CASES[name])
+    assert out.shape == y.shape
+    assert onum.rel_fro(out, y.double()) < 2e-3
+    assert onum.rel_fro(out, y32.double()) < 1e-2
+    assert float((out == y.double()).double().mean()) > 0.95
