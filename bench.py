@@ -72,12 +72,14 @@ def parse():
                     help="issue every kernel from Python instead of replaying the step's "
                          "CUDA graph")
     ap.add_argument("--micro", default=None,
-                    choices=["gemm", "attn", "quant", "ln", "rope", "conv", "upsampler"],
+                    choices=["gemm", "attn", "quant", "ln", "rope", "conv", "upsampler",
+                             "conv3d", "vae"],
                     help="time one kernel (or the latent upsampler) in isolation instead of "
                          "the model step")
     ap.add_argument("--shape", default=None,
                     help="micro shape: gemm M,N,K | attn f_kv | quant/ln/rope M,K | "
-                         "conv F,H,W,cin,n_src,cout | upsampler T,H,W (LR latent)")
+                         "conv F,H,W,cin,n_src,cout | upsampler T,H,W (LR latent) | "
+                         "conv3d F,H,W,cin,cout,kt,kh | vae T,h,w (latent)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--epi", default="store", choices=["store", "gelu", "gated_res", "res"],
                     help="micro gemm: the epilogue")
@@ -173,6 +175,26 @@ def run_micro(args):
                    frac_of_bf16_burst=fl / ms / 1e9 / peaks["bf16_tflops"])
     elif args.micro == "upsampler":
         res.update(run_upsampler_micro(args, dev, timeit, peaks))
+    elif args.micro == "conv3d":
+        F, H, W, cin, cout, kt, kh = (int(v) for v in (args.shape or "2,144,256,1024,1024,3,3")
+                                      .split(","))
+        x = torch.randn(F + kt - 1, H, W, cin, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(cout, cin, kt, kh, kh, device=dev, generator=g) * 0.01).to(torch.bfloat16)
+        b = torch.randn(cout, device=dev, generator=g)
+        w2 = ops.conv3d_weight(w)
+        out = torch.empty(F, H, W, cout, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda: ops.conv3d(x, w2, b, kt=kt, kh=kh, out=out))
+        # cuDNN: the reference's CausalConv3d on NCDHW (cache frames and the zero
+        # spatial padding concatenated / padded once, outside the timing)
+        xn = torch.nn.functional.pad(x.permute(3, 0, 1, 2)[None], (kh // 2,) * 4)
+        bb = b.to(torch.bfloat16)
+        ref = timeit(lambda: torch.nn.functional.conv3d(xn, w, bb))
+        fl = 2 * F * H * W * cout * cin * kt * kh * kh
+        res.update(shape=[F, H, W, cin, cout, kt, kh], ms=ms, tflops=fl / ms / 1e9,
+                   cudnn_ms=ref, cudnn_tflops=fl / ref / 1e9,
+                   frac_of_bf16_burst=fl / ms / 1e9 / peaks["bf16_tflops"])
+    elif args.micro == "vae":
+        res.update(run_vae_micro(args, dev, peaks))
     else:
         M, K = (int(v) for v in (args.shape or "6912,3072").split(","))
         x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
@@ -253,6 +275,51 @@ def run_upsampler_micro(args, dev, timeit, peaks):
             "frac_of_bf16_burst": fl / conv_ms / 1e9 / peaks["bf16_tflops"],
             "cudnn_ms": ref, "cudnn_tflops": fl / ref / 1e9, "speedup_vs_cudnn": ref / ms,
             "rel_fro_vs_cudnn": float((a - b).norm() / b.norm())}
+
+
+def run_vae_micro(args, dev, peaks):
+    """The Wan2.2 VAE decode (dec_dim 256, z 48) of a latent [48, T, h, w]
+    (default 2 frames of a 2K clip, 72 x 128 -> 5 frames of 1152 x 2048),
+    seeded weights: wall time per decode (CUDA events), output frames/s, the
+    algorithmic FLOP rate, and the share of the conv kernels."""
+    vae = importlib.import_module("dreamx-creator_b200.vae")
+    srdit_ops = importlib.import_module("dreamx-creator_b200.ops")
+    T, h, w = (int(v) for v in (args.shape or "2,72,128").split(","))
+    sd = vae.Wan22VAEDecoder.seeded_state_dict(seed=0)
+    d = vae.Wan22VAEDecoder(sd, device=dev)
+    g = torch.Generator(device=dev).manual_seed(2)
+    z = torch.randn(48, T, h, w, device=dev, generator=g)
+    mean, std = torch.zeros(48), torch.ones(48)
+    for _ in range(1):
+        d.decode(z, mean, std)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(max(1, args.iters)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        v = d.decode(z, mean, std)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ms = statistics.median(ts)
+    srdit_ops.Stats.events = []
+    d.decode(z, mean, std)
+    torch.cuda.synchronize()
+    evs, srdit_ops.Stats.events = srdit_ops.Stats.events, None
+    per_kind = {}
+    for kind, e0, e1, work in evs:
+        k = per_kind.setdefault(kind, [0, 0.0, 0])
+        k[0] += 1
+        k[1] += e0.elapsed_time(e1)
+        k[2] += work
+    fl = d.flops(T, h, w)
+    conv = per_kind.get("conv3d", [0, 0.0, 0])
+    return {"workload": f"Wan2.2 VAE decode (dec_dim 256, z 48), latent 48 x {T} x {h} x {w} "
+                        f"-> {tuple(v.shape)}", "ms": ms,
+            "frames_per_s": v.shape[1] / ms * 1e3, "tflops": fl / ms / 1e9,
+            "conv3d": {"launches": conv[0], "ms": conv[1], "tflops": conv[2] / conv[1] / 1e9,
+                       "frac_of_bf16_burst": conv[2] / conv[1] / 1e9 / peaks["bf16_tflops"]},
+            "kernels": {k: {"launches": n, "ms": t} for k, (n, t, _) in per_kind.items()}}
 
 
 def dist_setup(n):

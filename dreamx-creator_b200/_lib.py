@@ -69,6 +69,14 @@ class RopeHalo(ctypes.Structure):
                 ("done", c_vp)]
 
 
+class Conv3dArgs(ctypes.Structure):
+    _fields_ = [("x", c_vp), ("in_frames", c_int), ("out_frames", c_int), ("H", c_int),
+                ("W", c_int), ("cin", c_int), ("kt", c_int), ("kh", c_int), ("weight", c_vp),
+                ("bias", c_vp), ("cout", c_int), ("residual", c_vp), ("res_scale", c_float),
+                ("relu", c_int), ("shuffle", c_int), ("shuffle_t", c_int),
+                ("up2_phase", c_int), ("out", c_vp), ("status", c_vp)]
+
+
 # name -> argtypes (every function returns int)
 SIGNATURES = {
     "srdit_version": [],
@@ -102,6 +110,8 @@ SIGNATURES = {
                       c_int, c_int, c_vp],
     "srdit_conv3x3": [c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int,
                       c_vp, c_float, c_int, c_int, c_vp, c_vp, c_vp],
+    "srdit_conv3d": [ctypes.POINTER(Conv3dArgs), c_vp],
+    "srdit_rms_silu": [c_vp, c_ll, c_int, c_vp, c_int, c_vp, c_vp],
     "srdit_wait_counters": [c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp],
     "srdit_ipc_handle": [c_vp, c_vp, ctypes.POINTER(ctypes.c_ulonglong)],
     "srdit_ipc_open": [c_vp, ctypes.POINTER(c_vp)],

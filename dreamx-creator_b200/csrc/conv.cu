@@ -54,8 +54,10 @@ static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1024-byte aligned");
 static_assert(SMEM <= 232448, "shared memory budget");
 
 struct Params {
-  int F, H, W;          // frames (clips x frames per clip), frame height, width
+  int F, H, W;          // output frames, frame height, width
   int T;                // frames per clip (the previous-frame source stays inside a clip)
+  int kt, kh;           // temporal taps (output frame o reads input frames o .. o + kt - 1
+                        // when kt > 1) and the square spatial kernel (1 or 3)
   int cin_slices;       // input channels / 64 per source
   int n_src;            // 1, or 2 with the previous frame
   int replicate;        // a clip's first frame is its own previous frame (else zeros)
@@ -69,7 +71,13 @@ struct Params {
   const __nv_bfloat16* res;  // optional residual [F, H, W, cout]
   float res_scale;
   int relu;
-  int shuffle;          // PixelShuffle factor r (1: none); cout = r * r * cg
+  int shuffle;          // PixelShuffle factor r (1: none)
+  int shuffle_t;        // frame interleave (1: none): cout = shuffle_t * r * r * cg
+  // sub-pixel phase store (phase_r > 1): every output goes to pixel
+  // (phase_r h + phase_i, phase_r w + phase_j) of an out of phase_r x the size,
+  // and taps use the offsets below instead of the kh x kh grid
+  int phase_r, phase_i, phase_j;
+  signed char tap_dy[9], tap_dx[9];
   int cg;
   __nv_bfloat16* out;   // [F, H, W, cout], or [F, r H, r W, cg] with a shuffle
   uint32_t* status;
@@ -100,7 +108,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int num_tiles = p.pair_tiles * p.n_tiles;
-  const int num_kb = p.n_src * 9 * p.cin_slices;
+  const int num_kb = p.n_src * p.kt * p.kh * p.kh * p.cin_slices;
   const int cid = static_cast<int>(cluster_id_x());
   const int ncl = static_cast<int>(num_clusters_x());
   const int per_frame = p.tiles_h * p.tiles_w;
@@ -153,10 +161,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         // (outside the tensor: zeros)
         const int f_prev = t > 0 ? f - 1 : (p.replicate ? f : -1);
         int kb = 0;
+        const int ntap = p.kh * p.kh, half = p.kh / 2;
         for (int src = 0; src < p.n_src && ok; ++src) {
-          const int fs = src == 0 ? f : f_prev;
-          for (int tap = 0; tap < 9 && ok; ++tap) {
-            const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+          for (int dt = 0; dt < p.kt && ok; ++dt)
+          for (int tap = 0; tap < ntap && ok; ++tap) {
+            const int fs = p.kt > 1 ? f + dt : (src == 0 ? f : f_prev);
+            const int dy = p.phase_r > 1 ? p.tap_dy[tap] : tap / p.kh - half;
+            const int dx = p.phase_r > 1 ? p.tap_dx[tap] : tap % p.kh - half;
             for (int cs = 0; cs < p.cin_slices; ++cs, ++kb) {
               if (!mbar_wait(&empty[s], ph ^ 1u, p.status, abort_flag)) {
                 ok = false;
@@ -254,7 +265,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         w = (rr % p.tiles_w) * p.bw + row % p.bw;
         pix_ok = h < p.H && w < p.W;
       }
-      const long long pix = (static_cast<long long>(f) * p.H + h) * p.W + w;
+      // this pixel's row of the output (and of the residual, which has out's shape)
+      const int pr = p.phase_r;
+      const long long pix =
+          pr > 1 ? (static_cast<long long>(f) * pr * p.H + pr * h + p.phase_i) * (pr * p.W) +
+                       pr * w + p.phase_j
+                 : (static_cast<long long>(f) * p.H + h) * p.W + w;
       const float* bs = bias_s + acc * BN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
@@ -292,11 +308,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             for (int e = 0; e < 4; ++e) o[e] = bf2_relu(o[e]);
           }
           __nv_bfloat16* dst;
-          if (r > 1) {
+          if (r > 1 || p.shuffle_t > 1) {
+            // channel g * cg + c: frame group g / r^2, sub-pixel (i, jj) of g % r^2
             const int g = n / p.cg, c = n - g * p.cg;
-            const int i = g / r, jj = g - i * r;
-            const long long opix =
-                (static_cast<long long>(f) * r * p.H + r * h + i) * (r * p.W) + r * w + jj;
+            const int gt = g / (r * r), gs = g - gt * r * r;
+            const int i = gs / r, jj = gs - i * r;
+            const long long fo = static_cast<long long>(f) * p.shuffle_t + gt;
+            const long long opix = (fo * r * p.H + r * h + i) * (r * p.W) + r * w + jj;
             dst = p.out + opix * p.cg + c;
           } else {
             dst = p.out + pix * p.cout + n;
@@ -325,20 +343,26 @@ using namespace srdit;
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W,
-                             int cin, int n_src, int replicate, const void* weight,
-                             const float* bias, int cout, const void* residual, float res_scale,
-                             int relu, int shuffle, void* out, uint32_t* status,
-                             cudaStream_t stream) {
+// frames: output frames; in_frames: frames of x (frames, or frames + kt - 1
+// with temporal taps)
+static int conv_launch(const void* x, int frames, int in_frames, int frames_per_clip, int H,
+                       int W, int cin, int n_src, int replicate, int kt, int kh,
+                       const void* weight, const float* bias, int cout, const void* residual,
+                       float res_scale, int relu, int shuffle, int shuffle_t, int up2_phase,
+                       void* out, uint32_t* status, cudaStream_t stream) {
   if (frames == 0) return 0;
+  if (up2_phase < -1 || up2_phase > 3 ||
+      (up2_phase >= 0 && (kh != 3 || kt != 1 || shuffle != 1 || shuffle_t != 1)))
+    return SRDIT_EINVAL;
   if (!x || !weight || !bias || !out || frames < 0 || frames_per_clip <= 0 ||
       frames % frames_per_clip || H <= 0 || W <= 0 || cout <= 0 || (n_src != 1 && n_src != 2) ||
-      shuffle < 1 || shuffle > 4)
+      shuffle < 1 || shuffle > 4 || shuffle_t < 1 || shuffle_t > 2 || (kt != 1 && kt != 3) ||
+      (kh != 1 && kh != 3) || in_frames != frames + kt - 1 || (kt > 1 && n_src != 1))
     return SRDIT_EINVAL;
   if (cin <= 0 || cin % conv::BK) return SRDIT_EUNSUPPORTED;  // 64-channel slices
-  const int cg = cout / (shuffle * shuffle);
-  if (cg * shuffle * shuffle != cout || cg % 8 || cout % 8) return SRDIT_EUNSUPPORTED;
-  if (residual && shuffle != 1) return SRDIT_EINVAL;
+  const int cg = cout / (shuffle * shuffle * shuffle_t);
+  if (cg * shuffle * shuffle * shuffle_t != cout || cg % 8 || cout % 8) return SRDIT_EUNSUPPORTED;
+  if (residual && (shuffle != 1 || shuffle_t != 1)) return SRDIT_EINVAL;
   if (!al16(x) || !al16(weight) || !al16(out) || (residual && !al16(residual)) ||
       (reinterpret_cast<uintptr_t>(bias) & 3u))
     return SRDIT_EALIGN;
@@ -348,10 +372,10 @@ extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int
   while (bw > 1 && bw / 2 >= W) bw /= 2;
   const int bh = conv::BM / bw;
   const int n_tiles = (cout + conv::BN - 1) / conv::BN;
-  const long long kcols = static_cast<long long>(n_src) * 9 * cin;
+  const long long kcols = static_cast<long long>(n_src) * kt * kh * kh * cin;
 
   CUtensorMap ta, tb;
-  const long long dims[4] = {cin, W, H, frames};
+  const long long dims[4] = {cin, W, H, in_frames};
   const long long strides[3] = {static_cast<long long>(cin) * 2, static_cast<long long>(W) * cin * 2,
                                 static_cast<long long>(H) * W * cin * 2};
   const int box[4] = {conv::BK, bw, bh, 1};
@@ -367,6 +391,8 @@ extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int
   p.H = H;
   p.W = W;
   p.T = frames_per_clip;
+  p.kt = kt;
+  p.kh = kh;
   p.cin_slices = cin / conv::BK;
   p.n_src = n_src;
   p.replicate = replicate ? 1 : 0;
@@ -383,6 +409,22 @@ extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int
   p.res_scale = res_scale;
   p.relu = relu ? 1 : 0;
   p.shuffle = shuffle;
+  p.shuffle_t = shuffle_t;
+  p.phase_r = 1;
+  p.phase_i = p.phase_j = 0;
+  for (int t = 0; t < 9; ++t) p.tap_dy[t] = p.tap_dx[t] = 0;
+  if (up2_phase >= 0) {
+    // nearest 2x upsample, then this 3x3 tap (ky, kx) at output pixel (2h + i,
+    // 2w + j) reads low-res pixel (floor((2h + i + ky - 1) / 2), ...) = (h + dy, w + dx)
+    p.phase_r = 2;
+    p.phase_i = up2_phase >> 1;
+    p.phase_j = up2_phase & 1;
+    for (int t = 0; t < 9; ++t) {
+      const int a = p.phase_i + t / 3 - 1, b = p.phase_j + t % 3 - 1;
+      p.tap_dy[t] = static_cast<signed char>(a >= 0 ? a / 2 : -1);
+      p.tap_dx[t] = static_cast<signed char>(b >= 0 ? b / 2 : -1);
+    }
+  }
   p.cg = cg;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.status = status;
@@ -401,4 +443,22 @@ extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
   conv::conv3x3_kernel<<<grid, conv::NUM_THREADS, conv::SMEM, stream>>>(ta, tb, p);
   return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W,
+                             int cin, int n_src, int replicate, const void* weight,
+                             const float* bias, int cout, const void* residual, float res_scale,
+                             int relu, int shuffle, void* out, uint32_t* status,
+                             cudaStream_t stream) {
+  return conv_launch(x, frames, frames, frames_per_clip, H, W, cin, n_src, replicate, 1, 3,
+                     weight, bias, cout, residual, res_scale, relu, shuffle, 1, -1, out, status,
+                     stream);
+}
+
+extern "C" int srdit_conv3d(const srdit_conv3d_args* a, cudaStream_t stream) {
+  if (!a) return SRDIT_EINVAL;
+  return conv_launch(a->x, a->out_frames, a->in_frames, a->out_frames > 0 ? a->out_frames : 1,
+                     a->H, a->W, a->cin, 1, 0, a->kt, a->kh, a->weight, a->bias, a->cout,
+                     a->residual, a->res_scale, a->relu, a->shuffle, a->shuffle_t,
+                     a->up2_phase, a->out, a->status, stream);
 }

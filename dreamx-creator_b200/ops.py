@@ -318,6 +318,85 @@ def conv3x3(x, weight, bias, *, frames_per_clip, n_src=1, replicate=True, residu
     return out
 
 
+def conv3d(x, weight, bias, *, kt=1, kh=3, residual=None, res_scale=1.0, relu=False,
+           shuffle=1, shuffle_t=1, up2_phase=-1, out=None, status=None):
+    """srdit_conv3d: x [in_frames, H, W, cin] bf16 (the causal history of kt - 1
+    frames first), ``weight`` [cout, kt * kh * kh * cin] bf16 (``conv3d_weight``),
+    fp32 ``bias``; returns out [in_frames - kt + 1, H, W, cout] (shuffled shapes
+    as the header states; with ``up2_phase`` >= 0 the caller passes ``out`` of
+    the upsampled size, of which this launch writes one sub-pixel)."""
+    _need_cuda(x, weight, bias, residual, out, status)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or bias.dtype != torch.float32:
+        raise _lib.SrditError("conv3d takes bf16 frames and weights and fp32 bias")
+    if x.dim() != 4 or not x.is_contiguous() or not weight.is_contiguous():
+        raise _lib.SrditError("conv3d takes contiguous [F, H, W, C] frames")
+    Fi, H, W, cin = x.shape
+    Fo = Fi - kt + 1
+    cout = weight.shape[0]
+    if weight.shape[1] != kt * kh * kh * cin or bias.shape != (cout,):
+        raise _lib.SrditError(f"weight {tuple(weight.shape)} / bias {tuple(bias.shape)} do not "
+                              f"match a {kt}x{kh}x{kh} conv of {cin} channels")
+    r, st = int(shuffle), int(shuffle_t)
+    if up2_phase >= 0:
+        shape = (Fo, 2 * H, 2 * W, cout)
+        if out is None:
+            raise _lib.SrditError("an up2_phase launch writes into a given out")
+    else:
+        shape = (Fo * st, r * H, r * W, cout // (r * r * st))
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
+    elif tuple(out.shape) != shape or not out.is_contiguous() or out.dtype != torch.bfloat16:
+        raise _lib.SrditError(f"out must be a contiguous bf16 {shape}")
+    if residual is not None and (tuple(residual.shape) != tuple(out.shape)
+                                 or not residual.is_contiguous()
+                                 or residual.dtype != torch.bfloat16):
+        raise _lib.SrditError(f"residual must be a contiguous bf16 {tuple(out.shape)}")
+    a = _lib.Conv3dArgs()
+    a.x, a.in_frames, a.out_frames, a.H, a.W, a.cin = x.data_ptr(), Fi, Fo, H, W, cin
+    a.kt, a.kh, a.weight, a.bias, a.cout = kt, kh, weight.data_ptr(), bias.data_ptr(), cout
+    a.residual = residual.data_ptr() if residual is not None else None
+    a.res_scale, a.relu, a.shuffle, a.shuffle_t = float(res_scale), int(bool(relu)), r, st
+    a.up2_phase, a.out = int(up2_phase), out.data_ptr()
+    a.status = status.data_ptr() if status is not None else None
+    _launch("srdit_conv3d", ctypes.byref(a), _stream(x.device), kind="conv3d",
+            work=2 * Fo * H * W * cout * kt * kh * kh * cin)
+    return out
+
+
+def conv3d_weight(w, *, cin_pad=None):
+    """A Conv3d weight [cout, cin, kt, kh, kw] (or Conv2d [cout, cin, kh, kw]) as
+    srdit_conv3d's K-major [cout, kt * kh * kw * cin_pad] bf16 matrix (column
+    ((dt * kh + ky) * kw + kx) * cin_pad + c; channels past cin zero)."""
+    if w.dim() == 4:
+        w = w[:, :, None]
+    cout, cin, kt, kh, kw = w.shape
+    cin_pad = cin if cin_pad is None else int(cin_pad)
+    t = w.detach().to(torch.float32).permute(0, 2, 3, 4, 1)
+    if cin_pad != cin:
+        t = torch.nn.functional.pad(t, (0, cin_pad - cin))
+    return t.reshape(cout, kt * kh * kw * cin_pad).to(torch.bfloat16).contiguous()
+
+
+def rms_silu(x, gamma, *, silu=True, out=None):
+    """srdit_rms_silu over the channels of [..., C] bf16 frames (WanVAE RMS_norm, then
+    SiLU); ``out`` may be x or a same-shaped view of another buffer."""
+    _need_cuda(x, gamma, out)
+    if (x.dtype != torch.bfloat16 or gamma.dtype != torch.bfloat16 or not x.is_contiguous()
+            or not gamma.is_contiguous()):
+        raise _lib.SrditError("rms_silu takes contiguous bf16 frames and a contiguous bf16 gamma")
+    C = x.shape[-1]
+    if gamma.numel() != C:
+        raise _lib.SrditError(f"gamma of {gamma.numel()} for {C} channels")
+    if out is None:
+        out = torch.empty_like(x)
+    elif out.shape != x.shape or not out.is_contiguous() or out.dtype != torch.bfloat16:
+        raise _lib.SrditError("out must be a contiguous bf16 tensor of x's shape")
+    P = x.numel() // C
+    _launch("srdit_rms_silu", _ptr(x), P, C, _ptr(gamma), int(bool(silu)),
+            _ptr(out), _stream(x.device), kind="rms_silu", work=4 * x.numel())
+    return out
+
+
 def conv_weight(w, *, n_src=1, cin_pad=None, shuffle=1):
     """An nn.Conv2d weight [cout, n_src * cin, 3, 3] as srdit_conv3x3's K-major
     [cout, n_src * 9 * cin_pad] bf16 matrix (column (s * 9 + ky * 3 + kx) * cin_pad

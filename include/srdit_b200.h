@@ -366,6 +366,61 @@ int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W, 
                   uint32_t* status, cudaStream_t stream);
 
 /*
+ * Causal 3-D convolution (and its 2-D / 1x1 special cases) of channels-last
+ * bf16 frames, on the srdit_conv3x3 kernel:
+ *   y[o, h, w, n] = bias[n] + sum_{dt < kt, ky, kx < kh, c} x[o + dt, h + ky - kh/2,
+ *                        w + kx - kh/2, c] * weight[n, ((dt * kh + ky) * kh + kx) * cin + c]
+ * x: [in_frames = out_frames + kt - 1, H, W, cin] bf16, cin a multiple of 64:
+ * the caller lays the conv's causal history (the previous call's last kt - 1
+ * input frames, or zeros) in front of the new frames. kt in {1, 3}, kh in
+ * {1, 3} (zero padding kh / 2). Epilogue as srdit_conv3x3 (bias, bf16, an
+ * optional residual [out_frames, H, W, cout] times res_scale, ReLU); the
+ * output may be spatially pixel-shuffled (shuffle = r) and/or frame-interleaved
+ * (shuffle_t = 2): channel g * cg + c with g = gt * r^2 + i * r + j goes to
+ * out [out_frames * shuffle_t, r H, r W, cg] at frame o * shuffle_t + gt, pixel
+ * (r h + i, r w + j). cout, cg multiples of 8. up2_phase in 0..3 (else -1):
+ * the conv (kh 3, kt 1, no shuffles) of the 2x nearest-upsampled frame, for its
+ * output sub-pixel (i, j) = (up2_phase / 2, up2_phase % 2) only, computed from
+ * the low-resolution x (each tap reads the low-res pixel the upsample copied
+ * there, taps kept apart as the reference's sum has them); out and residual are
+ * [out_frames, 2H, 2W, cout] and only that sub-pixel of each 2x2 is written --
+ * four launches give the whole upsampled conv.
+ * Replaces: CausalConv3d.forward (wan/modules/vae2_2.py:17-42) with its
+ *   feature-cache concat, the upsample3d time_conv and its frame interleave
+ *   (:112-148), nn.Upsample(nearest) + Conv2d of Resample (:83-95, as a conv on
+ *   the low-resolution frame with one weight set per sub-pixel phase), and the
+ *   residual adds of ResidualBlock / Up_ResidualBlock (:214-236, :489-497).
+ */
+/*
+ * WanVAE RMS_norm (+ SiLU) per pixel of channels-last bf16 frames [pixels, C]
+ * (C a multiple of 8, at most 2048): y = x / max(||x||_2, 1e-12) * sqrt(C) *
+ * gamma[c], then silu(y) when `silu`, with the reference's bf16 rounding after
+ * the norm and after each step. out may be another tensor (e.g. frames of a
+ * conv's causal history buffer) or x itself.
+ * Replaces: RMS_norm.forward (wan/modules/vae2_2.py:45-59) and the nn.SiLU
+ *   after it in ResidualBlock and the decoder head (:199-208, :660-664).
+ */
+int srdit_rms_silu(const void* x, long long pixels, int C, const void* gamma, int silu, void* out,
+                   cudaStream_t stream);
+
+typedef struct srdit_conv3d_args {
+  const void* x;
+  int in_frames, out_frames, H, W, cin;
+  int kt, kh;
+  const void* weight;
+  const float* bias;
+  int cout;
+  const void* residual;
+  float res_scale;
+  int relu;
+  int shuffle, shuffle_t;
+  int up2_phase;
+  void* out;
+  uint32_t* status;
+} srdit_conv3d_args;
+int srdit_conv3d(const srdit_conv3d_args* args, cudaStream_t stream);
+
+/*
  * One-thread wait, bounded like every cross-GPU wait of the library: until
  * counters[s] >= expected for every bit s of `mask` (counters other ranks
  * release-add, e.g. srdit_rms_rope's halo signal). On timeout it records

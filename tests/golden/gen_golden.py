@@ -25,6 +25,8 @@ Files:
                 configurations: the shipped one's structure (x2, replicate
                 memory, no residual) and a x4 two-stage head with the residual
                 skip head and zero memory
+  vae.npz       ``WanVAE_.decode`` (the Wan2.2 decoder at a small width) of a
+                3-frame latent, bf16 and fp32
 
 The only argument is the path of the reference checkout; nothing here assumes
 where it lives.
@@ -367,7 +369,53 @@ def gen_upsampler(root: str):
     print("upsampler ok")
 
 
-GENERATORS = ("plans", "quant", "norms", "rope", "winattn", "block", "model", "upsampler")
+def gen_vae(root: str):
+    """WanVAE_.decode (the Wan2.2 decoder: dim_mult [1, 2, 4, 4], 2 residual
+    blocks, temporal upsampling [True, True, False]) at a small width (dec_dim
+    64) on a 48-channel latent of 3 frames x 4 x 6, in bf16 (the pipeline's
+    precision) and fp32. Seeded random weights (every decoder parameter, the RMS_norm
+    gammas and the attention projection included), regenerated by the tests from
+    the stored parameter names and shapes (``tests.golden_cases.vae_param``)."""
+    import importlib.util
+    path = pathlib.Path(root) / "video_refiner" / "wan" / "modules" / "vae2_2.py"
+    spec = importlib.util.spec_from_file_location("vae2_2", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    sys.path.insert(0, str(HERE.parents[1]))
+    from tests.golden_cases import vae_param
+    m = mod.WanVAE_(dim=32, dec_dim=64, z_dim=48, dim_mult=[1, 2, 4, 4], num_res_blocks=2,
+                    attn_scales=[], temperal_downsample=[False, True, True]).eval()
+    names = sorted(n for n, _ in m.named_parameters()
+                   if n.startswith("decoder.") or n.startswith("conv2."))
+    prms = dict(m.named_parameters())
+    with torch.no_grad():
+        for i, n in enumerate(names):
+            prms[n].copy_(vae_param(n, tuple(prms[n].shape), i))
+    z = torch.randn(1, 48, 3, 4, 6)
+    g = torch.Generator().manual_seed(3)
+    mean = 0.2 * torch.randn(48, generator=g)
+    std = 0.5 + torch.rand(48, generator=g)
+    out = {}
+    with torch.no_grad():
+        mb = m.to(torch.bfloat16)
+        zb = z.to(torch.bfloat16)
+        y = mb.decode(zb, [mean.to(torch.bfloat16), 1.0 / std.to(torch.bfloat16)])
+        m32 = mb.float()
+        y32 = m32.decode(zb.float(), [mean, 1.0 / std])
+    out["param_names"] = np.asarray(names)
+    shapes = [tuple(prms[n].shape) for n in names]
+    out["param_ndims"] = np.asarray([len(sh) for sh in shapes])
+    out["param_shapes"] = np.asarray([list(sh) + [0] * (5 - len(sh)) for sh in shapes])
+    out["z"] = zb[0].view(torch.int16).numpy()
+    out["mean"] = mean.numpy()
+    out["std"] = std.numpy()
+    out["y"] = y[0].view(torch.int16).numpy()
+    out["y32"] = y32[0].numpy()
+    np.savez_compressed(HERE / "vae.npz", **out)
+    print("vae ok", tuple(y.shape))
+
+
+GENERATORS = ("plans", "quant", "norms", "rope", "winattn", "block", "model", "upsampler", "vae")
 
 
 def main():
@@ -377,7 +425,7 @@ def main():
                          "files beside this script; all of them by default)")
     which = set(sys.argv[2:]) or set(GENERATORS)
     torch.set_num_threads(8)
-    if which - {"upsampler"}:
+    if which - {"upsampler", "vae"}:
         attention, bgt, fp8, models = load_reference(sys.argv[1])
     if "plans" in which:
         gen_plans(attention, bgt)
@@ -395,6 +443,8 @@ def main():
         gen_model(models)
     if "upsampler" in which:
         gen_upsampler(sys.argv[1])
+    if "vae" in which:
+        gen_vae(sys.argv[1])
 
 
 if __name__ == "__main__":

@@ -52,3 +52,35 @@ def stream_inputs():
 
 def bf16_from_bits(a):
     return torch.from_numpy(np.asarray(a)).view(torch.bfloat16)
+
+
+def vae_param(name: str, shape, index: int):
+    """The seeded value of parameter ``name`` (its ``index`` in the sorted names)
+    of the golden VAE decoder: RMS_norm gammas 1 + 0.2 N(0, 1), conv weights
+    N(0, 1) / sqrt(fan_in), biases 0.05 N(0, 1); fp32, rounded to bf16 by the
+    user. The fixture stores only the names and shapes."""
+    import torch
+    g = torch.Generator().manual_seed(1000 + index)
+    t = torch.randn(*shape, generator=g)
+    if name.endswith(".gamma"):
+        return 1 + 0.2 * t
+    if name.endswith(".bias"):
+        return 0.05 * t
+    fan_in = 1
+    for d in shape[1:]:
+        fan_in *= int(d)
+    return t / fan_in ** 0.5
+
+
+def vae_state_dict(g):
+    """The golden VAE decoder's bf16 state dict, regenerated from the fixture's
+    names and shapes."""
+    import torch
+    names = [str(n) for n in g["param_names"]]
+    shapes = g["param_shapes"]
+    ndims = g["param_ndims"]
+    sd = {}
+    for i, (n, shp, nd) in enumerate(zip(names, shapes, ndims)):
+        shape = tuple(int(v) for v in shp[:int(nd)])
+        sd[n] = vae_param(n, shape, i).to(torch.bfloat16)
+    return sd

@@ -199,3 +199,26 @@ def test_oracle_upsampler_matches_reference(golden, name):
     assert onum.rel_fro(out, y.double()) < 2e-3
     assert onum.rel_fro(out, y32.double()) < 1e-2
     assert float((out == y.double()).double().mean()) > 0.95
+
+
+def test_oracle_vae_decode_matches_reference(golden):
+    """The oracle's Wan2.2 VAE decode against the reference WanVAE_.decode:
+    unrounded, it reproduces the fp32 run to float precision (the caches, the
+    skipped first time_conv, DupUp3D, the phase of every upsample, attention and
+    unpatchify all as the reference has them); with the bf16 rounding points it
+    sits within the bf16 run's own distance from fp32 (about 1.3% at these
+    random weights: ~30 convs amplify each rounding), cosine 0.9999."""
+    from oracle import vae as ov
+    from tests.golden_cases import vae_state_dict
+    g = golden("vae")
+    sd = vae_state_dict(g)
+    z = torch.from_numpy(g["z"]).view(torch.bfloat16)
+    mean, std = torch.from_numpy(g["mean"]), torch.from_numpy(g["std"])
+    y = torch.from_numpy(g["y"]).view(torch.bfloat16).double()
+    y32 = torch.from_numpy(g["y32"]).double()
+    ye = ov.Decoder(sd, bf16=False).decode(z, mean, std)
+    assert ye.shape == y32.shape == (3, 9, 64, 96)
+    assert onum.rel_fro(ye, y32) < 1e-5
+    yb = ov.Decoder(sd).decode(z, mean, std)
+    assert onum.rel_fro(yb, y) < 2.5e-2 and onum.cosine(yb, y) > 0.9995
+    assert onum.rel_fro(y, y32) > 0.5 * onum.rel_fro(yb, y)   # the same noise level
