@@ -69,12 +69,18 @@ class RopeHalo(ctypes.Structure):
                 ("done", c_vp)]
 
 
+class DupUp(ctypes.Structure):
+    _fields_ = [("x", c_vp), ("frames", c_int), ("cin", c_int), ("ft", c_int),
+                ("repeats", c_int), ("shift", c_int)]
+
+
 class Conv3dArgs(ctypes.Structure):
     _fields_ = [("x", c_vp), ("in_frames", c_int), ("out_frames", c_int), ("H", c_int),
                 ("W", c_int), ("cin", c_int), ("kt", c_int), ("kh", c_int), ("weight", c_vp),
                 ("bias", c_vp), ("cout", c_int), ("residual", c_vp), ("res_scale", c_float),
                 ("relu", c_int), ("shuffle", c_int), ("shuffle_t", c_int),
-                ("up2_phase", c_int), ("out", c_vp), ("status", c_vp)]
+                ("up2_phase", c_int), ("dup", ctypes.POINTER(DupUp)), ("out", c_vp),
+                ("status", c_vp)]
 
 
 # name -> argtypes (every function returns int)

@@ -78,6 +78,13 @@ struct Params {
   // and taps use the offsets below instead of the kh x kh grid
   int phase_r, phase_i, phase_j;
   signed char tap_dy[9], tap_dx[9];
+  // phase store only: a DupUp3D residual gathered from the block input dup
+  // [frames, H, W, dup_cin] (the resample's low-resolution grid): output frame
+  // fo is repeated frame (fo + dup_shift) = t * dup_ft + a, and channel n of
+  // sub-pixel (i, j) reads input channel (n * dup_ft * 4 + a * 4 + i * 2 + j)
+  // / dup_repeats of frame t, pixel (h, w)
+  const __nv_bfloat16* dup;
+  int dup_cin, dup_ft, dup_repeats, dup_shift;
   int cg;
   __nv_bfloat16* out;   // [F, H, W, cout], or [F, r H, r W, cg] with a shuffle
   uint32_t* status;
@@ -292,10 +299,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                       *reinterpret_cast<const uint64_t*>(bs + j));
             o[e] = f2_to_bf2(y);
           }
-          if (p.res) {
-            const uint4 rv =
-                *reinterpret_cast<const uint4*>(p.res + pix * p.cout + n);
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+          if (p.res || p.dup) {
+            uint32_t rw[4];
+            if (p.res) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(p.res + pix * p.cout + n);
+              rw[0] = rv.x;
+              rw[1] = rv.y;
+              rw[2] = rv.z;
+              rw[3] = rv.w;
+            } else {
+              const int fr = f + p.dup_shift, t = fr / p.dup_ft, a = fr - t * p.dup_ft;
+              const __nv_bfloat16* src =
+                  p.dup + ((static_cast<long long>(t) * p.H + h) * p.W + w) * p.dup_cin;
+              const int off = a * 4 + p.phase_i * 2 + p.phase_j, F = p.dup_ft * 4;
+              if (F == p.dup_repeats) {
+                // channel n + off / F = n: the 8 channels are contiguous
+                const uint4 rv = __ldg(reinterpret_cast<const uint4*>(src + n));
+                rw[0] = rv.x;
+                rw[1] = rv.y;
+                rw[2] = rv.z;
+                rw[3] = rv.w;
+              } else if (F == 2 * p.dup_repeats) {
+                // channels 2 (n + e) + off / repeats: every other one of 16
+                const int sel = off / p.dup_repeats;
+                const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(src + 2 * n));
+                const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(src + 2 * n + 8));
+                const uint32_t wv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  rw[e] = sel ? __byte_perm(wv[2 * e], wv[2 * e + 1], 0x7632)
+                              : __byte_perm(wv[2 * e], wv[2 * e + 1], 0x5410);
+              } else {
+                uint16_t v16[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  v16[e] = __ldg(reinterpret_cast<const unsigned short*>(src) +
+                                 ((n + e) * F + off) / p.dup_repeats);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  rw[e] = static_cast<uint32_t>(v16[2 * e]) |
+                          (static_cast<uint32_t>(v16[2 * e + 1]) << 16);
+              }
+            }
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               uint64_t yb = bf2_unpack(o[e]);
@@ -349,7 +394,8 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
                        int W, int cin, int n_src, int replicate, int kt, int kh,
                        const void* weight, const float* bias, int cout, const void* residual,
                        float res_scale, int relu, int shuffle, int shuffle_t, int up2_phase,
-                       void* out, uint32_t* status, cudaStream_t stream) {
+                       const srdit_dup_up* dup, void* out, uint32_t* status,
+                       cudaStream_t stream) {
   if (frames == 0) return 0;
   if (up2_phase < -1 || up2_phase > 3 ||
       (up2_phase >= 0 && (kh != 3 || kt != 1 || shuffle != 1 || shuffle_t != 1)))
@@ -363,6 +409,16 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
   const int cg = cout / (shuffle * shuffle * shuffle_t);
   if (cg * shuffle * shuffle * shuffle_t != cout || cg % 8 || cout % 8) return SRDIT_EUNSUPPORTED;
   if (residual && (shuffle != 1 || shuffle_t != 1)) return SRDIT_EINVAL;
+  if (dup) {
+    // a DupUp3D residual: only for a phase launch, instead of `residual`; the
+    // gathered channel index stays inside the input's channels
+    if (up2_phase < 0 || residual || !dup->x || (dup->ft != 1 && dup->ft != 2) ||
+        dup->cin <= 0 || dup->repeats <= 0 || dup->shift < 0 || dup->shift >= dup->ft ||
+        static_cast<long long>(cout) * dup->ft * 4 != static_cast<long long>(dup->repeats) * dup->cin ||
+        (frames - 1 + dup->shift) / dup->ft >= dup->frames)
+      return SRDIT_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(dup->x) & 15u) || dup->cin % 8) return SRDIT_EALIGN;
+  }
   if (!al16(x) || !al16(weight) || !al16(out) || (residual && !al16(residual)) ||
       (reinterpret_cast<uintptr_t>(bias) & 3u))
     return SRDIT_EALIGN;
@@ -412,6 +468,11 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
   p.shuffle_t = shuffle_t;
   p.phase_r = 1;
   p.phase_i = p.phase_j = 0;
+  p.dup = dup ? static_cast<const __nv_bfloat16*>(dup->x) : nullptr;
+  p.dup_cin = dup ? dup->cin : 0;
+  p.dup_ft = dup ? dup->ft : 1;
+  p.dup_repeats = dup ? dup->repeats : 1;
+  p.dup_shift = dup ? dup->shift : 0;
   for (int t = 0; t < 9; ++t) p.tap_dy[t] = p.tap_dx[t] = 0;
   if (up2_phase >= 0) {
     // nearest 2x upsample, then this 3x3 tap (ky, kx) at output pixel (2h + i,
@@ -451,8 +512,8 @@ extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int
                              int relu, int shuffle, void* out, uint32_t* status,
                              cudaStream_t stream) {
   return conv_launch(x, frames, frames, frames_per_clip, H, W, cin, n_src, replicate, 1, 3,
-                     weight, bias, cout, residual, res_scale, relu, shuffle, 1, -1, out, status,
-                     stream);
+                     weight, bias, cout, residual, res_scale, relu, shuffle, 1, -1, nullptr, out,
+                     status, stream);
 }
 
 extern "C" int srdit_conv3d(const srdit_conv3d_args* a, cudaStream_t stream) {
@@ -460,5 +521,5 @@ extern "C" int srdit_conv3d(const srdit_conv3d_args* a, cudaStream_t stream) {
   return conv_launch(a->x, a->out_frames, a->in_frames, a->out_frames > 0 ? a->out_frames : 1,
                      a->H, a->W, a->cin, 1, 0, a->kt, a->kh, a->weight, a->bias, a->cout,
                      a->residual, a->res_scale, a->relu, a->shuffle, a->shuffle_t,
-                     a->up2_phase, a->out, a->status, stream);
+                     a->up2_phase, a->dup, a->out, a->status, stream);
 }

@@ -965,67 +965,81 @@ int ln_cs_launch(int mode, const __nv_bfloat16* x, long long ldx, int M, int K, 
 }
 
 // ---------------------------------------------------------------- rms_silu
-// One warp per pixel of channels-last frames [P, C] (C a multiple of 8, at most
+// Warps over pixels of channels-last frames [P, C] (C a multiple of 8, at most
 // 32 * 8 * NCH): WanVAE's RMS_norm -- F.normalize over the channels times
-// sqrt(C) times gamma -- then SiLU, rounded to bf16 at each step as the
-// reference's bf16 tensor ops are: n = bf16(sqrt(sum x^2)) (fp32 sum),
+// sqrt(C) times gamma -- then SiLU, rounded to bf16 after each step as the
+// reference's bf16 tensor ops are: n = bf16(sqrt(sum x^2)) (fp32 sum), then
 // bf16(x / max(n, eps)), bf16(. * sqrt(C)), bf16(. * gamma), bf16(silu(.)).
-template <int NCH>
+// The quotients are taken as products with the correctly rounded reciprocal
+// (within one fp32 ulp of the quotient, so the bf16 results differ only when a
+// quotient lies within that ulp of a bf16 rounding boundary). Each warp does
+// PPW pixels, all of their loads issued before any arithmetic.
+template <int NCH, int PPW>
 __global__ void __launch_bounds__(128) rms_silu_kernel(const __nv_bfloat16* __restrict__ x,
                                                        long long P, int C,
                                                        const __nv_bfloat16* __restrict__ gamma,
                                                        float scale, int silu,
                                                        __nv_bfloat16* __restrict__ out) {
-  const long long pix = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const long long pix0 = (static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5)) * PPW;
   const int lane = threadIdx.x & 31;
-  if (pix >= P) return;
+  if (pix0 >= P) return;
   const int nch = C / 8;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + pix * C);
-  uint4 v[NCH];
-  float ss = 0.f;
+  uint4 v[PPW][NCH];
 #pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    const int ch = lane + 32 * i;
-    v[i] = ch < nch ? ld_stream(xr + ch) : make_uint4(0u, 0u, 0u, 0u);
-    ss = bflo_sqadd(v[i].x, ss);
-    ss = bfhi_sqadd(v[i].x, ss);
-    ss = bflo_sqadd(v[i].y, ss);
-    ss = bfhi_sqadd(v[i].y, ss);
-    ss = bflo_sqadd(v[i].z, ss);
-    ss = bfhi_sqadd(v[i].z, ss);
-    ss = bflo_sqadd(v[i].w, ss);
-    ss = bfhi_sqadd(v[i].w, ss);
-  }
-  ss = warp_sum(ss);
-  // the norm rounded to bf16, then clamped at bf16(1e-12) (F.normalize's eps)
-  const float nrm = fmaxf(__bfloat162float(__float2bfloat16_rn(__fsqrt_rn(ss))),
-                          __bfloat162float(__float2bfloat16_rn(1e-12f)));
-  uint4* orow = reinterpret_cast<uint4*>(out + pix * C);
+  for (int q = 0; q < PPW; ++q) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (pix0 + q) * C);
 #pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    const int ch = lane + 32 * i;
-    if (ch >= nch) break;
-    const uint4 gv = ldg_inorder(reinterpret_cast<const uint4*>(gamma) + ch);
-    const uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 xf = f2_split(bf2_unpack(xw[e]));
-      const float2 gf = f2_split(bf2_unpack(gw[e]));
-      float y0 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(xf.x, nrm)));
-      float y1 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(xf.y, nrm)));
-      y0 = __bfloat162float(__float2bfloat16_rn(y0 * scale));
-      y1 = __bfloat162float(__float2bfloat16_rn(y1 * scale));
-      y0 = __bfloat162float(__float2bfloat16_rn(y0 * gf.x));
-      y1 = __bfloat162float(__float2bfloat16_rn(y1 * gf.y));
-      if (silu) {
-        y0 = __fdiv_rn(y0, 1.0f + expf(-y0));
-        y1 = __fdiv_rn(y1, 1.0f + expf(-y1));
-      }
-      o[e] = f2_to_bf2(f2_pack(y0, y1));
+    for (int i = 0; i < NCH; ++i) {
+      const int ch = lane + 32 * i;
+      v[q][i] = (ch < nch && pix0 + q < P) ? ld_stream(xr + ch) : make_uint4(0u, 0u, 0u, 0u);
     }
-    orow[ch] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  const float eps = __bfloat162float(__float2bfloat16_rn(1e-12f));
+  const uint64_t s2 = f2_pack(scale, scale);
+#pragma unroll
+  for (int q = 0; q < PPW; ++q) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      ss = bflo_sqadd(v[q][i].x, ss);
+      ss = bfhi_sqadd(v[q][i].x, ss);
+      ss = bflo_sqadd(v[q][i].y, ss);
+      ss = bfhi_sqadd(v[q][i].y, ss);
+      ss = bflo_sqadd(v[q][i].z, ss);
+      ss = bfhi_sqadd(v[q][i].z, ss);
+      ss = bflo_sqadd(v[q][i].w, ss);
+      ss = bfhi_sqadd(v[q][i].w, ss);
+    }
+    ss = warp_sum(ss);
+    if (pix0 + q >= P) break;
+    // the norm rounded to bf16, clamped at bf16(1e-12) (F.normalize's eps)
+    const float nrm = fmaxf(__bfloat162float(__float2bfloat16_rn(__fsqrt_rn(ss))), eps);
+    const float rn = __frcp_rn(nrm);
+    const uint64_t rn2 = f2_pack(rn, rn);
+    uint4* orow = reinterpret_cast<uint4*>(out + (pix0 + q) * C);
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const int ch = lane + 32 * i;
+      if (ch >= nch) break;
+      const uint4 gv = ldg_inorder(reinterpret_cast<const uint4*>(gamma) + ch);
+      const uint32_t xw[4] = {v[q][i].x, v[q][i].y, v[q][i].z, v[q][i].w};
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint32_t y = f2_to_bf2(f2_mul(bf2_unpack(xw[e]), rn2));
+        y = f2_to_bf2(f2_mul(bf2_unpack(y), s2));
+        y = bf2_mul(y, gw[e]);  // bf16(y * gamma), one rounding
+        if (silu) {
+          const float2 yf = f2_split(bf2_unpack(y));
+          const float d0 = 1.0f + exp2f(yf.x * -1.4426950408889634f);
+          const float d1 = 1.0f + exp2f(yf.y * -1.4426950408889634f);
+          y = f2_to_bf2(f2_pack(yf.x * __frcp_rn(d0), yf.y * __frcp_rn(d1)));
+        }
+        o[e] = y;
+      }
+      orow[ch] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
@@ -1260,22 +1274,24 @@ extern "C" int srdit_rms_silu(const void* x, long long pixels, int C, const void
   if (!x || !gamma || !out || pixels < 0 || C <= 0) return SRDIT_EINVAL;
   if (C % 8 || C > 2048) return SRDIT_EUNSUPPORTED;
   if (!aligned16(x) || !aligned16(gamma) || !aligned16(out)) return SRDIT_EALIGN;
-  const long long blocks = (pixels + 3) / 4;
-  if (blocks > 0x7fffffffLL) return SRDIT_EUNSUPPORTED;
   const float scale = static_cast<float>(sqrt(static_cast<double>(C)));
   const int nch = (C / 8 + 31) / 32;
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   const auto* gb = static_cast<const __nv_bfloat16*>(gamma);
   auto* ob = static_cast<__nv_bfloat16*>(out);
+  // pixels per warp: four 16-byte loads in flight per lane
+  const int ppw = nch <= 1 ? 4 : (nch <= 2 ? 2 : 1);
+  const long long blocks = (pixels + 4LL * ppw - 1) / (4LL * ppw);
+  if (blocks > 0x7fffffffLL) return SRDIT_EUNSUPPORTED;
   const int g = static_cast<int>(blocks);
   if (nch <= 1)
-    ew::rms_silu_kernel<1><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    ew::rms_silu_kernel<1, 4><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
   else if (nch <= 2)
-    ew::rms_silu_kernel<2><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    ew::rms_silu_kernel<2, 2><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
   else if (nch <= 4)
-    ew::rms_silu_kernel<4><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    ew::rms_silu_kernel<4, 1><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
   else
-    ew::rms_silu_kernel<8><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    ew::rms_silu_kernel<8, 1><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
   return static_cast<int>(cudaGetLastError());
 }
 

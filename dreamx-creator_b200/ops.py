@@ -319,12 +319,14 @@ def conv3x3(x, weight, bias, *, frames_per_clip, n_src=1, replicate=True, residu
 
 
 def conv3d(x, weight, bias, *, kt=1, kh=3, residual=None, res_scale=1.0, relu=False,
-           shuffle=1, shuffle_t=1, up2_phase=-1, out=None, status=None):
+           shuffle=1, shuffle_t=1, up2_phase=-1, dup=None, out=None, status=None):
     """srdit_conv3d: x [in_frames, H, W, cin] bf16 (the causal history of kt - 1
     frames first), ``weight`` [cout, kt * kh * kh * cin] bf16 (``conv3d_weight``),
     fp32 ``bias``; returns out [in_frames - kt + 1, H, W, cout] (shuffled shapes
     as the header states; with ``up2_phase`` >= 0 the caller passes ``out`` of
-    the upsampled size, of which this launch writes one sub-pixel)."""
+    the upsampled size, of which this launch writes one sub-pixel). ``dup`` =
+    (block input [frames, H, W, cin], ft, shift): a phase launch's DupUp3D
+    residual, gathered in the epilogue."""
     _need_cuda(x, weight, bias, residual, out, status)
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or bias.dtype != torch.float32:
         raise _lib.SrditError("conv3d takes bf16 frames and weights and fp32 bias")
@@ -357,6 +359,17 @@ def conv3d(x, weight, bias, *, kt=1, kh=3, residual=None, res_scale=1.0, relu=Fa
     a.residual = residual.data_ptr() if residual is not None else None
     a.res_scale, a.relu, a.shuffle, a.shuffle_t = float(res_scale), int(bool(relu)), r, st
     a.up2_phase, a.out = int(up2_phase), out.data_ptr()
+    if dup is not None:
+        xd, ft, shift = dup
+        _need_cuda(xd)
+        if (xd.dim() != 4 or tuple(xd.shape[1:3]) != (H, W) or not xd.is_contiguous()
+                or xd.dtype != torch.bfloat16):
+            raise _lib.SrditError(f"the DupUp3D source must be contiguous bf16 [frames, {H}, "
+                                  f"{W}, cin], got {tuple(xd.shape)}")
+        reps = cout * 4 * ft // xd.shape[3]
+        du = _lib.DupUp(ctypes.c_void_p(xd.data_ptr()), xd.shape[0], xd.shape[3], int(ft),
+                        int(reps), int(shift))
+        a.dup = ctypes.pointer(du)
     a.status = status.data_ptr() if status is not None else None
     _launch("srdit_conv3d", ctypes.byref(a), _stream(x.device), kind="conv3d",
             work=2 * Fo * H * W * cout * kt * kh * kh * cin)

@@ -24,8 +24,10 @@ structure and its cache semantics, on channels-last frames [T, H, W, C]:
   * AttentionBlock (:238-278): RMS_norm, the 1x1 qkv / proj convs on the conv
     kernel, single-head attention over a frame's pixels by torch's
     scaled_dot_product_attention (a library kernel, as in the reference);
-  * DupUp3D (:370-413), unpatchify (:299-313) and the latent un-normalisation
-    are index plumbing in torch.
+  * DupUp3D (:370-413) is gathered from the block input by the resample's
+    phase launches (``srdit_dup_up``) and added there;
+  * unpatchify (:299-313) and the latent un-normalisation are index plumbing
+    in torch.
 
 Channel counts must be multiples of 64 except the latent (48, zero-padded) and
 the 12 output channels.
@@ -77,7 +79,9 @@ class _Conv:
     def run_history(self, hist, T, **kw):
         """The conv over hist [2 + T, ...] (kt = 3), then the cache update."""
         y = ops.conv3d(hist, self.w, self.b, kt=3, kh=self.kh, **kw)
-        hist[:2].copy_(hist[T:T + 2].clone())
+        # frames T, T + 1 to the front, in order (they overlap frames 0, 1 when T = 1)
+        hist[0].copy_(hist[T])
+        hist[1].copy_(hist[T + 1])
         self.calls += 1
         return y
 
@@ -133,14 +137,14 @@ class _Attention:
 
 class _Resample:
     """Resample "upsample2d" / "upsample3d" (vae2_2.py:71-148) up to the final
-    2x nearest + Conv2d, whose launches take the block's shortcut residual."""
+    2x nearest + Conv2d, whose launches add the block's DupUp3D shortcut."""
 
     def __init__(self, sd, prefix, mode, device):
         self.mode = mode
         self.conv = _Conv(sd, prefix + ".resample.1", device)
         self.time = _Conv(sd, prefix + ".time_conv", device) if mode == "upsample3d" else None
 
-    def __call__(self, x, residual):
+    def __call__(self, x, dup):
         T, H, W, C = x.shape
         if self.time is not None:
             if self.time.calls == 0:
@@ -154,7 +158,7 @@ class _Resample:
                 T = x.shape[0]
         out = torch.empty(T, 2 * H, 2 * W, self.conv.cout, dtype=torch.bfloat16, device=x.device)
         for ph in range(4):
-            self.conv(x, up2_phase=ph, out=out, residual=residual)
+            self.conv(x, up2_phase=ph, out=out, dup=dup)
         return out
 
 
@@ -194,9 +198,9 @@ class _UpBlock:
             y = rb(y)
         if self.resample is None:
             return y
-        cout, ft, fs = self.dup
-        shortcut = _dup_up(x, cout, ft, fs, first_chunk)
-        return self.resample(y, residual=shortcut)
+        _, ft, _ = self.dup
+        # the DupUp3D shortcut of x, added by the resample's phase launches
+        return self.resample(y, dup=(x, ft, ft - 1 if first_chunk else 0))
 
 
 class Wan22VAEDecoder:

@@ -403,6 +403,18 @@ int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W, 
 int srdit_rms_silu(const void* x, long long pixels, int C, const void* gamma, int silu, void* out,
                    cudaStream_t stream);
 
+/* DupUp3D shortcut of an Up_ResidualBlock (vae2_2.py:370-413), gathered by a
+ * phase launch's epilogue instead of a materialised residual: x is the block's
+ * input [frames, H, W, cin] on the launch's low-resolution grid; output frame
+ * fo of the launch is repeated frame fo + shift = t * ft + a (shift = ft - 1 on
+ * a clip's first call, which drops those frames), and output channel n of
+ * sub-pixel (i, j) adds input channel (n * 4 ft + 4 a + 2 i + j) / repeats of
+ * frame t at the same low-resolution pixel (repeats = cout * 4 ft / cin). */
+typedef struct srdit_dup_up {
+  const void* x;
+  int frames, cin, ft, repeats, shift;
+} srdit_dup_up;
+
 typedef struct srdit_conv3d_args {
   const void* x;
   int in_frames, out_frames, H, W, cin;
@@ -415,6 +427,7 @@ typedef struct srdit_conv3d_args {
   int relu;
   int shuffle, shuffle_t;
   int up2_phase;
+  const srdit_dup_up* dup;  /* optional, phase launches only, instead of residual */
   void* out;
   uint32_t* status;
 } srdit_conv3d_args;

@@ -115,3 +115,26 @@ def test_decode_matches_the_reference(pkg, cuda_device, golden):
     outc = d.decode(z.to(cuda_device), mean, std).cpu()
     assert outc.min() >= -1 and outc.max() <= 1
     assert torch.equal(outc, out.float().clamp(-1, 1))
+
+
+@pytest.mark.parametrize("cin,cout,ft,shift", [(128, 128, 2, 0), (128, 128, 2, 1),
+                                               (256, 128, 1, 0)])
+def test_dup_up_gathered_in_the_epilogue(pkg, cuda_device, cin, cout, ft, shift):
+    """The phase launches' DupUp3D residual, gathered from the block input in the
+    epilogue, equals the materialised DupUp3D tensor added as a residual."""
+    ops, vae = pkg
+    g = torch.Generator().manual_seed(cin + 10 * ft + shift)
+    Tb, H, W = 2, 3, 5
+    Tc = Tb * ft - shift
+    xb = _rand((Tb, H, W, cin), g).to(cuda_device)
+    xc = _rand((Tc, H, W, cout), g).to(cuda_device)
+    w2 = ops.conv3d_weight(_rand((cout, cout, 3, 3), g, (1.0 / (9 * cout)) ** 0.5)).to(cuda_device)
+    b = (torch.randn(cout, generator=g) * 0.1).float().to(cuda_device)
+    fused = torch.empty(Tc, 2 * H, 2 * W, cout, dtype=torch.bfloat16, device=cuda_device)
+    mat = torch.empty_like(fused)
+    res = vae._dup_up(xb, cout, ft, 2, shift > 0)
+    for ph in range(4):
+        ops.conv3d(xc, w2, b, kt=1, kh=3, up2_phase=ph, out=fused, dup=(xb, ft, shift))
+        ops.conv3d(xc, w2, b, kt=1, kh=3, up2_phase=ph, out=mat, residual=res)
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(fused, mat)
