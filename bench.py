@@ -61,7 +61,12 @@ def parse():
                     help="N > 1: tensor parallelism over one clip (strong scaling, the "
                          "reference's DTensor-style TP), the spatial partition of one clip "
                          "(each GPU refines a strip of token columns with the full model; "
-                         "radius-0 windows), or one clip per GPU (weak scaling)")
+                         "a K/V halo for windows of radius > 0), or one clip per GPU (weak "
+                         "scaling)")
+    ap.add_argument("--halo", default="peer", choices=["peer", "collective"],
+                    help="--parallel spatial with windows of radius > 0 along w: the K/V "
+                         "halo columns stored into the neighbours' rings by the ring-write "
+                         "kernel over NVLink, or sent with NCCL point-to-point calls")
     ap.add_argument("--anchor", default="none", choices=["none", "serial", "overlap"],
                     help="LQ-anchor steps (the shipped default denoise): every step also "
                          "harvests an anchor from a 3-frame LR chunk and denoises frame-"
@@ -314,12 +319,22 @@ def run_vae_micro(args, dev, peaks):
         k[2] += work
     fl = d.flops(T, h, w)
     conv = per_kind.get("conv3d", [0, 0.0, 0])
+    # the conv launches grouped by their work (one group per layer shape)
+    shapes = {}
+    for kind, e0, e1, work in evs:
+        if kind == "conv3d":
+            k = shapes.setdefault(work, [0, 0.0])
+            k[0] += 1
+            k[1] += e0.elapsed_time(e1)
+    by_shape = sorted(((t, n, wk) for wk, (n, t) in shapes.items()), reverse=True)[:12]
     return {"workload": f"Wan2.2 VAE decode (dec_dim 256, z 48), latent 48 x {T} x {h} x {w} "
                         f"-> {tuple(v.shape)}", "ms": ms,
             "frames_per_s": v.shape[1] / ms * 1e3, "tflops": fl / ms / 1e9,
             "conv3d": {"launches": conv[0], "ms": conv[1], "tflops": conv[2] / conv[1] / 1e9,
                        "frac_of_bf16_burst": conv[2] / conv[1] / 1e9 / peaks["bf16_tflops"]},
-            "kernels": {k: {"launches": n, "ms": t} for k, (n, t, _) in per_kind.items()}}
+            "kernels": {k: {"launches": n, "ms": t} for k, (n, t, _) in per_kind.items()},
+            "conv3d_by_work": [{"gflop": wk / 1e9, "launches": n, "ms": t,
+                                "tflops": wk * n / t / 1e9} for t, n, wk in by_shape]}
 
 
 def dist_setup(n):
@@ -423,7 +438,8 @@ def workload_config(args):
             "parallelism": ({"tp": f"tp{args.gpus} (sequence-parallel residual stream, "
                                    f"{args.tp_comm} collectives)",
                              "spatial": f"spatial{args.gpus} (w-strips of whole windows, "
-                                        f"full model per GPU, one all-gather per forward)",
+                                        f"full model per GPU, one all-gather per forward"
+                                        f"{'; K/V halo by ' + args.halo if args.geometry != '8x8r0' else ''})",
                              "replicas": "replicas"}[args.parallel]) if args.gpus > 1
             else "single",
             "l2": "inputs larger than L2 (5 GB of fp8 weights stream every forward)",
@@ -503,7 +519,7 @@ def run_gpu_arm(args, rank, world, local):
         model = tp_mod.TPSRDiT.random_init(cfg, dev, seed=0, fused=args.tp_comm == "fused")
     elif world > 1 and args.parallel == "spatial":
         sp_mod = import_module("dreamx-creator_b200.spatial")
-        model = sp_mod.SpatialSRDiT.random_init(cfg, dev, seed=0)
+        model = sp_mod.SpatialSRDiT.random_init(cfg, dev, seed=0, halo=args.halo)
     else:
         model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
     # tensor parallelism refines one clip on all ranks; replicas one clip each
@@ -676,7 +692,7 @@ def run_clip(args, rank, world, local):
         model = tp_mod.TPSRDiT.random_init(cfg, dev, seed=0, fused=args.tp_comm == "fused")
     elif world > 1 and args.parallel == "spatial":
         sp_mod = import_module("dreamx-creator_b200.spatial")
-        model = sp_mod.SpatialSRDiT.random_init(cfg, dev, seed=0)
+        model = sp_mod.SpatialSRDiT.random_init(cfg, dev, seed=0, halo=args.halo)
     else:
         model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
     n_chunks, f = 11, 3

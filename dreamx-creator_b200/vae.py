@@ -36,7 +36,15 @@ from __future__ import annotations
 
 import torch
 
-from . import _lib, ops
+from . import _lib
+from . import ops as _ops
+
+# The kernel launchers the decoder calls (the libsrdit_b200.so wrappers). A test
+# may point this at a table of its own to run the host-side orchestration
+# without a GPU; the module has no other compute path.
+ops = _ops
+# single-head attention of the middle block (a library kernel, as in the reference)
+attend = torch.nn.functional.scaled_dot_product_attention
 
 
 def _pad64(c):
@@ -131,7 +139,7 @@ class _Attention:
         n = ops.rms_silu(x, self.g, silu=False)
         qkv = self.qkv(n).view(T, 1, H * W, 3 * C)
         q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
-        o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+        o = attend(q, k, v)
         return self.proj(o.reshape(T, H, W, C).contiguous(), residual=x)
 
 

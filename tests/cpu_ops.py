@@ -168,3 +168,94 @@ def winattn(q, k_hr, v_hr, out, *, params_dev, n_w, p_stride, anchor_mode, geom,
                      kv_w=geom.kv_w)
     out.copy_(o.reshape(out.shape).to(BF16))
     return out
+
+
+# --------------------------------------------------------------------------- VAE decode
+def emulate_conv3d(x, w2, bias, *, kt, kh, shuffle_t=1, up2_phase=-1, residual=None):
+    """srdit_conv3d in float64: output frame o, pixel (h, w) sums, over taps (dt,
+    ky, kx) and channels, x[o + dt, h + dy, w + dx] * w2[n, ((dt kh + ky) kh + kx)
+    cin + c] with (dy, dx) = (ky - kh/2, kx - kh/2), or, for an up2 phase (i, j),
+    (floor((i + ky - 1) / 2), floor((j + kx - 1) / 2)); zeros outside the frame;
+    bf16 rounding; interleaved or phase stores as the kernel's."""
+    Fi, H, W, cin = x.shape
+    Fo = Fi - kt + 1
+    cout = w2.shape[0]
+    xp = torch.nn.functional.pad(x.double(), (0, 0, 1, 1, 1, 1))   # one zero pixel around
+    pi, pj = (up2_phase >> 1, up2_phase & 1) if up2_phase >= 0 else (0, 0)
+    cols = []
+    for dt in range(kt):
+        for ky in range(kh):
+            for kx in range(kh):
+                if up2_phase >= 0:
+                    dy, dx = (pi + ky - 1) // 2, (pj + kx - 1) // 2
+                else:
+                    dy, dx = ky - kh // 2, kx - kh // 2
+                cols.append(xp[dt:dt + Fo, 1 + dy:1 + dy + H, 1 + dx:1 + dx + W, :])
+    a = torch.cat(cols, -1)
+    y = (a @ w2.double().t() + bias.double()).to(torch.float32).to(torch.bfloat16).double()
+    if up2_phase >= 0:
+        out = torch.zeros(Fo, 2 * H, 2 * W, cout, dtype=torch.float64)
+        out[:, pi::2, pj::2] = y
+        y = out
+    if residual is not None:
+        y = (residual.double() + y).to(torch.float32).to(torch.bfloat16).double()
+        if up2_phase >= 0:
+            keep = torch.zeros(2 * H, 2 * W, dtype=torch.bool)
+            keep[pi::2, pj::2] = True
+            y = torch.where(keep[None, :, :, None], y, torch.zeros_like(y))
+    if shuffle_t > 1:
+        cg = cout // shuffle_t
+        y = y.reshape(Fo, H, W, shuffle_t, cg).permute(0, 3, 1, 2, 4).reshape(Fo * shuffle_t,
+                                                                                H, W, cg)
+    return y
+
+
+def conv3d(x, weight, bias, *, kt=1, kh=3, residual=None, res_scale=1.0, relu=False,
+           shuffle=1, shuffle_t=1, up2_phase=-1, dup=None, out=None, status=None):
+    """srdit_conv3d by its emulation (float64 sums, the kernel's bf16 roundings and
+    stores); the DupUp3D gather of a phase launch as the materialised shortcut."""
+    if res_scale != 1.0 or relu or shuffle != 1:
+        raise NotImplementedError("the VAE decode's forms only")
+    if dup is not None:
+        import importlib
+        vae = importlib.import_module("dreamx-creator_b200.vae")
+        xd, ft, shift = dup
+        residual = vae._dup_up(xd, weight.shape[0], ft, 2, shift > 0)
+    y = emulate_conv3d(x, weight, bias, kt=kt, kh=kh, shuffle_t=shuffle_t, up2_phase=up2_phase,
+                       residual=residual).to(torch.bfloat16)
+    if up2_phase >= 0:
+        pi, pj = up2_phase >> 1, up2_phase & 1
+        out[:, pi::2, pj::2] = y[:, pi::2, pj::2]
+        return out
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def conv3d_weight(w, *, cin_pad=None):
+    import importlib
+    return importlib.import_module("dreamx-creator_b200.ops").conv3d_weight(w, cin_pad=cin_pad)
+
+
+def rms_silu(x, gamma, *, silu=True, out=None):
+    """srdit_rms_silu by the oracle's RMS_norm (+ SiLU) over the last dim."""
+    from oracle import vae as ov
+    y = ov.rms_norm(x.double().movedim(-1, 0), gamma.double())
+    if silu:
+        y = ov.silu(y)
+    y = y.movedim(0, -1).to(torch.bfloat16)
+    if out is None:
+        return y
+    out.copy_(y)
+    return out
+
+
+def vae_attend(q, k, v):
+    """The middle block's attention as the oracle computes it (float64 softmax,
+    the output rounded to bf16)."""
+    import math
+    qd, kd, vd = q.double(), k.double(), v.double()
+    p = torch.softmax(qd @ kd.transpose(-1, -2) / math.sqrt(q.shape[-1]), -1)
+    return (p @ vd).to(torch.float32).to(torch.bfloat16)
+

@@ -9,7 +9,7 @@ import torch
 from oracle import numerics as onum
 from oracle import vae as ov
 from tests.golden_cases import vae_state_dict
-from tests.test_vae_cpu import emulate_conv3d
+from tests.cpu_ops import emulate_conv3d
 
 pytestmark = pytest.mark.gpu
 
@@ -138,3 +138,20 @@ def test_dup_up_gathered_in_the_epilogue(pkg, cuda_device, cin, cout, ft, shift)
         ops.conv3d(xc, w2, b, kt=1, kh=3, up2_phase=ph, out=mat, residual=res)
     torch.cuda.synchronize(cuda_device)
     assert torch.equal(fused, mat)
+
+
+def test_decode_at_full_width(pkg, cuda_device):
+    """The shipped decoder's widths (dec_dim 256: 1024-channel layers, 8 output
+    tiles, 27 x 16 K slices per tap set) on a small latent (2 frames of 2 x 3,
+    seeded weights) against the oracle."""
+    _, vae = pkg
+    sd = vae.Wan22VAEDecoder.seeded_state_dict(seed=5)
+    g = torch.Generator().manual_seed(1)
+    z = torch.randn(48, 2, 2, 3, generator=g).to(torch.bfloat16)
+    mean, std = 0.1 * torch.randn(48, generator=g), 0.5 + torch.rand(48, generator=g)
+    d = vae.Wan22VAEDecoder(sd, device=cuda_device)
+    out = d.decode(z.to(cuda_device), mean, std, clamp=False).cpu().double()
+    ref = ov.Decoder(sd).decode(z, mean, std)
+    assert out.shape == ref.shape == (3, 5, 32, 48)
+    assert onum.rel_fro(out, ref) < 3e-2
+    assert onum.cosine(out, ref) > 0.9995

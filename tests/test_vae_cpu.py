@@ -9,6 +9,7 @@ import pytest
 import torch
 
 from oracle import vae as ov
+from tests.cpu_ops import emulate_conv3d
 
 
 @pytest.fixture(scope="module")
@@ -16,45 +17,6 @@ def pkg():
     importlib.import_module("dreamx-creator_b200")
     return (importlib.import_module("dreamx-creator_b200.ops"),
             importlib.import_module("dreamx-creator_b200.vae"))
-
-
-def emulate_conv3d(x, w2, bias, *, kt, kh, shuffle_t=1, up2_phase=-1, residual=None):
-    """srdit_conv3d in float64: output frame o, pixel (h, w) sums, over taps (dt,
-    ky, kx) and channels, x[o + dt, h + dy, w + dx] * w2[n, ((dt kh + ky) kh + kx)
-    cin + c] with (dy, dx) = (ky - kh/2, kx - kh/2), or, for an up2 phase (i, j),
-    (floor((i + ky - 1) / 2), floor((j + kx - 1) / 2)); zeros outside the frame;
-    bf16 rounding; interleaved or phase stores as the kernel's."""
-    Fi, H, W, cin = x.shape
-    Fo = Fi - kt + 1
-    cout = w2.shape[0]
-    xp = torch.nn.functional.pad(x.double(), (0, 0, 1, 1, 1, 1))   # one zero pixel around
-    pi, pj = (up2_phase >> 1, up2_phase & 1) if up2_phase >= 0 else (0, 0)
-    cols = []
-    for dt in range(kt):
-        for ky in range(kh):
-            for kx in range(kh):
-                if up2_phase >= 0:
-                    dy, dx = (pi + ky - 1) // 2, (pj + kx - 1) // 2
-                else:
-                    dy, dx = ky - kh // 2, kx - kh // 2
-                cols.append(xp[dt:dt + Fo, 1 + dy:1 + dy + H, 1 + dx:1 + dx + W, :])
-    a = torch.cat(cols, -1)
-    y = (a @ w2.double().t() + bias.double()).to(torch.float32).to(torch.bfloat16).double()
-    if up2_phase >= 0:
-        out = torch.zeros(Fo, 2 * H, 2 * W, cout, dtype=torch.float64)
-        out[:, pi::2, pj::2] = y
-        y = out
-    if residual is not None:
-        y = (residual.double() + y).to(torch.float32).to(torch.bfloat16).double()
-        if up2_phase >= 0:
-            keep = torch.zeros(2 * H, 2 * W, dtype=torch.bool)
-            keep[pi::2, pj::2] = True
-            y = torch.where(keep[None, :, :, None], y, torch.zeros_like(y))
-    if shuffle_t > 1:
-        cg = cout // shuffle_t
-        y = y.reshape(Fo, H, W, shuffle_t, cg).permute(0, 3, 1, 2, 4).reshape(Fo * shuffle_t,
-                                                                                H, W, cg)
-    return y
 
 
 def _rand(shape, g, scale=1.0):
@@ -156,3 +118,27 @@ def test_param_shapes_are_the_reference_decoders(pkg, golden):
     d = vae.Wan22VAEDecoder(sd, dim=64, device="cpu")
     # 3 latent frames of 4 x 6: the head alone is 27 taps x 64 -> 12 on 9 frames
     assert d.flops(3, 4, 6) > 2 * 9 * 32 * 48 * 12 * 64 * 27
+
+
+def test_decoder_host_logic_on_the_cpu_double(pkg, golden, monkeypatch):
+    """The decoder's orchestration -- the history buffers and their shifts, the
+    skipped first time conv, the phase launches and their DupUp3D source, the
+    attention, unpatchify -- run with the CPU double of its kernels (their
+    emulations, float64 sums with the kernels' roundings) and the oracle's
+    attention, reproduces the oracle's bf16 decode of the golden case."""
+    from oracle import numerics as onum
+    from tests import cpu_ops
+    from tests.golden_cases import vae_state_dict
+    _, vae = pkg
+    monkeypatch.setattr(vae, "ops", cpu_ops)
+    monkeypatch.setattr(vae, "attend", cpu_ops.vae_attend)
+    g = golden("vae")
+    sd = vae_state_dict(g)
+    z = torch.from_numpy(g["z"]).view(torch.bfloat16)
+    mean, std = torch.from_numpy(g["mean"]), torch.from_numpy(g["std"])
+    d = vae.Wan22VAEDecoder(sd, dim=64, device="cpu")
+    out = d.decode(z, mean, std, clamp=False).double()
+    ref = ov.Decoder(sd).decode(z, mean, std)
+    assert out.shape == ref.shape
+    assert onum.rel_fro(out, ref) < 1e-3
+    assert float((out == ref).double().mean()) > 0.95
