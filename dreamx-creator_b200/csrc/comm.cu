@@ -46,6 +46,7 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(const float* __restri
                                                            int op, Ptrs slots, Ptrs flags,
                                                            int rank, int world, uint32_t epoch,
                                                            uint32_t* status) {
+  pdl_begin();
   __shared__ int ok;
   const int share = (n + gridDim.x - 1) / gridDim.x;
   const int i0 = blockIdx.x * share, i1 = min(n, i0 + share);
@@ -80,6 +81,7 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(const float* __restri
 // One thread: make this stream's earlier writes to the peers visible, then add
 // 1 to counter `rank` of every other rank.
 __global__ void tp_signal_kernel(Ptrs flags, int rank, int world) {
+  pdl_begin();
   __threadfence_system();
   for (int d = 0; d < world; ++d)
     if (d != rank) flag_add_release(static_cast<uint32_t*>(flags.p[d]) + rank, 1u);
@@ -90,6 +92,7 @@ __global__ void tp_signal_kernel(Ptrs flags, int rank, int world) {
 // stored before their release-adds.
 __global__ void wait_counters_kernel(const uint32_t* counters, uint32_t mask, uint32_t expected,
                                      uint32_t* status) {
+  pdl_begin();
   for (int s = 0; s < 32; ++s)
     if ((mask >> s) & 1u)
       if (!flag_wait(counters + s, expected, status)) return;
@@ -157,7 +160,7 @@ extern "C" int srdit_tp_allreduce(const float* in, float* out, int n, int op,
     f.p[i] = i < world ? flags->p[i] : nullptr;
     if (i < world && (!s.p[i] || !f.p[i])) return SRDIT_EINVAL;
   }
-  comm::tp_allreduce_kernel<<<SRDIT_AR_BLOCKS, 256, 0, stream>>>(in, out, n, op, s, f, rank,
+  SRDIT_LAUNCH((comm::tp_allreduce_kernel), SRDIT_AR_BLOCKS, 256, 0, stream, in, out, n, op, s, f, rank,
                                                                 world, epoch, status);
   return static_cast<int>(cudaGetLastError());
 }
@@ -166,7 +169,7 @@ extern "C" int srdit_wait_counters(const uint32_t* counters, uint32_t mask, uint
                                    uint32_t* status, cudaStream_t stream) {
   if (!counters) return SRDIT_EINVAL;
   if (!mask) return 0;
-  comm::wait_counters_kernel<<<1, 1, 0, stream>>>(counters, mask, expected, status);
+  SRDIT_LAUNCH((comm::wait_counters_kernel), 1, 1, 0, stream, counters, mask, expected, status);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -190,6 +193,6 @@ extern "C" int srdit_tp_push(const void* src, const srdit_peer_ptrs* dst, unsign
       if (e != cudaSuccess) return static_cast<int>(e);
     }
   }
-  comm::tp_signal_kernel<<<1, 1, 0, stream>>>(f, rank, world);
+  SRDIT_LAUNCH((comm::tp_signal_kernel), 1, 1, 0, stream, f, rank, world);
   return static_cast<int>(cudaGetLastError());
 }

@@ -2,6 +2,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "srdit_internal.h"
@@ -25,6 +26,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return g_encode;
 }
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SRDIT_PDL");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
 
 int num_sms(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return 148;

@@ -99,6 +99,7 @@ SRDIT_DEV uint32_t bf2_relu(uint32_t w) {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     conv3x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const Params p) {
+  pdl_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -502,7 +503,7 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
   const int tiles = p.pair_tiles * n_tiles;
   const int pairs = num_sms(dev) / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  conv::conv3x3_kernel<<<grid, conv::NUM_THREADS, conv::SMEM, stream>>>(ta, tb, p);
+  SRDIT_LAUNCH((conv::conv3x3_kernel), grid, conv::NUM_THREADS, conv::SMEM, stream, ta, tb, p);
   return static_cast<int>(cudaGetLastError());
 }
 

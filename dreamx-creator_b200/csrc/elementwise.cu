@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(128) quant_rowwise_kernel(
     const __nv_bfloat16* __restrict__ x, long long ldx, int M,
     const float* __restrict__ amax_in, uint8_t* __restrict__ q, long long ldq,
     float* __restrict__ scale_out) {
+  pdl_begin();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -171,6 +172,7 @@ __global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
     const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K,
     const float* __restrict__ amax_in, uint8_t* __restrict__ q, long long ldq,
     float* __restrict__ scale_out) {
+  pdl_begin();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -218,6 +220,7 @@ __global__ void __launch_bounds__(128) quant_rowwise_stream_kernel(
 __global__ void __launch_bounds__(128) row_reduce_kernel(const __nv_bfloat16* __restrict__ x,
                                                          long long ldx, int M, int K, int op,
                                                          float* __restrict__ out) {
+  pdl_begin();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -252,6 +255,7 @@ __global__ void __launch_bounds__(256) residual_kernel(
     const __nv_bfloat16* __restrict__ parts, int n_parts, long long part_stride,
     long long ld_part, const __nv_bfloat16* __restrict__ bias, const float* __restrict__ gate,
     const uint32_t* flags, uint32_t expected, uint32_t* status) {
+  pdl_begin();
   if (flags) {
     __shared__ int ready;
     if (threadIdx.x == 0) {
@@ -320,6 +324,7 @@ __global__ void __launch_bounds__(128, (VEC <= 12 ? 5 : 3)) ln_mod_quant_kernel(
     const __nv_bfloat16* __restrict__ ln_w, const __nv_bfloat16* __restrict__ ln_b,
     const float* __restrict__ shift, const float* __restrict__ scale,
     uint8_t* __restrict__ q, long long ldq, float* __restrict__ qscale) {
+  pdl_begin();
   constexpr int K = VEC * 256;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -592,6 +597,7 @@ SRDIT_DEV void rope_row(const RopeArgs& a, int row, int lane, int K) {
 
 template <int VEC, bool kHalo>
 __global__ void __launch_bounds__(128, (VEC <= 12 ? 4 : 3)) rms_rope_kernel(RopeArgs a, int M, int K) {
+  pdl_begin();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row < M) rope_row<VEC, kHalo>(a, row, lane, K);
@@ -730,6 +736,7 @@ __global__ void __launch_bounds__(kMaxT, kMaxT <= 192 ? 2 : 1) ln_mod_quant_cs_k
     const __nv_bfloat16* __restrict__ ln_w, const __nv_bfloat16* __restrict__ ln_b,
     const float* __restrict__ shift, const float* __restrict__ scale,
     uint8_t* __restrict__ q, long long ldq, float* __restrict__ qscale, const LnPeer pe) {
+  pdl_begin();
   constexpr bool kMod = MODE & 1, kAff = MODE & 2;
   __shared__ float part[3][32 * kGroup];
   const int T = blockDim.x;
@@ -899,7 +906,7 @@ struct QuantLaunch {
   static int run(const __nv_bfloat16* x, long long ldx, int M, const float* amax_in,
                  uint8_t* q, long long ldq, float* s, cudaStream_t st) {
     const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
-    quant_rowwise_kernel<VEC><<<grid, kRowsPerBlock * 32, 0, st>>>(x, ldx, M, amax_in, q, ldq, s);
+    SRDIT_LAUNCH((quant_rowwise_kernel<VEC>), grid, kRowsPerBlock * 32, 0, st, x, ldx, M, amax_in, q, ldq, s);
     return static_cast<int>(cudaGetLastError());
   }
 };
@@ -910,7 +917,7 @@ struct LnLaunch {
                  const __nv_bfloat16* w, const __nv_bfloat16* b, const float* shift,
                  const float* scale, uint8_t* q, long long ldq, float* qs, cudaStream_t st) {
     const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
-    ln_mod_quant_kernel<VEC><<<grid, kRowsPerBlock * 32, 0, st>>>(x, ldx, M, eps, w, b, shift,
+    SRDIT_LAUNCH((ln_mod_quant_kernel<VEC>), grid, kRowsPerBlock * 32, 0, st, x, ldx, M, eps, w, b, shift,
                                                                   scale, q, ldq, qs);
     return static_cast<int>(cudaGetLastError());
   }
@@ -920,9 +927,9 @@ template <int VEC>
 int rope_launch(const RopeArgs& a, int M, int K, cudaStream_t st) {
   const int grid = (M + kRowsPerBlock - 1) / kRowsPerBlock;
   if (a.halo.done)
-    rms_rope_kernel<VEC, true><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M, K);
+    SRDIT_LAUNCH((rms_rope_kernel<VEC, true>), grid, kRowsPerBlock * 32, 0, st, a, M, K);
   else
-    rms_rope_kernel<VEC, false><<<grid, kRowsPerBlock * 32, 0, st>>>(a, M, K);
+    SRDIT_LAUNCH((rms_rope_kernel<VEC, false>), grid, kRowsPerBlock * 32, 0, st, a, M, K);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -934,7 +941,7 @@ int ln_cs_run_t(const __nv_bfloat16* x, long long ldx, int M, int K, float eps,
   int grid = 0;
   const int rc = cs_grid<ln_mod_quant_cs_kernel<MODE, kMaxT, kPeer>>(K / 16, M, &grid);
   if (rc) return rc;
-  ln_mod_quant_cs_kernel<MODE, kMaxT, kPeer><<<grid, K / 16, 0, st>>>(
+  SRDIT_LAUNCH((ln_mod_quant_cs_kernel<MODE, kMaxT, kPeer>), grid, K / 16, 0, st, 
       x, ldx, M, eps, w, b, shift, scale, q, ldq, qs, pe);
   return static_cast<int>(cudaGetLastError());
 }
@@ -980,6 +987,7 @@ __global__ void __launch_bounds__(128) rms_silu_kernel(const __nv_bfloat16* __re
                                                        const __nv_bfloat16* __restrict__ gamma,
                                                        float scale, int silu,
                                                        __nv_bfloat16* __restrict__ out) {
+  pdl_begin();
   const long long pix0 = (static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5)) * PPW;
   const int lane = threadIdx.x & 31;
   if (pix0 >= P) return;
@@ -1078,7 +1086,7 @@ extern "C" int srdit_quant_rowwise(const void* x, long long ldx, int M, int K,
     if (rc != SRDIT_EUNSUPPORTED) return rc;
   }
   const int grid = (M + ew::kRowsPerBlock - 1) / ew::kRowsPerBlock;
-  ew::quant_rowwise_stream_kernel<8><<<grid, ew::kRowsPerBlock * 32, 0, stream>>>(
+  SRDIT_LAUNCH((ew::quant_rowwise_stream_kernel<8>), grid, ew::kRowsPerBlock * 32, 0, stream, 
       xb, ldx, M, K, amax_in, qb, ldq, scale);
   return static_cast<int>(cudaGetLastError());
 }
@@ -1285,13 +1293,13 @@ extern "C" int srdit_rms_silu(const void* x, long long pixels, int C, const void
   if (blocks > 0x7fffffffLL) return SRDIT_EUNSUPPORTED;
   const int g = static_cast<int>(blocks);
   if (nch <= 1)
-    ew::rms_silu_kernel<1, 4><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    SRDIT_LAUNCH((ew::rms_silu_kernel<1, 4>), g, 128, 0, stream, xb, pixels, C, gb, scale, silu, ob);
   else if (nch <= 2)
-    ew::rms_silu_kernel<2, 2><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    SRDIT_LAUNCH((ew::rms_silu_kernel<2, 2>), g, 128, 0, stream, xb, pixels, C, gb, scale, silu, ob);
   else if (nch <= 4)
-    ew::rms_silu_kernel<4, 1><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    SRDIT_LAUNCH((ew::rms_silu_kernel<4, 1>), g, 128, 0, stream, xb, pixels, C, gb, scale, silu, ob);
   else
-    ew::rms_silu_kernel<8, 1><<<g, 128, 0, stream>>>(xb, pixels, C, gb, scale, silu, ob);
+    SRDIT_LAUNCH((ew::rms_silu_kernel<8, 1>), g, 128, 0, stream, xb, pixels, C, gb, scale, silu, ob);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -1302,7 +1310,7 @@ extern "C" int srdit_row_reduce(const void* x, long long ldx, int M, int K, int 
     return SRDIT_EINVAL;
   if ((K % 8) || (ldx % 8) || !aligned16(x)) return SRDIT_EALIGN;
   const int grid = (M + ew::kRowsPerBlock - 1) / ew::kRowsPerBlock;
-  ew::row_reduce_kernel<<<grid, ew::kRowsPerBlock * 32, 0, stream>>>(
+  SRDIT_LAUNCH((ew::row_reduce_kernel), grid, ew::kRowsPerBlock * 32, 0, stream, 
       static_cast<const __nv_bfloat16*>(x), ldx, M, K, op, out);
   return static_cast<int>(cudaGetLastError());
 }
@@ -1325,7 +1333,7 @@ extern "C" int srdit_residual_tp(void* x, long long ldx, int M, int N, const voi
     return SRDIT_EALIGN;
   const long long work = static_cast<long long>(M) * (N / 8);
   const unsigned grid = static_cast<unsigned>((work + 255) / 256);
-  ew::residual_kernel<<<grid, 256, 0, stream>>>(
+  SRDIT_LAUNCH((ew::residual_kernel), grid, 256, 0, stream, 
       static_cast<__nv_bfloat16*>(x), ldx, M, N, static_cast<const __nv_bfloat16*>(parts),
       n_parts, part_stride, ld_part, static_cast<const __nv_bfloat16*>(bias), gate, flags,
       expected, status);

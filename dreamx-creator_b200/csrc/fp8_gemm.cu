@@ -129,6 +129,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const Params p,
                     const __grid_constant__ PeerMaps pm, const __grid_constant__ TpArgs tp) {
+  pdl_begin();
   constexpr bool kRes = has_residual<EPI>();
   using C = Cfg<BN, kRes>;
   extern __shared__ uint8_t smem_raw[];
@@ -505,7 +506,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
   const int pairs = num_sms(dev) / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, to, p, pm, tp);
+  SRDIT_LAUNCH((kern), grid, NUM_THREADS, C::SMEM, stream, ta, tb, to, p, pm, tp);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -32,6 +32,15 @@ SRDIT_DEV uint64_t global_timer_ns() {
   return t;
 }
 
+// Programmatic dependent launch: wait until the stream's previous kernel has
+// completed and its memory is visible (a no-op for a launch without the
+// attribute); then let the next kernel of the stream be scheduled early. Every
+// kernel calls pdl_begin() before any global-memory access.
+SRDIT_DEV void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 SRDIT_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -308,6 +308,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap tmKA,
                    const __grid_constant__ CUtensorMap tmVA,
                    const __grid_constant__ CUtensorMap tmO, const Args a) {
+  pdl_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1588,10 +1589,10 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
   const int sms = num_sms(dev);
   dim3 grid(static_cast<unsigned>(items < sms ? items : sms));
   if (t->split_kv)
-    attn::winattn_kernel<true><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(
+    SRDIT_LAUNCH((attn::winattn_kernel<true>), grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream, 
         mq, mk, mv, mka, mva, mo, a);
   else
-    attn::winattn_kernel<false><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream>>>(
+    SRDIT_LAUNCH((attn::winattn_kernel<false>), grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream, 
         mq, mk, mv, mka, mva, mo, a);
   return static_cast<int>(cudaGetLastError());
 }
