@@ -14,9 +14,15 @@ work. Weights are seeded random (no checkpoint); inputs are seeded synthetic.
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
 N > 1 (under torchrun): tensor parallelism over N ranks on one clip (heads and
-FFN sharded, sequence-parallel residual stream; strong scaling), or with
+FFN sharded, sequence-parallel residual stream; strong scaling), with
+--parallel spatial a strip of token columns per rank (strong scaling), or with
 --parallel replicas every rank refines its own clip (weak scaling); the step
 time is the max over ranks.
+
+Other lines: --clip (config 5: a 121-frame clip over the rolling cache; with
+--pipeline the whole latent path -- upsampler, refiner loop, VAE decode);
+--micro (one kernel, or the latent upsampler / the VAE decode, in isolation,
+beside the reference's own GPU ops where they exist).
 """
 from __future__ import annotations
 
@@ -88,6 +94,10 @@ def parse():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--epi", default="store", choices=["store", "gelu", "gated_res", "res"],
                     help="micro gemm: the epilogue")
+    ap.add_argument("--pipeline", action="store_true",
+                    help="with --clip at N = 1: the whole latent path of a clip -- the "
+                         "latent upsampler on the LR latent, the noise mix, the refiner "
+                         "loop, and the Wan2.2 VAE decode to pixels -- timed stage by stage")
     ap.add_argument("--clip", action="store_true",
                     help="BASELINE config 5: a 121-frame clip (33 latent frames, 11 chunks) "
                          "over the rolling KV cache; sustained latent-frames/s and per-chunk "
@@ -696,6 +706,10 @@ def run_clip(args, rank, world, local):
     else:
         model = model_mod.SRDiT.random_init(cfg, dev, seed=0)
     n_chunks, f = 11, 3
+    if args.pipeline:
+        if world > 1:
+            raise SystemExit("--pipeline runs on one GPU")
+        return run_pipeline(args, model, dev, n_chunks, f)
     g = torch.Generator().manual_seed(1000 if tp else 1000 + rank)
     ctx = torch.randn(*CTX_SHAPE, generator=g).to(torch.bfloat16).to(dev)
     clip = torch.randn(48, n_chunks * f, 72, 128, generator=g).to(torch.bfloat16).to(dev)
@@ -739,6 +753,60 @@ def run_clip(args, rank, world, local):
         "cuda_graph": bool(stream.graphs), "config": workload_config(args),
         "data": "synthetic (seeded N(0,1) latent clip + text context, seeded random weights)"}),
         flush=True)
+
+
+def run_pipeline(args, model, dev, n_chunks, f):
+    """One 121-frame 2K clip through the latent path (seeded weights, synthetic LR
+    latent): FlashLatentUpsampler (the shipped config) 36 x 64 -> 72 x 128, the
+    noise mix at t = 625, 11 refiner chunks (graph replay, as in config 5), the
+    Wan2.2 VAE decode of the 33 refined latent frames to 129 frames of 1152 x
+    2048. One untimed pass, then one timed with CUDA events between stages."""
+    from importlib import import_module
+    pipe_mod = import_module("dreamx-creator_b200.pipeline")
+    up_mod = import_module("dreamx-creator_b200.upsampler")
+    vae_mod = import_module("dreamx-creator_b200.vae")
+    kw = dict(in_channels=48, out_channels=48, mid_channels=128, num_blocks=8, upsample_scale=2)
+    up = up_mod.FlashLatentUpsampler(up_mod.FlashLatentUpsampler.seeded_state_dict(**kw),
+                                     **kw, memory_init="replicate", device=dev)
+    dec = vae_mod.Wan22VAEDecoder(vae_mod.Wan22VAEDecoder.seeded_state_dict(seed=0), device=dev)
+    T = n_chunks * f
+    g = torch.Generator(device=dev).manual_seed(1000)
+    ctx = torch.randn(*CTX_SHAPE, device=dev, generator=g).to(torch.bfloat16)
+    lr = torch.randn(1, 48, T, 36, 64, device=dev, generator=g).to(torch.bfloat16)
+    noise = torch.randn(48, T, 72, 128, device=dev, generator=g).to(torch.bfloat16)
+    mean, std = torch.zeros(48), torch.ones(48)
+    stream = pipe_mod.RefinerStream(model, ctx, graphs=not args.no_graphs)
+    sigma = stream.denoise_t / stream.ntt
+
+    def once(evs):
+        evs[0].record()
+        lr_up = up(lr)[0]
+        evs[1].record()
+        noisy = pipe_mod.sr_noise(lr_up, noise, sigma)
+        stream.reset()
+        x0 = pipe_mod.refine_clip(stream, noisy, chunk=f)
+        evs[2].record()
+        video = dec.decode(x0, mean, std)
+        evs[3].record()
+        return video
+
+    with torch.no_grad():
+        once([torch.cuda.Event(enable_timing=True) for _ in range(4)])
+        torch.cuda.synchronize()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        video = once(evs)
+        torch.cuda.synchronize()
+        model.check_status()
+    st = [evs[i].elapsed_time(evs[i + 1]) for i in range(3)]
+    total = sum(st)
+    print(json.dumps({
+        "metric": "2K clip latent path seconds (upsample + 11-chunk refine + VAE decode)",
+        "value": total * 1e-3, "unit": "s", "n_gpus": 1, "higher_is_better": False,
+        "stages_ms": {"latent_upsampler": st[0], "refine_11_chunks": st[1], "vae_decode": st[2]},
+        "video": list(video.shape), "output_frames_per_s": video.shape[1] / (total * 1e-3),
+        "cuda_graph": bool(stream.graphs),
+        "data": "synthetic (seeded N(0,1) LR latent, noise and text context; seeded random "
+                "weights for the upsampler, the refiner and the VAE decoder)"}), flush=True)
 
 
 def main():

@@ -237,3 +237,33 @@ class RefinerStream:
         self.cache.commit(f)
         self.t_offset += f
         return out
+
+
+def sr_noise(lr_up: torch.Tensor, noise: torch.Tensor, sigma: float) -> torch.Tensor:
+    """The refiner's starting latent: (1 - sigma) * upsampled LR + sigma * noise
+    (causal_inference.py:667-668)."""
+    return ((1.0 - sigma) * lr_up.float() + sigma * noise.float()).to(lr_up.dtype)
+
+
+def refine_clip(stream: RefinerStream, noisy: torch.Tensor, chunk: int = 3,
+                lq: torch.Tensor | None = None, events: list | None = None) -> torch.Tensor:
+    """Every chunk of a clip's noisy latent [C, T, H, W] through ``stream`` (the
+    loop of causal_inference.py:858-976), each chunk's LQ anchor harvested from
+    the same frames of ``lq`` (the upsampled LR latent) when given, the next
+    chunk's harvest started ahead. Returns the refined latent [C, T, H, W];
+    ``events`` (a list) receives a CUDA event after each chunk."""
+    T = noisy.shape[1]
+    if T % chunk:
+        raise ValueError(f"{T} latent frames are not whole {chunk}-frame chunks")
+    outs = []
+    for i in range(0, T, chunk):
+        nxt = lq[:, i + chunk:i + 2 * chunk] if lq is not None and i + chunk < T else None
+        out = stream.step(noisy[:, i:i + chunk],
+                          lq_chunk=lq[:, i:i + chunk] if lq is not None else None,
+                          next_lq_chunk=nxt)
+        outs.append(out.clone() if stream.graphs else out)
+        if events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            events.append(ev)
+    return torch.cat(outs, dim=1)

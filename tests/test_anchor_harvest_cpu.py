@@ -109,3 +109,22 @@ def test_prefetched_harvest_gives_the_serial_stream():
         outs[prefetch] = res
     for a, b in zip(outs[False], outs[True]):
         assert torch.equal(a, b)
+
+
+def test_refine_clip_is_the_chunk_loop():
+    """pipeline.refine_clip over a 2-chunk clip (anchors from the LQ latent,
+    the second harvested ahead) equals stepping the chunks one by one."""
+    M, cfg, model = _model()
+    P = importlib.import_module("dreamx-creator_b200.pipeline")
+    g = torch.Generator().manual_seed(21)
+    ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(torch.bfloat16)
+    lq = torch.randn(cfg.in_dim, 6, 8, 16, generator=g).to(torch.bfloat16)
+    noise = torch.randn(cfg.in_dim, 6, 8, 16, generator=g).to(torch.bfloat16)
+    noisy = P.sr_noise(lq, noise, 0.625)
+    assert torch.equal(noisy, (0.375 * lq.float() + 0.625 * noise.float()).to(torch.bfloat16))
+    got = P.refine_clip(P.RefinerStream(model, ctx), noisy, lq=lq)
+    s = P.RefinerStream(model, ctx)
+    ref = torch.cat([s.step(noisy[:, i:i + 3], lq_chunk=lq[:, i:i + 3]) for i in (0, 3)], 1)
+    assert got.shape == noisy.shape and torch.equal(got, ref)
+    with pytest.raises(ValueError):
+        P.refine_clip(P.RefinerStream(model, ctx), noisy[:, :4])
