@@ -283,13 +283,21 @@ def run_upsampler_micro(args, dev, timeit, peaks):
     torch.cuda.synchronize()
     evs, srdit_ops.Stats.events = srdit_ops.Stats.events, None
     conv_ms = sum(e0.elapsed_time(e1) for _, e0, e1, _ in evs)
+    by_work = {}
+    for _, e0, e1, wk in evs:
+        k = by_work.setdefault(wk, [0, 0.0])
+        k[0] += 1
+        k[1] += e0.elapsed_time(e1)
     return {"workload": "FlashLatentUpsampler x2 (48 ch, mid 128, 8 blocks, replicate), "
                         f"LR latent 1 x 48 x {T} x {H} x {W}", "ms": ms,
             "latent_frames_per_s": T / ms * 1e3, "tflops": fl / ms / 1e9,
             "conv_launches": len(evs), "conv_ms": conv_ms, "conv_tflops": fl / conv_ms / 1e9,
             "frac_of_bf16_burst": fl / conv_ms / 1e9 / peaks["bf16_tflops"],
             "cudnn_ms": ref, "cudnn_tflops": fl / ref / 1e9, "speedup_vs_cudnn": ref / ms,
-            "rel_fro_vs_cudnn": float((a - b).norm() / b.norm())}
+            "rel_fro_vs_cudnn": float((a - b).norm() / b.norm()),
+            "conv_by_work": [{"gflop": wk / 1e9, "launches": n, "ms": t,
+                              "tflops": wk * n / t / 1e9}
+                             for wk, (n, t) in sorted(by_work.items(), reverse=True)]}
 
 
 def run_vae_micro(args, dev, peaks):

@@ -10,7 +10,7 @@
 // 320 and :452-476): the first frame of a clip sees itself ("replicate") or
 // zeros. Taps outside the frame read zeros (padding=1).
 //
-// Implicit GEMM: a CTA pair computes a 256-pixel x 128-channel output tile
+// Implicit GEMM: a CTA pair computes a 256-pixel x 128- (or 256-) channel output tile
 // with one tcgen05.mma.cta_group::2 (kind::f16, bf16 in, fp32 accumulate in
 // TMEM) per 16 deep K step. Each CTA owns 128 pixels: a bh x bw block of one
 // frame (bh * bw = 128), whose 64-channel slices for each tap and source are
@@ -18,7 +18,7 @@
 // lands as 128 rows of 128 bytes in the 128-byte swizzled K-major layout the
 // MMA reads, and the tensor map's zero fill at the frame edges is the conv's
 // zero padding. The weights are a K-major [Cout, sources * 9 * Cin] matrix;
-// each CTA stages half of a stage's 128 output channels. Per CTA: warp 0 =
+// each CTA stages half of a stage's output channels. Per CTA: warp 0 =
 // TMA producer (8-stage ring), warp 1 = MMA issuer (even CTA) / TMEM owner,
 // warps 2-5 = epilogue, which reads its 32 pixels x 128 fp32 accumulators
 // from TMEM (two accumulators, so the epilogue of one tile overlaps the MMAs
@@ -28,6 +28,7 @@
 // goes to channel c of sub-pixel (g / r, g % r); the host orders the weight
 // rows that way). Persistent: one pair per two SMs walks the tile list.
 #include <atomic>
+#include <cstdlib>
 
 #include "sm100.cuh"
 #include "srdit_internal.h"
@@ -38,20 +39,27 @@ namespace srdit {
 namespace conv {
 
 constexpr int BM = 128;            // pixels per CTA (256 per pair)
-constexpr int BN = 128;            // output channels per pair tile
 constexpr int BK = 64;             // input channels (bf16) per stage: one 128-byte row
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = (BN / 2) * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int STAGES = 8;
 constexpr int NUM_THREADS = 192;
 constexpr int EPI_WARPS = 4;
-constexpr uint32_t TMEM_COLS = 2 * BN;
-constexpr int OFF_BIAS = STAGES * STAGE_BYTES;
-constexpr int OFF_BAR = OFF_BIAS + 2 * BN * 4;
-constexpr int SMEM = OFF_BAR + 256 + 1024;
-static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1024-byte aligned");
-static_assert(SMEM <= 232448, "shared memory budget");
+
+// Output channels per pair tile: 128, or 256 for convs of 256+ output
+// channels (one MMA of N = 256 reads each A stage once for twice the outputs;
+// its two 256-column accumulators fill the TMEM).
+template <int BN_>
+struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 6 : 8;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr int OFF_BIAS = STAGES * STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_BIAS + 2 * BN * 4;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1024-byte aligned");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
 
 struct Params {
   int F, H, W;          // output frames, frame height, width
@@ -96,10 +104,15 @@ SRDIT_DEV uint32_t bf2_relu(uint32_t w) {
   return d;
 }
 
+template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     conv3x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const Params p) {
   pdl_begin();
+  using C = Cfg<BN>;
+  constexpr int STAGE_BYTES = C::STAGE_BYTES, STAGES = C::STAGES;
+  constexpr int OFF_BIAS = C::OFF_BIAS, OFF_BAR = C::OFF_BAR;
+  constexpr uint32_t TMEM_COLS = C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -389,6 +402,26 @@ using namespace srdit;
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+template <int BN>
+static int conv_run(const CUtensorMap& ta, const CUtensorMap& tb, const conv::Params& p,
+                    cudaStream_t stream) {
+  using C = conv::Cfg<BN>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<bool> attr_done[kMaxDevices] = {};
+  if (dev < kMaxDevices && !attr_done[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(conv::conv3x3_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_done[dev].store(true, std::memory_order_release);
+  }
+  const int tiles = p.pair_tiles * p.n_tiles;
+  const int pairs = num_sms(dev) / 2;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  SRDIT_LAUNCH((conv::conv3x3_kernel<BN>), grid, conv::NUM_THREADS, C::SMEM, stream, ta, tb, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
 // frames: output frames; in_frames: frames of x (frames, or frames + kt - 1
 // with temporal taps)
 static int conv_launch(const void* x, int frames, int in_frames, int frames_per_clip, int H,
@@ -428,7 +461,14 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
   int bw = 128;
   while (bw > 1 && bw / 2 >= W) bw /= 2;
   const int bh = conv::BM / bw;
-  const int n_tiles = (cout + conv::BN - 1) / conv::BN;
+  // tile width: 256 output channels for convs of 256 or more (SRDIT_CONV_BN=128
+  // or 256 in the environment forces one, for comparisons)
+  static const int bn_env = [] {
+    const char* e = getenv("SRDIT_CONV_BN");
+    return e ? atoi(e) : 0;
+  }();
+  const int bn = (bn_env == 128 || bn_env == 256) ? bn_env : (cout >= 256 ? 256 : 128);
+  const int n_tiles = (cout + bn - 1) / bn;
   const long long kcols = static_cast<long long>(n_src) * kt * kh * kh * cin;
 
   CUtensorMap ta, tb;
@@ -440,7 +480,7 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
   if (rc) return rc;
   // weights [cout rows, kcols], K-major (the boxes' rows past cout read zeros)
   rc = make_tmap_2d(&tb, weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<int>(kcols),
-                    cout, kcols, conv::BK, conv::BN / 2);
+                    cout, kcols, conv::BK, bn / 2);
   if (rc) return rc;
 
   conv::Params p;
@@ -491,20 +531,7 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
   p.out = static_cast<__nv_bfloat16*>(out);
   p.status = status;
 
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static std::atomic<bool> attr_done[kMaxDevices] = {};
-  if (dev < kMaxDevices && !attr_done[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(conv::conv3x3_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, conv::SMEM);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    attr_done[dev].store(true, std::memory_order_release);
-  }
-  const int tiles = p.pair_tiles * n_tiles;
-  const int pairs = num_sms(dev) / 2;
-  const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  SRDIT_LAUNCH((conv::conv3x3_kernel), grid, conv::NUM_THREADS, conv::SMEM, stream, ta, tb, p);
-  return static_cast<int>(cudaGetLastError());
+  return bn == 256 ? conv_run<256>(ta, tb, p, stream) : conv_run<128>(ta, tb, p, stream);
 }
 
 extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W,
