@@ -104,7 +104,9 @@ SRDIT_DEV uint32_t bf2_relu(uint32_t w) {
   return d;
 }
 
-template <int BN>
+// KH: the square spatial kernel (1 or 3), a compile-time constant so the
+// producer's per-tap offsets cost no integer division
+template <int BN, int KH>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     conv3x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const Params p) {
@@ -129,7 +131,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int num_tiles = p.pair_tiles * p.n_tiles;
-  const int num_kb = p.n_src * p.kt * p.kh * p.kh * p.cin_slices;
+  const int num_kb = p.n_src * p.kt * KH * KH * p.cin_slices;
   const int cid = static_cast<int>(cluster_id_x());
   const int ncl = static_cast<int>(num_clusters_x());
   const int per_frame = p.tiles_h * p.tiles_w;
@@ -182,13 +184,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         // (outside the tensor: zeros)
         const int f_prev = t > 0 ? f - 1 : (p.replicate ? f : -1);
         int kb = 0;
-        const int ntap = p.kh * p.kh, half = p.kh / 2;
+        const bool phase = p.phase_r > 1;
         for (int src = 0; src < p.n_src && ok; ++src) {
-          for (int dt = 0; dt < p.kt && ok; ++dt)
-          for (int tap = 0; tap < ntap && ok; ++tap) {
+          for (int dt = 0; dt < p.kt && ok; ++dt) {
             const int fs = p.kt > 1 ? f + dt : (src == 0 ? f : f_prev);
-            const int dy = p.phase_r > 1 ? p.tap_dy[tap] : tap / p.kh - half;
-            const int dx = p.phase_r > 1 ? p.tap_dx[tap] : tap % p.kh - half;
+#pragma unroll
+          for (int tap = 0; tap < KH * KH; ++tap) {
+            if (!ok) break;
+            const int dy = phase ? p.tap_dy[tap] : tap / KH - KH / 2;
+            const int dx = phase ? p.tap_dx[tap] : tap % KH - KH / 2;
             for (int cs = 0; cs < p.cin_slices; ++cs, ++kb) {
               if (!mbar_wait(&empty[s], ph ^ 1u, p.status, abort_flag)) {
                 ok = false;
@@ -204,6 +208,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 ph ^= 1u;
               }
             }
+          }
           }
         }
       }
@@ -402,7 +407,7 @@ using namespace srdit;
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <int BN>
+template <int BN, int KH>
 static int conv_run(const CUtensorMap& ta, const CUtensorMap& tb, const conv::Params& p,
                     cudaStream_t stream) {
   using C = conv::Cfg<BN>;
@@ -410,7 +415,7 @@ static int conv_run(const CUtensorMap& ta, const CUtensorMap& tb, const conv::Pa
   cudaGetDevice(&dev);
   static std::atomic<bool> attr_done[kMaxDevices] = {};
   if (dev < kMaxDevices && !attr_done[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(conv::conv3x3_kernel<BN>,
+    cudaError_t e = cudaFuncSetAttribute(conv::conv3x3_kernel<BN, KH>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done[dev].store(true, std::memory_order_release);
@@ -418,7 +423,8 @@ static int conv_run(const CUtensorMap& ta, const CUtensorMap& tb, const conv::Pa
   const int tiles = p.pair_tiles * p.n_tiles;
   const int pairs = num_sms(dev) / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  SRDIT_LAUNCH((conv::conv3x3_kernel<BN>), grid, conv::NUM_THREADS, C::SMEM, stream, ta, tb, p);
+  SRDIT_LAUNCH((conv::conv3x3_kernel<BN, KH>), grid, conv::NUM_THREADS, C::SMEM, stream, ta, tb,
+               p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -531,7 +537,9 @@ static int conv_launch(const void* x, int frames, int in_frames, int frames_per_
   p.out = static_cast<__nv_bfloat16*>(out);
   p.status = status;
 
-  return bn == 256 ? conv_run<256>(ta, tb, p, stream) : conv_run<128>(ta, tb, p, stream);
+  if (kh == 3)
+    return bn == 256 ? conv_run<256, 3>(ta, tb, p, stream) : conv_run<128, 3>(ta, tb, p, stream);
+  return bn == 256 ? conv_run<256, 1>(ta, tb, p, stream) : conv_run<128, 1>(ta, tb, p, stream);
 }
 
 extern "C" int srdit_conv3x3(const void* x, int frames, int frames_per_clip, int H, int W,
