@@ -167,6 +167,9 @@ def run_micro(args):
         fl = srdit.blockgrid.visible_flops(plan["params"], plan["p_stride"], 24, 128)
         res.update(geometry=args.geometry, f_kv=fkv, ms=ms, gflop=fl / 1e9,
                    tflops=fl / ms / 1e9, frac_of_bf16_burst=fl / ms / 1e9 / peaks["bf16_tflops"])
+        ref = reference_winattn(args, srdit, dev, timeit, fkv, bhw, rhw, fl, peaks)
+        if ref is not None:
+            res["reference_triton"] = ref
     elif args.micro == "conv":
         F, H, W, cin, n_src, cout = (int(v) for v in (args.shape or "33,72,128,128,2,128")
                                      .split(","))
@@ -234,6 +237,89 @@ def run_micro(args):
                    frac_of_hbm=byts / ms / 1e6 / peaks["hbm_gbs"])
     res["peaks"] = kind
     print(json.dumps(res), flush=True)
+
+
+REF_INSTALL = ROOT / "baseline" / "_ref"
+
+
+def reference_attention():
+    """The reference's attention module and Triton launcher module, imported from
+    its install under baseline/_ref; None when it is not installed."""
+    if not (REF_INSTALL / "wan" / "modules" / "sr_dit" / "attention.py").exists():
+        return None
+    if str(REF_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REF_INSTALL))
+    from wan.modules.sr_dit import attention as ref_attn
+    from wan.modules.sr_dit import blockgrid_triton as ref_bgt
+    return ref_attn, ref_bgt
+
+
+def reference_winattn(args, srdit, dev, timeit, fkv, bhw, rhw, flops, peaks):
+    """The reference's own GPU window attention on the same 2K chunk, on this GPU.
+
+    - kernel: its Triton launcher (run_blockgrid_triton, blockgrid_triton.py:392-422)
+      on the arguments its op passes it (its own plan, the cat([cache, chunk])
+      K/V), and srdit_winattn_fwd (run_blockgrid_b200) on the same arguments;
+    - op: the whole public op, mask_free_window_attention(attn_impl="triton")
+      (attention.py:1376-1648), with its stock launcher and with the B200
+      launcher installed at its seam (attention.install).
+    Both outputs are compared element by element."""
+    mods = reference_attention()
+    if mods is None:
+        return None
+    ref_attn, _ = mods
+    g = torch.Generator(device=dev).manual_seed(1)
+    L, f_cur, f_cache = 36 * 64, 3, fkv - 3
+
+    def rnd(frames):
+        return torch.randn(1, frames * L, 24, 128, device=dev, generator=g).to(torch.bfloat16)
+
+    q, k, v = rnd(f_cur), rnd(f_cur), rnd(f_cur)
+    ck, cv = (rnd(f_cache), rnd(f_cache)) if f_cache else (None, None)
+    grid = torch.tensor([[f_cur, 36, 64]])
+
+    def op():
+        return ref_attn.mask_free_window_attention(
+            q, k, v, grid, pre_cache_k=ck, pre_cache_v=cv, kv_len=f_cache,
+            attn_impl="triton", block_t=3, block_hw=bhw, block_radius_hw=rhw)[0]
+
+    stock = ref_attn._run_blockgrid_triton
+    seen = {}
+
+    def recorder(*a, **kw):
+        seen["a"], seen["kw"] = a, kw
+        return stock(*a, **kw)
+
+    ref_attn._run_blockgrid_triton = recorder
+    try:
+        op()
+    finally:
+        ref_attn._run_blockgrid_triton = stock
+    (qf, kext, vext, out_t), kw = seen["a"], seen["kw"]
+    out_b = torch.empty_like(out_t)
+    t_ref = timeit(lambda: stock(qf, kext, vext, out_t, **kw))
+    t_b = timeit(lambda: srdit.attention.run_blockgrid_b200(qf, kext, vext, out_b, **kw))
+    torch.cuda.synchronize()
+    diff = (out_b.float() - out_t.float()).abs()
+    rel = (diff.norm() / out_t.float().norm()).item()
+    t_op_ref = timeit(op)
+    o_ref = op()
+    srdit.attention.install(ref_attn)
+    try:
+        t_op_b = timeit(op)
+        o_b = op()
+    finally:
+        ref_attn._run_blockgrid_triton = stock
+    torch.cuda.synchronize()
+    return {
+        "source": "reference installed under baseline/_ref (blockgrid_triton.py, attention.py)",
+        "kernel_ms": t_ref, "kernel_tflops": flops / t_ref / 1e9,
+        "kernel_frac_of_bf16_burst": flops / t_ref / 1e9 / peaks["bf16_tflops"],
+        "b200_kernel_ms_same_args": t_b, "kernel_speedup": t_ref / t_b,
+        "max_abs_diff": diff.max().item(), "rel_fro_diff": rel,
+        "op_ms_triton": t_op_ref, "op_ms_b200": t_op_b, "op_speedup": t_op_ref / t_op_b,
+        "op_max_abs_diff": (o_b.float() - o_ref.float()).abs().max().item(),
+    }
 
 
 def cudnn_upsampler(sd, x, *, num_blocks, scale):
@@ -376,15 +462,79 @@ def geometry(name):
 
 
 # --------------------------------------------------------------------------- CPU arm
+_REF_BLOCK = {}
+
+
+def reference_block(args):
+    """The reference's own WanAttentionBlock (models.py:1207-1354) at full size,
+    from its install under baseline/_ref: bf16 weights (seeded, built once),
+    window attention on its CPU gather + SDPA backend (attention.py:660-802).
+    None when the reference is not installed."""
+    if not (REF_INSTALL / "wan" / "modules" / "sr_dit" / "models.py").exists():
+        return None
+    key = args.geometry
+    if key in _REF_BLOCK:
+        return _REF_BLOCK[key]
+    if str(REF_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REF_INSTALL))
+    import warnings
+    warnings.filterwarnings("ignore")
+    from wan.modules.sr_dit import models
+    D, F = 3072, 14336
+    blk = models.WanAttentionBlock("t2v_cross_attn", D, F, 24, (-1, -1), True, True, 1e-6,
+                                   stream_chunk_size=3)
+    g = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            if name.endswith("bias"):
+                p.copy_(torch.randn(p.shape, generator=g) * 0.01)
+            elif "norm" in name:
+                p.fill_(1.0)
+            elif name == "modulation":
+                p.copy_(torch.randn(p.shape, generator=g) / D ** 0.5)
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+    blk = blk.to(torch.bfloat16)
+    blk.modulation.data = blk.modulation.data.float()
+    bhw, rhw = geometry(args.geometry)
+    sa = blk.self_attn
+    sa.use_window_attn, sa.window_attn_impl = True, "sdpa"
+    sa.window_block_hw, sa.window_block_radius_hw = bhw, rhw
+    t, hd, wd = models._rope_axis_dims(128)
+    freqs = torch.cat([models.rope_params(1024, t), models.rope_params(1024, hd),
+                       models.rope_params(1024, wd)], dim=1)
+    _REF_BLOCK[key] = (blk, freqs)
+    return _REF_BLOCK[key]
+
+
 def cpu_block_sample(args, seed=0):
-    """Time one full-size SR-DiT block of the denoise forward on the host cores,
-    with the oracle's restatement of the reference block (bf16 Linears, fp32
-    window softmax), the reference's CPU-runnable computation."""
-    from oracle import block as oblock
-    from oracle import numerics as onum
+    """Time one full-size SR-DiT block of the denoise forward (3 frames of 36 x 64
+    tokens over a 3-frame cache, 512 text tokens) on the host cores.
+
+    With the reference installed under baseline/_ref this runs the reference's
+    own WanAttentionBlock.forward (kind "reference"); otherwise the oracle's
+    restatement of it (bf16 Linears, fp32 window softmax; kind "port").
+    Returns (seconds, threads, kind)."""
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(seed)
-    D, F = 3072, 14336
+    D, L = 3072, 36 * 64
+    ref = reference_block(args)
+    if ref is not None:
+        blk, freqs = ref
+        x = torch.randn(1, 3 * L, D, generator=g).to(torch.bfloat16)
+        e = torch.randn(1, 6, D, generator=g) * 0.1
+        ctx = torch.randn(1, 512, D, generator=g).to(torch.bfloat16)
+        ck = torch.randn(1, 3 * L, 24, 128, generator=g).to(torch.bfloat16)
+        cv = torch.randn(1, 3 * L, 24, 128, generator=g).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            blk(x, e=e, seq_lens=torch.tensor([3 * L]), grid_sizes=torch.tensor([[3, 36, 64]]),
+                freqs=freqs, context=ctx, context_lens=None, temporal_offset=3, is_stream=True,
+                pre_cache_k=ck, pre_cache_v=cv, kv_len=9)
+        return time.perf_counter() - t0, torch.get_num_threads(), "reference"
+    from oracle import block as oblock
+    from oracle import numerics as onum
+    F = 14336
     r = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16)  # noqa: E731
     wts = {}
     for m in ("self_attn", "cross_attn"):
@@ -396,7 +546,6 @@ def cpu_block_sample(args, seed=0):
     wts["ffn.0.weight"], wts["ffn.0.bias"] = r(F, D), r(F)
     wts["ffn.2.weight"], wts["ffn.2.bias"] = r(D, F), r(D)
     wts["modulation"] = torch.randn(1, 6, D, generator=g) / D ** 0.5
-    L = 36 * 64
     x = torch.randn(3 * L, D, generator=g).to(torch.bfloat16)
     ctx = torch.randn(512, D, generator=g).to(torch.bfloat16)
     ck = torch.randn(3 * L, 24, 128, generator=g).to(torch.bfloat16)
@@ -409,7 +558,14 @@ def cpu_block_sample(args, seed=0):
         oblock.block_forward(wts, x, e0, ctx, grid=(3, 36, 64), freqs=freqs, t_offset=3,
                              cache_k=ck, cache_v=cv, kv_len=9, block_hw=bhw, radius_hw=rhw,
                              block_t=3, heads=24, linear="bf16")
-    return time.perf_counter() - t0, torch.get_num_threads()
+    return time.perf_counter() - t0, torch.get_num_threads(), "port"
+
+
+CPU_SAMPLE = {
+    "reference": "the reference's own WanAttentionBlock.forward (bf16 Linears, window "
+                 "attention on its CPU gather + SDPA backend)",
+    "port": "the CPU restatement of WanAttentionBlock (bf16 Linears, fp32 window softmax)",
+}
 
 
 def cpu_value(block_s, layers=30):
@@ -422,8 +578,9 @@ def run_reference_arm(args, rank):
         return
     times = []
     cores = 1
+    kind = "port"
     for i in range(args.warmup + args.steps):
-        t, cores = cpu_block_sample(args, seed=i)
+        t, cores, kind = cpu_block_sample(args, seed=i)
         if i >= args.warmup:
             times.append(t)
     blk = statistics.mean(times)
@@ -436,10 +593,9 @@ def run_reference_arm(args, rank):
             "chunk_ms_extrapolated": 1e3 * FRAMES_PER_STEP / val, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": workload_config(args),
-            "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": "one full-size SR-DiT block per step (CPU restatement "
-                                       "of WanAttentionBlock, bf16 Linears), x60 for the "
-                                       "2-forward chunk"},
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": f"one full-size SR-DiT block per step: {CPU_SAMPLE[kind]}; "
+                                       f"x60 for the 2-forward chunk"},
             "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -681,11 +837,11 @@ def run_gpu_arm(args, rank, world, local):
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        t, cores = cpu_block_sample(args)
+        t, cores, kind = cpu_block_sample(args)
         line["cpu_baseline"] = {"value": cpu_value(t), "unit": UNIT, "cores": cores,
-                                "kind": "port",
-                                "sample": f"one full-size block on the host ({t:.2f} s), x60 "
-                                          f"for the 2-forward chunk"}
+                                "kind": kind,
+                                "sample": f"one full-size block on the host ({t:.2f} s): "
+                                          f"{CPU_SAMPLE[kind]}; x60 for the 2-forward chunk"}
     print(json.dumps(line), flush=True)
 
 
