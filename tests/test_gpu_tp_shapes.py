@@ -122,3 +122,61 @@ def test_row_reduce(srdit, cuda_device, K):
     am = srdit.ops.row_reduce(x.to(cuda_device), "absmax").cpu()
     np.testing.assert_allclose(ss.numpy(), x.float().pow(2).sum(-1).numpy(), rtol=1e-5)
     np.testing.assert_array_equal(am.numpy(), x.float().abs().amax(-1).numpy())
+
+
+@pytest.mark.parametrize("world,rank,M,affine", [(1, 0, 1000, False), (2, 1, 3456, False),
+                                                 (8, 5, 864, False), (8, 0, 1001, True),
+                                                 (4, 3, 7, True), (2, 0, 6913, False)])
+def test_ln_mod_quant_allgather_local_ranks(srdit, cuda_device, world, rank, M, affine):
+    """The LN-modulate-quantise all-gather with every rank's gather buffer on this
+    GPU: the rank's rows (a block of M rows at row rank * M) must land in all
+    `world` buffers byte-equal to the single-GPU kernel's, the row scales too, and
+    every other rank's flag word must count the launch once (none for the rank
+    itself). At 3456 and 6913 rows each CTA runs several row groups, so its two
+    staging buffers are reused while earlier copies may be in flight."""
+    K = 3072
+    g = torch.Generator().manual_seed(world * 100 + M)
+    x = (torch.randn(M, K, generator=g) * 2 + 0.3).to(torch.bfloat16)
+    shift = scale = w = b = None
+    if affine:
+        w = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
+        b = (0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
+    else:
+        shift, scale = 0.1 * torch.randn(K, generator=g), 0.1 * torch.randn(K, generator=g)
+    dev = lambda t: None if t is None else t.to(cuda_device)  # noqa: E731
+    rows = world * M
+    q = [torch.zeros(rows, K, dtype=torch.uint8, device=cuda_device) for _ in range(world)]
+    s = [torch.zeros(rows, dtype=torch.float32, device=cuda_device) for _ in range(world)]
+    flags = [torch.zeros(8, dtype=torch.int32, device=cuda_device) for _ in range(world)]
+    done = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    qt, st, ft = srdit._lib.PeerPtrs(), srdit._lib.PeerPtrs(), srdit._lib.PeerPtrs()
+    for d in range(world):
+        qt.p[d] = q[d][rank * M:].data_ptr()
+        st.p[d] = s[d][rank * M:].data_ptr()
+        ft.p[d] = flags[d].data_ptr()
+    srdit.ops.ln_mod_quant_tp(dev(x), 1e-6, ln_weight=dev(w), ln_bias=dev(b), shift=dev(shift),
+                              scale=dev(scale), q_rows=qt, s_rows=st, flags=ft, done=done,
+                              rank=rank, world=world, ldq=K)
+    torch.cuda.synchronize()
+    # the single-GPU kernel runs the same arithmetic: its bytes are the reference
+    q1, s1 = srdit.ops.ln_mod_quant(dev(x), 1e-6, ln_weight=dev(w), ln_bias=dev(b),
+                                    shift=dev(shift), scale=dev(scale))
+    blk = slice(rank * M, (rank + 1) * M)
+    for d in range(world):
+        assert torch.equal(q[d][blk], q1.view(torch.uint8)), d
+        assert torch.equal(s[d][blk], s1), d
+        # nothing outside the rank's block is written
+        assert int(q[d].view(-1).count_nonzero()) == int(q[d][blk].view(-1).count_nonzero())
+        want = [0] * 8
+        if d != rank:
+            want[rank] = 1
+        assert flags[d].cpu().tolist() == want, (d, flags[d])
+    assert int(done.item()) == 0
+    # and the oracle: the LN statistics are reduced in another order than torch's
+    # CPU kernel, so at thousands of rows a bf16 tie can move a row's amax by one
+    # ulp and rescale that row's bytes (measured up to 4.3e-4 on these inputs)
+    n = onum.layer_norm(x, 1e-6, w, b)
+    if not affine:
+        n = (n.float() * (1 + scale) + shift).to(torch.bfloat16)
+    qo, so = onum.quantize_rowwise(n)
+    assert onum.rel_fro(q1.float().cpu() * s1.cpu()[:, None], qo.float() * so) < 1e-3
