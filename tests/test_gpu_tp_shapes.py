@@ -132,8 +132,8 @@ def test_ln_mod_quant_allgather_local_ranks(srdit, cuda_device, world, rank, M, 
     GPU: the rank's rows (a block of M rows at row rank * M) must land in all
     `world` buffers byte-equal to the single-GPU kernel's, the row scales too, and
     every other rank's flag word must count the launch once (none for the rank
-    itself). At 3456 and 6913 rows each CTA runs several row groups, so its two
-    staging buffers are reused while earlier copies may be in flight."""
+    itself). At 3456 and 6913 rows each CTA of the persistent grid runs several
+    row groups."""
     K = 3072
     g = torch.Generator().manual_seed(world * 100 + M)
     x = (torch.randn(M, K, generator=g) * 2 + 0.3).to(torch.bfloat16)
