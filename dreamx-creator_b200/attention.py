@@ -134,22 +134,33 @@ def run_blockgrid_b200(q, k_ext, v_ext, out, *, plan, f_cur, h, w, n, d, anchor_
     L = h * w
     if q.numel() != f_cur * L * n * d or out.shape != q.shape:
         raise ValueError("q/out must be [f_cur*h*w, n, d]")
-    qf, of = q.view(-1, n * d), out.view(-1, n * d)
     kf, vf = k_ext.view(-1, n * d), v_ext.view(-1, n * d)
     if kf.shape != vf.shape or kf.shape[0] < hr_base or (kf.shape[0] - hr_base) % L:
         raise ValueError("k_ext/v_ext must hold the anchor prefix plus whole HR frames")
-    k_hr, v_hr = kf[hr_base:], vf[hr_base:]
-    kv_frames = k_hr.shape[0] // L
     ka = va = None
-    a_hw = None
-    a_frames = 0
     if anchor_mode is not None and hr_base > 0:
         ka, va = kf[:hr_base], vf[:hr_base]
+    _launch(q.view(-1, n * d), kf[hr_base:], vf[hr_base:], out.view(-1, n * d), plan=plan,
+            f_cur=f_cur, h=h, w=w, n=n, d=d, anchor_mode=anchor_mode, ka=ka, va=va,
+            status=status)
+    return out
+
+
+def _launch(qf, k_hr, v_hr, of, *, plan, f_cur, h, w, n, d, anchor_mode, ka=None, va=None,
+            status=None):
+    """The kernel launch on [tokens, n*d] row views: the HR K/V (whole frames) and,
+    for an anchored plan, the anchor K/V as separate tensors (the kernel reads
+    each through its own tensor maps, so they need not be concatenated)."""
+    L = h * w
+    kv_frames = k_hr.shape[0] // L
+    a_hw = None
+    a_frames = 0
+    if ka is not None:
         p0 = plan["params"][0]
         a_hw = (int(p0[-2]), int(p0[-1]))
-        a_frames = hr_base // (a_hw[0] * a_hw[1])
+        a_frames = ka.shape[0] // (a_hw[0] * a_hw[1])
     params_dev, tiling, n_w, mode, split_dev = _plan_device_state(
-        plan, q.device, anchor_mode, (f_cur, h, w, kv_frames, a_hw, a_frames),
+        plan, qf.device, anchor_mode, (f_cur, h, w, kv_frames, a_hw, a_frames),
         dict(f_cur=f_cur, h=h, w=w, kv_frames=kv_frames, a_hw=a_hw, a_frames=a_frames))
     g = _geom(qf, k_hr, f_cur=f_cur, h=h, w=w, n=n, d=d, kv_frames=kv_frames, anchor=ka, a_hw=a_hw)
     g.o_stride = of.stride(0)
@@ -157,7 +168,6 @@ def run_blockgrid_b200(q, k_ext, v_ext, out, *, plan, f_cur, h, w, n, d, anchor_
     ops.winattn(qf, k_hr, v_hr, of, params_dev=params_dev, n_w=n_w,
                 p_stride=int(plan["p_stride"]), anchor_mode=mode, geom=g, tiling=tiling,
                 k_anchor=ka, v_anchor=va, status=status)
-    return out
 
 
 _PLAN_CACHE: dict = {}
@@ -283,15 +293,20 @@ def mask_free_window_attention(q, k, v, grid_sizes, pre_cache_k=None, pre_cache_
                                    anchor_hw=a_hw if anchor_given else None)
         mode = None if not use_anchor else ("frame" if anchor_align == "frame" else "chunk")
         plan = cached_plan(spec, mode)
+        if d != 128:
+            raise _lib.SrditError(f"the B200 window kernel supports head_dim 128, got {d}")
         q_i = q[i].contiguous()
         out_i = torch.empty_like(q_i)
+        # the anchor goes to the kernel as its own tensors: no cat([anchor, HR])
+        # copy of the whole window K/V, which the reference's launcher layout needs
+        ka = va = None
         if use_anchor:
-            k_ext = torch.cat([anchor_k[i], full_k], dim=0)
-            v_ext = torch.cat([anchor_v[i], full_v], dim=0)
-        else:
-            k_ext, v_ext = full_k.contiguous(), full_v.contiguous()
-        run_blockgrid_b200(q_i, k_ext, v_ext, out_i, plan=plan, f_cur=f_cur, h=h, w=w, n=n,
-                           d=d, anchor_mode=mode)
+            ka = anchor_k[i].contiguous().view(-1, n * d)
+            va = anchor_v[i].contiguous().view(-1, n * d)
+        k_hr = full_k.contiguous().view(-1, n * d)
+        v_hr = full_v.contiguous().view(-1, n * d)
+        _launch(q_i.view(-1, n * d), k_hr, v_hr, out_i.view(-1, n * d), plan=plan, f_cur=f_cur,
+                h=h, w=w, n=n, d=d, anchor_mode=mode, ka=ka, va=va)
         outs.append(out_i)
         ck, cv = _truncate(full_k, full_v, kv_len, L, f_kv)
         cks.append(ck)
