@@ -776,25 +776,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                        ((m >> (i + 3)) & 1u) ? __uint_as_float(u[i + 3]) : neg_inf);
           }
         };
+        // Both passes walk the chunks two at a time in a rolled loop (one copy of
+        // each chunk body, the next chunk's load in flight): unrolled four
+        // times, the chunk code cost instruction fetch more than the loop costs.
         if (active) {  // nchunks is warp-uniform (tcgen05.ld is warp-collective)
           uint32_t ua[32], ub[32];
           tmem_ld32(s_tmem, ua);
-          tmem_ld_wait();
-          if (nchunks > 1) tmem_ld32(s_tmem + 32, ub);
-          chunk_max(ua, vm[0]);
-          if (nchunks > 1) {
+#pragma unroll 1
+          for (int qq = 0; qq < nchunks; qq += 2) {
             tmem_ld_wait();
-            if (nchunks > 2) tmem_ld32(s_tmem + 64, ua);
-            chunk_max(ub, vm[1]);
-          }
-          if (nchunks > 2) {
-            tmem_ld_wait();
-            if (nchunks > 3) tmem_ld32(s_tmem + 96, ub);
-            chunk_max(ua, vm[2]);
-          }
-          if (nchunks > 3) {
-            tmem_ld_wait();
-            chunk_max(ub, vm[3]);
+            if (qq + 1 < nchunks) tmem_ld32(s_tmem + 32 * (qq + 1), ub);
+            chunk_max(ua, qq == 0 ? vm[0] : vm[2]);
+            if (qq + 1 < nchunks) {
+              tmem_ld_wait();
+              if (qq + 2 < nchunks) tmem_ld32(s_tmem + 32 * (qq + 2), ua);
+              chunk_max(ub, qq == 0 ? vm[1] : vm[3]);
+            }
           }
           pmax = fmaxf(m0, m1);
         }
@@ -826,28 +823,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (active) {
           uint32_t ua[32], ub[32];
           tmem_ld32(s_tmem, ua);
-          tmem_ld_wait();
-          if (nchunks > 1) tmem_ld32(s_tmem + 32, ub);
-          chunk_exp(ua, vm[0], 0);
-          if (nchunks > 1) {
-            tmem_ld_wait();
-            if (nchunks > 2) tmem_ld32(s_tmem + 64, ua);
-            chunk_exp(ub, vm[1], 1);
-          } else {
-            chunk_exp(ub, 0u, 1);  // columns past the tile: P = 0 (masks are all off)
-          }
-          if (nchunks > 2) {
-            tmem_ld_wait();
-            if (nchunks > 3) tmem_ld32(s_tmem + 96, ub);
-            chunk_exp(ua, vm[2], 2);
-          } else {
-            chunk_exp(ua, 0u, 2);
-          }
-          if (nchunks > 3) {
-            tmem_ld_wait();
-            chunk_exp(ub, vm[3], 3);
-          } else {
-            chunk_exp(ub, 0u, 3);
+          // chunks past the tile run too, with their masks 0: their P is written as 0
+#pragma unroll 1
+          for (int qq = 0; qq < 4; qq += 2) {
+            if (qq < nchunks) tmem_ld_wait();
+            if (qq + 1 < nchunks) tmem_ld32(s_tmem + 32 * (qq + 1), ub);
+            chunk_exp(ua, qq == 0 ? vm[0] : vm[2], qq);
+            if (qq + 1 < nchunks) tmem_ld_wait();
+            if (qq + 2 < nchunks) tmem_ld32(s_tmem + 32 * (qq + 2), ua);
+            chunk_exp(ub, qq == 0 ? vm[1] : vm[3], qq + 1);
           }
           tmem_st_wait();
         }
