@@ -310,6 +310,14 @@ def reference_winattn(args, srdit, dev, timeit, fkv, bhw, rhw, flops, peaks):
         o_b = op()
     finally:
         ref_attn._run_blockgrid_triton = stock
+
+    def dropin():
+        return srdit.attention.mask_free_window_attention(
+            q, k, v, grid, pre_cache_k=ck, pre_cache_v=cv, kv_len=f_cache, attn_impl="b200",
+            block_t=3, block_hw=bhw, block_radius_hw=rhw)[0]
+
+    t_dropin = timeit(dropin)
+    o_d = dropin()
     torch.cuda.synchronize()
     return {
         "source": "reference installed under baseline/_ref (blockgrid_triton.py, attention.py)",
@@ -319,6 +327,9 @@ def reference_winattn(args, srdit, dev, timeit, fkv, bhw, rhw, flops, peaks):
         "max_abs_diff": diff.max().item(), "rel_fro_diff": rel,
         "op_ms_triton": t_op_ref, "op_ms_b200": t_op_b, "op_speedup": t_op_ref / t_op_b,
         "op_max_abs_diff": (o_b.float() - o_ref.float()).abs().max().item(),
+        # this repository's drop-in op (cache and chunk as two K/V segments, no cat)
+        "dropin_op_ms": t_dropin, "dropin_op_speedup": t_op_ref / t_dropin,
+        "dropin_max_abs_diff": (o_d.float() - o_ref.float()).abs().max().item(),
     }
 
 

@@ -31,7 +31,8 @@ class WinattnGeom(ctypes.Structure):
                 ("a_frames", c_int), ("a_h", c_int), ("a_w", c_int),
                 ("n_heads", c_int), ("head_dim", c_int),
                 ("q_stride", c_ll), ("kv_stride", c_ll), ("a_stride", c_ll),
-                ("o_stride", c_ll), ("scale", c_float), ("col_split", c_vp)]
+                ("o_stride", c_ll), ("scale", c_float), ("col_split", c_vp),
+                ("k_hr2", c_vp), ("v_hr2", c_vp), ("kv_split", c_int)]
 
 
 class WinattnTiling(ctypes.Structure):

@@ -147,12 +147,24 @@ def run_blockgrid_b200(q, k_ext, v_ext, out, *, plan, f_cur, h, w, n, d, anchor_
 
 
 def _launch(qf, k_hr, v_hr, of, *, plan, f_cur, h, w, n, d, anchor_mode, ka=None, va=None,
-            status=None):
+            k_hr2=None, v_hr2=None, status=None):
     """The kernel launch on [tokens, n*d] row views: the HR K/V (whole frames) and,
     for an anchored plan, the anchor K/V as separate tensors (the kernel reads
-    each through its own tensor maps, so they need not be concatenated)."""
+    each through its own tensor maps, so they need not be concatenated).
+    ``k_hr2`` / ``v_hr2``: an optional second HR segment holding the frames that
+    follow ``k_hr``'s (a cache and the current chunk in separate buffers)."""
     L = h * w
     kv_frames = k_hr.shape[0] // L
+    seg1 = kv_frames
+    if k_hr2 is not None:
+        for t in (k_hr2, v_hr2):
+            if (t is None or t.dtype != torch.bfloat16 or t.device != k_hr.device
+                    or t.stride() != k_hr.stride() or t.shape[1] != k_hr.shape[1]):
+                raise _lib.SrditError("the second K/V segment must match the first's "
+                                      "dtype, device, width and token stride")
+        if k_hr2.shape != v_hr2.shape or k_hr2.shape[0] % L:
+            raise ValueError("the second K/V segment must hold whole frames")
+        kv_frames += k_hr2.shape[0] // L
     a_hw = None
     a_frames = 0
     if ka is not None:
@@ -165,6 +177,8 @@ def _launch(qf, k_hr, v_hr, of, *, plan, f_cur, h, w, n, d, anchor_mode, ka=None
     g = _geom(qf, k_hr, f_cur=f_cur, h=h, w=w, n=n, d=d, kv_frames=kv_frames, anchor=ka, a_hw=a_hw)
     g.o_stride = of.stride(0)
     g.col_split = None if split_dev is None else split_dev.data_ptr()
+    if k_hr2 is not None:
+        g.k_hr2, g.v_hr2, g.kv_split = k_hr2.data_ptr(), v_hr2.data_ptr(), seg1
     ops.winattn(qf, k_hr, v_hr, of, params_dev=params_dev, n_w=n_w,
                 p_stride=int(plan["p_stride"]), anchor_mode=mode, geom=g, tiling=tiling,
                 k_anchor=ka, v_anchor=va, status=status)
@@ -219,11 +233,18 @@ def install(attention_module) -> None:
     attention_module._run_blockgrid_triton = run_blockgrid_b200
 
 
-def _truncate(full_k, full_v, kv_len, L, f_kv):
-    if kv_len is None or f_kv <= kv_len:
-        return full_k, full_v
-    keep = int(kv_len) * L
-    return full_k[-keep:], full_v[-keep:]
+def _new_cache(ck, cv, k, v, kv_len, L):
+    """The returned cache: the last ``kv_len`` frames of cat([cache, chunk]) (all of
+    them when kv_len is None), as the reference returns it (attention.py:964-974).
+    It is a view of the chunk when the chunk alone covers it; otherwise only the
+    frames kept are copied."""
+    total = k.shape[0] + (ck.shape[0] if ck is not None else 0)
+    keep = total if kv_len is None else min(total, int(kv_len) * L)
+    if ck is None or keep <= k.shape[0]:
+        return k[k.shape[0] - keep:], v[v.shape[0] - keep:]
+    tail = keep - k.shape[0]
+    return (torch.cat([ck[ck.shape[0] - tail:], k], dim=0),
+            torch.cat([cv[cv.shape[0] - tail:], v], dim=0))
 
 
 def mask_free_window_attention(q, k, v, grid_sizes, pre_cache_k=None, pre_cache_v=None,
@@ -256,13 +277,10 @@ def mask_free_window_attention(q, k, v, grid_sizes, pre_cache_k=None, pre_cache_
         if f_cur * h * w != s_cur:
             raise ValueError(f"grid {(f_cur, h, w)} inconsistent with s_cur={s_cur}")
         L = h * w
-        if pre_cache_k is not None and pre_cache_v is not None:
-            full_k = torch.cat([pre_cache_k[i], k[i]], dim=0)
-            full_v = torch.cat([pre_cache_v[i], v[i]], dim=0)
-        else:
-            full_k, full_v = k[i], v[i]
-        f_kv = full_k.shape[0] // L
-        if f_kv * L != full_k.shape[0]:
+        cached = pre_cache_k is not None and pre_cache_v is not None
+        kv_tokens = k.shape[1] + (pre_cache_k.shape[1] if cached else 0)
+        f_kv = kv_tokens // L
+        if f_kv * L != kv_tokens or (cached and pre_cache_k.shape[1] % L):
             raise ValueError("KV cache is not aligned to whole frames")
         a_hw = None if anchor_hw is None or tuple(int(x) for x in anchor_hw) == (h, w) \
             else (int(anchor_hw[0]), int(anchor_hw[1]))
@@ -303,12 +321,22 @@ def mask_free_window_attention(q, k, v, grid_sizes, pre_cache_k=None, pre_cache_
         if use_anchor:
             ka = anchor_k[i].contiguous().view(-1, n * d)
             va = anchor_v[i].contiguous().view(-1, n * d)
-        k_hr = full_k.contiguous().view(-1, n * d)
-        v_hr = full_v.contiguous().view(-1, n * d)
+        # the cached frames and the current chunk go to the kernel as two K/V
+        # segments: no cat([cache, chunk]) copy for the attention itself
+        k_cur = k[i].contiguous().view(-1, n * d)
+        v_cur = v[i].contiguous().view(-1, n * d)
+        k2 = v2 = None
+        if cached and pre_cache_k.shape[1] > 0:
+            k_hr = pre_cache_k[i].contiguous().view(-1, n * d)
+            v_hr = pre_cache_v[i].contiguous().view(-1, n * d)
+            k2, v2 = k_cur, v_cur
+        else:
+            k_hr, v_hr = k_cur, v_cur
         _launch(q_i.view(-1, n * d), k_hr, v_hr, out_i.view(-1, n * d), plan=plan, f_cur=f_cur,
-                h=h, w=w, n=n, d=d, anchor_mode=mode, ka=ka, va=va)
+                h=h, w=w, n=n, d=d, anchor_mode=mode, ka=ka, va=va, k_hr2=k2, v_hr2=v2)
         outs.append(out_i)
-        ck, cv = _truncate(full_k, full_v, kv_len, L, f_kv)
+        ck, cv = _new_cache(pre_cache_k[i] if cached else None,
+                            pre_cache_v[i] if cached else None, k[i], v[i], kv_len, L)
         cks.append(ck)
         cvs.append(cv)
     out = torch.stack(outs, dim=0)

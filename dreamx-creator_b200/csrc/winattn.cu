@@ -82,6 +82,7 @@ struct Args {
   float scale;
   uint32_t* status;
   const int32_t* split;  // optional [n_w, SRDIT_SPLIT_FIELDS]: rows that pair two windows
+  int kv_split;          // > 0: ring slots [kv_split, kv_slots) come from tmK2 / tmV2
 };
 
 struct Row {
@@ -307,7 +308,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap tmV,
                    const __grid_constant__ CUtensorMap tmKA,
                    const __grid_constant__ CUtensorMap tmVA,
-                   const __grid_constant__ CUtensorMap tmO, const Args a) {
+                   const __grid_constant__ CUtensorMap tmO,
+                   const __grid_constant__ CUtensorMap tmK2,
+                   const __grid_constant__ CUtensorMap tmV2, const Args a) {
   pdl_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -478,8 +481,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               } else {
                 c1 = r.kw0;
                 c2 = r.kh0 + hc * ti.bh;
-                c3 = slot;
-                map = kv ? &tmV : &tmK;
+                // a caller's second K/V segment (its current chunk) holds the
+                // slots from kv_split on, at frame slot - kv_split
+                if (a.kv_split > 0 && slot >= a.kv_split) {
+                  c3 = slot - a.kv_split;
+                  map = kv ? &tmV2 : &tmK2;
+                } else {
+                  c3 = slot;
+                  map = kv ? &tmV : &tmK;
+                }
                 if (++hc == w.hr_hchunks) {
                   hc = 0;
                   if (++slot == a.kv_slots) slot = 0;
@@ -1464,6 +1474,10 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
   if (p_stride != (frame_mode ? SRDIT_P_FRAME : SRDIT_P_PLAIN)) return SRDIT_EINVAL;
   if (t->has_anchor && (!k_anchor || !v_anchor || g->a_frames <= 0)) return SRDIT_EINVAL;
   if (g->kv_slots <= 0 || g->kv_slot0 < 0) return SRDIT_EINVAL;
+  const bool two_seg = g->k_hr2 != nullptr || g->v_hr2 != nullptr;
+  if (two_seg && (!g->k_hr2 || !g->v_hr2 || g->kv_split <= 0 || g->kv_split >= g->kv_slots))
+    return SRDIT_EINVAL;
+  if (!two_seg && g->kv_split != 0) return SRDIT_EINVAL;
   if (g->q_frames <= 0 || g->q_h <= 0 || g->q_w <= 0 || g->kv_h <= 0 || g->kv_w <= 0)
     return SRDIT_EINVAL;
   // a TMA box never exceeds the tensor it reads
@@ -1477,7 +1491,7 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
     return SRDIT_EINVAL;
 
   const long long C = static_cast<long long>(g->n_heads) * attn::D;
-  CUtensorMap mq, mk, mv, mka, mva;
+  CUtensorMap mq, mk, mv, mka, mva, mk2, mv2;
   {
     const long long dims[4] = {C, g->q_w, g->q_h, g->q_frames};
     const long long st[3] = {g->q_stride * 2, g->q_stride * 2 * g->q_w,
@@ -1487,7 +1501,8 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
     if (rc) return rc;
   }
   {
-    const long long dims[4] = {C, g->kv_w, g->kv_h, g->kv_slots};
+    // the first segment holds slots [0, kv_split) when a second one is given
+    const long long dims[4] = {C, g->kv_w, g->kv_h, two_seg ? g->kv_split : g->kv_slots};
     const long long st[3] = {g->kv_stride * 2, g->kv_stride * 2 * g->kv_w,
                              g->kv_stride * 2 * g->kv_w * g->kv_h};
     const int box[4] = {64, t->bw_k, t->bh_k, 1};
@@ -1495,6 +1510,16 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
     if (rc) return rc;
     rc = make_tmap_4d(&mv, v_hr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, st, box);
     if (rc) return rc;
+    if (two_seg) {
+      const long long dims2[4] = {C, g->kv_w, g->kv_h, g->kv_slots - g->kv_split};
+      rc = make_tmap_4d(&mk2, g->k_hr2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims2, st, box);
+      if (rc) return rc;
+      rc = make_tmap_4d(&mv2, g->v_hr2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims2, st, box);
+      if (rc) return rc;
+    } else {
+      mk2 = mk;  // never read: kv_split 0
+      mv2 = mv;
+    }
   }
   if (t->has_anchor) {
     const long long dims[4] = {C, g->a_w, g->a_h, g->a_frames};
@@ -1552,6 +1577,7 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
   a.scale = g->scale;
   a.status = status;
   a.split = g->col_split;
+  a.kv_split = two_seg ? g->kv_split : 0;
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1574,9 +1600,9 @@ extern "C" int srdit_winattn_fwd(const void* q, const void* k_hr, const void* v_
   dim3 grid(static_cast<unsigned>(items < sms ? items : sms));
   if (t->split_kv)
     SRDIT_LAUNCH((attn::winattn_kernel<true>), grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream, 
-        mq, mk, mv, mka, mva, mo, a);
+        mq, mk, mv, mka, mva, mo, mk2, mv2, a);
   else
     SRDIT_LAUNCH((attn::winattn_kernel<false>), grid, attn::NUM_THREADS, attn::SMEM_BYTES, stream, 
-        mq, mk, mv, mka, mva, mo, a);
+        mq, mk, mv, mka, mva, mo, mk2, mv2, a);
   return static_cast<int>(cudaGetLastError());
 }

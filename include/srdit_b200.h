@@ -490,6 +490,14 @@ typedef struct srdit_winattn_geom {
    * [an_lo_a, an_hi_a) (relative to kw0_a), B likewise. q_split 0: an
    * ordinary (unpaired) row. */
   const int32_t* col_split;
+  /* optional second HR K/V segment (NULL, kv_split 0: one segment). With
+   * k_hr2 / v_hr2 given, ring slots [0, kv_split) are read from k_hr / v_hr and
+   * slots [kv_split, kv_slots) from frame (slot - kv_split) of k_hr2 / v_hr2
+   * (same token stride kv_stride): a caller whose cached frames and current
+   * chunk sit in separate buffers passes both, with no concatenation. */
+  const void* k_hr2;
+  const void* v_hr2;
+  int kv_split;
 } srdit_winattn_geom;
 
 #define SRDIT_SPLIT_FIELDS 9
@@ -518,7 +526,8 @@ int srdit_winattn_plan(const int32_t* params_host, int n_w, int p_stride, int an
  * one CTA per (window, 128-row query tile, head). q/out are token-major
  * [q_frames*q_h*q_w, heads*128] (token stride q_stride / o_stride); k_hr/v_hr
  * hold kv_slots frames of kv_h*kv_w tokens (window frame f lives in slot
- * (kv_slot0 + f) % kv_slots); k_anchor/v_anchor hold the LQ anchor (may be NULL
+ * (kv_slot0 + f) % kv_slots), or the slots below geom->kv_split when the
+ * geometry gives a second segment; k_anchor/v_anchor hold the LQ anchor (may be NULL
  * without an anchor). params_dev: the plan's int32 rows on the device.
  * Replaces: run_blockgrid_triton (video_refiner/wan/modules/sr_dit/blockgrid_triton.py:392-422)
  *   launching _blockgrid_fused_kernel (:184-278) / _blockgrid_fused_frame_kernel (:281-389).
