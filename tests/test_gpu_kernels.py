@@ -258,6 +258,44 @@ def test_winattn_reference_plans(srdit, cuda_device, golden, geom):
     _check_attn(out, ref)
 
 
+def test_winattn_two_kv_segments_ring(srdit, cuda_device):
+    """srdit_winattn_fwd with its K/V ring split over two buffers (slots below
+    kv_split in the first, the rest in the second), the window's frames starting
+    past the split and wrapping round the ring: the same bytes as one buffer
+    holding the whole ring."""
+    att = srdit.attention
+    h, w, n, d = 8, 12, 2, 128
+    L, f_cur, f_kv, slots, slot0, split = h * w, 3, 6, 7, 5, 4
+    spec = srdit.blockgrid.make_spec(f_cur=f_cur, f_kv=f_kv, h=h, w=w, block_t=3,
+                                     block_hw=(4, 4), block_radius_hw=(1, 1), streaming=True)
+    plan = att.cached_plan(spec)
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(f_cur * L, n * d, generator=g).to(torch.bfloat16).to(cuda_device)
+    ring_k = torch.randn(slots * L, n * d, generator=g).to(torch.bfloat16).to(cuda_device)
+    ring_v = torch.randn(slots * L, n * d, generator=g).to(torch.bfloat16).to(cuda_device)
+    params_dev, tiling, n_w, mode, split_dev = att._plan_device_state(
+        plan, cuda_device, None, ("two_seg", f_kv),
+        dict(f_cur=f_cur, h=h, w=w, kv_frames=f_kv, a_hw=None, a_frames=0))
+    outs = []
+    for two in (False, True):
+        k1 = ring_k[:split * L] if two else ring_k
+        v1 = ring_v[:split * L] if two else ring_v
+        geo = att._geom(q, k1, f_cur=f_cur, h=h, w=w, n=n, d=d, kv_frames=slots, kv_slot0=slot0)
+        geo.col_split = None if split_dev is None else split_dev.data_ptr()
+        if two:
+            geo.k_hr2 = ring_k[split * L:].data_ptr()
+            geo.v_hr2 = ring_v[split * L:].data_ptr()
+            geo.kv_split = split
+        out = torch.zeros_like(q)
+        srdit.ops.winattn(q, k1, v1, out, params_dev=params_dev, n_w=n_w,
+                          p_stride=int(plan["p_stride"]), anchor_mode=mode, geom=geo,
+                          tiling=tiling)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert outs[0].abs().sum() > 0
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+
+
 def test_winattn_deterministic(srdit, cuda_device):
     ins = {k: v.to(torch.bfloat16) for k, v in stream_inputs().items()}
     d = lambda t: t[None].to(cuda_device)  # noqa: E731
